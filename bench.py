@@ -1,0 +1,387 @@
+"""Benchmark of threadcut's decode hot path on B200: split-KV GQA flash-decode µs/layer and % of HBM
+peak at 16k context (BASELINE metric), plus the RoPE-shift splice GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = decode attention for all 36 Qwen3-4B layers (one query token, 32 q / 8 KV heads,
+head_dim 128, bf16) over a 16384-token cache, every layer its own K/V buffer (36 x 67 MB = 2.4 GB
+per step, far above the 126 MB L2, so no flush is needed). `value` is µs per layer (device time,
+CUDA events, the 36 launches replayed from a CUDA graph), max over ranks; with N GPUs every rank
+runs its own 36 layers (weak scaling, no collective on the data path) and value = time / (36*N).
+`e2e` is the same metric through the public API (`threadcut_b200.flash_decode.decode_attention`,
+one Python call per layer) with each step's queries copied host->device from pinned memory and the
+outputs read back device->host inside the timed region.
+`--impl reference` times the reference's CPU path (the numpy restatement in oracle/, fp32, all host
+threads) on the same workload and prints the same line with "impl": "reference".
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import workloads  # noqa: E402
+
+METRIC = "flash-decode µs/layer & % of HBM peak (Qwen3-4B GQA, 16k ctx); shift GB/s"
+N_CTX = 16384
+LAYERS = workloads.LAYERS
+BYTES_PER_LAYER = 4096 * N_CTX + 16384          # K+V (2*8*n*128*2 B) + q + o
+SHIFT_BYTES_PER_LAYER = 4 * 4096 * 8 * 128 * 2  # K read+write and V read+write of |C| = 4096 rows
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks during the timed region
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.join(HERE, "gpurun_out"), exist_ok=True)
+            self.path = os.path.join(HERE, "gpurun_out", f"clocks_gpu{self.index}.csv")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        if args.impl == "reference":
+            return rank, local, world, None
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return rank, local, world, dist
+    if args.impl != "reference":
+        torch.cuda.set_device(0)
+    return 0, 0, 1, None
+
+
+def max_over_ranks(x, dist):
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------ our arm
+def build_layers(n, layers, dev, seed):
+    ks, vs = workloads.layer_kv(n, layers, dev, seed=seed)
+    g = torch.Generator(device=dev).manual_seed(seed + 1)
+    qs = [torch.randn(8, 4, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    return qs, ks, vs
+
+
+def capture_step(qs, ks, vs, outs, dev):
+    """CUDA graph of one step: the 36 decode launches through the C ABI with preallocated outputs."""
+    from threadcut_b200._lib import TC_BF16, check, lib, workspaces
+    L = lib()
+    n = ks[0].shape[1]
+    ws = workspaces.get("decode", dev, L.tc_decode_attention_workspace_size(1, 8, 4, 128, n, n, 0, TC_BF16))
+
+    def launch_all():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        for q, k, v, o in zip(qs, ks, vs, outs):
+            rc = L.tc_decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 4, 128, n,
+                                       q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+                                       o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16, ws.data_ptr(),
+                                       ws.numel(), st)
+            check("tc_decode_attention", rc)
+
+    launch_all()  # eager warm-up (also sets the kernels' shared-memory attributes)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    return graph
+
+
+def time_graph(graph, steps, warmup, dist):
+    for _ in range(warmup):
+        graph.replay()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    barrier(dist)
+    return e0.elapsed_time(e1) / steps  # ms per step on this rank
+
+
+def time_e2e(qs, ks, vs, steps, warmup, dist, dev):
+    """Public-API path: pinned host queries -> device, 36 decode_attention calls, outputs -> host."""
+    from threadcut_b200.flash_decode import decode_attention
+    host_q = torch.stack([q.cpu() for q in qs]).pin_memory()
+    host_out = torch.empty_like(host_q).pin_memory()
+    dq = torch.empty_like(host_q, device=dev)
+
+    def step():
+        dq.copy_(host_q, non_blocking=True)
+        outs = [decode_attention(dq[i], ks[i], vs[i], workloads.SCALE) for i in range(len(ks))]
+        host_out.copy_(torch.stack(outs), non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    barrier(dist)
+    return e0.elapsed_time(e1) / steps, host_q.numel() * host_q.element_size(), host_out.numel() * 2
+
+
+def time_shift(steps, warmup, dev, dist):
+    """Config 2 splice (Split(2048, 4096, 4096) of an 8192-token cache) on all 36 layers, one launch
+    per step, in place; returns ms per launch."""
+    from threadcut_b200.kv import splice, new_cache
+    from threadcut_b200.match import Split
+    from transformers import Qwen3Config
+    cfg = Qwen3Config(num_hidden_layers=LAYERS, num_key_value_heads=8, head_dim=128)
+    cache = new_cache(cfg)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for layer in cache.layers:
+        k = torch.randn(1, 8, workloads.CFG2_N, 128, generator=g, device=dev).to(torch.bfloat16)
+        layer.update(k, k.clone())
+    s = Split(*workloads.CFG2_SPLIT)
+    inv = workloads.inv_freq()
+
+    def run():
+        splice(cache, s, inv)
+        for layer in cache.layers:  # the next step splices the same rows again (same bytes moved)
+            layer.n = workloads.CFG2_N
+    for _ in range(warmup):
+        run()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    e1.synchronize()
+    barrier(dist)
+    return e0.elapsed_time(e1) / steps
+
+
+def cpu_reference_us_per_layer(seconds=10.0, layers_in_memory=4, max_layers=None):
+    """The reference's CPU path (oracle/ numpy restatement, fp32, all host threads) on 16k layers.
+    Returns (us per layer, layers timed, threads)."""
+    import numpy as np
+    from oracle.attention import decode_attention_ref
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"),
+                      default=os.cpu_count())
+    except Exception:  # threadpoolctl missing: numpy's BLAS uses every core by default
+        threads = os.cpu_count()
+    rng = np.random.default_rng(0)
+    bufs = [(rng.standard_normal((8, 4, 128), dtype=np.float32), rng.standard_normal((8, N_CTX, 128), dtype=np.float32),
+             rng.standard_normal((8, N_CTX, 128), dtype=np.float32)) for _ in range(layers_in_memory)]
+    decode_attention_ref(*bufs[0], workloads.SCALE, dtype=np.float32)  # warm-up
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        q, k, v = bufs[done % layers_in_memory]
+        decode_attention_ref(q, k, v, workloads.SCALE, dtype=np.float32)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_layers and done >= max_layers):
+            break
+    return el / done * 1e6, done, threads
+
+
+def run_ours(args, rank, local, world, dist):
+    dev = torch.device("cuda", local)
+    hbm, peak_kind = peaks()
+    qs, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
+    outs = [torch.empty_like(q) for q in qs]
+    graph = capture_step(qs, ks, vs, outs, dev)
+    with ClockSampler(local) as clk:
+        ms = time_graph(graph, args.steps, args.warmup, dist)
+    ms = max_over_ranks(ms, dist)
+    us_layer_rank = ms * 1000.0 / LAYERS  # one rank's launch duration (incl. back-to-back gaps)
+    value = ms * 1000.0 / (LAYERS * world)
+    achieved = BYTES_PER_LAYER / (us_layer_rank * 1e-6) / 1e9
+    e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev)
+    e2e_ms = max_over_ranks(e2e_ms, dist)
+    del graph
+    # context-length sweep of config 3 (same kernel, 4k and 32k), and the RoPE-shift splice
+    sweep = {}
+    for n in (4096, 32768):
+        q2, k2, v2 = build_layers(n, LAYERS, dev, seed=2000 + n)
+        o2 = [torch.empty_like(q) for q in q2]
+        g2 = capture_step(q2, k2, v2, o2, dev)
+        t = max_over_ranks(time_graph(g2, args.steps, args.warmup, dist), dist)
+        sweep[str(n)] = {"us_per_layer": round(t * 1000 / LAYERS, 3),
+                         "frac": round((4096 * n + 16384) / (t * 1e-3 / LAYERS) / 1e9 / hbm, 4)}
+        del g2, q2, k2, v2, o2
+    sweep[str(N_CTX)] = {"us_per_layer": round(us_layer_rank, 3), "frac": round(achieved / hbm, 4)}
+    torch.cuda.empty_cache()
+    shift_ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist), dist)
+    shift_gbs = SHIFT_BYTES_PER_LAYER * LAYERS / (shift_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        us, nl, thr = cpu_reference_us_per_layer(args.cpu_seconds)
+        cpu = {"value": round(us, 2), "unit": "us/layer", "cores": thr, "kind": "port",
+               "sample": f"{nl} layers of 16k decode (fp32 numpy restatement of the reference's folded SDPA, "
+                         f"4 distinct layer buffers cycled, ~{args.cpu_seconds:.0f}s)"}
+    traffic = None
+    tpath = os.path.join(HERE, "profiles", "decode_16k_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) K/V and queries",
+        "config": {"workload": "cfg3-16k: 36-layer split-KV GQA decode, n=16384, 32 q / 8 kv heads, head_dim 128, "
+                               "one K/V buffer per layer", "layers": LAYERS, "n": N_CTX, "batch": 1,
+                   "l2": "inputs larger than L2 (36 distinct 67 MB layers = 2.4 GB per step)",
+                   "parallelism": f"weak: every rank decodes its own 36 layers ({world} rank(s))"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "decode_mma_kernel<bf16,128,1>", "bytes_per_launch": BYTES_PER_LAYER},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms * 1000.0 / (LAYERS * world), 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "threadcut_b200.flash_decode.decode_attention"},
+        "gpu_launches": args.steps * LAYERS,
+        "clocks": clk.summary(),
+        "shift": {"value": round(shift_gbs, 1), "unit": "GB/s", "frac": round(shift_gbs / hbm, 4),
+                  "us_per_layer": round(shift_ms * 1000 / LAYERS, 3),
+                  "workload": "cfg2 splice Split(2048,4096,4096) of an 8192-token bf16 cache, 36 layers in one "
+                              "in-place launch; K rotated + V moved, read+write bytes"},
+        "cfg3_sweep": sweep,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    per_step = []
+    threads = os.cpu_count()
+    for i in range(args.warmup + args.steps):
+        us, nl, threads = cpu_reference_us_per_layer(seconds=1e9, max_layers=LAYERS)
+        if i >= args.warmup:
+            per_step.append(us * LAYERS / 1000.0)  # ms per 36-layer step
+    ms = statistics.mean(per_step)
+    value = ms * 1000.0 / LAYERS
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,1) K/V and queries",
+        "impl": "reference",
+        "config": {"workload": "cfg3-16k: 36-layer split-KV GQA decode, n=16384, 32 q / 8 kv heads, head_dim 128, "
+                               "one K/V buffer per layer", "layers": LAYERS, "n": N_CTX, "batch": 1,
+                   "parallelism": "rank 0 only (host CPU)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "us/layer", "cores": threads, "kind": "port",
+                         "sample": "each step: 36 layers of 16k decode through the numpy restatement of the "
+                                   "reference's folded SDPA (fp32), 4 distinct layer buffers cycled"},
+        "e2e": {"value": round(value, 2), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, local, world, dist = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, local, world, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

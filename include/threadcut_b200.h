@@ -1,0 +1,182 @@
+/*
+ * threadcut_b200 — C ABI of the B200 (sm_100a) decode-attention / KV-splice kernels.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes plus a cudaStream_t
+ * passed as `void*` (NULL = legacy default stream). Nothing here allocates, frees or synchronises
+ * unless its comment says so; tensors stay owned by the caller. All functions return a TC_* status
+ * (0 = TC_OK) and never abort the process. Launch errors are reported as TC_ERR_CUDA.
+ *
+ * Reference interfaces replaced (file:line inside the threadcut project):
+ *   tc_decode_attention*      threadcut/flash_decode.py:57-69   decode_attention(q, k, v, scale, split, block)
+ *                             (+ the folded decode branch of threadcut/attention.py:35-42,47)
+ *   tc_shift_keys             threadcut/kv.py:20-25             shift_keys(keys, delta, inv_freq)
+ *   tc_splice_inplace         threadcut/kv.py:83-92             GrowingLayer.splice(s, inv_freq)
+ *                             threadcut/kv.py:28-33             splice(cache, s, inv_freq), all layers
+ *   tc_splice_copy            threadcut/kv.py:34-41             splice(...) copy path (non-growing caches)
+ *   tc_merge_partials         threadcut/flash_decode.py:68-69   softmax(lse) merge of split partials
+ */
+#ifndef THREADCUT_B200_H
+#define THREADCUT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+enum {
+  TC_OK = 0,
+  TC_ERR_INVALID = 1,   /* a size/shape/argument is outside the supported range           */
+  TC_ERR_ALIGN = 2,     /* a pointer or stride breaks an alignment rule of the kernel      */
+  TC_ERR_DTYPE = 3,     /* unsupported dtype code                                          */
+  TC_ERR_WORKSPACE = 4, /* workspace missing or smaller than the *_workspace_size() figure */
+  TC_ERR_CUDA = 5       /* a CUDA runtime call or kernel launch failed                      */
+};
+
+/* ---- element types ------------------------------------------------------------------- */
+enum { TC_F32 = 0, TC_F16 = 1, TC_BF16 = 2 };
+
+/* ---- device-side error bits (see tc_device_errors) ------------------------------------ */
+enum {
+  TC_DEVERR_PIPE_TIMEOUT = 1, /* a K/V staging wait (mbarrier) ran past its poll limit        */
+  TC_DEVERR_FLAG_TIMEOUT = 2  /* an in-place splice wait on another tile ran past its limit  */
+};
+
+/* Human-readable name of a TC_* status. */
+const char* tc_status_string(int status);
+
+/* ABI version of this library (bumped on any signature change). */
+int tc_abi_version(void);
+
+/* Reads (and, if clear != 0, resets) the device error bits of the CURRENT device. This call
+ * synchronises the device. Returns the bits, or -1 if the CUDA calls failed. */
+int tc_device_errors(int clear);
+
+/* ======================================================================================
+ * Decode attention (one query token per sequence, grouped-query heads folded per KV head).
+ *
+ * Layout: q[hkv, g, d] (query head hq = kv_head*g + i, as q.reshape(hkv, g, d) in
+ * threadcut/attention.py:39), k/v[hkv, n, d], out[hkv, g, d]; the last dimension is contiguous,
+ * the other strides are free (a GrowingLayer view has head stride cap*d). Result in the input
+ * dtype; math in fp32: softmax(scale * q k^T) v, exactly what flash_decode.py:_partial computes.
+ *
+ * Limits: d in {16, 32, 64, 128, 256} (fp32: d <= 128), 1 <= g <= 16, n >= 0 (n == 0 gives
+ * zeros, as the reference's empty merge does). splits = 0 picks the KV partition from the SM
+ * count; splits > 0 forces that many KV slices per (sequence, head) (capped at 128).
+ *
+ * Workspace: at least tc_decode_attention_workspace_size(...) bytes of device memory whose first
+ * 4*batch*hkv bytes are ZERO before the first call; every call leaves them zero again. Calls
+ * that share a workspace must be ordered (same stream).
+ * ====================================================================================== */
+size_t tc_decode_attention_workspace_size(int batch, int hkv, int g, int d, int64_t max_n,
+                                          int64_t total_tokens, int splits, int dtype);
+
+int tc_decode_attention(const void* q, const void* k, const void* v, void* out,
+                        int hkv, int g, int d, int64_t n,
+                        int64_t q_stride_h, int64_t q_stride_g,
+                        int64_t k_stride_h, int64_t k_stride_n,
+                        int64_t v_stride_h, int64_t v_stride_n,
+                        int64_t out_stride_h, int64_t out_stride_g,
+                        float scale, int splits, int dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Batched decode over `batch` sequences sharing one strided K/V tensor [batch, hkv, n, d].
+ * `lengths` (device int32[batch], may be NULL = all n) gives each sequence's valid length
+ * (<= n); the folded SDPA branch of threadcut/attention.py:41-42 (b > 1) is the reference. */
+int tc_decode_attention_batched(const void* q, const void* k, const void* v, void* out,
+                                int batch, int hkv, int g, int d, int64_t n,
+                                const int32_t* lengths,
+                                int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_g,
+                                int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_n,
+                                int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_n,
+                                int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_g,
+                                float scale, int splits, int dtype,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Ragged decode: sequence b has its own K/V allocation k_ptrs[b]/v_ptrs[b] of shape
+ * [hkv, >= lengths[b], d] with head stride head_strides[b] (elements) and token stride
+ * kv_stride_n, shared by K and V. k_ptrs, v_ptrs, head_strides and lengths are DEVICE arrays.
+ * Every K/V base must be 16-byte aligned and head/token strides multiples of 8 elements (16-bit
+ * types) — the caller guarantees this; it cannot be checked without reading device memory.
+ * max_n >= every length; total_tokens = sum of lengths (a scheduling hint; 0 = batch*max_n). */
+int tc_decode_attention_ragged(const void* q, void* out,
+                               const void* const* k_ptrs, const void* const* v_ptrs,
+                               const int64_t* head_strides, const int32_t* lengths,
+                               int batch, int hkv, int g, int d, int64_t max_n, int64_t total_tokens,
+                               int64_t kv_stride_n,
+                               int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_g,
+                               int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_g,
+                               float scale, int splits, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ======================================================================================
+ * RoPE key shift: out = k*cos(delta*theta) + rotate_half(k)*sin(delta*theta), in fp32 with the
+ * products and the sum rounded separately (as torch evaluates threadcut/kv.py:25), then rounded
+ * to the storage dtype. `cos_sin` is a HOST array of d floats: d/2 cosines then d/2 sines of
+ * delta*inv_freq[i]; it is copied into the launch, so it may be freed on return.
+ * keys/out: [outer, n, d] with the given strides (last dim contiguous). d even, d <= 512.
+ * ====================================================================================== */
+int tc_shift_keys(const void* keys, void* out, int64_t outer, int64_t n, int d,
+                  int64_t in_stride_outer, int64_t in_stride_n,
+                  int64_t out_stride_outer, int64_t out_stride_n,
+                  const float* cos_sin, int dtype, void* stream);
+
+/* ======================================================================================
+ * In-place splice A.B.C -> A.C of `layers` growing K/V buffers in ONE launch
+ * (GrowingLayer.splice on every layer): rows [c0, c0+c) of each head move to [a, a+c); keys are
+ * re-rotated by -(c0-a) positions (cos_sin of delta = a-c0, as in tc_shift_keys), values copied.
+ * Source and destination may overlap: tiles are handed out in order and a tile writes only after
+ * the tiles whose sources it overwrites have been read (bounded waits, TC_DEVERR_FLAG_TIMEOUT).
+ * kbufs/vbufs: HOST arrays of `layers` device pointers (layers <= 128), each [hkv, cap, d] with
+ * strides (stride_h, stride_n); c0 + c <= cap is checked (TC_ERR_INVALID otherwise).
+ * c0 == a is a no-op (the reference clones C onto itself).
+ * Workspace: tc_splice_workspace_size() bytes, first 16 bytes ZERO before the first use (left
+ * zero again); `epoch` must differ from the epoch of every earlier call on this workspace
+ * (a counter starting at 1 does).
+ * ====================================================================================== */
+size_t tc_splice_workspace_size(int layers, int hkv, int64_t c);
+
+int tc_splice_inplace(void* const* kbufs, void* const* vbufs, int layers, int hkv, int d,
+                      int64_t cap, int64_t a, int64_t c0, int64_t c, int64_t stride_h, int64_t stride_n,
+                      const float* cos_sin, int dtype,
+                      void* workspace, size_t workspace_bytes, uint32_t epoch, void* stream);
+
+/* Copy splice into fresh buffers (the non-GrowingLayer path of threadcut/kv.py:34-41):
+ * out[:, :a] = in[:, :a]; out[:, a:a+c] = shift(in[:, c0:c0+c]) for keys (plain copy for
+ * values, or when c0 == a). In and out must not overlap. Strides per tensor, last dim contiguous. */
+int tc_splice_copy(const void* k_in, const void* v_in, void* k_out, void* v_out,
+                   int hkv, int d, int64_t a, int64_t c0, int64_t c,
+                   int64_t in_stride_h, int64_t in_stride_n,
+                   int64_t out_stride_h, int64_t out_stride_n,
+                   const float* cos_sin, int dtype, void* stream);
+
+/* ======================================================================================
+ * Log-sum-exp merge of `parts` partial attention results (the merge of
+ * threadcut/flash_decode.py:68-69, also the cross-GPU combine of sequence-sharded decode):
+ * o_parts: fp32 [parts, rows, d], each part's output normalised by its own softmax sum;
+ * lse_parts: fp32 [parts, rows] natural-log log-sum-exp of the scaled scores (-inf = empty part).
+ * out[rows, d] (row stride out_stride_row) = sum_p softmax_p(lse)[p] * o_parts[p].
+ * ====================================================================================== */
+int tc_merge_partials(const float* o_parts, const float* lse_parts, void* out, float* lse_out,
+                      int parts, int64_t rows, int d, int64_t out_stride_row,
+                      int dtype, void* stream);
+
+/* Decode attention that also returns each row's natural-log log-sum-exp (fp32 [hkv, g], may be
+ * NULL): the partial-result form used by sequence-sharded decode. Same rules as
+ * tc_decode_attention. */
+int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse,
+                            int hkv, int g, int d, int64_t n,
+                            int64_t q_stride_h, int64_t q_stride_g,
+                            int64_t k_stride_h, int64_t k_stride_n,
+                            int64_t v_stride_h, int64_t v_stride_n,
+                            int64_t out_stride_h, int64_t out_stride_g,
+                            float scale, int splits, int dtype,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THREADCUT_B200_H */

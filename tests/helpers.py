@@ -1,0 +1,72 @@
+"""Shared test helpers: golden-vector access and tolerance constants."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLDEN = os.path.join(HERE, "golden")
+
+# north_star tolerances
+ATTN_ATOL = 2e-3          # bf16 attention output, max-abs vs the fp32 SDPA math on the same inputs
+ORACLE_ATOL = 2e-5        # oracle (fp64) vs the reference's own fp32 SDPA on the CPU
+
+_gold = None
+_meta = None
+
+
+def gold():
+    global _gold
+    if _gold is None:
+        _gold = dict(np.load(os.path.join(GOLDEN, "golden.npz")))
+    return _gold
+
+
+def meta():
+    global _meta
+    if _meta is None:
+        with open(os.path.join(GOLDEN, "golden_meta.json")) as f:
+            _meta = json.load(f)
+    return _meta
+
+
+def split_cases():
+    with open(os.path.join(GOLDEN, "split_cases.json")) as f:
+        return json.load(f)
+
+
+def bf16_bits_to_f32(b):
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def values(a):
+    """Stored array -> fp32 values (uint16 arrays are bf16 bit patterns)."""
+    a = np.asarray(a)
+    if a.dtype == np.uint16:
+        return bf16_bits_to_f32(a)
+    return a.astype(np.float32)
+
+
+def storage_dtype(a):
+    a = np.asarray(a)
+    return {np.dtype(np.uint16): "bf16", np.dtype(np.float16): "f16", np.dtype(np.float32): "f32"}[a.dtype]
+
+
+TORCH_DTYPE = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
+
+def sha(t):
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return hashlib.sha256(t.view(torch.uint8).numpy().tobytes()).hexdigest()
+    return hashlib.sha256(t.numpy().tobytes()).hexdigest()
+
+
+def ref_cos_sin(delta, inv_freq):
+    """The reference's fp32 table for one shift (threadcut/kv.py:22-25), as numpy (cos, sin)."""
+    angle = delta * inv_freq.float()
+    emb = torch.cat((angle, angle))
+    h = angle.numel()
+    return emb.cos()[:h].numpy(), emb.sin()[:h].numpy()

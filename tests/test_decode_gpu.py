@@ -1,0 +1,288 @@
+"""Decode attention on the GPU vs the oracle and the reference's golden outputs (needs a B200).
+
+Tolerance (north_star): bf16/fp16 output max-abs error <= 2e-3 against the fp32 SDPA math on the
+same (rounded) inputs; the fp32 kernel is held to 1e-4.
+"""
+import numpy as np
+import pytest
+import torch
+
+import workloads
+from helpers import ATTN_ATOL, gold, meta, values
+from oracle.attention import attention_decode_ref, decode_attention_ref, merge_ref
+from threadcut_b200 import _lib
+from threadcut_b200.flash_decode import (RaggedKV, decode_attention, decode_attention_batched,
+                                         decode_attention_lse, decode_attention_ragged, merge_partials)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TOL = {torch.bfloat16: ATTN_ATOL, torch.float16: ATTN_ATOL, torch.float32: 1e-4}
+
+
+def to_dev(x, dtype):
+    return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(DEV).to(dtype)
+
+
+def check_decode(q, k, v, scale, dtype, splits=None, atol=None):
+    """q [hkv,g,d], k/v [hkv,n,d] device tensors (any strides). Returns max-abs error."""
+    out = decode_attention(q, k, v, scale, splits=splits)
+    torch.cuda.synchronize()
+    ref = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), scale)
+    err = float(np.abs(out.float().cpu().numpy() - ref).max()) if ref.size else 0.0
+    assert out.dtype == q.dtype and out.shape == q.shape
+    assert err <= (atol if atol is not None else TOL[dtype]), (err, tuple(k.shape), dtype, splits)
+    return err
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_device_errors():
+    _lib.device_errors(clear=True)
+    yield
+    assert _lib.device_errors(clear=True) == 0
+
+
+@pytest.mark.parametrize("ci", range(10))
+def test_golden_small_cases(ci):
+    G, M = gold(), meta()["cases"][f"dec{ci}"]
+    hkv, g, d, n = M["hkv"], M["g"], M["d"], M["n"]
+    q = to_dev(values(G[f"dec{ci}_q"]), torch.bfloat16).reshape(hkv, g, d)
+    k = to_dev(values(G[f"dec{ci}_k"])[0], torch.bfloat16)
+    v = to_dev(values(G[f"dec{ci}_v"])[0], torch.bfloat16)
+    out = decode_attention(q, k, v, M["scale"])
+    ref = G[f"dec{ci}_out"].reshape(hkv, g, d)
+    assert np.abs(out.float().cpu().numpy() - ref).max() <= ATTN_ATOL
+
+
+def test_cfg1_bf16_and_fp32_against_reference():
+    q, k, v = workloads.cfg1()
+    G = gold()
+    for dtype, key, tol in ((torch.bfloat16, "cfg1_out_bf16in", ATTN_ATOL), (torch.float32, "cfg1_out_f32", 1e-4)):
+        out = decode_attention(q.to(DEV, dtype).reshape(8, 4, 128), k[0].to(DEV, dtype), v[0].to(DEV, dtype),
+                               workloads.SCALE)
+        err = np.abs(out.float().cpu().numpy().reshape(1, 1, 32, 128) - G[key]).max()
+        assert err <= tol, (dtype, err)
+
+
+def test_16k_headline_layer_against_reference():
+    q, k, v = workloads.cfg1(n=16384)
+    out = decode_attention(q.to(DEV, torch.bfloat16).reshape(8, 4, 128), k[0].to(DEV, torch.bfloat16),
+                           v[0].to(DEV, torch.bfloat16), workloads.SCALE)
+    err = np.abs(out.float().cpu().numpy().reshape(1, 1, 32, 128) - gold()["cfg16k_out_bf16in"]).max()
+    assert err <= ATTN_ATOL, err
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("n", [1, 2, 31, 32, 33, 100, 257, 1536, 4097])
+def test_sweep_lengths_dtypes(dtype, n):
+    g = torch.Generator(device=DEV).manual_seed(n)
+    q = torch.randn(8, 4, 128, generator=g, device=DEV).to(dtype)
+    kb = torch.randn(8, n + 37, 128, generator=g, device=DEV).to(dtype)  # GrowingLayer-style capacity
+    vb = torch.randn(8, n + 37, 128, generator=g, device=DEV).to(dtype)
+    check_decode(q, kb[:, :n], vb[:, :n], 128 ** -0.5, dtype)
+
+
+@pytest.mark.parametrize("hkv,g,d", [(8, 4, 128), (2, 1, 128), (4, 2, 64), (2, 8, 64), (2, 16, 128), (1, 5, 32),
+                                     (3, 3, 16), (2, 4, 256), (2, 12, 256)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_sweep_group_and_head_dim(hkv, g, d, dtype):
+    gen = torch.Generator(device=DEV).manual_seed(hkv * 100 + g * 10 + d)
+    n = 700
+    q = torch.randn(hkv, g, d, generator=gen, device=DEV).to(dtype)
+    k = torch.randn(hkv, n, d, generator=gen, device=DEV).to(dtype)
+    v = torch.randn(hkv, n, d, generator=gen, device=DEV).to(dtype)
+    check_decode(q, k, v, d ** -0.5, dtype)
+
+
+@pytest.mark.parametrize("hkv,g,d", [(2, 2, 16), (4, 8, 64), (2, 16, 128), (1, 3, 32)])
+def test_fp32_generic_shapes(hkv, g, d):
+    gen = torch.Generator(device=DEV).manual_seed(d + g)
+    q = torch.randn(hkv, g, d, generator=gen, device=DEV)
+    k = torch.randn(hkv, 333, d, generator=gen, device=DEV)
+    v = torch.randn(hkv, 333, d, generator=gen, device=DEV)
+    check_decode(q, k, v, d ** -0.5, torch.float32)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 64, 128])
+def test_forced_splits_merge_exactly(splits):
+    gen = torch.Generator(device=DEV).manual_seed(splits)
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(8, 5000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = torch.randn(8, 5000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    check_decode(q, k, v, 128 ** -0.5, torch.bfloat16, splits=splits)
+
+
+def test_empty_cache_gives_zeros():
+    """n == 0: the reference merges zero slices, which sums to zeros (flash_decode.py:61-69)."""
+    for dtype in (torch.bfloat16, torch.float32):
+        q = torch.randn(8, 4, 128, device=DEV).to(dtype)
+        k = torch.empty(8, 0, 128, device=DEV, dtype=dtype)
+        out = decode_attention(q, k, k, 0.1)
+        assert torch.count_nonzero(out) == 0
+
+
+def test_misaligned_views_take_the_generic_path():
+    """K/V views whose rows are not 16-byte aligned (odd token offset into a buffer with an odd
+    row stride) are still computed correctly."""
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    buf = torch.randn(8, 600, 130, generator=gen, device=DEV).to(torch.bfloat16)
+    k = buf[:, 1:401, 1:129]  # row stride 130 elements = 260 bytes: not a multiple of 16
+    v = buf[:, 100:500, 2:130]
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    check_decode(q, k, v, 0.088, torch.bfloat16)
+
+
+def test_noncontiguous_query_and_scale_values():
+    gen = torch.Generator(device=DEV).manual_seed(6)
+    qq = torch.randn(4, 8, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    q = qq.transpose(0, 1)  # [8, 4, 128] with stride (128, 1024, 1)
+    k = torch.randn(8, 999, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = torch.randn(8, 999, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    for scale in (128 ** -0.5, 1.0, 0.01):
+        check_decode(q, k, v, scale, torch.bfloat16)
+
+
+def test_peaked_softmax_precision():
+    """One token dominates (large scale): the hi/lo P split keeps the error far below 2e-3."""
+    gen = torch.Generator(device=DEV).manual_seed(8)
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(8, 3000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = (4 * torch.randn(8, 3000, 128, generator=gen, device=DEV)).to(torch.bfloat16)
+    err = check_decode(q, k, v, 0.5, torch.bfloat16)
+    assert err < 5e-4
+
+
+def test_lse_output_matches_oracle():
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(8, 2049, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = torch.randn(8, 2049, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    for splits in (1, None):
+        out, lse = decode_attention_lse(q, k, v, 0.088, splits=splits)
+        ro, rl = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                                      0.088, return_lse=True)
+        assert np.abs(out.float().cpu().numpy() - ro).max() <= ATTN_ATOL
+        assert np.abs(lse.cpu().numpy() - rl).max() <= 1e-4
+
+
+def test_results_are_deterministic():
+    gen = torch.Generator(device=DEV).manual_seed(10)
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(8, 20000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    a = decode_attention(q, k, k, 0.088)
+    b = decode_attention(q, k, k, 0.088)
+    assert torch.equal(a, b)
+
+
+def test_batched_uniform_and_lengths():
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    b, n = 5, 1200
+    q = torch.randn(b, 8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(b, 8, n, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = torch.randn(b, 8, n, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    out = decode_attention_batched(q, k, v, 0.088)
+    lens = [1200, 1, 77, 640, 1199]
+    out_l = decode_attention_batched(q, k, v, 0.088, lengths=torch.tensor(lens, dtype=torch.int32))
+    qc, kc, vc = (t.float().cpu().numpy() for t in (q, k, v))
+    for i in range(b):
+        r = decode_attention_ref(qc[i], kc[i], vc[i], 0.088)
+        assert np.abs(out[i].float().cpu().numpy() - r).max() <= ATTN_ATOL
+        r = decode_attention_ref(qc[i], kc[i][:, :lens[i]], vc[i][:, :lens[i]], 0.088)
+        assert np.abs(out_l[i].float().cpu().numpy() - r).max() <= ATTN_ATOL
+
+
+def test_ragged_golden_cases():
+    G = gold()
+    lengths = meta()["ragged_lengths"]
+    qs, ks, vs = [], [], []
+    for bi, n in enumerate(lengths):
+        qs.append(to_dev(values(G[f"rag{bi}_q"]), torch.bfloat16).reshape(2, 4, 128))
+        kk = torch.zeros(2, n + 16, 128, device=DEV, dtype=torch.bfloat16)
+        vv = torch.zeros(2, n + 16, 128, device=DEV, dtype=torch.bfloat16)
+        kk[:, :n] = to_dev(values(G[f"rag{bi}_k"])[0], torch.bfloat16)
+        vv[:, :n] = to_dev(values(G[f"rag{bi}_v"])[0], torch.bfloat16)
+        ks.append(kk)
+        vs.append(vv)
+    kv = RaggedKV(ks, vs, lengths)
+    out = decode_attention_ragged(torch.stack(qs), kv, workloads.SCALE)
+    for bi in range(len(lengths)):
+        ref = G[f"rag{bi}_out"].reshape(2, 4, 128)
+        assert np.abs(out[bi].float().cpu().numpy() - ref).max() <= ATTN_ATOL
+
+
+def test_ragged_config4_shape_sample():
+    """Config 4 geometry (64 sequences, U[1024,16384] lengths, per-sequence contiguous caches) on
+    one layer; every 8th sequence is checked against the oracle, all others via LSE-free decode of
+    the same sequence alone (two independent kernel paths must agree)."""
+    lengths = workloads.cfg4_lengths()
+    gen = torch.Generator(device=DEV).manual_seed(12)
+    ks = [torch.randn(8, n, 128, generator=gen, device=DEV).to(torch.bfloat16) for n in lengths]
+    vs = [torch.randn(8, n, 128, generator=gen, device=DEV).to(torch.bfloat16) for n in lengths]
+    q = torch.randn(64, 8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    out = decode_attention_ragged(q, RaggedKV(ks, vs, lengths), workloads.SCALE)
+    for i in range(64):
+        single = decode_attention(q[i], ks[i], vs[i], workloads.SCALE)
+        assert (out[i].float() - single.float()).abs().max().item() <= ATTN_ATOL
+        if i % 8 == 0:
+            r = decode_attention_ref(q[i].float().cpu().numpy(), ks[i].float().cpu().numpy(),
+                                     vs[i].float().cpu().numpy(), workloads.SCALE)
+            assert np.abs(out[i].float().cpu().numpy() - r).max() <= ATTN_ATOL
+
+
+def test_merge_partials_kernel():
+    rng = np.random.default_rng(4)
+    o = rng.standard_normal((5, 32, 128)).astype(np.float32)
+    lse = rng.standard_normal((5, 32)).astype(np.float32) * 3
+    lse[2, 7] = -np.inf
+    out, l = merge_partials(torch.from_numpy(o).to(DEV), torch.from_numpy(lse).to(DEV), torch.float32)
+    ro, rl = merge_ref(o, lse)
+    assert np.abs(out.cpu().numpy() - ro).max() <= 1e-5
+    assert np.abs(l.cpu().numpy() - rl).max() <= 1e-5
+
+
+def test_long_context_full_size_properties():
+    """Config 3 at 32k on full layers: two layers against the oracle, and size-independent
+    properties on all of them — a token permutation leaves the output unchanged and decoding two
+    halves then LSE-merging equals decoding the whole."""
+    n = 32768
+    ks, vs = workloads.layer_kv(n, 4, DEV, seed=3)
+    gen = torch.Generator(device=DEV).manual_seed(13)
+    for li, (k, v) in enumerate(zip(ks, vs)):
+        q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+        out = decode_attention(q, k, v, workloads.SCALE)
+        if li < 2:
+            r = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                                     workloads.SCALE, dtype=np.float32)
+            assert np.abs(out.float().cpu().numpy() - r).max() <= ATTN_ATOL
+        perm = torch.randperm(n, device=DEV)
+        outp = decode_attention(q, k[:, perm].contiguous(), v[:, perm].contiguous(), workloads.SCALE)
+        assert (outp.float() - out.float()).abs().max().item() <= ATTN_ATOL
+        o1, l1 = decode_attention_lse(q, k[:, : n // 3], v[:, : n // 3], workloads.SCALE)
+        o2, l2 = decode_attention_lse(q, k[:, n // 3:], v[:, n // 3:], workloads.SCALE)
+        m, _ = merge_partials(torch.stack([o1.float().reshape(32, 128), o2.float().reshape(32, 128)]),
+                              torch.stack([l1.reshape(32), l2.reshape(32)]), torch.float32)
+        assert (m.reshape(8, 4, 128) - out.float()).abs().max().item() <= ATTN_ATOL
+
+
+def test_plugin_decode_and_prefill_branches():
+    from threadcut_b200.attention import attention
+    gen = torch.Generator(device=DEV).manual_seed(14)
+    query = torch.randn(1, 32, 1, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    key = torch.randn(1, 8, 300, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    val = torch.randn(1, 8, 300, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    out, w = attention(None, query, key, val, None, scaling=None)
+    assert w is None and out.shape == (1, 1, 32, 128) and out.is_contiguous()
+    ref = attention_decode_ref(query.float().cpu().numpy(), key.float().cpu().numpy(), val.float().cpu().numpy())
+    assert np.abs(out.float().cpu().numpy() - ref).max() <= ATTN_ATOL
+    # b > 1 decode goes through the batched kernel
+    q2 = torch.randn(3, 32, 1, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k2 = torch.randn(3, 8, 50, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    out2, _ = attention(None, q2, k2, k2, None, scaling=0.1)
+    ref2 = attention_decode_ref(q2.float().cpu().numpy(), k2.float().cpu().numpy(), k2.float().cpu().numpy(), 0.1)
+    assert np.abs(out2.float().cpu().numpy() - ref2).max() <= ATTN_ATOL
+    # prefill keeps the reference's expand + SDPA branch
+    qp = torch.randn(1, 32, 7, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    kp = torch.randn(1, 8, 7, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    outp, _ = attention(None, qp, kp, kp, None)
+    refp = torch.nn.functional.scaled_dot_product_attention(
+        qp.float(), kp.float().repeat_interleave(4, 1), kp.float().repeat_interleave(4, 1), is_causal=True)
+    assert (outp.float() - refp.transpose(1, 2)).abs().max().item() <= 2e-2

@@ -1,0 +1,164 @@
+"""End-to-end through the engine and the transformers plugin on the GPU.
+
+Mirrors the reference's engine tests (tests/test_core.py): T2 (splice == fresh compute), T3 (greedy
+tokens == stock transformers SDPA generate) on the reference's tiny Qwen3 configuration, and
+config 5: a random-init Qwen3-4B decoding one token over a 128k cache with a 32k span pruned, whose
+next-token logits must have the same top-1 as the torch SDPA path on the same spliced cache.
+"""
+import pytest
+import torch
+from transformers import AutoModelForCausalLM, DynamicCache, Qwen3Config
+
+import workloads
+from threadcut_b200 import _lib
+from threadcut_b200 import attention as tc_attention
+from threadcut_b200.engine import Engine
+from threadcut_b200.kv import new_cache, splice
+from threadcut_b200.match import Split
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+class StubTokenizer:
+    """The engine only needs the stop ids (threadcut/engine.py:36)."""
+    eos_token_id = 511
+
+    def convert_tokens_to_ids(self, tok):
+        return 510
+
+
+def tiny_engine(dtype):
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=4096)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=dtype, attn_implementation=tc_attention.NAME).to(DEV)
+    return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=7)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_device_errors():
+    _lib.device_errors(clear=True)
+    yield
+    assert _lib.device_errors(clear=True) == 0
+
+
+def rand_ids(n, seed, vocab=500):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(10, vocab, (n,), generator=g).tolist()
+
+
+def kv_alone(model, ids, start):
+    """KV of `ids` at positions start.., computed with no other context visible."""
+    cache = DynamicCache(config=model.config)
+    x = torch.tensor([ids], device=model.device)
+    pos = torch.arange(start, start + len(ids), device=model.device)[None]
+    model(input_ids=x, position_ids=pos, past_key_values=cache, use_cache=True)
+    return cache
+
+
+def concat(*caches):
+    out = caches[0]
+    for c in caches[1:]:
+        for lo, li in zip(out.layers, c.layers):
+            lo.keys = torch.cat((lo.keys, li.keys), 2)
+            lo.values = torch.cat((lo.values, li.values), 2)
+    return out
+
+
+@pytest.mark.parametrize("dtype,atol", [(torch.float32, 1e-4), (torch.bfloat16, 3e-2)])
+def test_T2_splice_matches_fresh_compute(dtype, atol):
+    engine = tiny_engine(dtype)
+    m = engine.model
+    A, B, C, D = rand_ids(9, 1), rand_ids(13, 2), rand_ids(11, 3), rand_ids(5, 4)
+    with torch.no_grad():
+        ref = concat(kv_alone(m, A, 0), kv_alone(m, C, len(A)))
+        ref_logits = m(input_ids=torch.tensor([D], device=DEV), past_key_values=ref).logits[0, -1]
+        engine.cache = concat(kv_alone(m, A, 0), kv_alone(m, B, len(A)), kv_alone(m, C, len(A) + len(B)))
+        engine.ids = A + B + C
+        logits, stats = engine.load(A + C + D)
+    assert (stats["reused_prefix"], stats["reused_suffix"], stats["computed_tokens"]) == (9, 11, 5)
+    assert torch.allclose(logits[0].float(), ref_logits.float(), atol=atol, rtol=0)
+
+
+def test_growing_cache_inplace_splice_matches_copy_splice():
+    """The engine's own GrowingLayer cache spliced in place (all layers, one launch) gives the same
+    logits as the copy-path splice (threadcut/kv.py:34-41) of a plain DynamicCache holding the same
+    A.B.C tensors."""
+    engine = tiny_engine(torch.float32)
+    m = engine.model
+    A, B, C, D = rand_ids(20, 5), rand_ids(17, 6), rand_ids(40, 7), rand_ids(6, 8)
+    with torch.no_grad():
+        engine.generate(A + B + C, max_new_tokens=0)
+        plain = DynamicCache(config=m.config)
+        for lp, lg in zip(plain.layers, engine.cache.layers):
+            lp.update(lg.keys.clone(), lg.values.clone())
+        logits, stats = engine.load(A + C + D)
+        splice(plain, Split(len(A), len(A) + len(B), len(C)), engine.inv_freq)
+        ref_logits = engine._forward(D, plain)
+    assert (stats["reused_prefix"], stats["reused_suffix"], stats["computed_tokens"]) == (20, 40, 6)
+    assert torch.allclose(logits.float(), ref_logits.float(), atol=1e-5, rtol=0)
+
+
+def hf_generate(m, ids, n, stop):
+    impl = m.config._attn_implementation
+    m.set_attn_implementation("sdpa")
+    try:
+        return m.generate(torch.tensor([ids], device=m.device), max_new_tokens=n, do_sample=False,
+                          eos_token_id=list(stop))[0, len(ids):].tolist()
+    finally:
+        m.set_attn_implementation(impl)
+
+
+def test_T3_no_pruning_matches_hf_generate():
+    engine = tiny_engine(torch.float32)
+    m = engine.model
+    p1 = rand_ids(20, 5)
+    out1, _ = engine.generate(p1, max_new_tokens=12)
+    ref1 = hf_generate(m, p1, 12, engine.stop_ids)
+    assert out1 == [t for t in ref1 if t not in engine.stop_ids][:len(out1)]
+    p2 = p1 + out1 + rand_ids(6, 6)
+    out2, s2 = engine.generate(p2, max_new_tokens=12)
+    assert s2["reused_tokens"] == len(p1) + len(out1) and s2["computed_tokens"] == 6
+    ref2 = hf_generate(m, p2, 12, engine.stop_ids)
+    assert out2 == [t for t in ref2 if t not in engine.stop_ids][:len(out2)]
+
+
+def qwen3_4b_config(layers=36):
+    """Qwen3-4B geometry (BASELINE: hidden 2560, 36 layers, 32/8 heads, head_dim 128, theta 1e6);
+    intermediate 9728, vocab 151936, tied embeddings and eps 1e-6 are the published values."""
+    return Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+                       tie_word_embeddings=True, max_position_embeddings=262144,
+                       rope_parameters={"rope_type": "default", "rope_theta": 1.0e6})
+
+
+def test_cfg5_full_model_128k_spliced_top1_matches_sdpa():
+    torch.manual_seed(0)
+    cfg = qwen3_4b_config()
+    with torch.device(DEV):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
+    model.eval()
+    inv = model.model.rotary_emb.inv_freq
+    ctx = workloads.CFG5_CTX
+    lo, hi = workloads.CFG5_PRUNE
+    s = Split(lo, hi, ctx - hi)
+    cache = new_cache(cfg)
+    gen = torch.Generator(device=DEV).manual_seed(0)
+    for layer in cache.layers:
+        k = torch.randn(1, 8, ctx, 128, generator=gen, device=DEV, dtype=torch.bfloat16)
+        v = torch.randn(1, 8, ctx, 128, generator=gen, device=DEV, dtype=torch.bfloat16)
+        layer.update(k, v)
+        del k, v
+    splice(cache, s, inv)
+    n = s.a + s.c
+    assert cache.get_seq_length() == n == 98304
+    x = torch.tensor([[1234]], device=DEV)
+    with torch.no_grad():
+        ours = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].float()
+        for layer in cache.layers:
+            layer.crop(n)  # drop the token the first pass appended
+        model.set_attn_implementation("sdpa")
+        ref = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].float()
+    assert int(ours.argmax()) == int(ref.argmax())
+    assert (ours - ref).abs().max().item() < 0.1

@@ -1,0 +1,173 @@
+"""Host-side logic and the C ABI boundary (CPU only: no kernel is launched here)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from helpers import split_cases
+from threadcut_b200 import _lib
+from threadcut_b200.match import Split, lcp, split
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "threadcut_b200.h")
+
+
+# ------------------------------------------------------------------ split (threadcut/match.py)
+def test_split_rule_reference_cases():
+    """The reference's own test_split_rule (tests/test_core.py:59-64)."""
+    A, B, C, D = [1, 2, 3], [7, 7], [4, 5, 6, 8, 9], [10, 11]
+    assert split(A + B + C, A + C + D, min_suffix=3) == Split(3, 5, 5)
+    assert split(A + B + C, A + C + D, min_suffix=3, suffix=False) == Split(3, 3, 0)
+    assert split(A + C, A + C + D, min_suffix=3) == Split(8, 8, 0)
+    assert split(A + C, A + C, min_suffix=3).a == len(A + C) - 1
+
+
+def test_split_matches_reference_golden_cases():
+    cases = split_cases()
+    assert len(cases) > 200
+    for cs in cases:
+        s = split(cs["cached"], cs["new"], min_suffix=cs["min_suffix"], suffix=cs["suffix"])
+        assert [s.a, s.c0, s.c] == cs["expect"], cs
+
+
+def test_lcp_and_gap():
+    assert lcp([], [1]) == 0
+    assert lcp([1, 2, 3], [1, 2, 4]) == 2
+    assert lcp([1, 2], [1, 2, 3]) == 2
+    assert Split(4, 9, 3).gap == 5
+
+
+# ------------------------------------------------------------------ C ABI library
+def header_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+char\s*\*|int|size_t)\s+(tc_\w+)\s*\(", text, re.M)))
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    L = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) >= 12, syms
+    for name in syms:
+        assert hasattr(L, name), f"{name} declared in include/threadcut_b200.h but not exported"
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_abi_version_and_status_strings():
+    L = _lib.lib()
+    assert L.tc_abi_version() == 1
+    for code in range(6):
+        assert L.tc_status_string(code)
+    assert L.tc_status_string(0) == b"ok"
+
+
+def test_argument_validation_without_a_gpu():
+    """Entry points reject bad arguments before touching CUDA."""
+    L = _lib.lib()
+    # unsupported dtype
+    assert L.tc_decode_attention(None, None, None, None, 8, 4, 128, 0, 0, 0, 0, 0, 0, 0, 0, 0,
+                                 0.1, 0, 7, None, 0, None) == 3
+    # K/V missing for a non-empty cache
+    assert L.tc_decode_attention(None, None, None, None, 8, 4, 128, 16, 0, 0, 0, 0, 0, 0, 0, 0,
+                                 0.1, 0, 2, None, 0, None) == 1
+    # odd head_dim for the rope shift
+    tab = (ctypes.c_float * 8)()
+    assert L.tc_shift_keys(None, None, 1, 1, 7, 0, 0, 0, 0, tab, 2, None) == 1
+    # missing cos/sin table
+    assert L.tc_shift_keys(None, None, 1, 1, 8, 0, 0, 0, 0, None, 2, None) == 1
+    # c0 < a is not a splice
+    kp = (ctypes.c_void_p * 1)(None)
+    assert L.tc_splice_inplace(kp, kp, 1, 8, 128, 100, 10, 5, 3, 0, 0, tab, 2, None, 0, 1, None) == 1
+    # splice with gap 0 is a no-op that succeeds without launching anything
+    assert L.tc_splice_inplace(kp, kp, 1, 8, 128, 100, 10, 10, 3, 0, 0, tab, 2, None, 0, 1, None) == 0
+    # too many layers
+    assert L.tc_splice_inplace(kp, kp, 129, 8, 128, 100, 1, 5, 3, 0, 0, tab, 2, None, 0, 1, None) == 1
+    # C reaching past the buffer's capacity
+    assert L.tc_splice_inplace(kp, kp, 1, 8, 128, 100, 1, 50, 51, 0, 0, tab, 2, None, 0, 1, None) == 1
+    # merge with no parts
+    assert L.tc_merge_partials(None, None, None, None, 0, 4, 128, 128, 2, None) == 1
+    # empty shift is fine
+    assert L.tc_shift_keys(None, None, 0, 5, 8, 0, 0, 0, 0, tab, 2, None) == 0
+
+
+def test_splice_workspace_bound():
+    L = _lib.lib()
+    assert L.tc_splice_workspace_size(36, 8, 4096) >= 16 + 4 * 36 * 8 * (4096 // 64)
+    assert L.tc_splice_workspace_size(0, 8, 10) == 0
+
+
+# ------------------------------------------------------------------ no CPU fallback
+def test_decode_on_cpu_tensors_fails_loudly():
+    from threadcut_b200.flash_decode import decode_attention
+    q = torch.randn(8, 4, 128)
+    k = torch.randn(8, 10, 128)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        decode_attention(q, k, k, 0.1)
+
+
+def test_shift_on_cpu_tensors_fails_loudly():
+    from threadcut_b200.kv import shift_keys
+    with pytest.raises(RuntimeError, match="CUDA"):
+        shift_keys(torch.randn(1, 2, 5, 16), -3, torch.ones(8))
+
+
+def test_plugin_decode_branch_on_cpu_fails_loudly():
+    from threadcut_b200.attention import attention
+    with pytest.raises(RuntimeError, match="CUDA"):
+        attention(None, torch.randn(1, 8, 1, 16), torch.randn(1, 2, 5, 16), torch.randn(1, 2, 5, 16), None)
+
+
+def test_missing_library_is_an_error(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="missing"):
+        _lib.lib()
+
+
+# ------------------------------------------------------------------ GrowingLayer bookkeeping
+def test_growing_layer_growth_policy_and_views():
+    from threadcut_b200.kv import GrowingLayer, new_cache
+    ly = GrowingLayer()
+    k = torch.randn(1, 2, 3, 16)
+    ly.update(k, k + 1)
+    assert ly.kbuf.shape[-2] == 2048 + 0 and ly.n == 3  # max(3, 0, 0 + 2048)
+    assert torch.equal(ly.keys, k) and torch.equal(ly.values, k + 1)
+    ly.update(torch.randn(1, 2, 2100, 16), torch.randn(1, 2, 2100, 16))
+    assert ly.kbuf.shape[-2] == max(2103, int(2048 * 1.25), 2048 + 2048)
+    assert torch.equal(ly.keys[..., :3, :], k)
+    ly.crop(5)
+    assert ly.get_seq_length() == 5
+    ly.crop(100)
+    assert ly.get_seq_length() == 5
+    from transformers import Qwen3Config
+    cache = new_cache(Qwen3Config(num_hidden_layers=3))
+    assert len(cache.layers) == 3 and all(isinstance(x, GrowingLayer) for x in cache.layers)
+
+
+def test_splice_c_zero_needs_no_device():
+    """Split with c == 0 only truncates (kv.py:85-91): no kernel, works on any tensors."""
+    from threadcut_b200.kv import GrowingLayer
+    ly = GrowingLayer()
+    k = torch.randn(1, 2, 10, 16)
+    ly.update(k, k)
+    ly.splice(Split(4, 4, 0), torch.ones(8))
+    assert ly.get_seq_length() == 4 and torch.equal(ly.keys, k[..., :4, :])
+
+
+def test_workspace_epochs_are_unique_and_nonzero():
+    ws = _lib._Workspaces()
+
+    class Dev:
+        index = None
+    seen = set()
+    # next_epoch keys on the current stream; emulate with a CPU-only key by monkeypatching
+    orig = _lib.stream_ptr
+    try:
+        _lib.stream_ptr = lambda d: 0
+        for _ in range(5):
+            e = ws.next_epoch("splice", Dev())
+            assert e != 0 and e not in seen
+            seen.add(e)
+    finally:
+        _lib.stream_ptr = orig

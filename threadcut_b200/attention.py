@@ -1,0 +1,52 @@
+"""GQA-aware attention plugin for transformers on B200 — drop-in for threadcut/attention.py.
+
+Registered as attention implementation "threadcut" (threadcut/attention.py:22,50-51), selected by
+`attn_implementation=attention.NAME`. Signature and result are the reference's
+(attention.py:30-47): `attention(module, query[b,Hq,q,D], key[b,Hkv,n,D], value, attention_mask,
+dropout=0.0, scaling=None, **kw) -> (out[b,q,Hq,D] contiguous, None)`.
+
+Decode (one query token, no mask): the g = Hq/Hkv query heads of each KV head are folded into a
+g-row query (query.reshape(hkv, g, d), attention.py:39) and run by the B200 split-KV kernel over
+the unexpanded cache, b == 1 through decode_attention and b > 1 through decode_attention_batched
+(the reference used folded SDPA there). Decode on a non-CUDA tensor raises: there is no CPU path.
+Prefill (q > 1 or a mask) is outside the decode hot path and keeps the reference's branch:
+expand KV once and call torch SDPA (attention.py:43-46).
+"""
+import torch.nn.functional as F
+from transformers import AttentionInterface
+from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+
+from .flash_decode import decode_attention, decode_attention_batched
+
+NAME = "threadcut"
+
+__all__ = ["NAME", "attention", "repeat_kv"]
+
+
+def repeat_kv(x, n):
+    """[b, h, s, d] -> [b, h*n, s, d], each KV head repeated n times (prefill only)."""
+    if n == 1:
+        return x
+    b, h, s, d = x.shape
+    return x.unsqueeze(2).expand(b, h, n, s, d).reshape(b, h * n, s, d)
+
+
+def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
+    b, hq, q, d = query.shape
+    hkv = key.shape[1]
+    g = hq // hkv
+    scaling = scaling if scaling is not None else d ** -0.5
+    if q == 1 and attention_mask is None:
+        if b == 1:
+            out = decode_attention(query.reshape(hkv, g, d), key[0], value[0], scaling).reshape(1, hq, 1, d)
+        else:
+            out = decode_attention_batched(query.reshape(b, hkv, g, d), key, value, scaling).reshape(b, hq, 1, d)
+    else:
+        is_causal = attention_mask is None and q > 1 and q == key.shape[2]
+        out = F.scaled_dot_product_attention(query, repeat_kv(key, g), repeat_kv(value, g),
+                                             attn_mask=attention_mask, scale=scaling, is_causal=is_causal)
+    return out.transpose(1, 2).contiguous(), None
+
+
+AttentionInterface.register(NAME, attention)
+AttentionMaskInterface.register(NAME, sdpa_mask)

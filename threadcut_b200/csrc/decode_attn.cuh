@@ -1,0 +1,562 @@
+// Split-KV GQA decode attention for sm_100a.
+//
+// Reference semantics: threadcut/flash_decode.py:21-69 (_partial + softmax(lse) merge) and the
+// folded decode branch of threadcut/attention.py:35-42: for each KV head h the g query heads that
+// share it form a g-row query; out = softmax(scale * q k^T) v over the n cached tokens, fp32 math,
+// result cast to the input dtype.
+//
+// B200 design (16-bit K/V, the hot path):
+//   * grid (split, kv_head, sequence); each CTA owns one contiguous KV slice of one head, so every
+//     K/V byte is read exactly once per step and the folded g heads share it.
+//   * warp 4 is a producer: per 32-token tile each lane issues one 1-D bulk (TMA) copy of its K row
+//     and one of its V row into a padded shared-memory stage (row pitch 2*d+16 bytes, which makes
+//     the ldmatrix reads below bank-conflict free), completing on the stage's mbarrier.
+//   * warps 0-3 are consumers, warp w owns stage w (tiles w, w+4, ...). Per tile:
+//       S^T[32 tok x 8 heads] = K . q^T     mma.m16n8k16 (K from ldmatrix, q^T fragments in regs)
+//       online softmax in the exp2 domain    (max via 3 xor-shuffles over the 8 token lanes)
+//       O^T[d x 8 heads] += V^T . P^T        mma.m16n8k16 (V^T from ldmatrix.trans, P^T from the
+//                                            score fragments by movmatrix.trans; P is split into a
+//                                            hi and lo 16-bit part so the product keeps ~16 more
+//                                            bits than a single bf16 P would)
+//     Only 4 of the 8 head columns are real for Qwen3 (g = 4); the tensor core has throughput to
+//     spare, the point is to take the per-token FMA/shuffle work off the issue slots so the CTA
+//     stays a pure HBM stream.
+//   * epilogue: the 4 warps' (m, l, o) are combined in shared memory; with one split the CTA
+//     writes the output, otherwise it writes an unnormalised partial and the LAST CTA of the head
+//     (atomic ticket) merges all partials by log-sum-exp and resets the ticket.
+// fp32 (or K/V whose strides break the 16-byte bulk-copy rule) use decode_generic_kernel: the same
+// partition and epilogue with plain loads and FMA math.
+#pragma once
+
+#include <math.h>
+
+#include "tc_common.cuh"
+
+namespace tc {
+
+constexpr int kTile = 32;        // tokens per staged tile (one K row + one V row per producer lane)
+constexpr int kCWarps = 4;       // consumer warps per CTA
+constexpr int kStages = 4;       // == kCWarps: consumer warp w owns stage w
+constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
+constexpr int kMmaCtasPerSm = 3; // resident CTAs per SM assumed by the split planner (mma kernel)
+constexpr int kGenCtasPerSm = 4; // same for the generic kernel
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DecodeParams {
+  const void* q;
+  void* out;
+  float* lse;                 // optional natural-log LSE out, [batch][hkv][g] (stride lse_b per b)
+  const void* k;
+  const void* v;
+  const void* const* k_ptrs;  // ragged: per-sequence K/V bases (device arrays) or null
+  const void* const* v_ptrs;
+  const int64_t* head_strides;  // ragged: per-sequence head stride (elements) or null
+  const int32_t* lengths;       // per-sequence valid length (device) or null (= n)
+  int64_t n;
+  int64_t sq_b, sq_h, sq_g, so_b, so_h, so_g;
+  int64_t sk_b, sk_h, sk_n, sv_b, sv_h, sv_n;
+  int64_t lse_b;
+  int hkv, g, batch;
+  int tiles_per_split;  // KV slice = tiles_per_split * kTile tokens
+  int max_splits;       // grid.x and the workspace stride between (sequence, head) rows
+  float c;              // scale * log2(e)
+  float* ws_o;          // [batch*hkv][max_splits][g][d]  unnormalised partial outputs
+  float* ws_ml;         // [batch*hkv][max_splits][g][2]  (running max (log2 domain), sum)
+  int* counters;        // [batch*hkv] arrival tickets, zero between calls
+};
+
+template <typename T>
+__device__ __forceinline__ void resolve_seq(const DecodeParams& p, int b, int h, const T*& kh, const T*& vh,
+                                            int64_t& n) {
+  n = p.lengths ? (int64_t)p.lengths[b] : p.n;
+  if (p.k_ptrs) {
+    const int64_t hs = p.head_strides ? p.head_strides[b] : p.sk_h;
+    kh = static_cast<const T*>(p.k_ptrs[b]) + h * hs;
+    vh = static_cast<const T*>(p.v_ptrs[b]) + h * hs;
+  } else {
+    kh = static_cast<const T*>(p.k) + b * p.sk_b + h * p.sk_h;
+    vh = static_cast<const T*>(p.v) + b * p.sv_b + h * p.sv_h;
+  }
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+__device__ __forceinline__ float lse_nat(float m2, float l) {
+  return l > 0.f ? (m2 + __log2f(l)) * kLn2 : -INFINITY;
+}
+
+// Per-warp softmax state in shared memory: m[HP], l[HP], then acc[HP][D + 4] (the +4 keeps the
+// fragment-ordered stores bank-conflict free).
+template <int D, int HP>
+struct Region {
+  static constexpr int kAccStride = D + 4;
+  static constexpr int kFloats = 2 * HP + HP * kAccStride;
+  __device__ static float* m(float* r) { return r; }
+  __device__ static float* l(float* r) { return r + HP; }
+  __device__ static float* acc(float* r, int i) { return r + 2 * HP + i * kAccStride; }
+};
+
+// Combine the per-warp states of this CTA, then either write the output (one split) or publish a
+// partial and, in the last CTA of this (sequence, head), merge all partials.
+// Preconditions: every thread of the CTA calls this after a __syncthreads() that follows the
+// region writes; `merge_smem` has room for max_splits * g floats and no longer holds live data.
+template <typename T, int D, int HP>
+__device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_stride_bytes, int nregions,
+                           float* merge_smem, int b, int h, int split, int nsplit) {
+  __shared__ float s_M[16], s_L[16];
+  __shared__ int s_last;
+  using R = Region<D, HP>;
+  const int g = p.g;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
+  const int64_t bh = (int64_t)b * p.hkv + h;
+  T* out = static_cast<T*>(p.out) + b * p.so_b + h * p.so_h;
+  auto region = [&](int w) { return reinterpret_cast<float*>(regions + (size_t)w * region_stride_bytes); };
+
+  if (tid < g) {
+    float M = -INFINITY;
+    for (int w = 0; w < nregions; ++w) M = fmaxf(M, R::m(region(w))[tid]);
+    float L = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < nregions; ++w) L += R::l(region(w))[tid] * fast_exp2(R::m(region(w))[tid] - M);
+    s_M[tid] = M;
+    s_L[tid] = L;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < g * D; idx += nthr) {
+    const int i = idx / D, d = idx - i * D;
+    const float M = s_M[i];
+    float o = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < nregions; ++w) o += R::acc(region(w), i)[d] * fast_exp2(R::m(region(w))[i] - M);
+    if (nsplit == 1) {
+      const float L = s_L[i];
+      out[i * p.so_g + d] = from_f32<T>(L > 0.f ? o / L : 0.f);
+    } else {
+      p.ws_o[((bh * p.max_splits + split) * g + i) * D + d] = o;
+    }
+  }
+  if (nsplit == 1) {
+    if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
+    return;
+  }
+  if (tid < g) {
+    float* ml = p.ws_ml + ((bh * p.max_splits + split) * g + tid) * 2;
+    ml[0] = s_M[tid];
+    ml[1] = s_L[tid];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(&p.counters[bh], 1) == nsplit - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // Last CTA of this head: merge nsplit partials. Weights w_s = 2^(m_s - M) per (split, head).
+  const float* mlb = p.ws_ml + bh * p.max_splits * g * 2;
+  for (int i = warp; i < g; i += nwarps) {
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(mlb + ((int64_t)s * g + i) * 2));
+    M = warp_max(M);
+    float L = 0.f;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float w = fast_exp2(__ldcg(mlb + ((int64_t)s * g + i) * 2) - M);
+      merge_smem[s * g + i] = w;
+      L += w * __ldcg(mlb + ((int64_t)s * g + i) * 2 + 1);
+    }
+    L = warp_sum(L);
+    if (lane == 0) {
+      s_M[i] = M;
+      s_L[i] = L;
+    }
+  }
+  __syncthreads();
+  const float* ob = p.ws_o + bh * p.max_splits * g * D;
+  for (int idx = tid; idx < g * D; idx += nthr) {
+    const int i = idx / D, d = idx - i * D;
+    float o0 = 0.f, o1 = 0.f;
+    int s = 0;
+    for (; s + 1 < nsplit; s += 2) {
+      o0 += merge_smem[s * g + i] * __ldcg(ob + ((int64_t)s * g + i) * D + d);
+      o1 += merge_smem[(s + 1) * g + i] * __ldcg(ob + ((int64_t)(s + 1) * g + i) * D + d);
+    }
+    if (s < nsplit) o0 += merge_smem[s * g + i] * __ldcg(ob + ((int64_t)s * g + i) * D + d);
+    const float L = s_L[i];
+    out[i * p.so_g + d] = from_f32<T>(L > 0.f ? (o0 + o1) / L : 0.f);
+  }
+  if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
+  if (tid == 0) p.counters[bh] = 0;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
+  uint16_t a, b;
+  memcpy(&a, &lo, 2);
+  memcpy(&b, &hi, 2);
+  return (uint32_t)a | ((uint32_t)b << 16);
+}
+
+template <int D>
+struct MmaGeom {
+  static constexpr int kPitch = D * 2 + 16;  // bytes per staged row: odd multiple of 16
+  static constexpr int kTileBytes = kTile * kPitch;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kPipeBytes = kStages * kStageBytes;
+  static constexpr int kSmem = kPipeBytes + 2 * kStages * 8;
+};
+
+// ------------------------------------------------------------------------------------------------
+// Tensor-core path: T in {bf16, f16}, D in {16..256}, NG = number of 8-head column tiles (g <= 8*NG).
+template <typename T, int D, int NG>
+__global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
+    decode_mma_kernel(const __grid_constant__ DecodeParams p) {
+  using G = MmaGeom<D>;
+  constexpr int HP = 8 * NG;
+  constexpr int KS = D / 16;
+  static_assert(Region<D, HP>::kFloats * 4 <= G::kStageBytes, "combine region must fit in a stage");
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes);
+  uint64_t* empty = full + kStages;
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const T* kh;
+  const T* vh;
+  int64_t n;
+  resolve_seq<T>(p, b, h, kh, vh, n);
+  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
+  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
+  if (split >= nsplit) return;  // whole CTA leaves before touching any barrier
+  const int64_t t0 = (int64_t)split * chunk;
+  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
+  const int ntiles = n > 0 ? (int)((t1 - t0 + kTile - 1) / kTile) : 0;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kCWarps) {
+    // ---------------- producer: one K row and one V row per lane per tile
+    const uint64_t pol = policy_evict_first();
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j % kStages;
+      const int r = j / kStages;
+      if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * kTile * D * sizeof(T));
+      __syncwarp();
+      int64_t tok = t0 + (int64_t)j * kTile + lane;
+      if (tok > n - 1) tok = n - 1;  // tail rows repeat the last token; their scores are masked
+      uint8_t* st = smem + s * G::kStageBytes;
+      bulk_g2s(st + lane * G::kPitch, kh + tok * p.sk_n, D * sizeof(T), &full[s], pol);
+      bulk_g2s(st + G::kTileBytes + lane * G::kPitch, vh + tok * p.sv_n, D * sizeof(T), &full[s], pol);
+    }
+  } else {
+    // ---------------- consumers
+    const int gid = lane >> 2, qd = lane & 3;
+    const float c = p.c;
+    uint32_t bq[NG][KS][2];
+    {
+      const T* qb = static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h;
+      const T zero = from_f32<T>(0.f);
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt) {
+        const int i = nt * 8 + gid;
+        const bool ok = i < p.g;
+        const T* qr = qb + (ok ? i : 0) * p.sq_g;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          const int d0 = ks * 16 + 2 * qd;
+          bq[nt][ks][0] = pack_raw<T>(ok ? qr[d0] : zero, ok ? qr[d0 + 1] : zero);
+          bq[nt][ks][1] = pack_raw<T>(ok ? qr[d0 + 8] : zero, ok ? qr[d0 + 9] : zero);
+        }
+      }
+    }
+    float m_run[NG][2], l_run[NG][2];
+    float oacc[KS][NG][4];
+#pragma unroll
+    for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        m_run[nt][e] = -INFINITY;
+        l_run[nt][e] = 0.f;
+      }
+#pragma unroll
+    for (int md = 0; md < KS; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) oacc[md][nt][r] = 0.f;
+
+    for (int j = warp; j < ntiles; j += kCWarps) {
+      const int s = j % kStages;
+      if (!mbar_wait(&full[s], (j / kStages) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
+      const uint32_t kst = smem_u32(smem + s * G::kStageBytes);
+      const uint32_t vst = kst + G::kTileBytes;
+      const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
+      const int valid = rem < kTile ? (int)rem : kTile;
+
+      // S^T = K q^T over two 16-token m-tiles
+      float sacc[2][NG][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) sacc[mt][nt][r] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a[4];
+          const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int col = ks * 16 + (lane >> 4) * 8;
+          ldsm_x4(kst + row * G::kPitch + col * 2, a);
+#pragma unroll
+          for (int nt = 0; nt < NG; ++nt) Mma<T>::run(sacc[mt][nt], a, bq[nt][ks][0], bq[nt][ks][1]);
+        }
+      }
+
+      // online softmax; this lane holds tokens {gid, gid+8, gid+16, gid+24} x heads {2qd, 2qd+1}
+      float alpha[NG][2];
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float x0 = sacc[0][nt][e] * c, x1 = sacc[0][nt][2 + e] * c;
+          float x2 = sacc[1][nt][e] * c, x3 = sacc[1][nt][2 + e] * c;
+          if (gid >= valid) x0 = -INFINITY;
+          if (gid + 8 >= valid) x1 = -INFINITY;
+          if (gid + 16 >= valid) x2 = -INFINITY;
+          if (gid + 24 >= valid) x3 = -INFINITY;
+          float mx = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mnew = fmaxf(m_run[nt][e], mx);
+          alpha[nt][e] = fast_exp2(m_run[nt][e] - mnew);
+          m_run[nt][e] = mnew;
+          const float p0 = fast_exp2(x0 - mnew), p1 = fast_exp2(x1 - mnew);
+          const float p2 = fast_exp2(x2 - mnew), p3 = fast_exp2(x3 - mnew);
+          l_run[nt][e] = l_run[nt][e] * alpha[nt][e] + ((p0 + p1) + (p2 + p3));
+          sacc[0][nt][e] = p0;
+          sacc[0][nt][2 + e] = p1;
+          sacc[1][nt][e] = p2;
+          sacc[1][nt][2 + e] = p3;
+        }
+      }
+#pragma unroll
+      for (int md = 0; md < KS; ++md)
+#pragma unroll
+        for (int nt = 0; nt < NG; ++nt) {
+          oacc[md][nt][0] *= alpha[nt][0];
+          oacc[md][nt][1] *= alpha[nt][1];
+          oacc[md][nt][2] *= alpha[nt][0];
+          oacc[md][nt][3] *= alpha[nt][1];
+        }
+
+      // P^T fragments: pack (hi, lo) 16-bit parts, transpose 8x8 blocks with movmatrix
+      uint32_t bhi[2][NG][2], blo[2][NG][2];
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+        for (int nt = 0; nt < NG; ++nt) {
+          const float* sp = sacc[kk][nt];
+          const uint32_t x0 = Mma<T>::pack(sp[0], sp[1]);
+          const uint32_t x1 = Mma<T>::pack(sp[2], sp[3]);
+          const uint32_t y0 = Mma<T>::pack(sp[0] - Mma<T>::lo(x0), sp[1] - Mma<T>::hi(x0));
+          const uint32_t y1 = Mma<T>::pack(sp[2] - Mma<T>::lo(x1), sp[3] - Mma<T>::hi(x1));
+          bhi[kk][nt][0] = movm_t(x0);
+          bhi[kk][nt][1] = movm_t(x1);
+          blo[kk][nt][0] = movm_t(y0);
+          blo[kk][nt][1] = movm_t(y1);
+        }
+
+      // O^T += V^T P^T
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+        for (int md = 0; md < KS; ++md) {
+          uint32_t a[4];
+          const int mi = lane >> 3;
+          const int tok = kk * 16 + (mi >> 1) * 8 + (lane & 7);
+          const int dim = md * 16 + (mi & 1) * 8;
+          ldsm_x4_t(vst + tok * G::kPitch + dim * 2, a);
+#pragma unroll
+          for (int nt = 0; nt < NG; ++nt) {
+            Mma<T>::run(oacc[md][nt], a, bhi[kk][nt][0], bhi[kk][nt][1]);
+            Mma<T>::run(oacc[md][nt], a, blo[kk][nt][0], blo[kk][nt][1]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // this warp's state -> its own (now idle) stage buffer
+#pragma unroll
+    for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float l = l_run[nt][e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_run[nt][e] = l;
+      }
+    using R = Region<D, HP>;
+    float* reg = reinterpret_cast<float*>(smem + warp * G::kStageBytes);
+    if (gid == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int i = nt * 8 + 2 * qd + e;
+          R::m(reg)[i] = m_run[nt][e];
+          R::l(reg)[i] = l_run[nt][e];
+        }
+    }
+#pragma unroll
+    for (int md = 0; md < KS; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int dim = md * 16 + gid + (r >> 1) * 8;
+          const int i = nt * 8 + 2 * qd + (r & 1);
+          R::acc(reg, i)[dim] = oacc[md][nt][r];
+        }
+  }
+  __syncthreads();
+  // merge weights may reuse the pipeline buffers once the combine has read them (finish_cta syncs)
+  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, reinterpret_cast<float*>(smem + G::kStageBytes * 0),
+                       b, h, split, nsplit);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Generic path (fp32, or 16-bit K/V that break the bulk-copy alignment rule): 4 warps, warp w takes
+// tokens t0+w, t0+w+4, ...; lane owns dims lane, lane+32, ...; scores by warp reduction.
+template <int D>
+struct GenGeom {
+  static constexpr int HP = 16;
+  static constexpr int kRegionBytes = ((Region<D, HP>::kFloats * 4 + 127) / 128) * 128;
+  static constexpr int kSmem = kCWarps * kRegionBytes;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(32 * kCWarps) decode_generic_kernel(const __grid_constant__ DecodeParams p) {
+  using G = GenGeom<D>;
+  constexpr int HP = G::HP;
+  constexpr int DPL = D >= 32 ? D / 32 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const T* kh;
+  const T* vh;
+  int64_t n;
+  resolve_seq<T>(p, b, h, kh, vh, n);
+  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
+  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
+  if (split >= nsplit) return;
+  const int64_t t0 = (int64_t)split * chunk;
+  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = p.g;
+
+  float qv[HP][DPL], acc[HP][DPL], m[HP], l[HP];
+  const T* qb = static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h;
+#pragma unroll
+  for (int i = 0; i < HP; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      const int d = lane + 32 * j;
+      qv[i][j] = (i < g && d < D) ? to_f32<T>(qb[i * p.sq_g + d]) : 0.f;
+      acc[i][j] = 0.f;
+    }
+  }
+  for (int64_t t = t0 + warp; t < t1; t += kCWarps) {
+    float kv[DPL], vv[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      const int d = lane + 32 * j;
+      kv[j] = d < D ? to_f32<T>(kh[t * p.sk_n + d]) : 0.f;
+      vv[j] = d < D ? to_f32<T>(vh[t * p.sv_n + d]) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < HP; ++i) {
+      if (i < g) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) s = fmaf(qv[i][j], kv[j], s);
+        s = warp_sum(s) * p.c;
+        const float mn = fmaxf(m[i], s);
+        const float al = fast_exp2(m[i] - mn);
+        const float pp = fast_exp2(s - mn);
+        l[i] = l[i] * al + pp;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(pp, vv[j], acc[i][j] * al);
+        m[i] = mn;
+      }
+    }
+  }
+  using R = Region<D, HP>;
+  float* reg = reinterpret_cast<float*>(smem + warp * G::kRegionBytes);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < HP; ++i) {
+      R::m(reg)[i] = m[i];
+      R::l(reg)[i] = l[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < HP; ++i)
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) {
+      const int d = lane + 32 * j;
+      if (d < D) R::acc(reg, i)[d] = acc[i][j];
+    }
+  __syncthreads();
+  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kCWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
+}
+
+// ------------------------------------------------------------------------------------------------
+// LSE merge of normalised partials (cross-GPU combine and the merge of flash_decode.py:68-69).
+template <typename T>
+__global__ void merge_partials_kernel(const float* __restrict__ o_parts, const float* __restrict__ lse_parts,
+                                      T* __restrict__ out, float* __restrict__ lse_out, int parts, int64_t rows,
+                                      int d, int64_t out_stride_row) {
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int pi = 0; pi < parts; ++pi) M = fmaxf(M, lse_parts[(int64_t)pi * rows + row]);
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int pi = 0; pi < parts; ++pi) L += __expf(lse_parts[(int64_t)pi * rows + row] - M);
+  for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
+    float o = 0.f;
+    if (M != -INFINITY)
+      for (int pi = 0; pi < parts; ++pi) {
+        const float w = __expf(lse_parts[(int64_t)pi * rows + row] - M);
+        o += w * o_parts[((int64_t)pi * rows + row) * d + dd];
+      }
+    out[row * out_stride_row + dd] = from_f32<T>(L > 0.f ? o / L : 0.f);
+  }
+  if (lse_out != nullptr && threadIdx.x == 0) lse_out[row] = L > 0.f ? M + __logf(L) : -INFINITY;
+}
+
+}  // namespace tc

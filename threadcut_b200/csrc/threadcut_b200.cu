@@ -1,0 +1,543 @@
+// threadcut_b200 C ABI: host launchers for the decode-attention and splice kernels.
+// This is the library's only translation unit; it includes every kernel header.
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "decode_attn.cuh"
+#include "rope_splice.cuh"
+
+using namespace tc;
+
+namespace {
+
+std::mutex g_mu;
+std::set<std::pair<const void*, int>> g_smem_configured;
+int g_sm_count[256] = {0};
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return 0;
+  return d;
+}
+
+int sm_count(int dev) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (dev < 0 || dev >= 256) return 148;
+  if (g_sm_count[dev] == 0) {
+    int c = 0;
+    if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+    g_sm_count[dev] = c;
+  }
+  return g_sm_count[dev];
+}
+
+// Opt a kernel into more than 48 KB of dynamic shared memory, once per (kernel, device).
+cudaError_t set_smem(const void* fn, int bytes, int dev) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  std::lock_guard<std::mutex> lk(g_mu);
+  const auto key = std::make_pair(fn, dev);
+  if (g_smem_configured.count(key)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) g_smem_configured.insert(key);
+  return e;
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+size_t esize(int dtype) { return dtype == TC_F32 ? 4 : 2; }
+bool valid_dtype(int dtype) { return dtype == TC_F32 || dtype == TC_F16 || dtype == TC_BF16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool stride16(int64_t s, int dtype) { return ((s * (int64_t)esize(dtype)) & 15) == 0; }
+size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+bool mma_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+bool gen_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128; }
+
+// ------------------------------------------------------------------------------- decode planning
+struct DecodePlan {
+  int64_t tps = 1;         // tiles per split
+  int64_t max_splits = 1;  // grid.x
+};
+
+DecodePlan plan_decode(int batch, int hkv, int64_t max_n, int64_t total_tokens, bool ragged, int splits_req,
+                       int ctas_per_sm, int sms) {
+  DecodePlan pl;
+  const int64_t slots = (int64_t)sms * ctas_per_sm;
+  const int64_t tiles = max_n > 0 ? cdiv(max_n, kTile) : 1;
+  int64_t tps;
+  if (splits_req > 0) {
+    int64_t s = splits_req;
+    if (s > kMaxSplits) s = kMaxSplits;
+    if (s > tiles) s = tiles;
+    tps = cdiv(tiles, s);
+  } else if (!ragged) {
+    // one resident wave: every (sequence, head) gets slots/(batch*hkv) slices of equal length
+    int64_t s = slots / ((int64_t)batch * hkv);
+    if (s < 1) s = 1;
+    if (s > tiles) s = tiles;
+    if (s > kMaxSplits) s = kMaxSplits;
+    tps = cdiv(tiles, s);
+  } else {
+    // ragged lengths: many equal-size slices that the block scheduler load-balances
+    const int64_t tt = total_tokens > 0 ? total_tokens : (int64_t)batch * max_n;
+    const int64_t total_tiles = (int64_t)hkv * (cdiv(tt, kTile) + batch);
+    tps = cdiv(total_tiles, 2 * slots);
+    if (tps < 1) tps = 1;
+    if (tps > 64) tps = 64;
+  }
+  if (tps < cdiv(tiles, kMaxSplits)) tps = cdiv(tiles, kMaxSplits);
+  pl.tps = tps;
+  pl.max_splits = cdiv(tiles, tps);
+  return pl;
+}
+
+struct WsLayout {
+  size_t counters = 0, ml = 0, o = 0, total = 0;
+};
+
+WsLayout decode_ws_layout(int batch, int hkv, int g, int d, int64_t max_splits) {
+  WsLayout w;
+  const int64_t rows = (int64_t)batch * hkv;
+  w.counters = 0;
+  w.ml = round256(sizeof(int) * rows);
+  w.o = w.ml + round256(sizeof(float) * rows * max_splits * g * 2);
+  w.total = w.o + round256(sizeof(float) * rows * max_splits * g * d);
+  return w;
+}
+
+template <typename T, int D, int NG>
+cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
+  auto fn = decode_mma_kernel<T, D, NG>;
+  const int smem = MmaGeom<D>::kSmem;
+  cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  if (e != cudaSuccess) return e;
+  fn<<<grid, 32 * (kCWarps + 1), smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_gen(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
+  auto fn = decode_generic_kernel<T, D>;
+  constexpr int merge_bytes = kMaxSplits * 16 * 4;
+  const int smem = GenGeom<D>::kSmem > merge_bytes ? GenGeom<D>::kSmem : merge_bytes;
+  cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  if (e != cudaSuccess) return e;
+  fn<<<grid, 32 * kCWarps, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_mma(const DecodeParams& p, int d, dim3 grid, cudaStream_t st, int dev) {
+  const bool two = p.g > 8;
+  switch (d) {
+    case 16: return two ? launch_mma<T, 16, 2>(p, grid, st, dev) : launch_mma<T, 16, 1>(p, grid, st, dev);
+    case 32: return two ? launch_mma<T, 32, 2>(p, grid, st, dev) : launch_mma<T, 32, 1>(p, grid, st, dev);
+    case 64: return two ? launch_mma<T, 64, 2>(p, grid, st, dev) : launch_mma<T, 64, 1>(p, grid, st, dev);
+    case 128: return two ? launch_mma<T, 128, 2>(p, grid, st, dev) : launch_mma<T, 128, 1>(p, grid, st, dev);
+    case 256: return two ? launch_mma<T, 256, 2>(p, grid, st, dev) : launch_mma<T, 256, 1>(p, grid, st, dev);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+cudaError_t dispatch_gen(const DecodeParams& p, int d, dim3 grid, cudaStream_t st, int dev) {
+  switch (d) {
+    case 16: return launch_gen<T, 16>(p, grid, st, dev);
+    case 32: return launch_gen<T, 32>(p, grid, st, dev);
+    case 64: return launch_gen<T, 64>(p, grid, st, dev);
+    case 128: return launch_gen<T, 128>(p, grid, st, dev);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Shared by every decode entry point. `kv_aligned` says whether every K/V row start is 16-byte
+// aligned (the bulk-copy rule); the 16-bit tensor-core kernel is used only then.
+int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int64_t total_tokens, int splits_req,
+               bool kv_aligned, float scale, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (p.hkv < 1 || p.hkv > 65535 || p.g < 1 || p.g > 16 || p.batch < 1 || p.batch > 65535 || max_n < 0)
+    return TC_ERR_INVALID;
+  if (!(scale == scale) || scale == INFINITY || scale == -INFINITY) return TC_ERR_INVALID;
+  if (p.q == nullptr || p.out == nullptr) return TC_ERR_INVALID;
+  const bool use_mma = dtype != TC_F32 && kv_aligned && mma_dim(d);
+  if (!use_mma && !gen_dim(d)) return mma_dim(d) ? TC_ERR_ALIGN : TC_ERR_INVALID;
+  const int dev = current_device();
+  const DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
+                                    use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
+  const WsLayout w = decode_ws_layout(p.batch, p.hkv, p.g, d, pl.max_splits);
+  if (ws == nullptr || ws_bytes < w.total) return TC_ERR_WORKSPACE;
+  uint8_t* wb = static_cast<uint8_t*>(ws);
+  p.counters = reinterpret_cast<int*>(wb + w.counters);
+  p.ws_ml = reinterpret_cast<float*>(wb + w.ml);
+  p.ws_o = reinterpret_cast<float*>(wb + w.o);
+  p.tiles_per_split = (int)pl.tps;
+  p.max_splits = (int)pl.max_splits;
+  p.c = scale * kLog2e;
+  const dim3 grid((unsigned)pl.max_splits, (unsigned)p.hkv, (unsigned)p.batch);
+  cudaError_t e;
+  if (use_mma) {
+    e = dtype == TC_BF16 ? dispatch_mma<__nv_bfloat16>(p, d, grid, st, dev) : dispatch_mma<__half>(p, d, grid, st, dev);
+  } else {
+    e = dtype == TC_F32    ? dispatch_gen<float>(p, d, grid, st, dev)
+        : dtype == TC_BF16 ? dispatch_gen<__nv_bfloat16>(p, d, grid, st, dev)
+                           : dispatch_gen<__half>(p, d, grid, st, dev);
+  }
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+DecodeParams base_params() {
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  return p;
+}
+
+// ------------------------------------------------------------------------------- splice helpers
+int rope_vec(int dtype, int half, const void* const* ptrs, int nptrs, const int64_t* strides, int nstrides) {
+  const int vec = dtype == TC_F32 ? 4 : 8;
+  if (half % vec != 0) return 1;
+  for (int i = 0; i < nptrs; ++i)
+    if (ptrs[i] != nullptr && !aligned16(ptrs[i])) return 1;
+  for (int i = 0; i < nstrides; ++i)
+    if (!stride16(strides[i], dtype)) return 1;
+  return vec;
+}
+
+bool load_cos_sin(float* dst, const float* cos_sin, int d) {
+  if (cos_sin == nullptr) return false;
+  std::memcpy(dst, cos_sin, sizeof(float) * d);
+  return true;
+}
+
+template <typename T, int VEC>
+cudaError_t launch_shift(const ShiftParams& p, int blocks, cudaStream_t st) {
+  shift_keys_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+template <typename T, int VEC>
+cudaError_t launch_splice_copy(const SpliceCopyParams& p, int blocks, cudaStream_t st) {
+  splice_copy_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+template <typename T, int VEC>
+cudaError_t launch_splice_inplace(const SpliceParams& p, int blocks, cudaStream_t st) {
+  splice_inplace_kernel<T, VEC><<<blocks, kSpliceThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+// Calls F<T, VEC>(args...) for the runtime (dtype, vec) pair.
+#define TC_ROPE_DISPATCH(LAUNCH, dtype, vec, ...)                                                     \
+  ((dtype) == TC_F32    ? ((vec) == 4 ? LAUNCH<float, 4>(__VA_ARGS__) : LAUNCH<float, 1>(__VA_ARGS__)) \
+   : (dtype) == TC_F16  ? ((vec) == 8 ? LAUNCH<__half, 8>(__VA_ARGS__) : LAUNCH<__half, 1>(__VA_ARGS__)) \
+                        : ((vec) == 8 ? LAUNCH<__nv_bfloat16, 8>(__VA_ARGS__)                           \
+                                      : LAUNCH<__nv_bfloat16, 1>(__VA_ARGS__)))
+
+int64_t splice_rows_per_unit(int d, int vec) {
+  const int cph = (d / 2) / vec;
+  const int64_t r = (int64_t)kSpliceThreads * kSpliceTasksPerThread / cph;
+  return r < 1 ? 1 : r;
+}
+
+int grid_for(int64_t tasks, int threads, int sms, int per_sm) {
+  int64_t b = cdiv(tasks, threads);
+  const int64_t cap = (int64_t)sms * per_sm;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tc_status_string(int status) {
+  switch (status) {
+    case TC_OK: return "ok";
+    case TC_ERR_INVALID: return "invalid argument (size, shape or pointer outside the supported range)";
+    case TC_ERR_ALIGN: return "alignment rule broken (pointer or stride)";
+    case TC_ERR_DTYPE: return "unsupported dtype";
+    case TC_ERR_WORKSPACE: return "workspace missing or too small";
+    case TC_ERR_CUDA: return "CUDA launch or runtime error";
+  }
+  return "unknown status";
+}
+
+int tc_abi_version(void) { return 1; }
+
+int tc_device_errors(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_errors, sizeof(v)) != cudaSuccess) return -1;
+  if (clear) {
+    const unsigned int z = 0;
+    if (cudaMemcpyToSymbol(g_device_errors, &z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return (int)v;
+}
+
+size_t tc_decode_attention_workspace_size(int batch, int hkv, int g, int d, int64_t max_n, int64_t total_tokens,
+                                          int splits, int dtype) {
+  (void)dtype;
+  if (batch < 1 || hkv < 1 || g < 1 || d < 1 || max_n < 0) return 0;
+  const int sms = sm_count(current_device());
+  // the plan differs between the tensor-core and the generic kernel and between uniform and
+  // ragged lengths; size for the largest so one figure serves every entry point
+  int64_t ms = 1;
+  for (int ragged = 0; ragged < 2; ++ragged)
+    for (int cps : {kMmaCtasPerSm, kGenCtasPerSm}) {
+      const DecodePlan pl = plan_decode(batch, hkv, max_n, total_tokens, ragged != 0, splits, cps, sms);
+      if (pl.max_splits > ms) ms = pl.max_splits;
+    }
+  return decode_ws_layout(batch, hkv, g, d, ms).total;
+}
+
+int tc_decode_attention(const void* q, const void* k, const void* v, void* out, int hkv, int g, int d, int64_t n,
+                        int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h, int64_t k_stride_n,
+                        int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g,
+                        float scale, int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return tc_decode_attention_lse(q, k, v, out, nullptr, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h,
+                                 k_stride_n, v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits,
+                                 dtype, workspace, workspace_bytes, stream);
+}
+
+int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,
+                            int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
+                            int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                            int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
+  DecodeParams p = base_params();
+  p.q = q;
+  p.out = out;
+  p.lse = lse;
+  p.lse_b = (int64_t)hkv * g;
+  p.k = k;
+  p.v = v;
+  p.n = n;
+  p.sq_h = q_stride_h;
+  p.sq_g = q_stride_g;
+  p.so_h = out_stride_h;
+  p.so_g = out_stride_g;
+  p.sk_h = k_stride_h;
+  p.sk_n = k_stride_n;
+  p.sv_h = v_stride_h;
+  p.sv_n = v_stride_n;
+  p.hkv = hkv;
+  p.g = g;
+  p.batch = 1;
+  const bool al = aligned16(k) && aligned16(v) && stride16(k_stride_h, dtype) && stride16(k_stride_n, dtype) &&
+                  stride16(v_stride_h, dtype) && stride16(v_stride_n, dtype);
+  return run_decode(p, dtype, d, false, n, n, splits, al, scale, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int tc_decode_attention_batched(const void* q, const void* k, const void* v, void* out, int batch, int hkv, int g,
+                                int d, int64_t n, const int32_t* lengths, int64_t q_stride_b, int64_t q_stride_h,
+                                int64_t q_stride_g, int64_t k_stride_b, int64_t k_stride_h, int64_t k_stride_n,
+                                int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_b,
+                                int64_t out_stride_h, int64_t out_stride_g, float scale, int splits, int dtype,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
+  DecodeParams p = base_params();
+  p.q = q;
+  p.out = out;
+  p.k = k;
+  p.v = v;
+  p.lengths = lengths;
+  p.n = n;
+  p.sq_b = q_stride_b;
+  p.sq_h = q_stride_h;
+  p.sq_g = q_stride_g;
+  p.so_b = out_stride_b;
+  p.so_h = out_stride_h;
+  p.so_g = out_stride_g;
+  p.sk_b = k_stride_b;
+  p.sk_h = k_stride_h;
+  p.sk_n = k_stride_n;
+  p.sv_b = v_stride_b;
+  p.sv_h = v_stride_h;
+  p.sv_n = v_stride_n;
+  p.hkv = hkv;
+  p.g = g;
+  p.batch = batch;
+  const bool al = aligned16(k) && aligned16(v) && stride16(k_stride_b, dtype) && stride16(k_stride_h, dtype) &&
+                  stride16(k_stride_n, dtype) && stride16(v_stride_b, dtype) && stride16(v_stride_h, dtype) &&
+                  stride16(v_stride_n, dtype);
+  return run_decode(p, dtype, d, lengths != nullptr, n, 0, splits, al, scale, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int tc_decode_attention_ragged(const void* q, void* out, const void* const* k_ptrs, const void* const* v_ptrs,
+                               const int64_t* head_strides, const int32_t* lengths, int batch, int hkv, int g, int d,
+                               int64_t max_n, int64_t total_tokens, int64_t kv_stride_n, int64_t q_stride_b,
+                               int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_b, int64_t out_stride_h,
+                               int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (k_ptrs == nullptr || v_ptrs == nullptr || head_strides == nullptr || lengths == nullptr) return TC_ERR_INVALID;
+  DecodeParams p = base_params();
+  p.q = q;
+  p.out = out;
+  p.k_ptrs = k_ptrs;
+  p.v_ptrs = v_ptrs;
+  p.head_strides = head_strides;
+  p.lengths = lengths;
+  p.n = max_n;
+  p.sq_b = q_stride_b;
+  p.sq_h = q_stride_h;
+  p.sq_g = q_stride_g;
+  p.so_b = out_stride_b;
+  p.so_h = out_stride_h;
+  p.so_g = out_stride_g;
+  p.sk_n = kv_stride_n;
+  p.sv_n = kv_stride_n;
+  p.hkv = hkv;
+  p.g = g;
+  p.batch = batch;
+  // base alignment and head strides are the caller's contract (device arrays); the token
+  // stride is checked here
+  const bool al = stride16(kv_stride_n, dtype);
+  return run_decode(p, dtype, d, true, max_n, total_tokens, splits, al, scale, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int tc_merge_partials(const float* o_parts, const float* lse_parts, void* out, float* lse_out, int parts,
+                      int64_t rows, int d, int64_t out_stride_row, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (parts < 1 || rows < 0 || d < 1 || rows > 0x7fffffff || o_parts == nullptr || lse_parts == nullptr ||
+      out == nullptr)
+    return TC_ERR_INVALID;
+  if (rows == 0) return TC_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int threads = d >= 128 ? 128 : ((d + 31) / 32) * 32;
+  const dim3 grid((unsigned)rows);
+  if (dtype == TC_F32)
+    merge_partials_kernel<float><<<grid, threads, 0, st>>>(o_parts, lse_parts, static_cast<float*>(out), lse_out,
+                                                          parts, rows, d, out_stride_row);
+  else if (dtype == TC_F16)
+    merge_partials_kernel<__half><<<grid, threads, 0, st>>>(o_parts, lse_parts, static_cast<__half*>(out), lse_out,
+                                                           parts, rows, d, out_stride_row);
+  else
+    merge_partials_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(
+        o_parts, lse_parts, static_cast<__nv_bfloat16*>(out), lse_out, parts, rows, d, out_stride_row);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_shift_keys(const void* keys, void* out, int64_t outer, int64_t n, int d, int64_t in_stride_outer,
+                  int64_t in_stride_n, int64_t out_stride_outer, int64_t out_stride_n, const float* cos_sin,
+                  int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (d < 2 || d % 2 || d > kMaxRopeDim || outer < 0 || n < 0 || cos_sin == nullptr) return TC_ERR_INVALID;
+  if (outer == 0 || n == 0) return TC_OK;
+  if (keys == nullptr || out == nullptr) return TC_ERR_INVALID;
+  ShiftParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.in = keys;
+  p.out = out;
+  p.outer = outer;
+  p.n = n;
+  p.in_so = in_stride_outer;
+  p.in_sn = in_stride_n;
+  p.out_so = out_stride_outer;
+  p.out_sn = out_stride_n;
+  p.d = d;
+  load_cos_sin(p.cs, cos_sin, d);
+  const void* ptrs[2] = {keys, out};
+  const int64_t strides[4] = {in_stride_outer, in_stride_n, out_stride_outer, out_stride_n};
+  const int vec = rope_vec(dtype, d / 2, ptrs, 2, strides, 4);
+  const int64_t tasks = outer * n * ((d / 2) / vec);
+  const int blocks = grid_for(tasks, 256, sm_count(current_device()), 16);
+  const cudaError_t e = TC_ROPE_DISPATCH(launch_shift, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+size_t tc_splice_workspace_size(int layers, int hkv, int64_t c) {
+  if (layers < 1 || hkv < 1 || c < 0) return 0;
+  // a unit covers at least kSpliceThreads*kSpliceTasksPerThread / (kMaxRopeDim/2) = 2 rows (the
+  // scalar path on the widest rows), which bounds the number of per-unit flags from above
+  const int64_t worst = c > 0 ? cdiv(c, 2) : 0;
+  return 16 + sizeof(unsigned int) * (size_t)layers * hkv * (size_t)worst;
+}
+
+int tc_splice_inplace(void* const* kbufs, void* const* vbufs, int layers, int hkv, int d, int64_t cap, int64_t a,
+                      int64_t c0, int64_t c, int64_t stride_h, int64_t stride_n, const float* cos_sin, int dtype,
+                      void* workspace, size_t workspace_bytes, uint32_t epoch, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (layers < 1 || layers > kMaxLayers || hkv < 1 || d < 2 || d % 2 || d > kMaxRopeDim || a < 0 || c < 0 ||
+      c0 < a || c0 + c > cap || kbufs == nullptr || vbufs == nullptr)
+    return TC_ERR_INVALID;
+  if (c == 0 || c0 == a) return TC_OK;  // nothing moves (kv.py:85-87 clones C onto itself)
+  if (cos_sin == nullptr || epoch == 0) return TC_ERR_INVALID;
+  for (int l = 0; l < layers; ++l)
+    if (kbufs[l] == nullptr || vbufs[l] == nullptr) return TC_ERR_INVALID;
+  SpliceParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int l = 0; l < layers; ++l) {
+    p.kb[l] = kbufs[l];
+    p.vb[l] = vbufs[l];
+  }
+  const int64_t strides[2] = {stride_h, stride_n};
+  int vec = rope_vec(dtype, d / 2, const_cast<const void* const*>(kbufs), layers, strides, 2);
+  if (vec > 1 && rope_vec(dtype, d / 2, const_cast<const void* const*>(vbufs), layers, strides, 2) == 1) vec = 1;
+  p.layers = layers;
+  p.hkv = hkv;
+  p.d = d;
+  p.rows_per_unit = (int)splice_rows_per_unit(d, vec);
+  p.a = a;
+  p.c0 = c0;
+  p.c = c;
+  p.gap = c0 - a;
+  p.nchunks = cdiv(c, p.rows_per_unit);
+  p.sh = stride_h;
+  p.sn = stride_n;
+  p.epoch = epoch;
+  load_cos_sin(p.cs, cos_sin, d);
+  const size_t need = 16 + sizeof(unsigned int) * (size_t)layers * hkv * (size_t)p.nchunks;
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return TC_ERR_WORKSPACE;
+  p.ws = static_cast<SpliceWs*>(workspace);
+  const int64_t units = (int64_t)layers * hkv * p.nchunks;
+  const int sms = sm_count(current_device());
+  int64_t blocks = (int64_t)sms * 6;
+  if (blocks > units) blocks = units;
+  const cudaError_t e =
+      TC_ROPE_DISPATCH(launch_splice_inplace, dtype, vec, p, (int)blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_splice_copy(const void* k_in, const void* v_in, void* k_out, void* v_out, int hkv, int d, int64_t a,
+                   int64_t c0, int64_t c, int64_t in_stride_h, int64_t in_stride_n, int64_t out_stride_h,
+                   int64_t out_stride_n, const float* cos_sin, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (hkv < 1 || d < 2 || d % 2 || d > kMaxRopeDim || a < 0 || c < 0 || c0 < a) return TC_ERR_INVALID;
+  if (a + c == 0) return TC_OK;
+  if (k_in == nullptr || v_in == nullptr || k_out == nullptr || v_out == nullptr) return TC_ERR_INVALID;
+  const bool rotate = c > 0 && c0 != a;
+  if (rotate && cos_sin == nullptr) return TC_ERR_INVALID;
+  SpliceCopyParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.kin = k_in;
+  p.vin = v_in;
+  p.kout = k_out;
+  p.vout = v_out;
+  p.hkv = hkv;
+  p.a = a;
+  p.c0 = c0;
+  p.c = c;
+  p.in_sh = in_stride_h;
+  p.in_sn = in_stride_n;
+  p.out_sh = out_stride_h;
+  p.out_sn = out_stride_n;
+  p.d = d;
+  p.rotate = rotate ? 1 : 0;
+  if (rotate) load_cos_sin(p.cs, cos_sin, d);
+  const void* ptrs[4] = {k_in, v_in, k_out, v_out};
+  const int64_t strides[4] = {in_stride_h, in_stride_n, out_stride_h, out_stride_n};
+  const int vec = rope_vec(dtype, d / 2, ptrs, 4, strides, 4);
+  const int64_t tasks = (int64_t)hkv * (a + c) * ((d / 2) / vec);
+  const int blocks = grid_for(tasks, 256, sm_count(current_device()), 16);
+  const cudaError_t e =
+      TC_ROPE_DISPATCH(launch_splice_copy, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+}  // extern "C"

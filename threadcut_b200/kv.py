@@ -1,0 +1,192 @@
+"""KV-cache surgery on B200 — drop-in for threadcut/kv.py.
+
+A request that prunes span B turns the cache A.B.C into A.C. Keys are cached after RoPE and
+rotations compose, so moving C left by gap = |B| positions only needs every key of C re-rotated by
+-gap (threadcut/kv.py:1-7); values move unchanged.
+
+* `shift_keys(keys, delta, inv_freq)` (kv.py:20-25): out-of-place re-rotation, kernel
+  tc_shift_keys. Bit-identical to the reference's fp32 torch expression for the same cos/sin table.
+* `GrowingLayer` (kv.py:44-92): the same preallocated, 1.25x-growing per-layer buffer
+  [b, hkv, cap, d] with `keys`/`values` views; `splice` runs tc_splice_inplace (one launch, in
+  place even when C's source and destination rows overlap).
+* `splice(cache, s, inv_freq)` (kv.py:28-41): when every layer is a GrowingLayer with the same
+  buffer geometry, ALL layers are spliced in ONE launch; otherwise the copy path (tc_splice_copy per
+  layer, new tensors, as the reference's index_select path).
+* `new_cache(config)` (kv.py:95-98).
+The cos/sin table is built on the host exactly as the reference builds it (fp32 angle
+delta*inv_freq, torch cos/sin) and passed by value into the launch.
+"""
+import ctypes
+
+import torch
+from transformers import DynamicCache
+from transformers.cache_utils import DynamicLayer
+
+from ._lib import check, cos_sin_table, dtype_code, lib, require_cuda, stream_ptr, workspaces
+from .match import Split
+
+__all__ = ["rotate_half", "shift_keys", "splice", "GrowingLayer", "new_cache"]
+
+
+def rotate_half(x):
+    """(x1, x2) -> (-x2, x1) over the two halves of the last dim (torch; used by callers' RoPE)."""
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def _rows_view(t):
+    """View t [..., n, d] as [outer, n, d] without copying when the leading dims collapse."""
+    if t.dim() == 2:
+        return t.unsqueeze(0)
+    return t.reshape(-1, t.shape[-2], t.shape[-1])
+
+
+def shift_keys(keys, delta, inv_freq):
+    """Move post-RoPE keys by `delta` positions (negative = left). Math in fp32, result in keys.dtype."""
+    what = "shift_keys"
+    require_cuda(keys, what=what)
+    code = dtype_code(keys, what)
+    d = keys.shape[-1]
+    if inv_freq.numel() * 2 != d:
+        raise ValueError(f"{what}: inv_freq has {inv_freq.numel()} entries, keys need {d // 2}")
+    src = keys if keys.stride(-1) == 1 else keys.contiguous()
+    src3 = _rows_view(src)
+    out = torch.empty(keys.shape, dtype=keys.dtype, device=keys.device)
+    out3 = out.view(src3.shape)
+    tab, tab_ptr = cos_sin_table(int(delta), inv_freq)
+    with torch.cuda.device(keys.device):
+        st = lib().tc_shift_keys(src3.data_ptr(), out3.data_ptr(), src3.shape[0], src3.shape[1], d,
+                                 src3.stride(0), src3.stride(1), out3.stride(0), out3.stride(1), tab_ptr, code,
+                                 stream_ptr(keys.device))
+    check("tc_shift_keys", st)
+    del tab
+    return out
+
+
+def _splice_growing(layers, s: Split, inv_freq):
+    """In-place A.B.C -> A.C over GrowingLayers that share buffer geometry: one kernel launch."""
+    kb0 = layers[0].kbuf
+    require_cuda(kb0, what="splice")
+    b, hkv, cap, d = kb0.shape
+    code = dtype_code(kb0, "splice")
+    L = len(layers)
+    # the batch dim folds into the head dim (b = 1 in the engine; b > 1 works when contiguous)
+    kptrs = (ctypes.c_void_p * L)(*[ly.kbuf.data_ptr() for ly in layers])
+    vptrs = (ctypes.c_void_p * L)(*[ly.vbuf.data_ptr() for ly in layers])
+    if b != 1 and kb0.stride(0) != hkv * kb0.stride(1):
+        raise ValueError("splice: batched GrowingLayer buffers must be contiguous over (b, hkv)")
+    if s.a < 0 or s.c < 0 or s.c0 < s.a or s.c0 + s.c > cap:
+        raise ValueError(f"splice: {s} does not fit a buffer of {cap} rows")
+    tab, tab_ptr = cos_sin_table(-s.gap, inv_freq)
+    dev = kb0.device
+    lk = lib()
+    ws = workspaces.get("splice", dev, lk.tc_splice_workspace_size(L, b * hkv, s.c))
+    epoch = workspaces.next_epoch("splice", dev)
+    with torch.cuda.device(dev):
+        st = lk.tc_splice_inplace(kptrs, vptrs, L, b * hkv, d, cap, s.a, s.c0, s.c, kb0.stride(1), kb0.stride(2),
+                                  tab_ptr, code, ws.data_ptr(), ws.numel(), epoch, stream_ptr(dev))
+    check("tc_splice_inplace", st)
+    del tab
+
+
+def _same_geometry(layers):
+    k0 = layers[0].kbuf
+    for ly in layers:
+        for t in (ly.kbuf, ly.vbuf):
+            if (t is None or t.shape != k0.shape or t.stride() != k0.stride() or t.dtype != k0.dtype
+                    or t.device != k0.device):
+                return False
+    return True
+
+
+def splice(cache, s: Split, inv_freq):
+    """Rewrite every layer of a DynamicCache from A.B.C.(tail) to A.C."""
+    layers = cache.layers
+    if all(isinstance(layer, GrowingLayer) for layer in layers):
+        live = [ly for ly in layers if ly.kbuf is not None]
+        if s.c and s.gap and live:
+            if _same_geometry(live):
+                _splice_growing(live, s, inv_freq)
+            else:
+                for ly in live:
+                    _splice_growing([ly], s, inv_freq)
+        for ly in layers:
+            ly.n = s.a + s.c
+            if ly.kbuf is not None:
+                ly._view()
+        return
+    for layer in layers:
+        k, v = layer.keys, layer.values
+        require_cuda(k, v, what="splice")
+        bsz, hkv, _, d = k.shape
+        nk = torch.empty((bsz, hkv, s.a + s.c, d), dtype=k.dtype, device=k.device)
+        nv = torch.empty_like(nk)
+        tab, tab_ptr = cos_sin_table(-s.gap, inv_freq)
+        code = dtype_code(k, "splice")
+        for i in range(bsz):
+            ki, vi = k[i], v[i]
+            if ki.stride(-1) != 1:
+                ki = ki.contiguous()
+            if vi.stride(-1) != 1 or vi.stride() != ki.stride():
+                vi = vi.contiguous()
+                ki = ki.contiguous()
+            with torch.cuda.device(k.device):
+                st = lib().tc_splice_copy(ki.data_ptr(), vi.data_ptr(), nk[i].data_ptr(), nv[i].data_ptr(), hkv, d,
+                                          s.a, s.c0, s.c, ki.stride(0), ki.stride(1), nk.stride(1), nk.stride(2),
+                                          tab_ptr, code, stream_ptr(k.device))
+            check("tc_splice_copy", st)
+        del tab
+        layer.keys, layer.values = nk, nv
+
+
+class GrowingLayer(DynamicLayer):
+    """DynamicLayer backed by a preallocated buffer: appending a token writes in place instead of
+    re-copying the whole cache with torch.cat. Grows by max(need, 1.25x, +2048 tokens), the same
+    policy as threadcut/kv.py:53-63."""
+
+    def lazy_initialization(self, key_states, value_states, *args, **kwargs):
+        super().lazy_initialization(key_states, value_states)
+        self.n, self.kbuf, self.vbuf = 0, None, None
+
+    def _reserve(self, need, like):
+        cap = 0 if self.kbuf is None else self.kbuf.shape[-2]
+        if need <= cap:
+            return
+        grown = max(need, int(cap * 1.25), cap + 2048)
+        kb = like.new_empty((*like.shape[:-2], grown, like.shape[-1]))
+        vb = torch.empty_like(kb)
+        if self.n:
+            kb[..., :self.n, :] = self.kbuf[..., :self.n, :]
+            vb[..., :self.n, :] = self.vbuf[..., :self.n, :]
+        self.kbuf, self.vbuf = kb, vb
+
+    def _view(self):
+        self.keys, self.values = self.kbuf[..., :self.n, :], self.vbuf[..., :self.n, :]
+
+    def update(self, key_states, value_states, *args, **kwargs):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        add = key_states.shape[-2]
+        self._reserve(self.n + add, key_states)
+        self.kbuf[..., self.n:self.n + add, :] = key_states
+        self.vbuf[..., self.n:self.n + add, :] = value_states
+        self.n += add
+        self._view()
+        return self.keys, self.values
+
+    def crop(self, max_length):
+        self.n = min(self.n, max_length)
+        self._view()
+
+    def splice(self, s: Split, inv_freq):
+        """In-place A.B.C -> A.C: only C is touched, O(|C|) bytes, one kernel launch."""
+        if s.c and s.gap:
+            _splice_growing([self], s, inv_freq)
+        self.n = s.a + s.c
+        self._view()
+
+
+def new_cache(config):
+    cache = DynamicCache(config=config)
+    cache.layers = [GrowingLayer() for _ in cache.layers]
+    return cache
