@@ -31,7 +31,14 @@ import workloads  # noqa: E402
 METRIC = "flash-decode µs/layer & % of HBM peak (Qwen3-4B GQA, 16k ctx); shift GB/s"
 N_CTX = 16384
 LAYERS = workloads.LAYERS
-BYTES_PER_LAYER = 4096 * N_CTX + 16384          # K+V (2*8*n*128*2 B) + q + o
+
+
+def decode_bytes(n):
+    """Algorithmic bytes of one decode launch: K+V (2 * 8 heads * n * 128 * 2 B) + q + o."""
+    return 4096 * n + 16384
+
+
+BYTES_PER_LAYER = decode_bytes(N_CTX)
 SHIFT_BYTES_PER_LAYER = 4 * 4096 * 8 * 128 * 2  # K read+write and V read+write of |C| = 4096 rows
 FALLBACK_HBM_GBS = 6650.0
 
@@ -209,25 +216,29 @@ def time_e2e(qs, ks, vs, steps, warmup, dist, dev):
     return e0.elapsed_time(e1) / steps, host_q.numel() * host_q.element_size(), host_out.numel() * 2
 
 
-def time_shift(steps, warmup, dev, dist):
-    """Config 2 splice (Split(2048, 4096, 4096) of an 8192-token cache) on all 36 layers, one launch
-    per step, in place; returns ms per launch."""
-    from threadcut_b200.kv import splice, new_cache
-    from threadcut_b200.match import Split
-    from transformers import Qwen3Config
-    cfg = Qwen3Config(num_hidden_layers=LAYERS, num_key_value_heads=8, head_dim=128)
-    cache = new_cache(cfg)
+def time_shift(steps, warmup, dev, dist, layers=LAYERS):
+    """Config 2 splice (Split(2048, 4096, 4096) of an 8192-token cache) on all layers, one in-place
+    launch per step through the C ABI (arguments prepared once, a fresh epoch per call); returns ms
+    per launch. Every step splices the same rows again, so the bytes moved are the same each time."""
+    import ctypes
+    from threadcut_b200._lib import TC_BF16, check, cos_sin_table, lib, workspaces
+    L = lib()
     g = torch.Generator(device=dev).manual_seed(7)
-    for layer in cache.layers:
-        k = torch.randn(1, 8, workloads.CFG2_N, 128, generator=g, device=dev).to(torch.bfloat16)
-        layer.update(k, k.clone())
-    s = Split(*workloads.CFG2_SPLIT)
-    inv = workloads.inv_freq()
+    n = workloads.CFG2_N
+    kbufs = [torch.randn(8, n, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    vbufs = [k.clone() for k in kbufs]
+    a, c0, c = workloads.CFG2_SPLIT
+    kp = (ctypes.c_void_p * layers)(*[k.data_ptr() for k in kbufs])
+    vp = (ctypes.c_void_p * layers)(*[v.data_ptr() for v in vbufs])
+    tab, tab_ptr = cos_sin_table(a - c0, workloads.inv_freq())
+    ws = workspaces.get("splice-bench", dev, L.tc_splice_workspace_size(layers, 8, c))
+    epoch = [0]
 
     def run():
-        splice(cache, s, inv)
-        for layer in cache.layers:  # the next step splices the same rows again (same bytes moved)
-            layer.n = workloads.CFG2_N
+        epoch[0] += 1
+        check("tc_splice_inplace", L.tc_splice_inplace(kp, vp, layers, 8, 128, n, a, c0, c, n * 128, 128, tab_ptr,
+                                                       TC_BF16, ws.data_ptr(), ws.numel(), epoch[0],
+                                                       torch.cuda.current_stream(dev).cuda_stream))
     for _ in range(warmup):
         run()
     barrier(dist)
@@ -238,6 +249,7 @@ def time_shift(steps, warmup, dev, dist):
     e1.record()
     e1.synchronize()
     barrier(dist)
+    del tab
     return e0.elapsed_time(e1) / steps
 
 
@@ -334,6 +346,26 @@ def run_ours(args, rank, local, world, dist):
         print(json.dumps(line), flush=True)
 
 
+def run_partial(args, rank, local, world, dist):
+    """Profiling helper: one leg at a chosen size, no CPU baseline or e2e (not the bench contract)."""
+    dev = torch.device("cuda", local)
+    out = {"only": args.only, "layers": args.layers, "ctx": args.ctx, "steps": args.steps}
+    if args.only == "decode":
+        qs, ks, vs = build_layers(args.ctx, args.layers, dev, seed=1000 + rank)
+        outs = [torch.empty_like(q) for q in qs]
+        graph = capture_step(qs, ks, vs, outs, dev)
+        ms = max_over_ranks(time_graph(graph, args.steps, args.warmup, dist), dist)
+        us = ms * 1000 / args.layers
+        out.update(us_per_layer=round(us, 3), gbs=round(decode_bytes(args.ctx) / (us * 1e-6) / 1e9, 1))
+        del graph
+    else:
+        ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist, layers=args.layers), dist)
+        out.update(us_per_layer=round(ms * 1000 / args.layers, 3),
+                   gbs=round(SHIFT_BYTES_PER_LAYER * args.layers / (ms * 1e-3) / 1e9, 1))
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -369,6 +401,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--only", choices=["all", "decode", "shift"], default="all",
+                    help="profiling runs: time only the decode graph or only the splice (smaller JSON line)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="profiling runs: layers per step")
+    ap.add_argument("--ctx", type=int, default=N_CTX, help="profiling runs: context length")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -376,6 +412,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.only != "all":
+            run_partial(args, rank, local, world, dist)
         else:
             run_ours(args, rank, local, world, dist)
     finally:

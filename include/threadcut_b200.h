@@ -62,7 +62,9 @@ int tc_device_errors(int clear);
  * the other strides are free (a GrowingLayer view has head stride cap*d). Result in the input
  * dtype; math in fp32: softmax(scale * q k^T) v, exactly what flash_decode.py:_partial computes.
  *
- * Limits: d in {16, 32, 64, 128, 256} (fp32: d <= 128), 1 <= g <= 16, n >= 0 (n == 0 gives
+ * Limits: d in {16, 32, 64, 128, 256}: 16-bit K/V with d in {64, 128, 256} and 16-byte aligned rows
+ * run the tensor-core TMA kernel, everything else (fp32 included, d <= 128) the generic kernel;
+ * 1 <= g <= 16, n >= 0 (n == 0 gives
  * zeros, as the reference's empty merge does). splits = 0 picks the KV partition from the SM
  * count; splits > 0 forces that many KV slices per (sequence, head) (capped at 128).
  *
@@ -96,20 +98,35 @@ int tc_decode_attention_batched(const void* q, const void* k, const void* v, voi
                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* Ragged decode: sequence b has its own K/V allocation k_ptrs[b]/v_ptrs[b] of shape
- * [hkv, >= lengths[b], d] with head stride head_strides[b] (elements) and token stride
+ * [hkv, cap_b >= lengths[b], d] with head stride head_strides[b] (elements) and token stride
  * kv_stride_n, shared by K and V. k_ptrs, v_ptrs, head_strides and lengths are DEVICE arrays.
  * Every K/V base must be 16-byte aligned and head/token strides multiples of 8 elements (16-bit
  * types) — the caller guarantees this; it cannot be checked without reading device memory.
+ * `tensormaps` (DEVICE, 64-byte aligned, may be NULL) holds the 2*batch maps written by
+ * tc_ragged_encode_tensormaps for these caches; with it 16-bit caches of d in {64,128,256} take
+ * the tensor-core TMA kernel, without it the generic kernel.
  * max_n >= every length; total_tokens = sum of lengths (a scheduling hint; 0 = batch*max_n). */
 int tc_decode_attention_ragged(const void* q, void* out,
                                const void* const* k_ptrs, const void* const* v_ptrs,
-                               const int64_t* head_strides, const int32_t* lengths,
+                               const int64_t* head_strides, const int32_t* lengths, const void* tensormaps,
                                int batch, int hkv, int g, int d, int64_t max_n, int64_t total_tokens,
                                int64_t kv_stride_n,
                                int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_g,
                                int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_g,
                                float scale, int splits, int dtype,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of the tensor-map array for `batch` ragged sequences (2 maps of 128 bytes each). */
+size_t tc_ragged_tensormaps_size(int batch);
+
+/* Encodes, on the host, the K and V tensor maps of each ragged sequence into host_out
+ * (tc_ragged_tensormaps_size(batch) bytes): k_ptrs/v_ptrs/caps/head_strides are HOST arrays here;
+ * cap_b is the row capacity of sequence b's allocation (rows in [length, cap) are masked). Copy the
+ * result to 64-byte aligned device memory and pass it to tc_decode_attention_ragged. 16-bit dtypes,
+ * d in {64, 128, 256}. */
+int tc_ragged_encode_tensormaps(void* host_out, const void* const* k_ptrs, const void* const* v_ptrs,
+                                const int64_t* caps, const int64_t* head_strides, int64_t kv_stride_n,
+                                int batch, int hkv, int d, int dtype);
 
 /* ======================================================================================
  * RoPE key shift: out = k*cos(delta*theta) + rotate_half(k)*sin(delta*theta), in fp32 with the

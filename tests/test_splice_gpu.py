@@ -132,7 +132,7 @@ def test_inplace_splice_overlap_sweep(a, c0, c):
     ly.update(kb, vb)
     ly.splice(Split(a, c0, c), workloads.inv_freq())
     assert ly.get_seq_length() == n
-    assert exact(ly.kbuf[0], kref) and exact(ly.vbuf[0], vref)
+    assert exact(ly.kbuf[0, :, :cap], kref) and exact(ly.vbuf[0, :, :cap], vref)
 
 
 def test_all_layers_one_launch_equals_per_layer():
@@ -178,7 +178,7 @@ def test_repeated_splices_reuse_the_workspace():
         kref, vref, n = growing_splice_ref(kref, vref, a, a + gap, c, dtype="bf16",
                                            cos_sin=ref_cos_sin(-gap, inv))
         ly.splice(Split(a, a + gap, c), inv)
-    assert exact(ly.kbuf[0], kref) and exact(ly.vbuf[0], vref)
+    assert exact(ly.kbuf[0, :, :3000], kref) and exact(ly.vbuf[0, :, :3000], vref)
 
 
 def test_splice_dtypes_and_head_dims():
@@ -193,4 +193,4 @@ def test_splice_dtypes_and_head_dims():
             ly = GrowingLayer()
             ly.update(kb, vb)
             ly.splice(Split(20, 90, 800), inv)
-            assert exact(ly.kbuf[0], kref) and exact(ly.vbuf[0], vref)
+            assert exact(ly.kbuf[0, :, :900], kref) and exact(ly.vbuf[0, :, :900], vref)

@@ -32,8 +32,11 @@ SIGNATURES = {
                                 + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_decode_attention_batched": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _vp] + [_i64] * 12
                                     + [_f, _i, _i, _vp, _sz, _vp]),
-    "tc_decode_attention_ragged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64, _i64]
+    "tc_decode_attention_ragged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64, _i64]
                                    + [_i64] * 6 + [_f, _i, _i, _vp, _sz, _vp]),
+    "tc_ragged_tensormaps_size": (_sz, [_i]),
+    "tc_ragged_encode_tensormaps": (_i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_i64),
+                                         ctypes.POINTER(_i64), _i64, _i, _i, _i, _i]),
     "tc_shift_keys": (_i, [_vp, _vp, _i64, _i64, _i] + [_i64] * 4 + [_fp, _i, _vp]),
     "tc_splice_workspace_size": (_sz, [_i, _i, _i64]),
     "tc_splice_inplace": (_i, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i, _i, _i, _i64, _i64, _i64, _i64,

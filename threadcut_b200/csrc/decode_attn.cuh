@@ -6,12 +6,15 @@
 // result cast to the input dtype.
 //
 // B200 design (16-bit K/V, the hot path):
-//   * grid (split, kv_head, sequence); each CTA owns one contiguous KV slice of one head, so every
-//     K/V byte is read exactly once per step and the folded g heads share it.
-//   * warp 4 is a producer: per 32-token tile each lane issues one 1-D bulk (TMA) copy of its K row
-//     and one of its V row into a padded shared-memory stage (row pitch 2*d+16 bytes, which makes
-//     the ldmatrix reads below bank-conflict free), completing on the stage's mbarrier.
-//   * warps 0-3 are consumers, warp w owns stage w (tiles w, w+4, ...). Per tile:
+//   * grid (split, kv_head, sequence), one CTA per SM (about 192 KB of K/V in flight per CTA); each
+//     CTA owns one contiguous KV slice of one head, so every K/V byte is read exactly once per step
+//     and the folded g heads share it.
+//   * warp 6 is the producer: for every 32-token tile one elected lane issues tensor-map TMA copies
+//     (cp.async.bulk.tensor, one per 64-column box of K and of V: 4 copies per 16 KB stage at
+//     d = 128) with the 128-byte swizzle, which makes the ldmatrix reads below bank-conflict free;
+//     each stage completes on its mbarrier. The 4-D maps (d, tokens, heads, batch) carry the real
+//     strides of the cache views, and rows past the end of the tensor arrive as zeros.
+//   * warps 0-5 are consumers; tile j goes to warp j % 6 and stage j % 12. Per tile:
 //       S^T[32 tok x 8 heads] = K . q^T     mma.m16n8k16 (K from ldmatrix, q^T fragments in regs)
 //       online softmax in the exp2 domain    (max via 3 xor-shuffles over the 8 token lanes)
 //       O^T[d x 8 heads] += V^T . P^T        mma.m16n8k16 (V^T from ldmatrix.trans, P^T from the
@@ -21,10 +24,12 @@
 //     Only 4 of the 8 head columns are real for Qwen3 (g = 4); the tensor core has throughput to
 //     spare, the point is to take the per-token FMA/shuffle work off the issue slots so the CTA
 //     stays a pure HBM stream.
-//   * epilogue: the 4 warps' (m, l, o) are combined in shared memory; with one split the CTA
-//     writes the output, otherwise it writes an unnormalised partial and the LAST CTA of the head
-//     (atomic ticket) merges all partials by log-sum-exp and resets the ticket.
-// fp32 (or K/V whose strides break the 16-byte bulk-copy rule) use decode_generic_kernel: the same
+//   * epilogue: the warps' (m, l, o) are combined in shared memory; with one split the CTA writes
+//     the output, otherwise it writes an unnormalised partial and the LAST CTA of the head (atomic
+//     ticket) merges all partials by log-sum-exp and resets the ticket.
+//   * launched with programmatic dependent launch: the prologue overlaps the previous kernel's
+//     tail, and nothing the previous kernel may write is read before griddepcontrol.wait.
+// fp32, d < 64, or K/V whose strides break the 16-byte TMA rule use decode_generic_kernel: the same
 // partition and epilogue with plain loads and FMA math.
 #pragma once
 
@@ -34,16 +39,19 @@
 
 namespace tc {
 
-constexpr int kTile = 32;        // tokens per staged tile (one K row + one V row per producer lane)
-constexpr int kCWarps = 4;       // consumer warps per CTA
-constexpr int kStages = 4;       // == kCWarps: consumer warp w owns stage w
+constexpr int kTile = 32;        // tokens per staged tile (the TMA box height)
+constexpr int kCWarps = 6;       // consumer warps per CTA of the tensor-core kernel (+1 producer warp)
+constexpr int kGenWarps = 4;     // warps per CTA of the generic kernel
 constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
-constexpr int kMmaCtasPerSm = 3; // resident CTAs per SM assumed by the split planner (mma kernel)
+constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM assumed by the split planner (mma kernel)
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct DecodeParams {
+  CUtensorMap tmk;               // 4-D maps (d, tokens, heads, batch) of K and V for the tensor-core
+  CUtensorMap tmv;               // kernel; unused in ragged mode and by the generic kernel
+  const CUtensorMap* tm_ragged;  // ragged mode: device array, maps of sequence b at [2b] (K), [2b+1] (V)
   const void* q;
   void* out;
   float* lse;                 // optional natural-log LSE out, [batch][hkv][g] (stride lse_b per b)
@@ -161,37 +169,81 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   if (!s_last) return;
   __threadfence();
 
-  // Last CTA of this head: merge nsplit partials. Weights w_s = 2^(m_s - M) per (split, head).
-  const float* mlb = p.ws_ml + bh * p.max_splits * g * 2;
+  // Last CTA of this head: merge nsplit partials. Each lane loads the (m, l) pair of its splits
+  // once; weights w_s = 2^(m_s - M) / L go to shared memory; then every thread owns float4 columns
+  // of the output and keeps 8 split loads in flight.
+  const float2* mlb = reinterpret_cast<const float2*>(p.ws_ml + bh * p.max_splits * g * 2);
   for (int i = warp; i < g; i += nwarps) {
+    float2 ml[kMaxSplits / 32];
+#pragma unroll
+    for (int k = 0; k < kMaxSplits / 32; ++k) {
+      const int s = lane + 32 * k;
+      ml[k] = s < nsplit ? __ldcg(mlb + (int64_t)s * g + i) : make_float2(-INFINITY, 0.f);
+    }
     float M = -INFINITY;
-    for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(mlb + ((int64_t)s * g + i) * 2));
+#pragma unroll
+    for (int k = 0; k < kMaxSplits / 32; ++k) M = fmaxf(M, ml[k].x);
     M = warp_max(M);
     float L = 0.f;
-    for (int s = lane; s < nsplit; s += 32) {
-      const float w = fast_exp2(__ldcg(mlb + ((int64_t)s * g + i) * 2) - M);
-      merge_smem[s * g + i] = w;
-      L += w * __ldcg(mlb + ((int64_t)s * g + i) * 2 + 1);
+#pragma unroll
+    for (int k = 0; k < kMaxSplits / 32; ++k) {
+      ml[k].x = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - M);
+      L += ml[k].x * ml[k].y;
     }
     L = warp_sum(L);
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxSplits / 32; ++k) {
+      const int s = lane + 32 * k;
+      if (s < nsplit) merge_smem[s * g + i] = ml[k].x * inv;
+    }
     if (lane == 0) {
       s_M[i] = M;
       s_L[i] = L;
     }
   }
   __syncthreads();
-  const float* ob = p.ws_o + bh * p.max_splits * g * D;
-  for (int idx = tid; idx < g * D; idx += nthr) {
-    const int i = idx / D, d = idx - i * D;
-    float o0 = 0.f, o1 = 0.f;
+  const float4* ob = reinterpret_cast<const float4*>(p.ws_o + bh * p.max_splits * g * D);
+  constexpr int Q = D / 4;  // float4 columns per head row
+  for (int u = tid; u < g * Q; u += nthr) {
+    const int i = u / Q;
+    float4 acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     int s = 0;
-    for (; s + 1 < nsplit; s += 2) {
-      o0 += merge_smem[s * g + i] * __ldcg(ob + ((int64_t)s * g + i) * D + d);
-      o1 += merge_smem[(s + 1) * g + i] * __ldcg(ob + ((int64_t)(s + 1) * g + i) * D + d);
+    for (; s + 8 <= nsplit; s += 8) {
+      float4 x[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = __ldcg(ob + ((int64_t)(s + k) * g) * Q + u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float w = merge_smem[(s + k) * g + i];
+        acc[k].x += w * x[k].x;
+        acc[k].y += w * x[k].y;
+        acc[k].z += w * x[k].z;
+        acc[k].w += w * x[k].w;
+      }
     }
-    if (s < nsplit) o0 += merge_smem[s * g + i] * __ldcg(ob + ((int64_t)s * g + i) * D + d);
-    const float L = s_L[i];
-    out[i * p.so_g + d] = from_f32<T>(L > 0.f ? (o0 + o1) / L : 0.f);
+    for (; s < nsplit; ++s) {
+      const float4 x = __ldcg(ob + ((int64_t)s * g) * Q + u);
+      const float w = merge_smem[s * g + i];
+      acc[0].x += w * x.x;
+      acc[0].y += w * x.y;
+      acc[0].z += w * x.z;
+      acc[0].w += w * x.w;
+    }
+#pragma unroll
+    for (int k = 1; k < 8; ++k) {
+      acc[0].x += acc[k].x;
+      acc[0].y += acc[k].y;
+      acc[0].z += acc[k].z;
+      acc[0].w += acc[k].w;
+    }
+    T* o = out + i * p.so_g + (u - i * Q) * 4;
+    o[0] = from_f32<T>(acc[0].x);
+    o[1] = from_f32<T>(acc[0].y);
+    o[2] = from_f32<T>(acc[0].z);
+    o[3] = from_f32<T>(acc[0].w);
   }
   if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
   if (tid == 0) p.counters[bh] = 0;
@@ -207,37 +259,43 @@ __device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
 
 template <int D>
 struct MmaGeom {
-  static constexpr int kPitch = D * 2 + 16;  // bytes per staged row: odd multiple of 16
-  static constexpr int kTileBytes = kTile * kPitch;
-  static constexpr int kStageBytes = 2 * kTileBytes;
+  static_assert(D % 64 == 0, "the tensor-core kernel stages 64-column (128-byte) swizzled boxes");
+  static constexpr int kBoxBytes = kTile * 128;      // one TMA box: 32 rows x 64 columns of 16-bit data
+  static constexpr int kTileBytes = kTile * D * 2;   // D/64 boxes side by side
+  static constexpr int kStageBytes = 2 * kTileBytes; // K tile then V tile
+  // ~192 KB of K/V in flight per CTA (one CTA per SM): 12 stages at d <= 128, 6 at d = 256.
+  // A multiple of kCWarps, so tile j always goes to consumer warp j % kCWarps and stage j % kStages.
+  static constexpr int kStages = D <= 128 ? 12 : 6;
+  static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
-  static constexpr int kSmem = kPipeBytes + 2 * kStages * 8;
+  static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + slack to align the base to 1 KB
 };
 
+// Byte offset of element (row, col) of a staged tile: 64-column boxes of 32 rows x 128 bytes, each
+// written by TMA with the 128-byte swizzle (16-byte chunk c of row r lands at chunk c ^ (r & 7)), so
+// the 8 rows an ldmatrix phase reads fall in 8 different bank groups.
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  const int box = col >> 6, chunk = (col & 63) >> 3;
+  return (uint32_t)(box * (kTile * 128) + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
 // ------------------------------------------------------------------------------------------------
-// Tensor-core path: T in {bf16, f16}, D in {16..256}, NG = number of 8-head column tiles (g <= 8*NG).
+// Tensor-core path: T in {bf16, f16}, D in {64, 128, 256}, NG = number of 8-head column tiles
+// (g <= 8*NG). K/V tiles arrive by tensor-map TMA: one cp.async.bulk.tensor per 64-column box.
 template <typename T, int D, int NG>
-__global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
+__global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     decode_mma_kernel(const __grid_constant__ DecodeParams p) {
   using G = MmaGeom<D>;
   constexpr int HP = 8 * NG;
   constexpr int KS = D / 16;
+  constexpr int NBOX = D / 64;
+  constexpr int kStages = G::kStages;
   static_assert(Region<D, HP>::kFloats * 4 <= G::kStageBytes, "combine region must fit in a stage");
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  // TMA 128-byte swizzle is defined on absolute shared addresses: align the pipeline to 1 KB
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes);
   uint64_t* empty = full + kStages;
-
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const T* kh;
-  const T* vh;
-  int64_t n;
-  resolve_seq<T>(p, b, h, kh, vh, n);
-  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
-  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
-  if (split >= nsplit) return;  // whole CTA leaves before touching any barrier
-  const int64_t t0 = (int64_t)split * chunk;
-  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
-  const int ntiles = n > 0 ? (int)((t1 - t0 + kTile - 1) / kTile) : 0;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -247,23 +305,43 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
       mbar_init(&empty[s], 1);
     }
     fence_mbar_init();
+    if (p.tm_ragged == nullptr) {
+      prefetch_tensormap(&p.tmk);
+      prefetch_tensormap(&p.tmv);
+    }
   }
+  pdl_launch();
+  pdl_wait();  // everything below may read what the previous kernel in the stream wrote
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
+  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
+  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
+  if (split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
+  const int64_t t0 = (int64_t)split * chunk;
+  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
+  const int ntiles = n > 0 ? (int)((t1 - t0 + kTile - 1) / kTile) : 0;
   __syncthreads();
 
   if (warp == kCWarps) {
-    // ---------------- producer: one K row and one V row per lane per tile
-    const uint64_t pol = policy_evict_first();
-    for (int j = 0; j < ntiles; ++j) {
-      const int s = j % kStages;
-      const int r = j / kStages;
-      if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * kTile * D * sizeof(T));
-      __syncwarp();
-      int64_t tok = t0 + (int64_t)j * kTile + lane;
-      if (tok > n - 1) tok = n - 1;  // tail rows repeat the last token; their scores are masked
-      uint8_t* st = smem + s * G::kStageBytes;
-      bulk_g2s(st + lane * G::kPitch, kh + tok * p.sk_n, D * sizeof(T), &full[s], pol);
-      bulk_g2s(st + G::kTileBytes + lane * G::kPitch, vh + tok * p.sv_n, D * sizeof(T), &full[s], pol);
+    // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
+    if (lane == 0 && ntiles > 0) {
+      const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
+      const CUtensorMap* mv = p.tm_ragged ? p.tm_ragged + 2 * b + 1 : &p.tmv;
+      const int cb = p.tm_ragged ? 0 : b;
+      const uint64_t pol = policy_evict_first();
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % kStages;
+        const int r = j / kStages;
+        if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)G::kStageBytes);
+        uint8_t* st = smem + s * G::kStageBytes;
+        const int tok = (int)(t0 + (int64_t)j * kTile);  // rows past the tensor end arrive as zeros
+#pragma unroll
+        for (int bx = 0; bx < NBOX; ++bx) {
+          tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, h, cb, &full[s], pol);
+          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, h, cb, &full[s], pol);
+        }
+      }
     }
   } else {
     // ---------------- consumers
@@ -305,10 +383,21 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
     for (int j = warp; j < ntiles; j += kCWarps) {
       const int s = j % kStages;
       if (!mbar_wait(&full[s], (j / kStages) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
-      const uint32_t kst = smem_u32(smem + s * G::kStageBytes);
+      uint8_t* stage = smem + s * G::kStageBytes;
+      const uint32_t kst = smem_u32(stage);
       const uint32_t vst = kst + G::kTileBytes;
       const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
       const int valid = rem < kTile ? (int)rem : kTile;
+      if (valid < kTile) {
+        // rows past this slice may hold another sequence's or uninitialised data (ragged caches
+        // are mapped to their capacity): zero those V rows so a masked p = 0 never meets a NaN
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int idx = lane; idx < (kTile - valid) * (D / 8); idx += 32) {
+          const int row = valid + idx / (D / 8), cc = idx % (D / 8);
+          *reinterpret_cast<uint4*>(stage + G::kTileBytes + (cc >> 3) * G::kBoxBytes + row * 128 + (cc & 7) * 16) = z;
+        }
+        __syncwarp();
+      }
 
       // S^T = K q^T over two 16-token m-tiles
       float sacc[2][NG][4];
@@ -325,7 +414,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
           uint32_t a[4];
           const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int col = ks * 16 + (lane >> 4) * 8;
-          ldsm_x4(kst + row * G::kPitch + col * 2, a);
+          ldsm_x4(kst + swz(row, col), a);
 #pragma unroll
           for (int nt = 0; nt < NG; ++nt) Mma<T>::run(sacc[mt][nt], a, bq[nt][ks][0], bq[nt][ks][1]);
         }
@@ -395,7 +484,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
           const int mi = lane >> 3;
           const int tok = kk * 16 + (mi >> 1) * 8 + (lane & 7);
           const int dim = md * 16 + (mi & 1) * 8;
-          ldsm_x4_t(vst + tok * G::kPitch + dim * 2, a);
+          ldsm_x4_t(vst + swz(tok, dim), a);
 #pragma unroll
           for (int nt = 0; nt < NG; ++nt) {
             Mma<T>::run(oacc[md][nt], a, bhi[kk][nt][0], bhi[kk][nt][1]);
@@ -403,6 +492,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
           }
         }
       }
+      if (valid < kTile) fence_proxy_async_smem();  // the zeroing above precedes the next TMA write
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -443,8 +533,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), kMmaCtasPerSm)
   }
   __syncthreads();
   // merge weights may reuse the pipeline buffers once the combine has read them (finish_cta syncs)
-  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, reinterpret_cast<float*>(smem + G::kStageBytes * 0),
-                       b, h, split, nsplit);
+  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -454,15 +543,17 @@ template <int D>
 struct GenGeom {
   static constexpr int HP = 16;
   static constexpr int kRegionBytes = ((Region<D, HP>::kFloats * 4 + 127) / 128) * 128;
-  static constexpr int kSmem = kCWarps * kRegionBytes;
+  static constexpr int kSmem = kGenWarps * kRegionBytes;
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(32 * kCWarps) decode_generic_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __grid_constant__ DecodeParams p) {
   using G = GenGeom<D>;
   constexpr int HP = G::HP;
   constexpr int DPL = D >= 32 ? D / 32 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_launch();
+  pdl_wait();
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const T* kh;
   const T* vh;
@@ -489,7 +580,7 @@ __global__ void __launch_bounds__(32 * kCWarps) decode_generic_kernel(const __gr
       acc[i][j] = 0.f;
     }
   }
-  for (int64_t t = t0 + warp; t < t1; t += kCWarps) {
+  for (int64_t t = t0 + warp; t < t1; t += kGenWarps) {
     float kv[DPL], vv[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; ++j) {
@@ -531,7 +622,7 @@ __global__ void __launch_bounds__(32 * kCWarps) decode_generic_kernel(const __gr
       if (d < D) R::acc(reg, i)[d] = acc[i][j];
     }
   __syncthreads();
-  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kCWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
+  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kGenWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -1,10 +1,11 @@
 // Shared device helpers for the threadcut_b200 kernels (sm_100a only).
 //
-// Everything here is a thin inline-PTX wrapper: mbarriers and 1-D bulk (TMA) copies for the
+// Everything here is a thin inline-PTX wrapper: mbarriers and tensor-map (TMA) copies for the
 // K/V staging pipeline, ldmatrix / movmatrix / mma.sync fragments for the folded-GQA tiles, and
 // bounded spin-waits that report a timeout instead of hanging the GPU.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the type only; no driver-API symbol is linked)
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -80,6 +81,33 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t 
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+
+// Tiled 4-D tensor copy (global -> shared) described by a tensor map (generic address of a
+// __grid_constant__ parameter or of a 64-byte aligned global copy); completes on `bar`.
+// Coordinates are element indices, innermost first; the innermost one must be a multiple of 8 for
+// 16-bit data (16 bytes), which holds because it is always 0 or a multiple of 64 here.
+__device__ __forceinline__ void tma_load_4d(void* sdst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(sdst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute may
+// start while the previous kernel in the stream finishes; it must call pdl_wait() before touching
+// anything that kernel writes. pdl_launch() lets the next such kernel start early. Both are no-ops
+// for launches without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- warp-level tensor-core fragments
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {

@@ -1,5 +1,8 @@
 // threadcut_b200 C ABI: host launchers for the decode-attention and splice kernels.
 // This is the library's only translation unit; it includes every kernel header.
+#include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
+
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -52,8 +55,46 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool stride16(int64_t s, int dtype) { return ((s * (int64_t)esize(dtype)) & 15) == 0; }
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-bool mma_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+bool mma_dim(int d) { return d == 64 || d == 128 || d == 256; }
 bool gen_dim(int d) { return d == 16 || d == 32 || d == 64 || d == 128; }
+
+// ------------------------------------------------------------------------------- tensor maps
+// cuTensorMapEncodeTiled is reached through the runtime's driver entry point, so the library
+// does not link libcuda directly.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 4-D map (d, rows, heads, batch) of a 16-bit K or V tensor, box 64 x kTile x 1 x 1, 128-byte
+// swizzle, rows past `rows` read as zeros. Strides in elements; extents of 1 get a harmless
+// stride. Returns false if the driver rejects the description (the caller then uses the generic
+// kernel).
+bool encode_kv_map(CUtensorMap* m, const void* base, int dtype, int d, int64_t rows, int64_t heads, int64_t batch,
+                   int64_t s_row, int64_t s_head, int64_t s_batch) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (fn == nullptr || base == nullptr) return false;
+  if (rows < 1) rows = 1;
+  if (heads == 1 || s_head <= 0) s_head = s_row * rows;
+  if (batch == 1 || s_batch <= 0) s_batch = s_head * heads;
+  const cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)batch};
+  const cuuint64_t strides[3] = {(cuuint64_t)s_row * 2, (cuuint64_t)s_head * 2, (cuuint64_t)s_batch * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)kTile, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(m, dtype == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 // ------------------------------------------------------------------------------- decode planning
 struct DecodePlan {
@@ -107,14 +148,38 @@ WsLayout decode_ws_layout(int batch, int hkv, int g, int d, int64_t max_splits) 
   return w;
 }
 
+// Programmatic dependent launch (the kernel's prologue overlaps the previous kernel's tail); set
+// TC_PDL=0 in the environment to launch plainly.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TC_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename Kern, typename Params>
+cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
 template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
   auto fn = decode_mma_kernel<T, D, NG>;
   const int smem = MmaGeom<D>::kSmem;
   cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
   if (e != cudaSuccess) return e;
-  fn<<<grid, 32 * (kCWarps + 1), smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_ex(fn, grid, dim3(32 * (kCWarps + 1)), smem, st, p);
 }
 
 template <typename T, int D>
@@ -124,16 +189,13 @@ cudaError_t launch_gen(const DecodeParams& p, dim3 grid, cudaStream_t st, int de
   const int smem = GenGeom<D>::kSmem > merge_bytes ? GenGeom<D>::kSmem : merge_bytes;
   cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
   if (e != cudaSuccess) return e;
-  fn<<<grid, 32 * kCWarps, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_ex(fn, grid, dim3(32 * kGenWarps), smem, st, p);
 }
 
 template <typename T>
 cudaError_t dispatch_mma(const DecodeParams& p, int d, dim3 grid, cudaStream_t st, int dev) {
   const bool two = p.g > 8;
   switch (d) {
-    case 16: return two ? launch_mma<T, 16, 2>(p, grid, st, dev) : launch_mma<T, 16, 1>(p, grid, st, dev);
-    case 32: return two ? launch_mma<T, 32, 2>(p, grid, st, dev) : launch_mma<T, 32, 1>(p, grid, st, dev);
     case 64: return two ? launch_mma<T, 64, 2>(p, grid, st, dev) : launch_mma<T, 64, 1>(p, grid, st, dev);
     case 128: return two ? launch_mma<T, 128, 2>(p, grid, st, dev) : launch_mma<T, 128, 1>(p, grid, st, dev);
     case 256: return two ? launch_mma<T, 256, 2>(p, grid, st, dev) : launch_mma<T, 256, 1>(p, grid, st, dev);
@@ -161,7 +223,13 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
     return TC_ERR_INVALID;
   if (!(scale == scale) || scale == INFINITY || scale == -INFINITY) return TC_ERR_INVALID;
   if (p.q == nullptr || p.out == nullptr) return TC_ERR_INVALID;
-  const bool use_mma = dtype != TC_F32 && kv_aligned && mma_dim(d);
+  bool use_mma = dtype != TC_F32 && kv_aligned && mma_dim(d);
+  if (use_mma && p.k_ptrs != nullptr) {
+    use_mma = p.tm_ragged != nullptr;  // ragged caches need their pre-encoded maps
+  } else if (use_mma) {
+    use_mma = encode_kv_map(&p.tmk, p.k, dtype, d, max_n, p.hkv, p.batch, p.sk_n, p.sk_h, p.sk_b) &&
+              encode_kv_map(&p.tmv, p.v, dtype, d, max_n, p.hkv, p.batch, p.sv_n, p.sv_h, p.sv_b);
+  }
   if (!use_mma && !gen_dim(d)) return mma_dim(d) ? TC_ERR_ALIGN : TC_ERR_INVALID;
   const int dev = current_device();
   const DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
@@ -369,7 +437,8 @@ int tc_decode_attention_batched(const void* q, const void* k, const void* v, voi
 }
 
 int tc_decode_attention_ragged(const void* q, void* out, const void* const* k_ptrs, const void* const* v_ptrs,
-                               const int64_t* head_strides, const int32_t* lengths, int batch, int hkv, int g, int d,
+                               const int64_t* head_strides, const int32_t* lengths, const void* tensormaps,
+                               int batch, int hkv, int g, int d,
                                int64_t max_n, int64_t total_tokens, int64_t kv_stride_n, int64_t q_stride_b,
                                int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_b, int64_t out_stride_h,
                                int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
@@ -381,6 +450,8 @@ int tc_decode_attention_ragged(const void* q, void* out, const void* const* k_pt
   p.k_ptrs = k_ptrs;
   p.v_ptrs = v_ptrs;
   p.head_strides = head_strides;
+  p.tm_ragged = static_cast<const CUtensorMap*>(tensormaps);
+  if (tensormaps != nullptr && (reinterpret_cast<uintptr_t>(tensormaps) & 63u) != 0) return TC_ERR_ALIGN;
   p.lengths = lengths;
   p.n = max_n;
   p.sq_b = q_stride_b;
@@ -399,6 +470,29 @@ int tc_decode_attention_ragged(const void* q, void* out, const void* const* k_pt
   const bool al = stride16(kv_stride_n, dtype);
   return run_decode(p, dtype, d, true, max_n, total_tokens, splits, al, scale, workspace, workspace_bytes,
                     static_cast<cudaStream_t>(stream));
+}
+
+size_t tc_ragged_tensormaps_size(int batch) { return batch > 0 ? 2 * (size_t)batch * sizeof(CUtensorMap) : 0; }
+
+int tc_ragged_encode_tensormaps(void* host_out, const void* const* k_ptrs, const void* const* v_ptrs,
+                                const int64_t* caps, const int64_t* head_strides, int64_t kv_stride_n, int batch,
+                                int hkv, int d, int dtype) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (host_out == nullptr || k_ptrs == nullptr || v_ptrs == nullptr || caps == nullptr || head_strides == nullptr ||
+      batch < 1 || hkv < 1 || !mma_dim(d))
+    return TC_ERR_INVALID;
+  if (!stride16(kv_stride_n, dtype)) return TC_ERR_ALIGN;
+  for (int b = 0; b < batch; ++b) {
+    if (caps[b] < 0) return TC_ERR_INVALID;
+    if (!aligned16(k_ptrs[b]) || !aligned16(v_ptrs[b]) || !stride16(head_strides[b], dtype)) return TC_ERR_ALIGN;
+    CUtensorMap mk, mv;
+    if (!encode_kv_map(&mk, k_ptrs[b], dtype, d, caps[b], hkv, 1, kv_stride_n, head_strides[b], 0) ||
+        !encode_kv_map(&mv, v_ptrs[b], dtype, d, caps[b], hkv, 1, kv_stride_n, head_strides[b], 0))
+      return TC_ERR_CUDA;
+    std::memcpy(static_cast<uint8_t*>(host_out) + (2 * (size_t)b) * sizeof(CUtensorMap), &mk, sizeof(mk));
+    std::memcpy(static_cast<uint8_t*>(host_out) + (2 * (size_t)b + 1) * sizeof(CUtensorMap), &mv, sizeof(mv));
+  }
+  return TC_OK;
 }
 
 int tc_merge_partials(const float* o_parts, const float* lse_parts, void* out, float* lse_out, int parts,

@@ -12,6 +12,8 @@ LSE, the partial form for sequence-sharded decode), `decode_attention_batched` (
 in one strided tensor, the b > 1 decode branch of threadcut/attention.py:41-42),
 `decode_attention_ragged` (per-sequence caches and lengths) and `merge_partials` (LSE merge).
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -135,6 +137,20 @@ class RaggedKV:
                 raise ValueError(f"{what}: K/V bases must be 16-byte aligned and strides multiples of 16 bytes")
         dev = ks[0].device
         self.ks, self.vs = list(ks), list(vs)  # keep the storage alive
+        self.tensormaps = None
+        code = _lib.DTYPE_CODE[ks[0].dtype]
+        if code != _lib.TC_F32 and d in (64, 128, 256):
+            # tensor maps (one per K and V of every sequence) for the TMA kernel, encoded once here
+            L = lib()
+            bsz = len(ks)
+            host = torch.empty(L.tc_ragged_tensormaps_size(bsz), dtype=torch.uint8)
+            arr = ctypes.c_void_p * bsz
+            i64 = ctypes.c_int64 * bsz
+            st = L.tc_ragged_encode_tensormaps(
+                host.data_ptr(), arr(*[k.data_ptr() for k in ks]), arr(*[v.data_ptr() for v in vs]),
+                i64(*[k.shape[1] for k in ks]), i64(*[k.stride(0) for k in ks]), sn, bsz, hkv, d, code)
+            check("tc_ragged_encode_tensormaps", st)
+            self.tensormaps = host.to(dev)
         self.lengths_host = [int(n) for n in lengths]
         self.k_ptrs = torch.tensor([k.data_ptr() for k in ks], dtype=torch.int64).to(dev)
         self.v_ptrs = torch.tensor([v.data_ptr() for v in vs], dtype=torch.int64).to(dev)
@@ -166,7 +182,8 @@ def decode_attention_ragged(q, kv: RaggedKV, scale, *, splits=None, out=None):
     with torch.cuda.device(dev):
         st = L.tc_decode_attention_ragged(
             q.data_ptr(), out.data_ptr(), kv.k_ptrs.data_ptr(), kv.v_ptrs.data_ptr(), kv.head_strides.data_ptr(),
-            kv.lengths.data_ptr(), b, hkv, g, d, kv.max_n, kv.total, kv.token_stride,
+            kv.lengths.data_ptr(), kv.tensormaps.data_ptr() if kv.tensormaps is not None else None,
+            b, hkv, g, d, kv.max_n, kv.total, kv.token_stride,
             q.stride(0), q.stride(1), q.stride(2), out.stride(0), out.stride(1), out.stride(2),
             float(scale), s, code, ws.data_ptr(), ws.numel(), stream_ptr(dev))
     check("tc_decode_attention_ragged", st)
