@@ -84,6 +84,28 @@ int tc_decode_attention(const void* q, const void* k, const void* v, void* out,
                         float scale, int splits, int dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
+ * example a plugin running inside another runtime that owns every device allocation and forbids
+ * allocating in its execute hook, a loop where the implicit synchronisation of cudaMalloc is not
+ * acceptable, or plain C code with no allocator at hand. Same arguments and result as
+ * tc_decode_attention, minus the workspace. (This entry point has no counterpart in the reference.)
+ *
+ * Its scratch is one fixed 4 MiB array compiled into the library; every GPU that loads the library
+ * keeps it for the life of the process. Problems whose workspace (tc_decode_attention_workspace_size
+ * with batch 1) exceeds 4 MiB are rejected with TC_ERR_WORKSPACE; Qwen3-4B's geometry (8 KV heads,
+ * 4 query heads each, head_dim 128) fits at every context length. The first call on a device looks
+ * up the array's device address (with that device current), so make that first call before any
+ * stream capture. All calls share the one array and it keeps the last call's contents: each call
+ * clears what must start at zero, but calls that run at the same time on the GPU (different streams,
+ * different host threads) race with each other — order them. */
+int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, void* out,
+                                int hkv, int g, int d, int64_t n,
+                                int64_t q_stride_h, int64_t q_stride_g,
+                                int64_t k_stride_h, int64_t k_stride_n,
+                                int64_t v_stride_h, int64_t v_stride_n,
+                                int64_t out_stride_h, int64_t out_stride_g,
+                                float scale, int splits, int dtype, void* stream);
+
 /* Batched decode over `batch` sequences sharing one strided K/V tensor [batch, hkv, n, d].
  * `lengths` (device int32[batch], may be NULL = all n) gives each sequence's valid length
  * (<= n); the folded SDPA branch of threadcut/attention.py:41-42 (b > 1) is the reference. */

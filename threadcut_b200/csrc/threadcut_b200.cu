@@ -317,6 +317,35 @@ int grid_for(int64_t tasks, int threads, int sms, int per_sm) {
 
 }  // namespace
 
+// ------------------------------------------------------------------------------- no-allocation decode
+// Scratch for tc_decode_attention_noalloc: a fixed array that lives in every GPU's memory for as
+// long as the library is loaded, so that entry point never allocates. Host code must not pass the
+// symbol itself to a kernel (on the host it only stands in for the device array); it asks the
+// runtime for the device address once per device, below.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[256] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up on the first call for that
+// device (with the device current) and remembered afterwards.
+int noalloc_scratch(void** addr) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TC_ERR_CUDA;
+  if (dev < 0 || dev >= 256) return TC_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return TC_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *addr = g_noalloc_addr[dev];
+  return TC_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char* tc_status_string(int status) {
@@ -632,6 +661,27 @@ int tc_splice_copy(const void* k_in, const void* v_in, void* k_out, void* v_out,
   const cudaError_t e =
       TC_ROPE_DISPATCH(launch_splice_copy, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, void* out, int hkv, int g, int d,
+                                int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
+                                int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                                int64_t out_stride_g, float scale, int splits, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  const size_t need = tc_decode_attention_workspace_size(1, hkv, g, d, n, n, splits, dtype);
+  if (need == 0) return TC_ERR_INVALID;
+  if (need > kNoAllocScratchBytes) return TC_ERR_WORKSPACE;  // the problem is larger than the fixed array
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != TC_OK) return rc;
+  // the arrival tickets at the start of the workspace must be zero; they are left zero by every
+  // finished call, but an earlier call that failed part-way could have left them set
+  if (cudaMemsetAsync(scratch, 0, round256(sizeof(int) * (size_t)hkv), static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return TC_ERR_CUDA;
+  return tc_decode_attention(q, k, v, out, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n, v_stride_h,
+                             v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, scratch,
+                             kNoAllocScratchBytes, stream);
 }
 
 }  // extern "C"
