@@ -153,7 +153,7 @@ def capture_step(qs, ks, vs, outs, dev):
     from threadcut_b200._lib import TC_BF16, check, lib, workspaces
     L = lib()
     n = ks[0].shape[1]
-    ws = workspaces.get("decode", dev, L.tc_decode_attention_workspace_size(1, 8, 4, 128, n, n, 0, TC_BF16))
+    ws = workspaces.get(("decode", 8), dev, L.tc_decode_attention_workspace_size(1, 8, 4, 128, n, n, 0, TC_BF16))
 
     def launch_all():
         st = torch.cuda.current_stream(dev).cuda_stream

@@ -113,8 +113,10 @@ def cos_sin_table(delta, inv_freq):
 
 
 class _Workspaces:
-    """Per (device, stream) scratch buffers, zero-initialised, grown on demand. The kernels leave
-    their counters at zero, so a buffer is only zeroed when it is (re)allocated."""
+    """Per (kind, device, stream) scratch buffers, zero-initialised, grown on demand. The kernels
+    leave their ticket counters at zero, so a buffer is only zeroed when it is (re)allocated.
+    Decode workspaces are keyed by ("decode", batch*hkv): the ticket prefix grows with batch*hkv,
+    and a prefix that overlapped an earlier call's partials would not start at zero."""
 
     def __init__(self):
         self._bufs = {}

@@ -25,8 +25,9 @@
 //     spare, the point is to take the per-token FMA/shuffle work off the issue slots so the CTA
 //     stays a pure HBM stream.
 //   * epilogue: the warps' (m, l, o) are combined in shared memory; with one split the CTA writes
-//     the output, otherwise it writes an unnormalised partial and the LAST CTA of the head (atomic
-//     ticket) merges all partials by log-sum-exp and resets the ticket.
+//     the output, otherwise it publishes an unnormalised partial to the workspace (red.release) —
+//     except the CTA that took the head's last start ticket, which waits for the others' partials
+//     and merges them with its own by log-sum-exp (see finish_cta).
 //   * launched with programmatic dependent launch: the prologue overlaps the previous kernel's
 //     tail, and nothing the previous kernel may write is read before griddepcontrol.wait.
 // fp32, d < 64, or K/V whose strides break the 16-byte TMA rule use decode_generic_kernel: the same
@@ -43,7 +44,8 @@ constexpr int kTile = 32;        // tokens per staged tile (the TMA box height)
 constexpr int kCWarps = 6;       // consumer warps per CTA of the tensor-core kernel (+1 producer warp)
 constexpr int kGenWarps = 4;     // warps per CTA of the generic kernel
 constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
-constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM assumed by the split planner (mma kernel)
+constexpr int kMergeChunk = 12;  // partials one merger thread loads per L2 round trip
+constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM of the tensor-core kernel
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -71,8 +73,15 @@ struct DecodeParams {
   float c;              // scale * log2(e)
   float* ws_o;          // [batch*hkv][max_splits][g][d]  unnormalised partial outputs
   float* ws_ml;         // [batch*hkv][max_splits][g][2]  (running max (log2 domain), sum)
-  int* counters;        // [batch*hkv] arrival tickets, zero between calls
+  unsigned int* counters;  // [batch*hkv][4]: start ticket, published partials (zero between calls)
 };
+
+// Tiles [t0, t1) of split `split` out of `nsplit` over a sequence of `tiles` tiles: as even as
+// integer division allows (no split is more than one tile longer than another).
+__device__ __forceinline__ void split_range(int64_t tiles, int split, int nsplit, int64_t& t0, int64_t& t1) {
+  t0 = tiles * split / nsplit;
+  t1 = tiles * (split + 1) / nsplit;
+}
 
 template <typename T>
 __device__ __forceinline__ void resolve_seq(const DecodeParams& p, int b, int h, const T*& kh, const T*& vh,
@@ -113,21 +122,27 @@ struct Region {
   __device__ static float* acc(float* r, int i) { return r + 2 * HP + i * kAccStride; }
 };
 
-// Combine the per-warp states of this CTA, then either write the output (one split) or publish a
-// partial and, in the last CTA of this (sequence, head), merge all partials.
-// Preconditions: every thread of the CTA calls this after a __syncthreads() that follows the
-// region writes; `merge_smem` has room for max_splits * g floats and no longer holds live data.
+// Combine the per-warp states of this CTA, then write the output (one split), publish a partial
+// (most splits), or — in the merger CTA of this (sequence, head) — wait for every other split's
+// partial and merge them with this CTA's own by log-sum-exp.
+//
+// The merger is the CTA that took the last START ticket of its (sequence, head). Every other CTA of
+// that head took its ticket earlier, so it is already running (or done) and will publish without
+// waiting on anything: the merger's bounded wait for them needs no co-residency guarantee. The
+// merger keeps its own partial in shared memory, and resets both tickets for the next call.
+// Preconditions: every thread calls this after a __syncthreads() that follows the region writes;
+// `epi` holds 16*D floats that overlap no region.
 template <typename T, int D, int HP>
 __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_stride_bytes, int nregions,
-                           float* merge_smem, int b, int h, int split, int nsplit) {
+                           float* epi, int b, int h, int split, int nsplit, bool merger) {
   __shared__ float s_M[16], s_L[16];
-  __shared__ int s_last;
+  __shared__ int s_ok;
   using R = Region<D, HP>;
   const int g = p.g;
   const int tid = threadIdx.x, nthr = blockDim.x;
-  const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
   const int64_t bh = (int64_t)b * p.hkv + h;
   T* out = static_cast<T*>(p.out) + b * p.so_b + h * p.so_h;
+  float* own = epi;  // the merger's own unnormalised output [g][D]
   auto region = [&](int w) { return reinterpret_cast<float*>(regions + (size_t)w * region_stride_bytes); };
 
   if (tid < g) {
@@ -149,6 +164,8 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
     if (nsplit == 1) {
       const float L = s_L[i];
       out[i * p.so_g + d] = from_f32<T>(L > 0.f ? o / L : 0.f);
+    } else if (merger) {
+      own[idx] = o;
     } else {
       p.ws_o[((bh * p.max_splits + split) * g + i) * D + d] = o;
     }
@@ -157,97 +174,93 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
     if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
     return;
   }
-  if (tid < g) {
-    float* ml = p.ws_ml + ((bh * p.max_splits + split) * g + tid) * 2;
-    ml[0] = s_M[tid];
-    ml[1] = s_L[tid];
+  unsigned int* ctr = p.counters + bh * 4;
+  if (!merger) {
+    if (tid < g) {
+      float* ml = p.ws_ml + ((bh * p.max_splits + split) * g + tid) * 2;
+      ml[0] = s_M[tid];
+      ml[1] = s_L[tid];
+    }
+    __syncthreads();
+    if (tid == 0) red_release_add_u32(ctr + 1, 1u);
+    return;
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(&p.counters[bh], 1) == nsplit - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
 
-  // Last CTA of this head: merge nsplit partials. Each lane loads the (m, l) pair of its splits
-  // once; weights w_s = 2^(m_s - M) / L go to shared memory; then every thread owns float4 columns
-  // of the output and keeps 8 split loads in flight.
-  const float2* mlb = reinterpret_cast<const float2*>(p.ws_ml + bh * p.max_splits * g * 2);
-  for (int i = warp; i < g; i += nwarps) {
-    float2 ml[kMaxSplits / 32];
-#pragma unroll
-    for (int k = 0; k < kMaxSplits / 32; ++k) {
-      const int s = lane + 32 * k;
-      ml[k] = s < nsplit ? __ldcg(mlb + (int64_t)s * g + i) : make_float2(-INFINITY, 0.f);
+  // ---- merger: wait (bounded) until the other nsplit-1 partials are published
+  if (tid == 0) {
+    int ok = 1;
+    uint32_t spin = 0;
+    while (ld_acquire_u32(ctr + 1) < (unsigned int)(nsplit - 1)) {
+      if (++spin >= kSpinLimit) {
+        raise_error(TC_DEVERR_PIPE_TIMEOUT);
+        ok = 0;
+        break;
+      }
+      __nanosleep(32);
     }
-    float M = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < kMaxSplits / 32; ++k) M = fmaxf(M, ml[k].x);
-    M = warp_max(M);
-    float L = 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxSplits / 32; ++k) {
-      ml[k].x = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - M);
-      L += ml[k].x * ml[k].y;
-    }
-    L = warp_sum(L);
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxSplits / 32; ++k) {
-      const int s = lane + 32 * k;
-      if (s < nsplit) merge_smem[s * g + i] = ml[k].x * inv;
-    }
-    if (lane == 0) {
-      s_M[i] = M;
-      s_L[i] = L;
-    }
+    s_ok = ok;
   }
   __syncthreads();
+  if (!s_ok) return;
+
+  // out = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s over all splits, this CTA's own from shared
+  // memory. Every thread owns one float4 column of one head; it loads the (m, l) pair and that column
+  // of up to kMergeChunk splits at once (one L2 round trip per chunk) and folds chunks in online.
+  const float2* mlb = reinterpret_cast<const float2*>(p.ws_ml + bh * p.max_splits * g * 2);
   const float4* ob = reinterpret_cast<const float4*>(p.ws_o + bh * p.max_splits * g * D);
+  const float4* ownv = reinterpret_cast<const float4*>(own);
   constexpr int Q = D / 4;  // float4 columns per head row
   for (int u = tid; u < g * Q; u += nthr) {
     const int i = u / Q;
-    float4 acc[8];
+    float M = s_M[i], L = s_L[i];
+    float4 acc = ownv[u];
+    for (int s0 = 0; s0 < nsplit; s0 += kMergeChunk) {
+      float2 ml[kMergeChunk];
+      float4 x[kMergeChunk];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    int s = 0;
-    for (; s + 8 <= nsplit; s += 8) {
-      float4 x[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = __ldcg(ob + ((int64_t)(s + k) * g) * Q + u);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float w = merge_smem[(s + k) * g + i];
-        acc[k].x += w * x[k].x;
-        acc[k].y += w * x[k].y;
-        acc[k].z += w * x[k].z;
-        acc[k].w += w * x[k].w;
+      for (int k = 0; k < kMergeChunk; ++k) {
+        const int s = s0 + k;
+        const bool use = s < nsplit && s != split;
+        ml[k] = use ? __ldcg(mlb + (int64_t)s * g + i) : make_float2(-INFINITY, 0.f);
+        x[k] = use ? __ldcg(ob + ((int64_t)s * g) * Q + u) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
-    for (; s < nsplit; ++s) {
-      const float4 x = __ldcg(ob + ((int64_t)s * g) * Q + u);
-      const float w = merge_smem[s * g + i];
-      acc[0].x += w * x.x;
-      acc[0].y += w * x.y;
-      acc[0].z += w * x.z;
-      acc[0].w += w * x.w;
-    }
+      float mc = M;
 #pragma unroll
-    for (int k = 1; k < 8; ++k) {
-      acc[0].x += acc[k].x;
-      acc[0].y += acc[k].y;
-      acc[0].z += acc[k].z;
-      acc[0].w += acc[k].w;
+      for (int k = 0; k < kMergeChunk; ++k) mc = fmaxf(mc, ml[k].x);
+      const float a = fast_exp2(M - mc);
+      L *= a;
+      acc.x *= a;
+      acc.y *= a;
+      acc.z *= a;
+      acc.w *= a;
+#pragma unroll
+      for (int k = 0; k < kMergeChunk; ++k) {
+        const float w = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - mc);
+        L += w * ml[k].y;
+        acc.x += w * x[k].x;
+        acc.y += w * x[k].y;
+        acc.z += w * x[k].z;
+        acc.w += w * x[k].w;
+      }
+      M = mc;
     }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
     T* o = out + i * p.so_g + (u - i * Q) * 4;
-    o[0] = from_f32<T>(acc[0].x);
-    o[1] = from_f32<T>(acc[0].y);
-    o[2] = from_f32<T>(acc[0].z);
-    o[3] = from_f32<T>(acc[0].w);
+    o[0] = from_f32<T>(acc.x * inv);
+    o[1] = from_f32<T>(acc.y * inv);
+    o[2] = from_f32<T>(acc.z * inv);
+    o[3] = from_f32<T>(acc.w * inv);
+    if (p.lse != nullptr && u == i * Q) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(M, L);
   }
-  if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
-  if (tid == 0) p.counters[bh] = 0;
+  if (tid == 0) {  // every other CTA of this head is done with both tickets
+    ctr[0] = 0u;
+    ctr[1] = 0u;
+  }
 }
+
+// Bytes of the epilogue area: the merger's own partial, o [16][D].
+template <int D>
+constexpr int epi_bytes() { return 16 * D * 4; }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
@@ -268,7 +281,8 @@ struct MmaGeom {
   static constexpr int kStages = D <= 128 ? 12 : 6;
   static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
-  static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + slack to align the base to 1 KB
+  static constexpr int kEpiBytes = epi_bytes<D>();
+  static constexpr int kSmem = 1024 + kPipeBytes + kEpiBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
 };
 
 // Byte offset of element (row, col) of a staged tile: 64-column boxes of 32 rows x 128 bytes, each
@@ -294,10 +308,13 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   extern __shared__ uint8_t smem_raw[];
   // TMA 128-byte swizzle is defined on absolute shared addresses: align the pipeline to 1 KB
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes);
+  float* epi = reinterpret_cast<float*>(smem + G::kPipeBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes + G::kEpiBytes);
   uint64_t* empty = full + kStages;
+  __shared__ int s_merger;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
@@ -305,24 +322,51 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       mbar_init(&empty[s], 1);
     }
     fence_mbar_init();
-    if (p.tm_ragged == nullptr) {
-      prefetch_tensormap(&p.tmk);
-      prefetch_tensormap(&p.tmv);
+  }
+  if (warp == kCWarps && lane == 0) {
+    // Before waiting for the previous kernel: warm L2 with the first pipeline-depth of this CTA's
+    // tiles. Only L2 prefetches (no shared memory, nothing consumed): a length read here may be
+    // stale and the rows may still be being written, and both are harmless; everything used for
+    // the result is read again after pdl_wait().
+    const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
+    const CUtensorMap* mv = p.tm_ragged ? p.tm_ragged + 2 * b + 1 : &p.tmv;
+    const int cb = p.tm_ragged ? 0 : b;
+    prefetch_tensormap(mk);
+    prefetch_tensormap(mv);
+    const int64_t n_hint = p.lengths ? (int64_t)p.lengths[b] : p.n;
+    const int64_t tiles_hint = (n_hint + kTile - 1) / kTile;
+    const int ns_hint = n_hint > 0 ? (int)((tiles_hint + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
+    if (n_hint > 0 && split < ns_hint) {
+      int64_t a0, a1;
+      split_range(tiles_hint, split, ns_hint, a0, a1);
+      const int64_t pre = a1 - a0 < kStages ? a1 - a0 : kStages;
+      for (int64_t j = 0; j < pre; ++j)
+#pragma unroll
+        for (int bx = 0; bx < NBOX; ++bx) {
+          tma_prefetch_4d(mk, bx * 64, (int)((a0 + j) * kTile), h, cb);
+          tma_prefetch_4d(mv, bx * 64, (int)((a0 + j) * kTile), h, cb);
+        }
     }
   }
   pdl_launch();
   pdl_wait();  // everything below may read what the previous kernel in the stream wrote
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
-  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
-  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
+  const int64_t seq_tiles = (n + kTile - 1) / kTile;
+  const int nsplit = n > 0 ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
   if (split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
-  const int64_t t0 = (int64_t)split * chunk;
-  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
-  const int ntiles = n > 0 ? (int)((t1 - t0 + kTile - 1) / kTile) : 0;
+  int64_t tt0, tt1;
+  split_range(seq_tiles, split, nsplit, tt0, tt1);
+  const int64_t t0 = tt0 * kTile;
+  const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
+  const int ntiles = (int)(tt1 - tt0);
+  if (threadIdx.x == 0) s_merger = 0;
   __syncthreads();
 
   if (warp == kCWarps) {
+    // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
+    // the result is read only after the final __syncthreads
+    if (lane == 1 && nsplit > 1)
+      s_merger = atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * 4, 1u) == (unsigned int)(nsplit - 1);
     // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
     if (lane == 0 && ntiles > 0) {
       const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
@@ -532,8 +576,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         }
   }
   __syncthreads();
-  // merge weights may reuse the pipeline buffers once the combine has read them (finish_cta syncs)
-  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
+  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, epi, b, h, split, nsplit, s_merger != 0);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -543,7 +586,7 @@ template <int D>
 struct GenGeom {
   static constexpr int HP = 16;
   static constexpr int kRegionBytes = ((Region<D, HP>::kFloats * 4 + 127) / 128) * 128;
-  static constexpr int kSmem = kGenWarps * kRegionBytes;
+  static constexpr int kSmem = kGenWarps * kRegionBytes + epi_bytes<D>();
 };
 
 template <typename T, int D>
@@ -554,16 +597,21 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_launch();
   pdl_wait();
+  __shared__ int s_merger;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const T* kh;
   const T* vh;
   int64_t n;
   resolve_seq<T>(p, b, h, kh, vh, n);
-  const int64_t chunk = (int64_t)p.tiles_per_split * kTile;
-  const int nsplit = n > 0 ? (int)((n + chunk - 1) / chunk) : 1;
+  const int64_t seq_tiles = (n + kTile - 1) / kTile;
+  const int nsplit = n > 0 ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
   if (split >= nsplit) return;
-  const int64_t t0 = (int64_t)split * chunk;
-  const int64_t t1 = n < t0 + chunk ? n : t0 + chunk;
+  int64_t tt0, tt1;
+  split_range(seq_tiles, split, nsplit, tt0, tt1);
+  const int64_t t0 = tt0 * kTile;
+  const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
+  if (threadIdx.x == 0)
+    s_merger = nsplit > 1 && atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * 4, 1u) == (unsigned int)(nsplit - 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.g;
 
@@ -622,7 +670,9 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
       if (d < D) R::acc(reg, i)[d] = acc[i][j];
     }
   __syncthreads();
-  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kGenWarps, reinterpret_cast<float*>(smem), b, h, split, nsplit);
+  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kGenWarps,
+                       reinterpret_cast<float*>(smem + kGenWarps * G::kRegionBytes), b, h, split, nsplit,
+                       s_merger != 0);
 }
 
 // ------------------------------------------------------------------------------------------------

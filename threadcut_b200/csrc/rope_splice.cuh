@@ -169,15 +169,6 @@ struct SpliceParams {
   float cs[kMaxRopeDim];
 };
 
-__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_u32(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kSpliceThreads) splice_inplace_kernel(const __grid_constant__ SpliceParams p) {
   __shared__ float s_cs[kMaxRopeDim];

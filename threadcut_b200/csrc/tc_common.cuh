@@ -65,6 +65,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   return false;
 }
 
+// ---------------------------------------------------------------- gpu-scope flags between CTAs
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Fire-and-forget increment that makes this CTA's earlier global writes (ordered to this thread by
+// a preceding __syncthreads) visible at gpu scope no later than the increment itself.
+__device__ __forceinline__ void red_release_add_u32(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- bulk (TMA) copies
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
@@ -93,6 +108,15 @@ __device__ __forceinline__ void tma_load_4d(void* sdst, const CUtensorMap* map, 
       " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(sdst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
       : "memory");
+}
+// L2 prefetch of the same box a tma_load_4d with these coordinates would fetch (no shared memory,
+// no completion). L2 is the coherence point of the GPU, so prefetching data another kernel is still
+// writing is harmless: later loads see the final values.
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
 }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

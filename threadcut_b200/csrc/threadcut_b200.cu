@@ -138,11 +138,14 @@ struct WsLayout {
   size_t counters = 0, ml = 0, o = 0, total = 0;
 };
 
+// Ticket region at the start of a decode workspace: 4 uint32 per (sequence, head).
+size_t decode_counter_bytes(int64_t rows) { return round256(16 * (size_t)rows); }
+
 WsLayout decode_ws_layout(int batch, int hkv, int g, int d, int64_t max_splits) {
   WsLayout w;
   const int64_t rows = (int64_t)batch * hkv;
   w.counters = 0;
-  w.ml = round256(sizeof(int) * rows);
+  w.ml = decode_counter_bytes(rows);
   w.o = w.ml + round256(sizeof(float) * rows * max_splits * g * 2);
   w.total = w.o + round256(sizeof(float) * rows * max_splits * g * d);
   return w;
@@ -166,10 +169,14 @@ cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st,
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
@@ -177,16 +184,16 @@ template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
   auto fn = decode_mma_kernel<T, D, NG>;
   const int smem = MmaGeom<D>::kSmem;
+  const int threads = 32 * (kCWarps + 1);
   cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
   if (e != cudaSuccess) return e;
-  return launch_ex(fn, grid, dim3(32 * (kCWarps + 1)), smem, st, p);
+  return launch_ex(fn, grid, dim3(threads), smem, st, p);
 }
 
 template <typename T, int D>
 cudaError_t launch_gen(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
   auto fn = decode_generic_kernel<T, D>;
-  constexpr int merge_bytes = kMaxSplits * 16 * 4;
-  const int smem = GenGeom<D>::kSmem > merge_bytes ? GenGeom<D>::kSmem : merge_bytes;
+  const int smem = GenGeom<D>::kSmem;
   cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
   if (e != cudaSuccess) return e;
   return launch_ex(fn, grid, dim3(32 * kGenWarps), smem, st, p);
@@ -237,7 +244,7 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
   const WsLayout w = decode_ws_layout(p.batch, p.hkv, p.g, d, pl.max_splits);
   if (ws == nullptr || ws_bytes < w.total) return TC_ERR_WORKSPACE;
   uint8_t* wb = static_cast<uint8_t*>(ws);
-  p.counters = reinterpret_cast<int*>(wb + w.counters);
+  p.counters = reinterpret_cast<unsigned int*>(wb + w.counters);
   p.ws_ml = reinterpret_cast<float*>(wb + w.ml);
   p.ws_o = reinterpret_cast<float*>(wb + w.o);
   p.tiles_per_split = (int)pl.tps;
@@ -676,7 +683,7 @@ int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, voi
   if (rc != TC_OK) return rc;
   // the arrival tickets at the start of the workspace must be zero; they are left zero by every
   // finished call, but an earlier call that failed part-way could have left them set
-  if (cudaMemsetAsync(scratch, 0, round256(sizeof(int) * (size_t)hkv), static_cast<cudaStream_t>(stream)) !=
+  if (cudaMemsetAsync(scratch, 0, decode_counter_bytes(hkv), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
     return TC_ERR_CUDA;
   return tc_decode_attention(q, k, v, out, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n, v_stride_h,

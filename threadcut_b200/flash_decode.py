@@ -52,7 +52,7 @@ def _decode(q, k, v, scale, splits, want_lse):
     L = lib()
     s = int(splits or 0)
     nbytes = L.tc_decode_attention_workspace_size(1, hkv, g, d, n, n, s, code)
-    ws = workspaces.get("decode", dev, nbytes)
+    ws = workspaces.get(("decode", hkv), dev, nbytes)
     with torch.cuda.device(dev):
         st = L.tc_decode_attention_lse(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
@@ -97,7 +97,7 @@ def decode_attention_batched(q, k, v, scale, lengths=None, *, splits=None):
     out = torch.empty((b, hkv, g, d), dtype=q.dtype, device=dev)
     L = lib()
     s = int(splits or 0)
-    ws = workspaces.get("decode", dev, L.tc_decode_attention_workspace_size(b, hkv, g, d, n, b * n, s, code))
+    ws = workspaces.get(("decode", b * hkv), dev, L.tc_decode_attention_workspace_size(b, hkv, g, d, n, b * n, s, code))
     with torch.cuda.device(dev):
         st = L.tc_decode_attention_batched(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, hkv, g, d, n, lens_ptr,
@@ -177,7 +177,7 @@ def decode_attention_ragged(q, kv: RaggedKV, scale, *, splits=None, out=None):
         out = torch.empty((b, hkv, g, d), dtype=q.dtype, device=dev)
     L = lib()
     s = int(splits or 0)
-    ws = workspaces.get("decode", dev, L.tc_decode_attention_workspace_size(b, hkv, g, d, kv.max_n, kv.total, s,
+    ws = workspaces.get(("decode", b * hkv), dev, L.tc_decode_attention_workspace_size(b, hkv, g, d, kv.max_n, kv.total, s,
                                                                             code))
     with torch.cuda.device(dev):
         st = L.tc_decode_attention_ragged(
