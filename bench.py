@@ -315,11 +315,12 @@ def run_ours(args, rank, local, world, dist):
         cpu = {"value": round(us, 2), "unit": "us/layer", "cores": thr, "kind": "port",
                "sample": f"{nl} layers of 16k decode (fp32 numpy restatement of the reference's folded SDPA, "
                          f"4 distinct layer buffers cycled, ~{args.cpu_seconds:.0f}s)"}
-    traffic = None
-    tpath = os.path.join(HERE, "profiles", "decode_16k_traffic.json")
+    traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and size
+    tpath = os.path.join(HERE, "profiles", "decode_16k_traffic.txt")
     if os.path.exists(tpath):
-        with open(tpath) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+        for line in open(tpath):
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = int(line.split(":", 1)[1])
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
