@@ -99,7 +99,25 @@ def dtype_code(t, what):
 
 
 def stream_ptr(device):
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw cudaStream_t of torch's current stream on `device` (what every launch goes to)."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None
+                                             else torch.cuda.current_device())
+
+
+_MAX_N_FOR_BOUND = 1 << 31
+_ws_bound_cache = {}
+
+
+def decode_workspace_bound(batch, hkv, g, d, code):
+    """Workspace bytes that suffice for every decode call of this geometry whatever n or splits is
+    (the planner never uses more than 128 slices per head), cached per geometry."""
+    key = (batch, hkv, g, d, code)
+    nb = _ws_bound_cache.get(key)
+    if nb is None:
+        nb = lib().tc_decode_attention_workspace_size(batch, hkv, g, d, _MAX_N_FOR_BOUND, batch * _MAX_N_FOR_BOUND,
+                                                      128, code)
+        _ws_bound_cache[key] = nb
+    return nb
 
 
 def cos_sin_table(delta, inv_freq):
@@ -123,8 +141,11 @@ class _Workspaces:
         self._epochs = {}
         self._lock = threading.Lock()
 
-    def get(self, kind, device, nbytes):
-        key = (kind, device.index, stream_ptr(device))
+    def get(self, kind, device, nbytes, stream=None):
+        key = (kind, device.index, stream_ptr(device) if stream is None else stream)
+        buf = self._bufs.get(key)
+        if buf is not None and buf.numel() >= nbytes:
+            return buf
         with self._lock:
             buf = self._bufs.get(key)
             if buf is None or buf.numel() < nbytes:

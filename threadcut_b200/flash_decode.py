@@ -35,30 +35,39 @@ def _check_same_dtype(what, *ts):
 
 def _decode(q, k, v, scale, splits, want_lse):
     what = "decode_attention"
-    require_cuda(q, k, v, what=what)
-    _check_same_dtype(what, q, k, v)
+    dev = q.device
+    if dev.type != "cuda" or k.device != dev or v.device != dev:
+        require_cuda(q, k, v, what=what)
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        _check_same_dtype(what, q, k, v)
     if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
         raise ValueError(f"{what}: expected q [hkv, g, d], k/v [hkv, n, d]; got {tuple(q.shape)}, "
                          f"{tuple(k.shape)}, {tuple(v.shape)}")
     hkv, g, d = q.shape
     n = k.shape[1]
-    if tuple(k.shape) != (hkv, n, d) or tuple(v.shape) != (hkv, n, d):
+    if k.shape[0] != hkv or k.shape[2] != d or v.shape != k.shape:
         raise ValueError(f"{what}: k/v shape {tuple(k.shape)}/{tuple(v.shape)} does not match q {tuple(q.shape)}")
-    q, k, v = _last_contig(q), _last_contig(k), _last_contig(v)
-    code = dtype_code(q, what)
-    dev = q.device
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        q, k, v = _last_contig(q), _last_contig(k), _last_contig(v)
+    code = _lib.DTYPE_CODE.get(q.dtype)
+    if code is None:
+        dtype_code(q, what)
     out = torch.empty((hkv, g, d), dtype=q.dtype, device=dev)
     lse = torch.empty((hkv, g), dtype=torch.float32, device=dev) if want_lse else None
     L = lib()
     s = int(splits or 0)
-    nbytes = L.tc_decode_attention_workspace_size(1, hkv, g, d, n, n, s, code)
-    ws = workspaces.get(("decode", hkv), dev, nbytes)
-    with torch.cuda.device(dev):
-        st = L.tc_decode_attention_lse(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
+    stream = stream_ptr(dev)
+    ws = workspaces.get(("decode", hkv), dev, _lib.decode_workspace_bound(1, hkv, g, d, code), stream)
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
             hkv, g, d, n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-            out.stride(0), out.stride(1), float(scale), s, code, ws.data_ptr(), ws.numel(), stream_ptr(dev))
-    check("tc_decode_attention", st)
+            out.stride(0), out.stride(1), float(scale), s, code, ws.data_ptr(), ws.numel(), stream)
+    if torch.cuda.current_device() == dev.index:
+        st = L.tc_decode_attention_lse(*args)
+    else:
+        with torch.cuda.device(dev):
+            st = L.tc_decode_attention_lse(*args)
+    if st:
+        check("tc_decode_attention", st)
     return (out, lse) if want_lse else out
 
 
