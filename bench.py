@@ -253,6 +253,45 @@ def time_shift(steps, warmup, dev, dist, layers=LAYERS):
     return e0.elapsed_time(e1) / steps
 
 
+def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
+    """Strong scaling of one long sequence (config 5's 128k context, attention only): the 8 KV heads
+    are sharded over the ranks (head_shard), each rank decodes its heads for all layers, no
+    collective on the data path. Returns ms per 36-layer step on this rank."""
+    from threadcut_b200.sharded import head_shard
+    from threadcut_b200._lib import TC_BF16, check, lib, workspaces
+    n = workloads.CFG5_CTX
+    h0, h1 = head_shard(workloads.HKV, rank, world)
+    hl = h1 - h0
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    ks = [torch.randn(hl, n, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(hl, n, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    qs = [torch.randn(hl, 4, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    outs = [torch.empty_like(q) for q in qs]
+    L = lib()
+    ws = workspaces.get(("decode", hl), dev, L.tc_decode_attention_workspace_size(1, hl, 4, 128, n, n, 0, TC_BF16))
+
+    def launch_all():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        for q, k, v, o in zip(qs, ks, vs, outs):
+            check("tc_decode_attention", L.tc_decode_attention(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128, n, q.stride(0), q.stride(1),
+                k.stride(0), k.stride(1), v.stride(0), v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0,
+                TC_BF16, ws.data_ptr(), ws.numel(), st))
+    launch_all()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    ms = time_graph(graph, steps, warmup, dist)
+    del graph, ks, vs
+    torch.cuda.empty_cache()
+    return ms
+
+
 def cpu_reference_us_per_layer(seconds=10.0, layers_in_memory=4, max_layers=None):
     """The reference's CPU path (oracle/ numpy restatement, fp32, all host threads) on 16k layers.
     Returns (us per layer, layers timed, threads)."""
@@ -309,6 +348,13 @@ def run_ours(args, rank, local, world, dist):
     torch.cuda.empty_cache()
     shift_ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist), dist)
     shift_gbs = SHIFT_BYTES_PER_LAYER * LAYERS / (shift_ms * 1e-3) / 1e9
+    strong_ms = max_over_ranks(time_strong_128k(args.steps, args.warmup, dev, dist, rank, world), dist)
+    strong = {"us_per_layer": round(strong_ms * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
+              "kv_heads_per_rank": workloads.HKV // world,
+              "workload": "one 128k-token sequence, 36 layers, KV heads sharded over the ranks (no collective); "
+                          "per-layer latency, max over ranks",
+              "frac_per_gpu": round(decode_bytes(workloads.CFG5_CTX) / world / (strong_ms * 1e-3 / LAYERS) / 1e9
+                                    / hbm, 4)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         us, nl, thr = cpu_reference_us_per_layer(args.cpu_seconds)
@@ -342,6 +388,7 @@ def run_ours(args, rank, local, world, dist):
                   "workload": "cfg2 splice Split(2048,4096,4096) of an 8192-token bf16 cache, 36 layers in one "
                               "in-place launch; K rotated + V moved, read+write bytes"},
         "cfg3_sweep": sweep,
+        "strong_128k": strong,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -216,6 +216,20 @@ int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* o
                             float scale, int splits, int dtype,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* The partial form of a KV slice for sequence-sharded decode across GPUs: like
+ * tc_decode_attention_lse, but the output is written unrounded as fp32 [hkv, g, d] (strides of
+ * out_f32 in elements) and `lse` is required. Partials of disjoint token ranges of one sequence
+ * combine exactly with tc_merge_partials (threadcut/flash_decode.py:68-69 does the same merge over
+ * the slices of one GPU). */
+int tc_decode_attention_partial(const void* q, const void* k, const void* v, float* out_f32, float* lse,
+                                int hkv, int g, int d, int64_t n,
+                                int64_t q_stride_h, int64_t q_stride_g,
+                                int64_t k_stride_h, int64_t k_stride_n,
+                                int64_t v_stride_h, int64_t v_stride_n,
+                                int64_t out_stride_h, int64_t out_stride_g,
+                                float scale, int splits, int dtype,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,7 +74,17 @@ struct DecodeParams {
   float* ws_o;          // [batch*hkv][max_splits][g][d]  unnormalised partial outputs
   float* ws_ml;         // [batch*hkv][max_splits][g][2]  (running max (log2 domain), sum)
   unsigned int* counters;  // [batch*hkv][4]: start ticket, published partials (zero between calls)
+  int out_f32;             // 1: `out` is fp32 (unrounded partial for a cross-GPU merge), else T
 };
+
+// Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
+template <typename T>
+__device__ __forceinline__ void put_out(const DecodeParams& p, int64_t off, float v) {
+  if (p.out_f32)
+    static_cast<float*>(p.out)[off] = v;
+  else
+    static_cast<T*>(p.out)[off] = from_f32<T>(v);
+}
 
 // Tiles [t0, t1) of split `split` out of `nsplit` over a sequence of `tiles` tiles: as even as
 // integer division allows (no split is more than one tile longer than another).
@@ -141,7 +151,7 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   const int g = p.g;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t bh = (int64_t)b * p.hkv + h;
-  T* out = static_cast<T*>(p.out) + b * p.so_b + h * p.so_h;
+  const int64_t out0 = b * p.so_b + h * p.so_h;
   float* own = epi;  // the merger's own unnormalised output [g][D]
   auto region = [&](int w) { return reinterpret_cast<float*>(regions + (size_t)w * region_stride_bytes); };
 
@@ -163,7 +173,7 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
       for (int w = 0; w < nregions; ++w) o += R::acc(region(w), i)[d] * fast_exp2(R::m(region(w))[i] - M);
     if (nsplit == 1) {
       const float L = s_L[i];
-      out[i * p.so_g + d] = from_f32<T>(L > 0.f ? o / L : 0.f);
+      put_out<T>(p, out0 + i * p.so_g + d, L > 0.f ? o / L : 0.f);
     } else if (merger) {
       own[idx] = o;
     } else {
@@ -245,11 +255,11 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
       M = mc;
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* o = out + i * p.so_g + (u - i * Q) * 4;
-    o[0] = from_f32<T>(acc.x * inv);
-    o[1] = from_f32<T>(acc.y * inv);
-    o[2] = from_f32<T>(acc.z * inv);
-    o[3] = from_f32<T>(acc.w * inv);
+    const int64_t o = out0 + i * p.so_g + (u - i * Q) * 4;
+    put_out<T>(p, o, acc.x * inv);
+    put_out<T>(p, o + 1, acc.y * inv);
+    put_out<T>(p, o + 2, acc.z * inv);
+    put_out<T>(p, o + 3, acc.w * inv);
     if (p.lse != nullptr && u == i * Q) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(M, L);
   }
   if (tid == 0) {  // every other CTA of this head is done with both tickets

@@ -405,16 +405,17 @@ int tc_decode_attention(const void* q, const void* k, const void* v, void* out, 
                                  dtype, workspace, workspace_bytes, stream);
 }
 
-int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,
-                            int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
-                            int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
-                            int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
-                            size_t workspace_bytes, void* stream) {
+namespace {
+int decode_single(const void* q, const void* k, const void* v, void* out, float* lse, bool out_f32, int hkv, int g,
+                  int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h, int64_t k_stride_n,
+                  int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g, float scale,
+                  int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
   DecodeParams p = base_params();
   p.q = q;
   p.out = out;
   p.lse = lse;
+  p.out_f32 = out_f32 ? 1 : 0;
   p.lse_b = (int64_t)hkv * g;
   p.k = k;
   p.v = v;
@@ -434,6 +435,28 @@ int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* o
                   stride16(v_stride_h, dtype) && stride16(v_stride_n, dtype);
   return run_decode(p, dtype, d, false, n, n, splits, al, scale, workspace, workspace_bytes,
                     static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
+int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,
+                            int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
+                            int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                            int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return decode_single(q, k, v, out, lse, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream);
+}
+
+int tc_decode_attention_partial(const void* q, const void* k, const void* v, float* out_f32, float* lse, int hkv,
+                                int g, int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
+                                int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                                int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (lse == nullptr) return TC_ERR_INVALID;
+  return decode_single(q, k, v, out_f32, lse, true, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream);
 }
 
 int tc_decode_attention_batched(const void* q, const void* k, const void* v, void* out, int batch, int hkv, int g,

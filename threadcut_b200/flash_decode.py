@@ -19,8 +19,8 @@ import torch
 from . import _lib
 from ._lib import check, dtype_code, lib, require_cuda, stream_ptr, workspaces
 
-__all__ = ["decode_attention", "decode_attention_lse", "decode_attention_batched", "decode_attention_ragged",
-           "merge_partials", "RaggedKV"]
+__all__ = ["decode_attention", "decode_attention_lse", "decode_attention_partial", "decode_attention_batched",
+           "decode_attention_ragged", "merge_partials", "RaggedKV"]
 
 
 def _last_contig(t):
@@ -33,7 +33,7 @@ def _check_same_dtype(what, *ts):
             raise TypeError(f"threadcut_b200.{what}: dtype mismatch {ts[0].dtype} vs {t.dtype}")
 
 
-def _decode(q, k, v, scale, splits, want_lse):
+def _decode(q, k, v, scale, splits, want_lse, partial=False):
     what = "decode_attention"
     dev = q.device
     if dev.type != "cuda" or k.device != dev or v.device != dev:
@@ -52,7 +52,7 @@ def _decode(q, k, v, scale, splits, want_lse):
     code = _lib.DTYPE_CODE.get(q.dtype)
     if code is None:
         dtype_code(q, what)
-    out = torch.empty((hkv, g, d), dtype=q.dtype, device=dev)
+    out = torch.empty((hkv, g, d), dtype=torch.float32 if partial else q.dtype, device=dev)
     lse = torch.empty((hkv, g), dtype=torch.float32, device=dev) if want_lse else None
     L = lib()
     s = int(splits or 0)
@@ -61,11 +61,12 @@ def _decode(q, k, v, scale, splits, want_lse):
     args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
             hkv, g, d, n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
             out.stride(0), out.stride(1), float(scale), s, code, ws.data_ptr(), ws.numel(), stream)
+    fn = L.tc_decode_attention_partial if partial else L.tc_decode_attention_lse
     if torch.cuda.current_device() == dev.index:
-        st = L.tc_decode_attention_lse(*args)
+        st = fn(*args)
     else:
         with torch.cuda.device(dev):
-            st = L.tc_decode_attention_lse(*args)
+            st = fn(*args)
     if st:
         check("tc_decode_attention", st)
     return (out, lse) if want_lse else out
@@ -82,6 +83,12 @@ def decode_attention(q, k, v, scale, split=256, block=16, *, splits=None):
 def decode_attention_lse(q, k, v, scale, *, splits=None):
     """Like decode_attention, plus the natural-log log-sum-exp of the scaled scores, fp32 [hkv, g]."""
     return _decode(q, k, v, scale, splits, True)
+
+
+def decode_attention_partial(q, k, v, scale, *, splits=None):
+    """Partial result of a KV slice for sequence-sharded decode: (o fp32 [hkv, g, d], natural-log
+    lse fp32 [hkv, g]). Partials of disjoint token ranges merge exactly with merge_partials."""
+    return _decode(q, k, v, scale, splits, True, partial=True)
 
 
 def decode_attention_batched(q, k, v, scale, lengths=None, *, splits=None):
