@@ -69,10 +69,10 @@ int tc_device_errors(int clear);
  * count; splits > 0 forces that many KV slices per (sequence, head) (capped at 128).
  *
  * Workspace: at least tc_decode_attention_workspace_size(...) bytes of device memory whose first
- * 16*batch*hkv bytes (the per-head tickets) are ZERO before the first call; every call leaves them
- * zero again. Beyond that prefix a call writes partial results, so reusing a workspace for a larger
- * batch*hkv needs the larger prefix zeroed first (keep one workspace per batch*hkv). Calls that
- * share a workspace must be ordered (same stream).
+ * 16*batch*hkv bytes (per-head tickets and counters) are ZERO before the first call; every call
+ * leaves them zero again. Beyond that prefix a call writes partial results, so reusing a workspace
+ * for a larger batch*hkv needs the larger prefix zeroed first (keep one workspace per batch*hkv).
+ * Calls that share a workspace must be ordered (same stream).
  * ====================================================================================== */
 size_t tc_decode_attention_workspace_size(int batch, int hkv, int g, int d, int64_t max_n,
                                           int64_t total_tokens, int splits, int dtype);

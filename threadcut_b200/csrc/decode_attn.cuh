@@ -25,9 +25,11 @@
 //     spare, the point is to take the per-token FMA/shuffle work off the issue slots so the CTA
 //     stays a pure HBM stream.
 //   * epilogue: the warps' (m, l, o) are combined in shared memory; with one split the CTA writes
-//     the output, otherwise it publishes an unnormalised partial to the workspace (red.release) —
-//     except the CTA that took the head's last start ticket, which waits for the others' partials
-//     and merges them with its own by log-sum-exp (see finish_cta).
+//     the output, otherwise it publishes an unnormalised partial to the workspace (red.release on
+//     the head's counter). The CTAs that took the head's last min(g, splits) start tickets are its
+//     mergers: each waits for all partials and merges one query head's columns by log-sum-exp,
+//     every thread folding one column of a share of the splits in a single L2 round trip
+//     (see finish_cta).
 //   * launched with programmatic dependent launch: the prologue overlaps the previous kernel's
 //     tail, and nothing the previous kernel may write is read before griddepcontrol.wait.
 // fp32, d < 64, or K/V whose strides break the 16-byte TMA rule use decode_generic_kernel: the same
@@ -44,7 +46,10 @@ constexpr int kTile = 32;        // tokens per staged tile (the TMA box height)
 constexpr int kCWarps = 6;       // consumer warps per CTA of the tensor-core kernel (+1 producer warp)
 constexpr int kGenWarps = 4;     // warps per CTA of the generic kernel
 constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
-constexpr int kMergeChunk = 12;  // partials one merger thread loads per L2 round trip
+// Per (sequence, head) control words at the start of the workspace, all zero between calls:
+// [0] start ticket, [1] published partials, [2] mergers done waiting, [3] spare.
+constexpr int kCtrWords = 4;
+constexpr int kMergeLoads = 8;   // partials one merger thread loads per L2 round trip
 constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM of the tensor-core kernel
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
@@ -72,8 +77,8 @@ struct DecodeParams {
   int max_splits;       // grid.x and the workspace stride between (sequence, head) rows
   float c;              // scale * log2(e)
   float* ws_o;          // [batch*hkv][max_splits][g][d]  unnormalised partial outputs
-  float* ws_ml;         // [batch*hkv][max_splits][g][2]  (running max (log2 domain), sum)
-  unsigned int* counters;  // [batch*hkv][4]: start ticket, published partials (zero between calls)
+  float2* ws_ml;        // [batch*hkv][max_splits][g]  (running max (log2 domain), sum)
+  unsigned int* counters;  // [batch*hkv][kCtrWords] (zero between calls)
   int out_f32;             // 1: `out` is fp32 (unrounded partial for a cross-GPU merge), else T
 };
 
@@ -132,19 +137,32 @@ struct Region {
   __device__ static float* acc(float* r, int i) { return r + 2 * HP + i * kAccStride; }
 };
 
-// Combine the per-warp states of this CTA, then write the output (one split), publish a partial
-// (most splits), or — in the merger CTA of this (sequence, head) — wait for every other split's
-// partial and merge them with this CTA's own by log-sum-exp.
+// Takes this CTA's start ticket for (sequence b, head h) and returns its merger index: ticket -
+// (nsplit - min(g, nsplit)) for the last min(g, nsplit) tickets, -1 before them.
+__device__ __forceinline__ int merger_index(const DecodeParams& p, int b, int h, int nsplit) {
+  const unsigned int t = atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * kCtrWords, 1u);
+  const int nm = p.g < nsplit ? p.g : nsplit;
+  const int mi = (int)t - (nsplit - nm);
+  return mi >= 0 ? mi : -1;
+}
+
+// Combine the per-warp states of this CTA, then write the output (one split) or publish a partial;
+// in a merger CTA of this (sequence, head), then merge the partials of its query heads.
 //
-// The merger is the CTA that took the last START ticket of its (sequence, head). Every other CTA of
-// that head took its ticket earlier, so it is already running (or done) and will publish without
-// waiting on anything: the merger's bounded wait for them needs no co-residency guarantee. The
-// merger keeps its own partial in shared memory, and resets both tickets for the next call.
+// Every CTA of a multi-split head publishes its unnormalised partial and bumps the head's published
+// counter with a release. The CTAs that took the last nm = min(g, nsplit) START tickets are the
+// head's mergers (`mi` = ticket - (nsplit - nm), -1 for the others): every other CTA of the head
+// took its ticket earlier, so it is already running (or done) and publishes without waiting on
+// anything, and the mergers' bounded waits need no co-residency guarantee. Merger mi handles query
+// heads mi, mi + nm, ...: thread t folds float4 column t % Q (Q = D/4) of the splits
+// t / Q, t / Q + nsg, ... (nsg = blockDim.x / Q split groups), loading up to kMergeLoads of them
+// per L2 round trip, and the split groups are combined through shared memory. The last merger past
+// the wait clears the published count; the merger with the last ticket clears the ticket.
 // Preconditions: every thread calls this after a __syncthreads() that follows the region writes;
-// `epi` holds 16*D floats that overlap no region.
+// the region area holds at least merge_scratch_bytes(blockDim.x) bytes.
 template <typename T, int D, int HP>
 __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_stride_bytes, int nregions,
-                           float* epi, int b, int h, int split, int nsplit, bool merger) {
+                           int b, int h, int split, int nsplit, int mi) {
   __shared__ float s_M[16], s_L[16];
   __shared__ int s_ok;
   using R = Region<D, HP>;
@@ -152,7 +170,6 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t bh = (int64_t)b * p.hkv + h;
   const int64_t out0 = b * p.so_b + h * p.so_h;
-  float* own = epi;  // the merger's own unnormalised output [g][D]
   auto region = [&](int w) { return reinterpret_cast<float*>(regions + (size_t)w * region_stride_bytes); };
 
   if (tid < g) {
@@ -163,8 +180,10 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
       for (int w = 0; w < nregions; ++w) L += R::l(region(w))[tid] * fast_exp2(R::m(region(w))[tid] - M);
     s_M[tid] = M;
     s_L[tid] = L;
+    if (nsplit > 1) p.ws_ml[(bh * p.max_splits + split) * g + tid] = make_float2(M, L);
   }
   __syncthreads();
+  float* wo = p.ws_o + (bh * p.max_splits + split) * g * D;
   for (int idx = tid; idx < g * D; idx += nthr) {
     const int i = idx / D, d = idx - i * D;
     const float M = s_M[i];
@@ -174,33 +193,25 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
     if (nsplit == 1) {
       const float L = s_L[i];
       put_out<T>(p, out0 + i * p.so_g + d, L > 0.f ? o / L : 0.f);
-    } else if (merger) {
-      own[idx] = o;
     } else {
-      p.ws_o[((bh * p.max_splits + split) * g + i) * D + d] = o;
+      wo[idx] = o;
     }
   }
   if (nsplit == 1) {
     if (p.lse != nullptr && tid < g) p.lse[b * p.lse_b + (int64_t)h * g + tid] = lse_nat(s_M[tid], s_L[tid]);
     return;
   }
-  unsigned int* ctr = p.counters + bh * 4;
-  if (!merger) {
-    if (tid < g) {
-      float* ml = p.ws_ml + ((bh * p.max_splits + split) * g + tid) * 2;
-      ml[0] = s_M[tid];
-      ml[1] = s_L[tid];
-    }
-    __syncthreads();
-    if (tid == 0) red_release_add_u32(ctr + 1, 1u);
-    return;
-  }
+  unsigned int* ctr = p.counters + bh * kCtrWords;
+  __syncthreads();  // every thread's partial writes precede the release below
+  if (tid == 0) red_release_add_u32(ctr + 1, 1u);
+  if (mi < 0) return;
 
-  // ---- merger: wait (bounded) until the other nsplit-1 partials are published
+  // ---- merger mi: wait (bounded) until all nsplit partials are published
+  const int nm = g < nsplit ? g : nsplit;
   if (tid == 0) {
     int ok = 1;
     uint32_t spin = 0;
-    while (ld_acquire_u32(ctr + 1) < (unsigned int)(nsplit - 1)) {
+    while (ld_acquire_u32(ctr + 1) < (unsigned int)nsplit) {
       if (++spin >= kSpinLimit) {
         raise_error(TC_DEVERR_PIPE_TIMEOUT);
         ok = 0;
@@ -209,68 +220,93 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
       __nanosleep(32);
     }
     s_ok = ok;
+    // the last merger past the wait clears the published count (the result is needed only at the end)
+    if (ok && atomicAdd(ctr + 2, 1u) == (unsigned int)(nm - 1)) {
+      ctr[1] = 0u;
+      ctr[2] = 0u;
+    }
+    if (mi == nm - 1) ctr[0] = 0u;  // every CTA of this head has taken its ticket
   }
-  __syncthreads();
+  __syncthreads();  // also: the regions are free for the merge scratch
   if (!s_ok) return;
 
-  // out = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s over all splits, this CTA's own from shared
-  // memory. Every thread owns one float4 column of one head; it loads the (m, l) pair and that column
-  // of up to kMergeChunk splits at once (one L2 round trip per chunk) and folds chunks in online.
-  const float2* mlb = reinterpret_cast<const float2*>(p.ws_ml + bh * p.max_splits * g * 2);
-  const float4* ob = reinterpret_cast<const float4*>(p.ws_o + bh * p.max_splits * g * D);
-  const float4* ownv = reinterpret_cast<const float4*>(own);
-  constexpr int Q = D / 4;  // float4 columns per head row
-  for (int u = tid; u < g * Q; u += nthr) {
-    const int i = u / Q;
-    float M = s_M[i], L = s_L[i];
-    float4 acc = ownv[u];
-    for (int s0 = 0; s0 < nsplit; s0 += kMergeChunk) {
-      float2 ml[kMergeChunk];
-      float4 x[kMergeChunk];
+  constexpr int Q = D / 4;  // float4 columns per query head
+  const int nsg = nthr / Q;  // split groups
+  const int sg = tid / Q, col = tid - (tid / Q) * Q;
+  float* sM = reinterpret_cast<float*>(regions);  // [nsg][Q] per-thread states
+  float* sL = sM + nsg * Q;
+  float4* sA = reinterpret_cast<float4*>(sL + nsg * Q);
+  for (int i = mi; i < g; i += nm) {
+    float M = -INFINITY, L = 0.f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sg < nsg) {
+      const float2* mlb = p.ws_ml + bh * p.max_splits * g + i;
+      const float4* ob = reinterpret_cast<const float4*>(p.ws_o + (bh * p.max_splits * g + i) * D) + col;
+      for (int s0 = sg; s0 < nsplit; s0 += nsg * kMergeLoads) {
+        float2 ml[kMergeLoads];
+        float4 x[kMergeLoads];
 #pragma unroll
-      for (int k = 0; k < kMergeChunk; ++k) {
-        const int s = s0 + k;
-        const bool use = s < nsplit && s != split;
-        ml[k] = use ? __ldcg(mlb + (int64_t)s * g + i) : make_float2(-INFINITY, 0.f);
-        x[k] = use ? __ldcg(ob + ((int64_t)s * g) * Q + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < kMergeLoads; ++k) {
+          const int s = s0 + k * nsg;
+          const bool use = s < nsplit;
+          ml[k] = use ? __ldcg(mlb + (int64_t)s * g) : make_float2(-INFINITY, 0.f);
+          x[k] = use ? __ldcg(ob + (int64_t)s * g * Q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float mc = M;
+#pragma unroll
+        for (int k = 0; k < kMergeLoads; ++k) mc = fmaxf(mc, ml[k].x);
+        const float a = M == -INFINITY ? 0.f : fast_exp2(M - mc);
+        L *= a;
+        A.x *= a;
+        A.y *= a;
+        A.z *= a;
+        A.w *= a;
+#pragma unroll
+        for (int k = 0; k < kMergeLoads; ++k) {
+          const float w = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - mc);
+          L += w * ml[k].y;
+          A.x += w * x[k].x;
+          A.y += w * x[k].y;
+          A.z += w * x[k].z;
+          A.w += w * x[k].w;
+        }
+        M = mc;
       }
-      float mc = M;
-#pragma unroll
-      for (int k = 0; k < kMergeChunk; ++k) mc = fmaxf(mc, ml[k].x);
-      const float a = fast_exp2(M - mc);
-      L *= a;
-      acc.x *= a;
-      acc.y *= a;
-      acc.z *= a;
-      acc.w *= a;
-#pragma unroll
-      for (int k = 0; k < kMergeChunk; ++k) {
-        const float w = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - mc);
-        L += w * ml[k].y;
-        acc.x += w * x[k].x;
-        acc.y += w * x[k].y;
-        acc.z += w * x[k].z;
-        acc.w += w * x[k].w;
-      }
-      M = mc;
+      sM[sg * Q + col] = M;
+      sL[sg * Q + col] = L;
+      sA[sg * Q + col] = A;
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int64_t o = out0 + i * p.so_g + (u - i * Q) * 4;
-    put_out<T>(p, o, acc.x * inv);
-    put_out<T>(p, o + 1, acc.y * inv);
-    put_out<T>(p, o + 2, acc.z * inv);
-    put_out<T>(p, o + 3, acc.w * inv);
-    if (p.lse != nullptr && u == i * Q) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(M, L);
-  }
-  if (tid == 0) {  // every other CTA of this head is done with both tickets
-    ctr[0] = 0u;
-    ctr[1] = 0u;
+    __syncthreads();
+    if (tid < Q) {
+      float Mt = -INFINITY;
+      for (int w = 0; w < nsg; ++w) Mt = fmaxf(Mt, sM[w * Q + tid]);
+      float Lt = 0.f;
+      float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int w = 0; w < nsg; ++w) {
+        const float mw = sM[w * Q + tid];
+        const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - Mt);
+        const float4 v = sA[w * Q + tid];
+        Lt += wt * sL[w * Q + tid];
+        At.x += wt * v.x;
+        At.y += wt * v.y;
+        At.z += wt * v.z;
+        At.w += wt * v.w;
+      }
+      const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+      const int64_t o = out0 + i * p.so_g + tid * 4;
+      put_out<T>(p, o, At.x * inv);
+      put_out<T>(p, o + 1, At.y * inv);
+      put_out<T>(p, o + 2, At.z * inv);
+      put_out<T>(p, o + 3, At.w * inv);
+      if (p.lse != nullptr && tid == 0) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(Mt, Lt);
+    }
+    __syncthreads();  // the scratch is rewritten by the next query head
   }
 }
 
-// Bytes of the epilogue area: the merger's own partial, o [16][D].
-template <int D>
-constexpr int epi_bytes() { return 16 * D * 4; }
+// Shared-memory scratch of a merger: (m, l, float4 o) per thread.
+__host__ __device__ constexpr int merge_scratch_bytes(int nthreads) { return nthreads * 24; }
+
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
@@ -291,8 +327,7 @@ struct MmaGeom {
   static constexpr int kStages = D <= 128 ? 12 : 6;
   static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
-  static constexpr int kEpiBytes = epi_bytes<D>();
-  static constexpr int kSmem = 1024 + kPipeBytes + kEpiBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
+  static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
 };
 
 // Byte offset of element (row, col) of a staged tile: 64-column boxes of 32 rows x 128 bytes, each
@@ -315,13 +350,13 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   constexpr int NBOX = D / 64;
   constexpr int kStages = G::kStages;
   static_assert(Region<D, HP>::kFloats * 4 <= G::kStageBytes, "combine region must fit in a stage");
+  static_assert(merge_scratch_bytes(32 * (kCWarps + 1)) <= G::kPipeBytes, "merge scratch must fit in the pipeline");
   extern __shared__ uint8_t smem_raw[];
   // TMA 128-byte swizzle is defined on absolute shared addresses: align the pipeline to 1 KB
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  float* epi = reinterpret_cast<float*>(smem + G::kPipeBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes + G::kEpiBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes);
   uint64_t* empty = full + kStages;
-  __shared__ int s_merger;
+  __shared__ int s_mi;  // merger index of this CTA (-1: not a merger)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -369,14 +404,14 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   const int64_t t0 = tt0 * kTile;
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
   const int ntiles = (int)(tt1 - tt0);
-  if (threadIdx.x == 0) s_merger = 0;
+  if (threadIdx.x == 0) s_mi = -1;
   __syncthreads();
 
   if (warp == kCWarps) {
     // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
     // the result is read only after the final __syncthreads
     if (lane == 1 && nsplit > 1)
-      s_merger = atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * 4, 1u) == (unsigned int)(nsplit - 1);
+      s_mi = merger_index(p, b, h, nsplit);
     // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
     if (lane == 0 && ntiles > 0) {
       const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
@@ -586,7 +621,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         }
   }
   __syncthreads();
-  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, epi, b, h, split, nsplit, s_merger != 0);
+  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, b, h, split, nsplit, s_mi);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -596,7 +631,9 @@ template <int D>
 struct GenGeom {
   static constexpr int HP = 16;
   static constexpr int kRegionBytes = ((Region<D, HP>::kFloats * 4 + 127) / 128) * 128;
-  static constexpr int kSmem = kGenWarps * kRegionBytes + epi_bytes<D>();
+  static constexpr int kSmem = kGenWarps * kRegionBytes > merge_scratch_bytes(32 * kGenWarps)
+                                   ? kGenWarps * kRegionBytes
+                                   : merge_scratch_bytes(32 * kGenWarps);
 };
 
 template <typename T, int D>
@@ -607,7 +644,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_launch();
   pdl_wait();
-  __shared__ int s_merger;
+  __shared__ int s_mi;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const T* kh;
   const T* vh;
@@ -620,8 +657,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
   split_range(seq_tiles, split, nsplit, tt0, tt1);
   const int64_t t0 = tt0 * kTile;
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
-  if (threadIdx.x == 0)
-    s_merger = nsplit > 1 && atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * 4, 1u) == (unsigned int)(nsplit - 1);
+  if (threadIdx.x == 0) s_mi = nsplit > 1 ? merger_index(p, b, h, nsplit) : -1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.g;
 
@@ -680,9 +716,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
       if (d < D) R::acc(reg, i)[d] = acc[i][j];
     }
   __syncthreads();
-  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kGenWarps,
-                       reinterpret_cast<float*>(smem + kGenWarps * G::kRegionBytes), b, h, split, nsplit,
-                       s_merger != 0);
+  finish_cta<T, D, HP>(p, smem, G::kRegionBytes, kGenWarps, b, h, split, nsplit, s_mi);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -18,7 +18,11 @@
 // "read" flag, and writes only after the units whose source rows it overwrites have published
 // theirs (at most two earlier units; bounded wait). Writers never precede the readers they could
 // clobber, and no unit waits on one that has not been handed out, so the grid cannot deadlock.
+// When the rows are contiguous and 16-byte aligned (every GrowingLayer buffer), splice_bulk_kernel
+// runs the same protocol with the unit moved by bulk copies through a shared-memory ring.
 #pragma once
+
+#include <type_traits>
 
 #include "tc_common.cuh"
 
@@ -256,6 +260,255 @@ __global__ void __launch_bounds__(kSpliceThreads) splice_inplace_kernel(const __
   }
   // the last CTA to leave resets the ticket for the next call on this workspace
   if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&p.ws->exits, 1u) == gridDim.x - 1) {
+      p.ws->ticket = 0;
+      p.ws->exits = 0;
+      __threadfence();
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Rotation of one 16-byte chunk pair held as raw words (x from the first half of a row, y from the
+// second), element e of the pair at half-index i0 + e; the same separately rounded fp32 products and
+// sum as rotate_pair. cs is 16-byte aligned with i0 and half multiples of 4.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+  else
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  uint32_t w;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    memcpy(&w, &v, 4);
+  } else {
+    const __half2 v = __floats2half2_rn(a, b);
+    memcpy(&w, &v, 4);
+  }
+  return w;
+}
+__device__ __forceinline__ void rot1(float x, float y, float c, float s, float& o0, float& o1) {
+  o0 = __fadd_rn(__fmul_rn(x, c), __fmul_rn(-y, s));
+  o1 = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
+}
+template <typename T>
+__device__ __forceinline__ void rotate_words(uint4& x, uint4& y, const float* cs, int half, int i0) {
+  uint32_t* xw = reinterpret_cast<uint32_t*>(&x);
+  uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 c = *reinterpret_cast<const float4*>(cs + i0);
+    const float4 sn = *reinterpret_cast<const float4*>(cs + half + i0);
+    const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float o0, o1;
+      rot1(__uint_as_float(xw[e]), __uint_as_float(yw[e]), cc[e], ss[e], o0, o1);
+      xw[e] = __float_as_uint(o0);
+      yw[e] = __float_as_uint(o1);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // 4 elements per float4 of the table
+      const float4 c = *reinterpret_cast<const float4*>(cs + i0 + 4 * q);
+      const float4 sn = *reinterpret_cast<const float4*>(cs + half + i0 + 4 * q);
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const float2 a = unpack2<T>(xw[2 * q + w]), b = unpack2<T>(yw[2 * q + w]);
+        float o0a, o1a, o0b, o1b;
+        rot1(a.x, b.x, cc[2 * w], ss[2 * w], o0a, o1a);
+        rot1(a.y, b.y, cc[2 * w + 1], ss[2 * w + 1], o0b, o1b);
+        xw[2 * q + w] = pack2<T>(o0a, o0b);
+        yw[2 * q + w] = pack2<T>(o1a, o1b);
+      }
+    }
+  }
+}
+
+// In-place splice through shared memory (rows contiguous, 16-byte aligned). Same units, ticket
+// order and read flags as splice_inplace_kernel; a unit's K rows and V rows (16 KB each at most)
+// arrive by two bulk copies into one stage of a kBulkStages ring, the K rows are rotated in shared
+// memory, and two bulk stores write them to the destination. Thread 0 drives the ring with no
+// memory round trip on a unit's path: the next ticket is always taken one fetch ahead, a unit's read
+// flag is stored as soon as its bulk loads have completed, and the flags a unit must wait for are
+// read one iteration ahead and only polled again if they were not yet set.
+//   Ordering: a read flag is written after the mbarrier reported the unit's loads complete, and
+//   the bulk stores that overwrite those rows are issued only after another thread has seen the
+//   flag, so the overwrite cannot reach the rows before they were read; relaxed accesses suffice.
+//   Progress: a unit's flag is written only when this CTA reaches it, but the CTA's earlier units
+//   hold smaller tickets and wait only on smaller ones, so the smallest unwritten flag always
+//   progresses: no deadlock, with or without co-resident CTAs.
+constexpr int kBulkStages = 3;
+constexpr int kBulkCtasPerSm = 2;
+constexpr int kBulkUnitBytes = 16384;  // K (or V) bytes of one unit, upper bound
+constexpr int kBulkThreads = 256;
+constexpr unsigned int kNoUnit = 0xffffffffu;
+
+// Flags unit (lh, chunk i) waits for: chunks [j_lo, j_hi] of the same layer-head (none if j_lo > j_hi).
+__device__ __forceinline__ void splice_deps(const SpliceParams& p, int64_t i, int64_t& j_lo, int64_t& j_hi) {
+  const int64_t r0 = i * p.rows_per_unit;
+  const int64_t r1 = (r0 + p.rows_per_unit < p.c) ? r0 + p.rows_per_unit : p.c;
+  const int64_t lo_t = r0 - p.gap, hi_t = r1 - 1 - p.gap;  // C-index range of overwritten sources
+  j_lo = 1;
+  j_hi = 0;
+  if (hi_t < 0) return;
+  j_lo = (lo_t > 0 ? lo_t : 0) / p.rows_per_unit;
+  j_hi = hi_t / p.rows_per_unit;
+  if (j_hi > i - 1) j_hi = i - 1;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBulkThreads) splice_bulk_kernel(const __grid_constant__ SpliceParams p) {
+  constexpr int VEC = 16 / (int)sizeof(T);
+  extern __shared__ __align__(128) uint8_t smem[];  // kBulkStages x (K rows, V rows)
+  __shared__ __align__(8) uint64_t full[kBulkStages];
+  __shared__ __align__(16) float s_cs[kMaxRopeDim];
+  __shared__ unsigned int s_unit[kBulkStages];
+  __shared__ int s_ok;
+  const int tid = threadIdx.x;
+  const int half = p.d / 2, cph = half / VEC;
+  const int64_t lh_count = (int64_t)p.layers * p.hkv;
+  const int64_t units = lh_count * p.nchunks;
+  const int64_t row_elems = p.d;  // rows are contiguous: token stride == d
+  for (int i = tid; i < p.d; i += blockDim.x) s_cs[i] = p.cs[i];
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ---- thread 0 state
+  int fetched = 0;             // iterations whose stage has been filled (or marked as the end)
+  unsigned int next_ticket = 0;  // taken one fetch ahead
+  uint64_t pol = 0;
+  unsigned int dep_seen = 0;   // the next unit's dependency flags were all set when read ahead
+  auto fetch = [&](int it) {   // start the loads of iteration `it` (or mark it as the end)
+    const int s = it % kBulkStages;
+    const unsigned int u = next_ticket;
+    next_ticket = atomicAdd(&p.ws->ticket, 1u);  // consumed by the next fetch
+    ++fetched;
+    if ((int64_t)u >= units) {
+      s_unit[s] = kNoUnit;
+      mbar_arrive(&full[s]);
+      return;
+    }
+    s_unit[s] = u;
+    const int64_t i = u / lh_count, lh = u - i * lh_count;
+    const int layer = (int)(lh / p.hkv), h = (int)(lh - (int64_t)layer * p.hkv);
+    const int64_t r0 = i * p.rows_per_unit;
+    const int64_t r1 = (r0 + p.rows_per_unit < p.c) ? r0 + p.rows_per_unit : p.c;
+    const uint32_t bytes = (uint32_t)((r1 - r0) * row_elems * (int64_t)sizeof(T));
+    const T* ks = static_cast<const T*>(p.kb[layer]) + h * p.sh + (p.c0 + r0) * row_elems;
+    const T* vs = static_cast<const T*>(p.vb[layer]) + h * p.sh + (p.c0 + r0) * row_elems;
+    uint8_t* st = smem + (size_t)s * 2 * kBulkUnitBytes;
+    mbar_arrive_expect_tx(&full[s], 2 * bytes);
+    bulk_g2s(st, ks, bytes, &full[s], pol);
+    bulk_g2s(st + kBulkUnitBytes, vs, bytes, &full[s], pol);
+  };
+  auto read_deps_ahead = [&](int it) {  // read the dependency flags of iteration `it`'s unit
+    dep_seen = 0;
+    if (it >= fetched) return;
+    const unsigned int u = s_unit[it % kBulkStages];
+    if (u == kNoUnit) return;
+    const int64_t i = u / lh_count, lh = u - i * lh_count;
+    int64_t j_lo, j_hi;
+    splice_deps(p, i, j_lo, j_hi);
+    unsigned int all = 1;
+    for (int64_t j = j_lo; j <= j_hi; ++j) all &= ld_relaxed_u32(&p.ws->flags[lh * p.nchunks + j]) == p.epoch;
+    dep_seen = all;
+  };
+  if (tid == 0) {
+    pol = policy_evict_first();
+    next_ticket = atomicAdd(&p.ws->ticket, 1u);
+    for (int it = 0; it < kBulkStages; ++it) fetch(it);
+    read_deps_ahead(0);
+  }
+
+  int it = 0;
+  for (;; ++it) {
+    const int s = it % kBulkStages;
+    if (tid == 0) {
+      const bool ok = mbar_wait(&full[s], (uint32_t)((it / kBulkStages) & 1), TC_DEVERR_PIPE_TIMEOUT);
+      s_ok = ok;
+      // the unit's source rows are in shared memory: later units may overwrite them
+      if (ok && s_unit[s] != kNoUnit) {
+        const int64_t u = s_unit[s];
+        const int64_t i = u / lh_count, lh = u - i * lh_count;
+        st_relaxed_u32(&p.ws->flags[lh * p.nchunks + i], p.epoch);
+      }
+    }
+    __syncthreads();
+    if (!s_ok || s_unit[s] == kNoUnit) break;  // uniform
+    const int64_t u = s_unit[s];
+    const int64_t i = u / lh_count, lh = u - i * lh_count;
+    const int layer = (int)(lh / p.hkv), h = (int)(lh - (int64_t)layer * p.hkv);
+    const int64_t r0 = i * p.rows_per_unit;
+    const int64_t r1 = (r0 + p.rows_per_unit < p.c) ? r0 + p.rows_per_unit : p.c;
+    uint8_t* st = smem + (size_t)s * 2 * kBulkUnitBytes;
+
+    // rotate the K rows in place in shared memory (a quarter warp covers 128 contiguous bytes)
+    const int ntask = (int)(r1 - r0) * cph;
+    for (int t = tid; t < ntask; t += kBulkThreads) {
+      const int r = t / cph, ch = t - (t / cph) * cph;
+      T* row = reinterpret_cast<T*>(st) + (int64_t)r * row_elems;
+      uint4* xp = reinterpret_cast<uint4*>(row + ch * VEC);
+      uint4* yp = reinterpret_cast<uint4*>(row + half + ch * VEC);
+      uint4 x = *xp, y = *yp;
+      rotate_words<T>(x, y, s_cs, half, ch * VEC);
+      *xp = x;
+      *yp = y;
+    }
+    fence_proxy_async_smem();  // the rotated rows are read next by the bulk store (async proxy)
+
+    int ok = 1;
+    if (tid == 0 && !dep_seen) {
+      // some flag this unit waits for was not set when read ahead: poll it now (bounded)
+      int64_t j_lo, j_hi;
+      splice_deps(p, i, j_lo, j_hi);
+      for (int64_t j = j_lo; j <= j_hi && ok; ++j) {
+        const unsigned int* f = &p.ws->flags[lh * p.nchunks + j];
+        uint32_t spin = 0;
+        while (ld_relaxed_u32(f) != p.epoch) {
+          if (++spin >= kSpinLimit) {
+            raise_error(TC_DEVERR_FLAG_TIMEOUT);
+            ok = 0;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+    }
+    __syncthreads();  // every thread's rotation is written and fenced
+    if (tid == 0) {
+      if (ok) {
+        const uint32_t bytes = (uint32_t)((r1 - r0) * row_elems * (int64_t)sizeof(T));
+        T* kd = static_cast<T*>(p.kb[layer]) + h * p.sh + (p.a + r0) * row_elems;
+        T* vd = static_cast<T*>(p.vb[layer]) + h * p.sh + (p.a + r0) * row_elems;
+        bulk_s2g(kd, st, bytes);
+        bulk_s2g(vd, st + kBulkUnitBytes, bytes);
+      }
+      bulk_commit();
+      // refill the previous iteration's stage once its stores have read it
+      if (it > 0) {
+        bulk_wait_read<1>();
+        fetch(it - 1 + kBulkStages);
+      }
+      read_deps_ahead(it + 1);
+    }
+  }
+  if (tid == 0) {
+    // drain: stages filled for iterations this CTA never reached (end markers, or loads still in
+    // flight after a timeout), then this thread's stores
+    for (int j = s_ok ? it + 1 : it; j < fetched; ++j)
+      mbar_wait(&full[j % kBulkStages], (uint32_t)((j / kBulkStages) & 1), TC_DEVERR_PIPE_TIMEOUT);
+    bulk_wait<0>();
+    // the last CTA to leave resets the ticket for the next call on this workspace
     __threadfence();
     if (atomicAdd(&p.ws->exits, 1u) == gridDim.x - 1) {
       p.ws->ticket = 0;

@@ -138,8 +138,9 @@ struct WsLayout {
   size_t counters = 0, ml = 0, o = 0, total = 0;
 };
 
-// Ticket region at the start of a decode workspace: 4 uint32 per (sequence, head).
-size_t decode_counter_bytes(int64_t rows) { return round256(16 * (size_t)rows); }
+// Control region at the start of a decode workspace: kCtrWords uint32 per (sequence, head) (start
+// ticket, published partials, mergers done), zero between calls.
+size_t decode_counter_bytes(int64_t rows) { return round256(sizeof(unsigned int) * tc::kCtrWords * (size_t)rows); }
 
 WsLayout decode_ws_layout(int batch, int hkv, int g, int d, int64_t max_splits) {
   WsLayout w;
@@ -245,7 +246,7 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
   if (ws == nullptr || ws_bytes < w.total) return TC_ERR_WORKSPACE;
   uint8_t* wb = static_cast<uint8_t*>(ws);
   p.counters = reinterpret_cast<unsigned int*>(wb + w.counters);
-  p.ws_ml = reinterpret_cast<float*>(wb + w.ml);
+  p.ws_ml = reinterpret_cast<float2*>(wb + w.ml);
   p.ws_o = reinterpret_cast<float*>(wb + w.o);
   p.tiles_per_split = (int)pl.tps;
   p.max_splits = (int)pl.max_splits;
@@ -298,6 +299,16 @@ cudaError_t launch_splice_copy(const SpliceCopyParams& p, int blocks, cudaStream
 template <typename T, int VEC>
 cudaError_t launch_splice_inplace(const SpliceParams& p, int blocks, cudaStream_t st) {
   splice_inplace_kernel<T, VEC><<<blocks, kSpliceThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_splice_bulk(const SpliceParams& p, int blocks, cudaStream_t st, int dev) {
+  auto fn = splice_bulk_kernel<T>;
+  const int smem = kBulkStages * 2 * kBulkUnitBytes;
+  const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  if (e != cudaSuccess) return e;
+  fn<<<blocks, kBulkThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -649,11 +660,23 @@ int tc_splice_inplace(void* const* kbufs, void* const* vbufs, int layers, int hk
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return TC_ERR_WORKSPACE;
   p.ws = static_cast<SpliceWs*>(workspace);
   const int64_t units = (int64_t)layers * hkv * p.nchunks;
-  const int sms = sm_count(current_device());
-  int64_t blocks = (int64_t)sms * 6;
-  if (blocks > units) blocks = units;
-  const cudaError_t e =
-      TC_ROPE_DISPATCH(launch_splice_inplace, dtype, vec, p, (int)blocks, static_cast<cudaStream_t>(stream));
+  if (units >= (int64_t)0xffffffffLL) return TC_ERR_INVALID;  // unit tickets are 32-bit
+  const int dev = current_device();
+  const int sms = sm_count(dev);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (vec > 1 && stride_n == d) {
+    // contiguous, aligned rows: a unit is one 16 KB block of K rows and one of V rows
+    int64_t blocks = (int64_t)sms * kBulkCtasPerSm;
+    if (blocks > units) blocks = units;
+    e = dtype == TC_F32   ? launch_splice_bulk<float>(p, (int)blocks, st, dev)
+        : dtype == TC_F16 ? launch_splice_bulk<__half>(p, (int)blocks, st, dev)
+                          : launch_splice_bulk<__nv_bfloat16>(p, (int)blocks, st, dev);
+  } else {
+    int64_t blocks = (int64_t)sms * 6;
+    if (blocks > units) blocks = units;
+    e = TC_ROPE_DISPATCH(launch_splice_inplace, dtype, vec, p, (int)blocks, st);
+  }
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
@@ -704,7 +727,7 @@ int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, voi
   void* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != TC_OK) return rc;
-  // the arrival tickets at the start of the workspace must be zero; they are left zero by every
+  // the control words at the start of the workspace must be zero; they are left zero by every
   // finished call, but an earlier call that failed part-way could have left them set
   if (cudaMemsetAsync(scratch, 0, decode_counter_bytes(hkv), static_cast<cudaStream_t>(stream)) !=
       cudaSuccess)
