@@ -50,6 +50,7 @@ constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
 // [0] start ticket, [1] published partials, [2] mergers done waiting, [3] spare.
 constexpr int kCtrWords = 4;
 constexpr int kMergeLoads = 8;   // partials one merger thread loads per L2 round trip
+constexpr int kLastSplitsPerWarp = 3;  // last-arrival merge: partials per warp (one round trip)
 constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM of the tensor-core kernel
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
@@ -137,6 +138,13 @@ struct Region {
   __device__ static float* acc(float* r, int i) { return r + 2 * HP + i * kAccStride; }
 };
 
+// Heads with at most kLastSplitsPerWarp splits per warp of the CTA are merged by the CTA that
+// publishes last (one atomic round trip after the last partial); heads with more splits by
+// min(g, nsplit) mergers chosen by start ticket.
+__host__ __device__ __forceinline__ bool last_arrival_merge(int nsplit, int nthreads) {
+  return nsplit <= (nthreads >> 5) * kLastSplitsPerWarp;
+}
+
 // Takes this CTA's start ticket for (sequence b, head h) and returns its merger index: ticket -
 // (nsplit - min(g, nsplit)) for the last min(g, nsplit) tickets, -1 before them.
 __device__ __forceinline__ int merger_index(const DecodeParams& p, int b, int h, int nsplit) {
@@ -146,11 +154,109 @@ __device__ __forceinline__ int merger_index(const DecodeParams& p, int b, int h,
   return mi >= 0 ? mi : -1;
 }
 
+// Last-arrival merge of all nsplit partials of (sequence b, head h), every one visible to the calling
+// CTA: warp w folds splits w, w + nwarps, ... (at most kLastSplitsPerWarp), lane l the float4 columns
+// c0 + l + 32k of each 128-column pass, and the warps' states are combined through `scratch`
+// (merge_scratch_bytes(blockDim.x) bytes). Called by all threads of the CTA.
+template <typename T, int D>
+__device__ void merge_last(const DecodeParams& p, uint8_t* scratch, int b, int h, int nsplit) {
+  constexpr int Q = D / 4;   // float4 columns per query head
+  constexpr int C = 128;     // columns per pass, 4 per lane
+  const int g = p.g;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int nwarps = nthr >> 5, warp = tid >> 5, lane = tid & 31;
+  const int64_t bh = (int64_t)b * p.hkv + h;
+  const int64_t out0 = b * p.so_b + h * p.so_h;
+  const int ncols = g * Q;
+  float* sM = reinterpret_cast<float*>(scratch);  // [nwarps][C]
+  float* sL = sM + nwarps * C;
+  float4* sA = reinterpret_cast<float4*>(sL + nwarps * C);
+  const float2* mlb = p.ws_ml + bh * p.max_splits * g;
+  const float4* ob = reinterpret_cast<const float4*>(p.ws_o + bh * p.max_splits * g * D);
+  for (int c0 = 0; c0 < ncols; c0 += C) {
+    float M[4], L[4];
+    float4 A[4];
+    int hd[4];
+    float2 ml[kLastSplitsPerWarp][4];
+    float4 x[kLastSplitsPerWarp][4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + lane + 32 * k;
+      hd[k] = c < ncols ? c / Q : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kLastSplitsPerWarp; ++j) {
+      const int s = warp + j * nwarps;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const bool use = s < nsplit && hd[k] >= 0;
+        ml[j][k] = use ? __ldcg(mlb + (int64_t)s * g + hd[k]) : make_float2(-INFINITY, 0.f);
+        x[j][k] = use ? __ldcg(ob + (int64_t)s * ncols + c0 + lane + 32 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float mc = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kLastSplitsPerWarp; ++j) mc = fmaxf(mc, ml[j][k].x);
+      L[k] = 0.f;
+      A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kLastSplitsPerWarp; ++j) {
+        const float w = ml[j][k].x == -INFINITY ? 0.f : fast_exp2(ml[j][k].x - mc);
+        L[k] += w * ml[j][k].y;
+        A[k].x += w * x[j][k].x;
+        A[k].y += w * x[j][k].y;
+        A[k].z += w * x[j][k].z;
+        A[k].w += w * x[j][k].w;
+      }
+      M[k] = mc;
+      sM[warp * C + lane + 32 * k] = M[k];
+      sL[warp * C + lane + 32 * k] = L[k];
+      sA[warp * C + lane + 32 * k] = A[k];
+    }
+    __syncthreads();
+    const int cn = ncols - c0 < C ? ncols - c0 : C;
+    for (int c = tid; c < cn; c += nthr) {
+      const int i = (c0 + c) / Q;
+      float Mt = -INFINITY;
+      for (int w = 0; w < nwarps; ++w) Mt = fmaxf(Mt, sM[w * C + c]);
+      float Lt = 0.f;
+      float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int w = 0; w < nwarps; ++w) {
+        const float mw = sM[w * C + c];
+        const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - Mt);
+        const float4 v = sA[w * C + c];
+        Lt += wt * sL[w * C + c];
+        At.x += wt * v.x;
+        At.y += wt * v.y;
+        At.z += wt * v.z;
+        At.w += wt * v.w;
+      }
+      const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+      const int64_t o = out0 + i * p.so_g + (c0 + c - i * Q) * 4;
+      put_out<T>(p, o, At.x * inv);
+      put_out<T>(p, o + 1, At.y * inv);
+      put_out<T>(p, o + 2, At.z * inv);
+      put_out<T>(p, o + 3, At.w * inv);
+      if (p.lse != nullptr && c0 + c == i * Q) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(Mt, Lt);
+    }
+    __syncthreads();  // the scratch is rewritten by the next pass
+  }
+}
+
 // Combine the per-warp states of this CTA, then write the output (one split) or publish a partial;
-// in a merger CTA of this (sequence, head), then merge the partials of its query heads.
+// in a merger CTA of this (sequence, head), then merge the partials.
 //
-// Every CTA of a multi-split head publishes its unnormalised partial and bumps the head's published
-// counter with a release. The CTAs that took the last nm = min(g, nsplit) START tickets are the
+// Few splits (last_arrival_merge): each CTA publishes its partial and bumps the head's counter with
+// an acq_rel atomic; the CTA that sees nsplit - 1 published last, so every partial is visible to it,
+// and it merges all query heads at once: warp w folds splits w, w + nwarps, w + 2*nwarps (one L2
+// round trip), lane l columns l, l+32, l+64, l+96, and the warps are combined in shared memory. It
+// clears the counter. No start ticket and no waiting.
+//
+// Many splits:
+// every CTA publishes its unnormalised partial and bumps the head's published counter with a
+// release. The CTAs that took the last nm = min(g, nsplit) START tickets are the
 // head's mergers (`mi` = ticket - (nsplit - nm), -1 for the others): every other CTA of the head
 // took its ticket earlier, so it is already running (or done) and publishes without waiting on
 // anything, and the mergers' bounded waits need no co-residency guarantee. Merger mi handles query
@@ -203,6 +309,14 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   }
   unsigned int* ctr = p.counters + bh * kCtrWords;
   __syncthreads();  // every thread's partial writes precede the release below
+  if (last_arrival_merge(nsplit, nthr)) {
+    if (tid == 0) s_ok = atom_add_acq_rel_u32(ctr + 1, 1u) == (unsigned int)(nsplit - 1);
+    __syncthreads();  // also: the regions are free for the merge scratch
+    if (!s_ok) return;
+    merge_last<T, D>(p, regions, b, h, nsplit);
+    if (tid == 0) ctr[1] = 0u;
+    return;
+  }
   if (tid == 0) red_release_add_u32(ctr + 1, 1u);
   if (mi < 0) return;
 
@@ -304,8 +418,9 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   }
 }
 
-// Shared-memory scratch of a merger: (m, l, float4 o) per thread.
-__host__ __device__ constexpr int merge_scratch_bytes(int nthreads) { return nthreads * 24; }
+// Shared-memory scratch of a merger: (m, l, float4 o) states, 128 per warp (last-arrival merge)
+// or one per thread (start-ticket mergers).
+__host__ __device__ constexpr int merge_scratch_bytes(int nthreads) { return (nthreads >> 5) * 128 * 24; }
 
 
 template <typename T>
@@ -410,7 +525,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   if (warp == kCWarps) {
     // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
     // the result is read only after the final __syncthreads
-    if (lane == 1 && nsplit > 1)
+    if (lane == 1 && nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x))
       s_mi = merger_index(p, b, h, nsplit);
     // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
     if (lane == 0 && ntiles > 0) {
@@ -657,7 +772,8 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
   split_range(seq_tiles, split, nsplit, tt0, tt1);
   const int64_t t0 = tt0 * kTile;
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
-  if (threadIdx.x == 0) s_mi = nsplit > 1 ? merger_index(p, b, h, nsplit) : -1;
+  if (threadIdx.x == 0)
+    s_mi = nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x) ? merger_index(p, b, h, nsplit) : -1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.g;
 

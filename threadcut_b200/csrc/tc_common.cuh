@@ -82,6 +82,14 @@ __device__ __forceinline__ unsigned int ld_relaxed_u32(const unsigned int* p) {
 __device__ __forceinline__ void st_relaxed_u32(unsigned int* p, unsigned int v) {
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Increment with release (this CTA's earlier writes, ordered to this thread by a preceding
+// __syncthreads, are visible no later than the increment) and acquire (the writes released by the
+// increments it observes are visible to this thread afterwards); returns the old value.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_u32(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 // Fire-and-forget increment that makes this CTA's earlier global writes (ordered to this thread by
 // a preceding __syncthreads) visible at gpu scope no later than the increment itself.
 __device__ __forceinline__ void red_release_add_u32(unsigned int* p, unsigned int v) {
