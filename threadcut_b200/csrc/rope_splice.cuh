@@ -343,6 +343,32 @@ __device__ __forceinline__ void rotate_words(uint4& x, uint4& y, const float* cs
 //   Progress: a unit's flag is written only when this CTA reaches it, but the CTA's earlier units
 //   hold smaller tickets and wait only on smaller ones, so the smallest unwritten flag always
 //   progresses: no deadlock, with or without co-resident CTAs.
+// Same rotation with this chunk's cos (c) and sin (sn) already in registers: VEC values each.
+template <typename T>
+__device__ __forceinline__ void rotate_words_reg(uint4& x, uint4& y, const float* c, const float* sn) {
+  uint32_t* xw = reinterpret_cast<uint32_t*>(&x);
+  uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
+  if constexpr (std::is_same<T, float>::value) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float o0, o1;
+      rot1(__uint_as_float(xw[e]), __uint_as_float(yw[e]), c[e], sn[e], o0, o1);
+      xw[e] = __float_as_uint(o0);
+      yw[e] = __float_as_uint(o1);
+    }
+  } else {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float2 a = unpack2<T>(xw[w]), b = unpack2<T>(yw[w]);
+      float o0a, o1a, o0b, o1b;
+      rot1(a.x, b.x, c[2 * w], sn[2 * w], o0a, o1a);
+      rot1(a.y, b.y, c[2 * w + 1], sn[2 * w + 1], o0b, o1b);
+      xw[w] = pack2<T>(o0a, o0b);
+      yw[w] = pack2<T>(o1a, o1b);
+    }
+  }
+}
+
 constexpr int kBulkStages = 3;
 constexpr int kBulkCtasPerSm = 2;
 constexpr int kBulkUnitBytes = 16384;  // K (or V) bytes of one unit, upper bound
@@ -384,6 +410,17 @@ __global__ void __launch_bounds__(kBulkThreads) splice_bulk_kernel(const __grid_
   __syncthreads();
 
   // ---- thread 0 state
+  // every task of a thread has the same chunk index when the stride divides by the chunks per
+  // half-row: then its cos/sin live in registers (no shared-memory table reads in the loop)
+  const bool fixed_ch = kBulkThreads % cph == 0;
+  const int my_ch = tid % cph;
+  float my_c[VEC], my_s[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+    my_c[e] = fixed_ch ? s_cs[my_ch * VEC + e] : 0.f;
+    my_s[e] = fixed_ch ? s_cs[half + my_ch * VEC + e] : 0.f;
+  }
+
   int fetched = 0;             // iterations whose stage has been filled (or marked as the end)
   unsigned int next_ticket = 0;  // taken one fetch ahead
   uint64_t pol = 0;
@@ -454,15 +491,27 @@ __global__ void __launch_bounds__(kBulkThreads) splice_bulk_kernel(const __grid_
 
     // rotate the K rows in place in shared memory (a quarter warp covers 128 contiguous bytes)
     const int ntask = (int)(r1 - r0) * cph;
-    for (int t = tid; t < ntask; t += kBulkThreads) {
-      const int r = t / cph, ch = t - (t / cph) * cph;
-      T* row = reinterpret_cast<T*>(st) + (int64_t)r * row_elems;
-      uint4* xp = reinterpret_cast<uint4*>(row + ch * VEC);
-      uint4* yp = reinterpret_cast<uint4*>(row + half + ch * VEC);
-      uint4 x = *xp, y = *yp;
-      rotate_words<T>(x, y, s_cs, half, ch * VEC);
-      *xp = x;
-      *yp = y;
+    if (fixed_ch) {
+      for (int t = tid; t < ntask; t += kBulkThreads) {
+        T* row = reinterpret_cast<T*>(st) + (int64_t)(t / cph) * row_elems;
+        uint4* xp = reinterpret_cast<uint4*>(row + my_ch * VEC);
+        uint4* yp = reinterpret_cast<uint4*>(row + half + my_ch * VEC);
+        uint4 x = *xp, y = *yp;
+        rotate_words_reg<T>(x, y, my_c, my_s);
+        *xp = x;
+        *yp = y;
+      }
+    } else {
+      for (int t = tid; t < ntask; t += kBulkThreads) {
+        const int r = t / cph, ch = t - (t / cph) * cph;
+        T* row = reinterpret_cast<T*>(st) + (int64_t)r * row_elems;
+        uint4* xp = reinterpret_cast<uint4*>(row + ch * VEC);
+        uint4* yp = reinterpret_cast<uint4*>(row + half + ch * VEC);
+        uint4 x = *xp, y = *yp;
+        rotate_words<T>(x, y, s_cs, half, ch * VEC);
+        *xp = x;
+        *yp = y;
+      }
     }
     fence_proxy_async_smem();  // the rotated rows are read next by the bulk store (async proxy)
 
