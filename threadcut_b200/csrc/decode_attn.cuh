@@ -51,6 +51,7 @@ constexpr int kMaxSplits = 128;  // KV slices per (sequence, head)
 constexpr int kCtrWords = 4;
 constexpr int kMergeLoads = 8;   // partials one merger thread loads per L2 round trip
 constexpr int kLastSplitsPerWarp = 3;  // last-arrival merge: partials per warp (one round trip)
+constexpr int kMaxMergers = 16;        // start-ticket mergers per (sequence, head), column slices
 constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM of the tensor-core kernel
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
@@ -146,10 +147,17 @@ __host__ __device__ __forceinline__ bool last_arrival_merge(int nsplit, int nthr
 }
 
 // Takes this CTA's start ticket for (sequence b, head h) and returns its merger index: ticket -
-// (nsplit - min(g, nsplit)) for the last min(g, nsplit) tickets, -1 before them.
-__device__ __forceinline__ int merger_index(const DecodeParams& p, int b, int h, int nsplit) {
+// (nsplit - nm) for the last nm = merger_count() tickets, -1 before them.
+// Number of start-ticket mergers of a head: one per slice of the g*D/4 float4 output columns, at
+// most kMaxMergers and at most one per split.
+__device__ __forceinline__ int merger_count(int nsplit, int ncols) {
+  int nm = nsplit < kMaxMergers ? nsplit : kMaxMergers;
+  return nm < ncols ? nm : ncols;
+}
+
+__device__ __forceinline__ int merger_index(const DecodeParams& p, int b, int h, int nsplit, int ncols) {
   const unsigned int t = atomicAdd(p.counters + ((int64_t)b * p.hkv + h) * kCtrWords, 1u);
-  const int nm = p.g < nsplit ? p.g : nsplit;
+  const int nm = merger_count(nsplit, ncols);
   const int mi = (int)t - (nsplit - nm);
   return mi >= 0 ? mi : -1;
 }
@@ -254,16 +262,16 @@ __device__ void merge_last(const DecodeParams& p, uint8_t* scratch, int b, int h
 // round trip), lane l columns l, l+32, l+64, l+96, and the warps are combined in shared memory. It
 // clears the counter. No start ticket and no waiting.
 //
-// Many splits:
-// every CTA publishes its unnormalised partial and bumps the head's published counter with a
-// release. The CTAs that took the last nm = min(g, nsplit) START tickets are the
-// head's mergers (`mi` = ticket - (nsplit - nm), -1 for the others): every other CTA of the head
-// took its ticket earlier, so it is already running (or done) and publishes without waiting on
-// anything, and the mergers' bounded waits need no co-residency guarantee. Merger mi handles query
-// heads mi, mi + nm, ...: thread t folds float4 column t % Q (Q = D/4) of the splits
-// t / Q, t / Q + nsg, ... (nsg = blockDim.x / Q split groups), loading up to kMergeLoads of them
-// per L2 round trip, and the split groups are combined through shared memory. The last merger past
-// the wait clears the published count; the merger with the last ticket clears the ticket.
+// Many splits: every CTA publishes its unnormalised partial and bumps the head's published counter
+// with a release. The CTAs that took the last nm = merger_count() START tickets are the head's
+// mergers (`mi` = ticket - (nsplit - nm), -1 for the others): every other CTA of the head took its
+// ticket earlier, so it is already running (or done) and publishes without waiting on anything,
+// and the mergers' bounded waits need no co-residency guarantee. Merger mi owns the mi-th of nm
+// equal slices of the g*D/4 float4 output columns: thread t folds one column of the splits
+// t / w, t / w + nsg, ... (w = slice width, nsg = blockDim.x / w split groups), loading up to
+// kMergeLoads of them per L2 round trip, and the split groups are combined through shared memory.
+// The last merger past the wait clears the published count; the merger with the last ticket clears
+// the ticket.
 // Preconditions: every thread calls this after a __syncthreads() that follows the region writes;
 // the region area holds at least merge_scratch_bytes(blockDim.x) bytes.
 template <typename T, int D, int HP>
@@ -321,7 +329,9 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   if (mi < 0) return;
 
   // ---- merger mi: wait (bounded) until all nsplit partials are published
-  const int nm = g < nsplit ? g : nsplit;
+  constexpr int Q = D / 4;  // float4 columns per query head
+  const int ncols = g * Q;
+  const int nm = merger_count(nsplit, ncols);
   if (tid == 0) {
     int ok = 1;
     uint32_t spin = 0;
@@ -344,18 +354,22 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
   __syncthreads();  // also: the regions are free for the merge scratch
   if (!s_ok) return;
 
-  constexpr int Q = D / 4;  // float4 columns per query head
-  const int nsg = nthr / Q;  // split groups
-  const int sg = tid / Q, col = tid - (tid / Q) * Q;
-  float* sM = reinterpret_cast<float*>(regions);  // [nsg][Q] per-thread states
-  float* sL = sM + nsg * Q;
-  float4* sA = reinterpret_cast<float4*>(sL + nsg * Q);
-  for (int i = mi; i < g; i += nm) {
+  // this merger's float4 columns [c_lo, c_hi) of the g*Q, in chunks of at most nthr columns: thread
+  // t folds column t % w of the splits t / w, t / w + nsg, ... (nsg = nthr / w split groups)
+  const int c_lo = (int)((int64_t)ncols * mi / nm), c_hi = (int)((int64_t)ncols * (mi + 1) / nm);
+  const float2* mlb = p.ws_ml + bh * p.max_splits * g;
+  const float4* ob = reinterpret_cast<const float4*>(p.ws_o + bh * p.max_splits * g * D);
+  for (int cc = c_lo; cc < c_hi; cc += nthr) {
+    const int w = c_hi - cc < nthr ? c_hi - cc : nthr;
+    const int nsg = nthr / w;
+    const int sg = tid / w, col = cc + (tid - (tid / w) * w);
+    const int hd = col / Q;
+    float* sM = reinterpret_cast<float*>(regions);  // [nsg][w] per-thread states
+    float* sL = sM + nsg * w;
+    float4* sA = reinterpret_cast<float4*>(sL + nsg * w);
     float M = -INFINITY, L = 0.f;
     float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
     if (sg < nsg) {
-      const float2* mlb = p.ws_ml + bh * p.max_splits * g + i;
-      const float4* ob = reinterpret_cast<const float4*>(p.ws_o + (bh * p.max_splits * g + i) * D) + col;
       for (int s0 = sg; s0 < nsplit; s0 += nsg * kMergeLoads) {
         float2 ml[kMergeLoads];
         float4 x[kMergeLoads];
@@ -363,8 +377,8 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
         for (int k = 0; k < kMergeLoads; ++k) {
           const int s = s0 + k * nsg;
           const bool use = s < nsplit;
-          ml[k] = use ? __ldcg(mlb + (int64_t)s * g) : make_float2(-INFINITY, 0.f);
-          x[k] = use ? __ldcg(ob + (int64_t)s * g * Q) : make_float4(0.f, 0.f, 0.f, 0.f);
+          ml[k] = use ? __ldcg(mlb + (int64_t)s * g + hd) : make_float2(-INFINITY, 0.f);
+          x[k] = use ? __ldcg(ob + (int64_t)s * ncols + col) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         float mc = M;
 #pragma unroll
@@ -377,44 +391,45 @@ __device__ void finish_cta(const DecodeParams& p, uint8_t* regions, int region_s
         A.w *= a;
 #pragma unroll
         for (int k = 0; k < kMergeLoads; ++k) {
-          const float w = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - mc);
-          L += w * ml[k].y;
-          A.x += w * x[k].x;
-          A.y += w * x[k].y;
-          A.z += w * x[k].z;
-          A.w += w * x[k].w;
+          const float wk = ml[k].x == -INFINITY ? 0.f : fast_exp2(ml[k].x - mc);
+          L += wk * ml[k].y;
+          A.x += wk * x[k].x;
+          A.y += wk * x[k].y;
+          A.z += wk * x[k].z;
+          A.w += wk * x[k].w;
         }
         M = mc;
       }
-      sM[sg * Q + col] = M;
-      sL[sg * Q + col] = L;
-      sA[sg * Q + col] = A;
+      sM[sg * w + (col - cc)] = M;
+      sL[sg * w + (col - cc)] = L;
+      sA[sg * w + (col - cc)] = A;
     }
     __syncthreads();
-    if (tid < Q) {
+    if (tid < w) {
+      const int c = cc + tid, i = c / Q;
       float Mt = -INFINITY;
-      for (int w = 0; w < nsg; ++w) Mt = fmaxf(Mt, sM[w * Q + tid]);
+      for (int j = 0; j < nsg; ++j) Mt = fmaxf(Mt, sM[j * w + tid]);
       float Lt = 0.f;
       float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int w = 0; w < nsg; ++w) {
-        const float mw = sM[w * Q + tid];
+      for (int j = 0; j < nsg; ++j) {
+        const float mw = sM[j * w + tid];
         const float wt = mw == -INFINITY ? 0.f : fast_exp2(mw - Mt);
-        const float4 v = sA[w * Q + tid];
-        Lt += wt * sL[w * Q + tid];
+        const float4 v = sA[j * w + tid];
+        Lt += wt * sL[j * w + tid];
         At.x += wt * v.x;
         At.y += wt * v.y;
         At.z += wt * v.z;
         At.w += wt * v.w;
       }
       const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
-      const int64_t o = out0 + i * p.so_g + tid * 4;
+      const int64_t o = out0 + i * p.so_g + (c - i * Q) * 4;
       put_out<T>(p, o, At.x * inv);
       put_out<T>(p, o + 1, At.y * inv);
       put_out<T>(p, o + 2, At.z * inv);
       put_out<T>(p, o + 3, At.w * inv);
-      if (p.lse != nullptr && tid == 0) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(Mt, Lt);
+      if (p.lse != nullptr && c == i * Q) p.lse[b * p.lse_b + (int64_t)h * g + i] = lse_nat(Mt, Lt);
     }
-    __syncthreads();  // the scratch is rewritten by the next query head
+    __syncthreads();  // the scratch is rewritten by the next chunk
   }
 }
 
@@ -526,7 +541,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
     // the result is read only after the final __syncthreads
     if (lane == 1 && nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x))
-      s_mi = merger_index(p, b, h, nsplit);
+      s_mi = merger_index(p, b, h, nsplit, p.g * (D / 4));
     // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
     if (lane == 0 && ntiles > 0) {
       const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
@@ -773,7 +788,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) decode_generic_kernel(const __
   const int64_t t0 = tt0 * kTile;
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
   if (threadIdx.x == 0)
-    s_mi = nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x) ? merger_index(p, b, h, nsplit) : -1;
+    s_mi = nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x) ? merger_index(p, b, h, nsplit, p.g * (D / 4)) : -1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = p.g;
 
