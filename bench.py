@@ -253,6 +253,72 @@ def time_shift(steps, warmup, dev, dist, layers=LAYERS):
     return e0.elapsed_time(e1) / steps
 
 
+def time_sdpa_16k(qs, ks, vs, steps, warmup, dist):
+    """GPU comparator on the same box: the reference's own torch decode path (folded GQA SDPA,
+    threadcut/attention.py:41-42: q [1, hkv, g, d] against k/v [1, hkv, n, d]) over the same 36 layers,
+    replayed from a CUDA graph. Returns ms per 36-layer step."""
+    import torch.nn.functional as F
+    dev = qs[0].device
+    q4 = [q.unsqueeze(0) for q in qs]
+    k4 = [k.unsqueeze(0) for k in ks]
+    v4 = [v.unsqueeze(0) for v in vs]
+
+    def launch_all():
+        for q, k, v in zip(q4, k4, v4):
+            F.scaled_dot_product_attention(q, k, v, scale=workloads.SCALE)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    ms = time_graph(graph, steps, warmup, dist)
+    del graph
+    return ms
+
+
+def time_cfg4(steps, warmup, dev, dist, distinct=2):
+    """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
+    cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
+    cycling `distinct` layer caches (~2.3 GB each, far above L2), replayed from a CUDA graph. Returns
+    (ms per step, algorithmic bytes per launch)."""
+    from threadcut_b200.flash_decode import RaggedKV, decode_attention_ragged
+    lengths = workloads.cfg4_lengths()
+    g = torch.Generator(device=dev).manual_seed(44)
+    kvs = []
+    for _ in range(distinct):
+        ks = [torch.randn(8, n, 128, generator=g, device=dev).to(torch.bfloat16) for n in lengths]
+        vs = [torch.randn(8, n, 128, generator=g, device=dev).to(torch.bfloat16) for n in lengths]
+        kvs.append(RaggedKV(ks, vs, lengths))
+    q = torch.randn(len(lengths), 8, 4, 128, generator=g, device=dev).to(torch.bfloat16)
+
+    def launch_all():
+        for i in range(LAYERS):
+            decode_attention_ragged(q, kvs[i % distinct], workloads.SCALE)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        launch_all()  # warm-up on the capture stream (its workspace exists before capture)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    ms = time_graph(graph, steps, warmup, dist)
+    del graph, kvs
+    torch.cuda.empty_cache()
+    return ms, 4096 * sum(lengths) + len(lengths) * 16384
+
+
 def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
     """Strong scaling of one long sequence (config 5's 128k context, attention only): the 8 KV heads
     are sharded over the ranks (head_shard), each rank decodes its heads for all layers, no
@@ -333,6 +399,7 @@ def run_ours(args, rank, local, world, dist):
     achieved = BYTES_PER_LAYER / (us_layer_rank * 1e-6) / 1e9
     e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev)
     e2e_ms = max_over_ranks(e2e_ms, dist)
+    sdpa_ms = max_over_ranks(time_sdpa_16k(qs, ks, vs, args.steps, args.warmup, dist), dist)
     del graph
     # context-length sweep of config 3 (same kernel, 4k and 32k), and the RoPE-shift splice
     sweep = {}
@@ -348,6 +415,12 @@ def run_ours(args, rank, local, world, dist):
     torch.cuda.empty_cache()
     shift_ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist), dist)
     shift_gbs = SHIFT_BYTES_PER_LAYER * LAYERS / (shift_ms * 1e-3) / 1e9
+    c4_ms, c4_bytes = time_cfg4(args.steps, args.warmup, dev, dist)
+    c4_ms = max_over_ranks(c4_ms, dist)
+    cfg4 = {"us_per_layer": round(c4_ms * 1000 / LAYERS, 3),
+            "frac": round(c4_bytes / (c4_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4), "bytes_per_layer": c4_bytes,
+            "workload": "cfg4: 64 ragged sequences, lengths uniform in [1024,16384] (seeded), per-sequence bf16 "
+                        "K/V caches, 32 q / 8 kv heads, d 128, 36 launches per step over 2 distinct layer caches"}
     strong_ms = max_over_ranks(time_strong_128k(args.steps, args.warmup, dev, dist, rank, world), dist)
     strong = {"us_per_layer": round(strong_ms * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
               "kv_heads_per_rank": workloads.HKV // world,
@@ -388,6 +461,11 @@ def run_ours(args, rank, local, world, dist):
                   "workload": "cfg2 splice Split(2048,4096,4096) of an 8192-token bf16 cache, 36 layers in one "
                               "in-place launch; K rotated + V moved, read+write bytes"},
         "cfg3_sweep": sweep,
+        "cfg4_ragged": cfg4,
+        "gpu_comparators": {"torch_sdpa_folded_16k": {
+            "us_per_layer": round(sdpa_ms * 1000 / LAYERS, 3),
+            "frac": round(BYTES_PER_LAYER / (sdpa_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
+            "what": "the reference's own torch decode path (folded GQA SDPA) on the same 36 layers, same GPU"}},
         "strong_128k": strong,
     }
     if rank == 0:
