@@ -148,21 +148,25 @@ def build_layers(n, layers, dev, seed):
     return qs, ks, vs
 
 
-def capture_step(qs, ks, vs, outs, dev):
-    """CUDA graph of one step: the 36 decode launches through the C ABI with preallocated outputs."""
+def capture_step(qs, ks, vs, outs, dev, stable=True):
+    """CUDA graph of one step: the 36 decode launches through the C ABI with preallocated outputs.
+    stable: declare rows [0, n-1) stable (tc_decode_attention_stable), as a decode step may: every
+    row but the newest was written before the step; False runs plain tc_decode_attention."""
     from threadcut_b200._lib import TC_BF16, check, lib, workspaces
     L = lib()
     n = ks[0].shape[1]
     ws = workspaces.get(("decode", 8), dev, L.tc_decode_attention_workspace_size(1, 8, 4, 128, n, n, 0, TC_BF16))
 
+    stable_rows = n - 1 if stable else 0
+
     def launch_all():
         st = torch.cuda.current_stream(dev).cuda_stream
         for q, k, v, o in zip(qs, ks, vs, outs):
-            rc = L.tc_decode_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 4, 128, n,
-                                       q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-                                       o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16, ws.data_ptr(),
-                                       ws.numel(), st)
-            check("tc_decode_attention", rc)
+            rc = L.tc_decode_attention_stable(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 4, 128, n,
+                                              q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0),
+                                              v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16,
+                                              stable_rows, ws.data_ptr(), ws.numel(), st)
+            check("tc_decode_attention_stable", rc)
 
     launch_all()  # eager warm-up (also sets the kernels' shared-memory attributes)
     torch.cuda.synchronize()
@@ -198,9 +202,11 @@ def time_e2e(qs, ks, vs, steps, warmup, dist, dev):
     host_out = torch.empty_like(host_q).pin_memory()
     dq = torch.empty_like(host_q, device=dev)
 
+    n = ks[0].shape[1]
+
     def step():
         dq.copy_(host_q, non_blocking=True)
-        outs = [decode_attention(dq[i], ks[i], vs[i], workloads.SCALE) for i in range(len(ks))]
+        outs = [decode_attention(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1) for i in range(len(ks))]
         host_out.copy_(torch.stack(outs), non_blocking=True)
 
     for _ in range(warmup):
@@ -339,10 +345,10 @@ def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
     def launch_all():
         st = torch.cuda.current_stream(dev).cuda_stream
         for q, k, v, o in zip(qs, ks, vs, outs):
-            check("tc_decode_attention", L.tc_decode_attention(
+            check("tc_decode_attention_stable", L.tc_decode_attention_stable(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128, n, q.stride(0), q.stride(1),
                 k.stride(0), k.stride(1), v.stride(0), v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0,
-                TC_BF16, ws.data_ptr(), ws.numel(), st))
+                TC_BF16, n - 1, ws.data_ptr(), ws.numel(), st))
     launch_all()
     torch.cuda.synchronize()
     s = torch.cuda.Stream(device=dev)
@@ -397,6 +403,9 @@ def run_ours(args, rank, local, world, dist):
     us_layer_rank = ms * 1000.0 / LAYERS  # one rank's launch duration (incl. back-to-back gaps)
     value = ms * 1000.0 / (LAYERS * world)
     achieved = BYTES_PER_LAYER / (us_layer_rank * 1e-6) / 1e9
+    g_plain = capture_step(qs, ks, vs, outs, dev, stable=False)
+    plain_ms = max_over_ranks(time_graph(g_plain, args.steps, args.warmup, dist), dist)
+    del g_plain
     e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev)
     e2e_ms = max_over_ranks(e2e_ms, dist)
     sdpa_ms = max_over_ranks(time_sdpa_16k(qs, ks, vs, args.steps, args.warmup, dist), dist)
@@ -447,7 +456,9 @@ def run_ours(args, rank, local, world, dist):
         "config": {"workload": "cfg3-16k: 36-layer split-KV GQA decode, n=16384, 32 q / 8 kv heads, head_dim 128, "
                                "one K/V buffer per layer", "layers": LAYERS, "n": N_CTX, "batch": 1,
                    "l2": "inputs larger than L2 (36 distinct 67 MB layers = 2.4 GB per step)",
-                   "parallelism": f"weak: every rank decodes its own 36 layers ({world} rank(s))"},
+                   "parallelism": f"weak: every rank decodes its own 36 layers ({world} rank(s))",
+                   "stable_rows": "n-1: every row but the newest declared stable, as in a decode step "
+                                  "(tc_decode_attention_stable); see no_stable_rows for the plain entry point"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": "decode_mma_kernel<bf16,128,1>", "bytes_per_launch": BYTES_PER_LAYER},
@@ -462,6 +473,10 @@ def run_ours(args, rank, local, world, dist):
                               "in-place launch; K rotated + V moved, read+write bytes"},
         "cfg3_sweep": sweep,
         "cfg4_ragged": cfg4,
+        "no_stable_rows": {"us_per_layer": round(plain_ms * 1000.0 / LAYERS, 3),
+                           "frac": round(BYTES_PER_LAYER / (plain_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
+                           "what": "the same 36-layer step through plain tc_decode_attention (nothing declared "
+                                   "stable: K/V are read only after the preceding launch finished)"},
         "gpu_comparators": {"torch_sdpa_folded_16k": {
             "us_per_layer": round(sdpa_ms * 1000 / LAYERS, 3),
             "frac": round(BYTES_PER_LAYER / (sdpa_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),

@@ -86,6 +86,24 @@ int tc_decode_attention(const void* q, const void* k, const void* v, void* out,
                         float scale, int splits, int dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* tc_decode_attention plus a declaration that lets the kernel start reading K/V before the kernel
+ * ahead of it in the stream has finished: rows [0, stable_rows) of K and V (clamped to n) are
+ * written by no kernel that may still be running when this launch starts. The kernel is launched
+ * with programmatic dependent launch; when the kernel ahead of it is one of these decode kernels
+ * it lets this one start early, and this one then loads the stable rows of its first pipeline
+ * stages before waiting for that kernel to finish; q and every other input are read after the
+ * wait. In a decode step every row but the one just appended is stable (stable_rows = n - 1).
+ * stable_rows = 0 is tc_decode_attention exactly. (No counterpart in the reference: its decode
+ * reads the cache after the append has completed.) */
+int tc_decode_attention_stable(const void* q, const void* k, const void* v, void* out,
+                               int hkv, int g, int d, int64_t n,
+                               int64_t q_stride_h, int64_t q_stride_g,
+                               int64_t k_stride_h, int64_t k_stride_n,
+                               int64_t v_stride_h, int64_t v_stride_n,
+                               int64_t out_stride_h, int64_t out_stride_g,
+                               float scale, int splits, int dtype, int64_t stable_rows,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
  * example a plugin running inside another runtime that owns every device allocation and forbids
  * allocating in its execute hook, a loop where the implicit synchronisation of cudaMalloc is not

@@ -288,3 +288,27 @@ def test_plugin_decode_and_prefill_branches():
     refp = torch.nn.functional.scaled_dot_product_attention(
         qp.float(), kp.float().repeat_interleave(4, 1), kp.float().repeat_interleave(4, 1), is_causal=True)
     assert (outp.float() - refp.transpose(1, 2)).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("n", [31, 1536, 16384, 40000])
+def test_stable_rows_back_to_back_matches_plain(n):
+    """Layers decoded back to back with every row but the newest declared stable (the early-start
+    path: the stable tiles are loaded before the previous launch has finished) give bit-identical
+    results to the plain entry point, and out-of-range declarations are clamped or rejected."""
+    g = torch.Generator(device=DEV).manual_seed(n)
+    layers = 6
+    ks = [torch.randn(8, n, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(8, n, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(layers)]
+    qs = [torch.randn(8, 4, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(layers)]
+    plain = [decode_attention(q, k, v, 0.0883) for q, k, v in zip(qs, ks, vs)]
+    early = [decode_attention(q, k, v, 0.0883, stable_rows=n - 1) for q, k, v in zip(qs, ks, vs)]
+    over = [decode_attention(q, k, v, 0.0883, stable_rows=10 * n) for q, k, v in zip(qs, ks, vs)]
+    torch.cuda.synchronize()
+    for a, b, c in zip(plain, early, over):
+        assert torch.equal(a, b) and torch.equal(a, c)
+    ref = decode_attention_ref(qs[0].float().cpu().numpy(), ks[0].float().cpu().numpy(),
+                               vs[0].float().cpu().numpy(), 0.0883)
+    assert attn_error(early[0].float().cpu().numpy(), ref, torch.bfloat16) <= ATTN_ATOL
+    with pytest.raises(ValueError):
+        decode_attention(qs[0], ks[0], vs[0], 0.0883, stable_rows=-1)
+    assert _lib.device_errors(clear=True) == 0

@@ -82,6 +82,8 @@ struct DecodeParams {
   float2* ws_ml;        // [batch*hkv][max_splits][g]  (running max (log2 domain), sum)
   unsigned int* counters;  // [batch*hkv][kCtrWords] (zero between calls)
   int out_f32;             // 1: `out` is fp32 (unrounded partial for a cross-GPU merge), else T
+  int64_t stable_rows;     // uniform lengths only: rows [0, stable_rows) of K/V are written by no
+                           // kernel that can still be running when this one starts (0: none)
 };
 
 // Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
@@ -498,11 +500,15 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     }
     fence_mbar_init();
   }
+  __syncthreads();  // barriers initialised before the producer may arm them below
+  int staged = 0;   // producer lane: leading tiles already issued before pdl_wait()
   if (warp == kCWarps && lane == 0) {
-    // Before waiting for the previous kernel: warm L2 with the first pipeline-depth of this CTA's
-    // tiles. Only L2 prefetches (no shared memory, nothing consumed): a length read here may be
-    // stale and the rows may still be being written, and both are harmless; everything used for
-    // the result is read again after pdl_wait().
+    // Before waiting for the previous kernel (it may still be running):
+    //  * tiles whose rows the caller declared stable (p.stable_rows, uniform lengths, where n and
+    //    the partition come from kernel parameters) are loaded into the pipeline right away;
+    //  * the rest of the first pipeline-depth is only prefetched into L2: a length read here may
+    //    be stale and the rows may still be being written, both harmless for a prefetch.
+    // q, the workspace and everything else used for the result are read after pdl_wait().
     const CUtensorMap* mk = p.tm_ragged ? p.tm_ragged + 2 * b : &p.tmk;
     const CUtensorMap* mv = p.tm_ragged ? p.tm_ragged + 2 * b + 1 : &p.tmv;
     const int cb = p.tm_ragged ? 0 : b;
@@ -515,7 +521,22 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       int64_t a0, a1;
       split_range(tiles_hint, split, ns_hint, a0, a1);
       const int64_t pre = a1 - a0 < kStages ? a1 - a0 : kStages;
-      for (int64_t j = 0; j < pre; ++j)
+      if (p.lengths == nullptr && p.stable_rows > 0) {
+        const uint64_t pol = policy_evict_first();
+        while (staged < pre && (a0 + staged + 1) * kTile <= p.stable_rows) {
+          const int s = staged;  // round 0 of stage s: no empty wait
+          mbar_arrive_expect_tx(&full[s], (uint32_t)G::kStageBytes);
+          uint8_t* st = smem + s * G::kStageBytes;
+          const int tok = (int)((a0 + staged) * kTile);
+#pragma unroll
+          for (int bx = 0; bx < NBOX; ++bx) {
+            tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, h, cb, &full[s], pol);
+            tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, h, cb, &full[s], pol);
+          }
+          ++staged;
+        }
+      }
+      for (int64_t j = staged; j < pre; ++j)
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx) {
           tma_prefetch_4d(mk, bx * 64, (int)((a0 + j) * kTile), h, cb);
@@ -548,7 +569,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       const CUtensorMap* mv = p.tm_ragged ? p.tm_ragged + 2 * b + 1 : &p.tmv;
       const int cb = p.tm_ragged ? 0 : b;
       const uint64_t pol = policy_evict_first();
-      for (int j = 0; j < ntiles; ++j) {
+      for (int j = staged; j < ntiles; ++j) {
         const int s = j % kStages;
         const int r = j / kStages;
         if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;

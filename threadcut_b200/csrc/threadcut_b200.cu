@@ -420,9 +420,12 @@ namespace {
 int decode_single(const void* q, const void* k, const void* v, void* out, float* lse, bool out_f32, int hkv, int g,
                   int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h, int64_t k_stride_n,
                   int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g, float scale,
-                  int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                  int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream,
+                  int64_t stable_rows = 0) {
   if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
+  if (stable_rows < 0) return TC_ERR_INVALID;
   DecodeParams p = base_params();
+  p.stable_rows = stable_rows < n ? stable_rows : n;
   p.q = q;
   p.out = out;
   p.lse = lse;
@@ -448,6 +451,16 @@ int decode_single(const void* q, const void* k, const void* v, void* out, float*
                     static_cast<cudaStream_t>(stream));
 }
 }  // namespace
+
+int tc_decode_attention_stable(const void* q, const void* k, const void* v, void* out, int hkv, int g, int d,
+                               int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,
+                               int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                               int64_t out_stride_g, float scale, int splits, int dtype, int64_t stable_rows,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream, stable_rows);
+}
 
 int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,
                             int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h,

@@ -33,7 +33,7 @@ def _check_same_dtype(what, *ts):
             raise TypeError(f"threadcut_b200.{what}: dtype mismatch {ts[0].dtype} vs {t.dtype}")
 
 
-def _decode(q, k, v, scale, splits, want_lse, partial=False):
+def _decode(q, k, v, scale, splits, want_lse, partial=False, stable_rows=0):
     what = "decode_attention"
     dev = q.device
     if dev.type != "cuda" or k.device != dev or v.device != dev:
@@ -58,10 +58,16 @@ def _decode(q, k, v, scale, splits, want_lse, partial=False):
     s = int(splits or 0)
     stream = stream_ptr(dev)
     ws = workspaces.get(("decode", hkv), dev, _lib.decode_workspace_bound(1, hkv, g, d, code), stream)
-    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
-            hkv, g, d, n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-            out.stride(0), out.stride(1), float(scale), s, code, ws.data_ptr(), ws.numel(), stream)
-    fn = L.tc_decode_attention_partial if partial else L.tc_decode_attention_lse
+    if stable_rows and not want_lse:
+        args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), hkv, g, d, n, q.stride(0), q.stride(1),
+                k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(0), out.stride(1), float(scale), s,
+                code, int(stable_rows), ws.data_ptr(), ws.numel(), stream)
+        fn = L.tc_decode_attention_stable
+    else:
+        args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
+                hkv, g, d, n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+                out.stride(0), out.stride(1), float(scale), s, code, ws.data_ptr(), ws.numel(), stream)
+        fn = L.tc_decode_attention_partial if partial else L.tc_decode_attention_lse
     if torch.cuda.current_device() == dev.index:
         st = fn(*args)
     else:
@@ -72,12 +78,18 @@ def _decode(q, k, v, scale, splits, want_lse, partial=False):
     return (out, lse) if want_lse else out
 
 
-def decode_attention(q, k, v, scale, split=256, block=16, *, splits=None):
+def decode_attention(q, k, v, scale, split=256, block=16, *, splits=None, stable_rows=0):
     """q: [hkv, g, d]; k, v: [hkv, n, d] (last dim contiguous). Returns [hkv, g, d].
 
     `split` and `block` are accepted for call compatibility with the reference; the B200 kernel
-    plans its own partition. `splits` (keyword only) forces the number of KV slices per head."""
-    return _decode(q, k, v, scale, splits, False)
+    plans its own partition. `splits` (keyword only) forces the number of KV slices per head.
+    `stable_rows` (keyword only) declares that rows [0, stable_rows) of k and v are written by no
+    kernel still in flight on the GPU (e.g. n - 1 in a decode step whose append wrote only the last
+    row); the kernel may then load them before the preceding decode launch has finished. The
+    default 0 declares nothing."""
+    if stable_rows < 0:
+        raise ValueError("decode_attention: stable_rows must be >= 0")
+    return _decode(q, k, v, scale, splits, False, stable_rows=stable_rows)
 
 
 def decode_attention_lse(q, k, v, scale, *, splits=None):
