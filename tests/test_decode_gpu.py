@@ -312,3 +312,23 @@ def test_stable_rows_back_to_back_matches_plain(n):
     with pytest.raises(ValueError):
         decode_attention(qs[0], ks[0], vs[0], 0.0883, stable_rows=-1)
     assert _lib.device_errors(clear=True) == 0
+
+
+def test_host_binding_matches_the_ctypes_path():
+    """decode_attention goes through the compiled host binding; its result is bit-identical to the
+    ctypes path into the same library, and inputs it declines still raise from the checked path."""
+    from threadcut_b200 import flash_decode
+    assert _lib.host() is not None
+    gen = torch.Generator(device=DEV).manual_seed(12)
+    q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    k = torch.randn(8, 5000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    v = torch.randn(8, 5000, 128, generator=gen, device=DEV).to(torch.bfloat16)
+    fast = flash_decode._decode_fast(q, k, v, 0.0883, None, 0)
+    assert fast is not None
+    slow = flash_decode._decode(q, k, v, 0.0883, None, False)
+    assert torch.equal(fast, slow) and torch.equal(fast, decode_attention(q, k, v, 0.0883))
+    qs = q[:, :, ::2]  # non-contiguous last dim: declined by the binding, copied by the Python path
+    assert flash_decode._decode_fast(qs, k[..., :64], v[..., :64], 0.1, None, 0) is None
+    check_decode(qs, k[..., :64].contiguous(), v[..., :64].contiguous(), 0.1, torch.bfloat16)
+    with pytest.raises(ValueError):
+        decode_attention(q, k[:4], v, 0.1)

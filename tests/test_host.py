@@ -171,3 +171,26 @@ def test_workspace_epochs_are_unique_and_nonzero():
             seen.add(e)
     finally:
         _lib.stream_ptr = orig
+
+
+def test_host_binding_loads_without_a_gpu():
+    """The compiled host binding of decode_attention loads, is wired to the library's
+    tc_decode_attention_stable, and declines CPU tensors so the checked path raises as before."""
+    hb = _lib.host()
+    assert hb is not None, "threadcut_b200/_host/threadcut_b200_host.so is missing: run threadcut_b200.build"
+    assert callable(hb.decode) and callable(hb.init)
+    t = torch.zeros(8, 4, 128, dtype=torch.bfloat16)
+    assert hb.decode(t, t, t, 0.1, 0, 0, torch.zeros(16, dtype=torch.uint8)) is None
+
+
+def test_host_binding_first_use_in_a_fresh_process():
+    """The first decode call of a process loads the library and the binding in one go (no lock
+    taken twice): run it in a fresh interpreter with a deadline."""
+    import subprocess
+    import sys
+    code = ("import torch; from threadcut_b200 import _lib; from threadcut_b200.flash_decode import _decode_fast; "
+            "assert _lib.host() is not None; t = torch.zeros(2, 1, 64); "
+            "assert _decode_fast(t, t, t, 0.1, None, 0) is None; print('ok')")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr

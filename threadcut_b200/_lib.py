@@ -72,6 +72,30 @@ def lib():
     return _lib
 
 
+HOST_PATH = os.path.join(_HERE, "_host", "threadcut_b200_host.so")
+_host = None
+
+
+def host():
+    """The compiled host binding (csrc/host_binding.cpp) with its pointer to this package's loaded
+    tc_decode_attention_stable, or None when it has not been built (the ctypes path is used then).
+    It only moves the argument marshalling out of the interpreter; the kernels are the same."""
+    global _host
+    if _host is None:
+        handle = lib()  # outside the lock below: lib() takes it itself
+        with _lock:
+            if _host is None:
+                mod = False
+                if os.path.exists(HOST_PATH):
+                    import importlib.util
+                    spec = importlib.util.spec_from_file_location("threadcut_b200_host", HOST_PATH)
+                    mod = importlib.util.module_from_spec(spec)
+                    spec.loader.exec_module(mod)
+                    mod.init(ctypes.cast(handle.tc_decode_attention_stable, ctypes.c_void_p).value)
+                _host = mod
+    return _host or None
+
+
 class TCError(RuntimeError):
     def __init__(self, fn, status):
         msg = lib().tc_status_string(status).decode()

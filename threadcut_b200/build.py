@@ -52,5 +52,24 @@ def build(force=False, verbose=False):
     return OUT
 
 
+HOST_SRC = os.path.join(HERE, "csrc", "host_binding.cpp")
+HOST_DIR = os.path.join(HERE, "_host")
+HOST_NAME = "threadcut_b200_host"
+HOST_OUT = os.path.join(HOST_DIR, HOST_NAME + ".so")
+
+
+def build_host(force=False):
+    """Compile the host-only Python binding (csrc/host_binding.cpp, torch C++ API, no device code)
+    into threadcut_b200/_host/ with torch's extension builder. Returns the .so path."""
+    if not force and os.path.exists(HOST_OUT) and os.path.getmtime(HOST_OUT) >= os.path.getmtime(HOST_SRC):
+        return HOST_OUT
+    from torch.utils import cpp_extension
+    os.makedirs(HOST_DIR, exist_ok=True)
+    cpp_extension.load(name=HOST_NAME, sources=[HOST_SRC], build_directory=HOST_DIR, extra_cflags=["-O2"],
+                       with_cuda=True, verbose=False)
+    return HOST_OUT
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_host(force="--force" in sys.argv))

@@ -33,6 +33,23 @@ def _check_same_dtype(what, *ts):
             raise TypeError(f"threadcut_b200.{what}: dtype mismatch {ts[0].dtype} vs {t.dtype}")
 
 
+def _decode_fast(q, k, v, scale, splits, stable_rows):
+    """decode_attention through the compiled host binding (one crossing, checks in C++); None when
+    it is unavailable or declines the inputs, so that the checked Python path below runs."""
+    hb = _lib.host()
+    if hb is None:
+        return None
+    dev = q.device
+    if dev.type != "cuda":
+        return None
+    code = _lib.DTYPE_CODE.get(q.dtype)
+    if code is None or q.dim() != 3:
+        return None
+    hkv, g, d = q.shape
+    ws = workspaces.get(("decode", hkv), dev, _lib.decode_workspace_bound(1, hkv, g, d, code))
+    return hb.decode(q, k, v, float(scale), int(splits or 0), int(stable_rows), ws)
+
+
 def _decode(q, k, v, scale, splits, want_lse, partial=False, stable_rows=0):
     what = "decode_attention"
     dev = q.device
@@ -89,6 +106,9 @@ def decode_attention(q, k, v, scale, split=256, block=16, *, splits=None, stable
     default 0 declares nothing."""
     if stable_rows < 0:
         raise ValueError("decode_attention: stable_rows must be >= 0")
+    out = _decode_fast(q, k, v, scale, splits, stable_rows)
+    if out is not None:
+        return out
     return _decode(q, k, v, scale, splits, False, stable_rows=stable_rows)
 
 
