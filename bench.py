@@ -289,6 +289,46 @@ def time_sdpa_16k(qs, ks, vs, steps, warmup, dist):
     return ms
 
 
+def time_append_16k(qs, ks, vs, steps, warmup, dist):
+    """One decode step's append + attention per layer over the 36 16k layers (the cache views end at
+    the appended row), replayed from CUDA graphs two ways: fused (decode_attention_append: one
+    launch writes the row and attends) and the reference's order (two row copies, then decode).
+    Returns (fused ms, copy-then-decode ms) per 36-layer step."""
+    from threadcut_b200.flash_decode import decode_attention, decode_attention_append
+    dev = qs[0].device
+    n = ks[0].shape[1]
+    g = torch.Generator(device=dev).manual_seed(77)
+    kn = [torch.randn(8, 128, generator=g, device=dev).to(torch.bfloat16) for _ in ks]
+    vn = [torch.randn(8, 128, generator=g, device=dev).to(torch.bfloat16) for _ in ks]
+
+    def fused():
+        for q, k, v, a, b in zip(qs, ks, vs, kn, vn):
+            decode_attention_append(q, k, v, a, b, workloads.SCALE, stable_rows=n - 1)
+
+    def unfused():
+        for q, k, v, a, b in zip(qs, ks, vs, kn, vn):
+            k[:, n - 1] = a
+            v[:, n - 1] = b
+            decode_attention(q, k, v, workloads.SCALE, stable_rows=n - 1)
+
+    out = []
+    for fn in (fused, unfused):
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        out.append(time_graph(graph, steps, warmup, dist))
+        del graph
+    return out[0], out[1]
+
+
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
     """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
     cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
@@ -409,6 +449,8 @@ def run_ours(args, rank, local, world, dist):
     e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev)
     e2e_ms = max_over_ranks(e2e_ms, dist)
     sdpa_ms = max_over_ranks(time_sdpa_16k(qs, ks, vs, args.steps, args.warmup, dist), dist)
+    fused_ms, unfused_ms = time_append_16k(qs, ks, vs, args.steps, args.warmup, dist)
+    fused_ms, unfused_ms = max_over_ranks(fused_ms, dist), max_over_ranks(unfused_ms, dist)
     del graph
     # context-length sweep of config 3 (same kernel, 4k and 32k), and the RoPE-shift splice
     sweep = {}
@@ -473,6 +515,10 @@ def run_ours(args, rank, local, world, dist):
                               "in-place launch; K rotated + V moved, read+write bytes"},
         "cfg3_sweep": sweep,
         "cfg4_ragged": cfg4,
+        "append_16k": {"fused_us_per_layer": round(fused_ms * 1000.0 / LAYERS, 3),
+                       "copy_then_decode_us_per_layer": round(unfused_ms * 1000.0 / LAYERS, 3),
+                       "what": "a decode step's K/V append + attention per 16k layer: decode_attention_append "
+                               "(one launch) vs two row copies then decode_attention (the reference's order)"},
         "no_stable_rows": {"us_per_layer": round(plain_ms * 1000.0 / LAYERS, 3),
                            "frac": round(BYTES_PER_LAYER / (plain_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
                            "what": "the same 36-layer step through plain tc_decode_attention (nothing declared "

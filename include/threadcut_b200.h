@@ -104,6 +104,24 @@ int tc_decode_attention_stable(const void* q, const void* k, const void* v, void
                                float scale, int splits, int dtype, int64_t stable_rows,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* GrowingLayer.update of one token fused with the decode that follows it (threadcut/kv.py:64-77
+ * then flash_decode.py:57-69): k_new/v_new [hkv, d] (head strides k_new_stride_h/v_new_stride_h,
+ * last dim contiguous) are written as row n-1 of the cache views k/v [hkv, n, d], and `out` is
+ * attention of q over all n rows, rows [0, n-1) read from the cache and row n-1 from k_new/v_new.
+ * One launch with the tensor-core kernel (the CTA whose tile holds row n-1 patches it into its
+ * staged tile and stores it to the cache); otherwise two strided copies, then the decode. The
+ * cache rows [0, n-1) must not be written by the caller meanwhile; stable_rows as for
+ * tc_decode_attention_stable. (The reference appends with a separate copy before attention.) */
+int tc_decode_attention_append(const void* q, const void* k_new, const void* v_new, void* k, void* v, void* out,
+                               int hkv, int g, int d, int64_t n,
+                               int64_t q_stride_h, int64_t q_stride_g,
+                               int64_t k_new_stride_h, int64_t v_new_stride_h,
+                               int64_t k_stride_h, int64_t k_stride_n,
+                               int64_t v_stride_h, int64_t v_stride_n,
+                               int64_t out_stride_h, int64_t out_stride_g,
+                               float scale, int splits, int dtype, int64_t stable_rows,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
  * example a plugin running inside another runtime that owns every device allocation and forbids
  * allocating in its execute hook, a loop where the implicit synchronisation of cudaMalloc is not

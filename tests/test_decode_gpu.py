@@ -332,3 +332,73 @@ def test_host_binding_matches_the_ctypes_path():
     check_decode(qs, k[..., :64].contiguous(), v[..., :64].contiguous(), 0.1, torch.bfloat16)
     with pytest.raises(ValueError):
         decode_attention(q, k[:4], v, 0.1)
+
+
+@pytest.mark.parametrize("n,d,dtype", [(1, 128, torch.bfloat16), (32, 128, torch.bfloat16), (33, 128, torch.bfloat16),
+                                       (16384, 128, torch.bfloat16), (5000, 64, torch.float16),
+                                       (700, 256, torch.bfloat16), (100, 32, torch.bfloat16)])
+def test_fused_append_matches_copy_then_decode(n, d, dtype):
+    """tc_decode_attention_append writes the new row into the cache and attends over it in one
+    launch: the cache afterwards holds the row, and the output is bit-identical to copying the row
+    first and decoding (d = 32 takes the two-copies fallback)."""
+    from threadcut_b200.flash_decode import decode_attention_append
+    g = torch.Generator(device=DEV).manual_seed(n + d)
+    cap = n + 40
+    kb = torch.randn(8, cap, d, generator=g, device=DEV).to(dtype)
+    vb = torch.randn(8, cap, d, generator=g, device=DEV).to(dtype)
+    q = torch.randn(8, 4, d, generator=g, device=DEV).to(dtype)
+    kn = torch.randn(8, d, generator=g, device=DEV).to(dtype)
+    vn = torch.randn(8, d, generator=g, device=DEV).to(dtype)
+    kb2, vb2 = kb.clone(), vb.clone()
+    kb2[:, n - 1], vb2[:, n - 1] = kn, vn
+    want = decode_attention(q, kb2[:, :n], vb2[:, :n], 0.09)
+    for stable in (0, n - 1):
+        kb3, vb3 = kb.clone(), vb.clone()
+        got = decode_attention_append(q, kb3[:, :n], vb3[:, :n], kn, vn, 0.09, stable_rows=stable)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (n, d, stable)
+        assert torch.equal(kb3, kb2) and torch.equal(vb3, vb2)
+    assert _lib.device_errors(clear=True) == 0
+
+
+def test_growing_layer_fused_append_through_the_plugin():
+    """A GrowingLayer with fused append leaves the decode step's row pending; the plugin's decode
+    branch writes it in the fused launch; prefill and explicit reads flush it; results match a cache
+    that wrote every row eagerly."""
+    from threadcut_b200.attention import attention
+    from threadcut_b200.kv import GrowingLayer, pending_append
+    g = torch.Generator(device=DEV).manual_seed(21)
+    fused, eager = GrowingLayer(), GrowingLayer()
+    fused.fuse_append = True
+    k0 = torch.randn(1, 8, 500, 128, generator=g, device=DEV).to(torch.bfloat16)
+    v0 = torch.randn(1, 8, 500, 128, generator=g, device=DEV).to(torch.bfloat16)
+    for layer in (fused, eager):
+        layer.update(k0, v0)
+    for step in range(5):
+        q = torch.randn(1, 32, 1, 128, generator=g, device=DEV).to(torch.bfloat16)
+        kn = torch.randn(1, 8, 1, 128, generator=g, device=DEV).to(torch.bfloat16)
+        vn = torch.randn(1, 8, 1, 128, generator=g, device=DEV).to(torch.bfloat16)
+        kf, vf = fused.update(kn, vn)
+        ke, ve = eager.update(kn, vn)
+        assert pending_append(kf) is fused and pending_append(ke) is None
+        of, _ = attention(None, q, kf, vf, None)
+        oe, _ = attention(None, q, ke, ve, None)
+        assert pending_append(kf) is None
+        torch.cuda.synchronize()
+        assert torch.equal(of, oe), step
+        assert torch.equal(fused.keys, eager.keys) and torch.equal(fused.values, eager.values)
+    # a pending row is flushed by the next update, by crop and by a prefill-branch call
+    kn = torch.randn(1, 8, 1, 128, generator=g, device=DEV).to(torch.bfloat16)
+    kf, vf = fused.update(kn, kn)
+    eager.update(kn, kn)
+    fused.update(kn[:, :, :0], kn[:, :, :0])  # zero-token update: flushes, appends nothing
+    assert torch.equal(fused.keys, eager.keys)
+    kf, vf = fused.update(kn, kn)
+    ke, ve = eager.update(kn, kn)
+    qp = torch.randn(1, 32, 2, 128, generator=g, device=DEV).to(torch.bfloat16)
+    mask = torch.zeros(1, 1, 2, kf.shape[2], dtype=torch.bool, device=DEV)
+    mask[..., :] = True
+    op, _ = attention(None, qp, kf, vf, mask)
+    oq, _ = attention(None, qp, ke, ve, mask)
+    assert torch.equal(op, oq) and pending_append(kf) is None
+    assert _lib.device_errors(clear=True) == 0

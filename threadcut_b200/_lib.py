@@ -31,6 +31,8 @@ SIGNATURES = {
     "tc_decode_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8 + [_f, _i, _i, _vp]),
     "tc_decode_attention_stable": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                                    + [_f, _i, _i, _i64, _vp, _sz, _vp]),
+    "tc_decode_attention_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 10
+                                   + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_decode_attention_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                                     + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_decode_attention_lse": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8

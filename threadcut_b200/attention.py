@@ -8,7 +8,10 @@ dropout=0.0, scaling=None, **kw) -> (out[b,q,Hq,D] contiguous, None)`.
 Decode (one query token, no mask): the g = Hq/Hkv query heads of each KV head are folded into a
 g-row query (query.reshape(hkv, g, d), attention.py:39) and run by the B200 split-KV kernel over
 the unexpanded cache, b == 1 through decode_attention and b > 1 through decode_attention_batched
-(the reference used folded SDPA there). Decode on a non-CUDA tensor raises: there is no CPU path.
+(the reference used folded SDPA there). When the cache is a GrowingLayer whose newest row is still
+pending (fused append, set up by new_cache for this attention), that row is written by the same
+launch (decode_attention_append) instead of a separate copy before attention (kv.py:71-72).
+Decode on a non-CUDA tensor raises: there is no CPU path.
 Prefill (q > 1 or a mask) is outside the decode hot path and keeps the reference's branch:
 expand KV once and call torch SDPA (attention.py:43-46).
 """
@@ -16,9 +19,10 @@ import torch.nn.functional as F
 from transformers import AttentionInterface
 from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
 
-from .flash_decode import decode_attention, decode_attention_batched
+from .flash_decode import decode_attention, decode_attention_append, decode_attention_batched
+from .kv import FUSED_ATTENTION, pending_append
 
-NAME = "threadcut"
+NAME = FUSED_ATTENTION  # "threadcut", as threadcut/attention.py:22
 
 __all__ = ["NAME", "attention", "repeat_kv"]
 
@@ -36,6 +40,16 @@ def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=No
     hkv = key.shape[1]
     g = hq // hkv
     scaling = scaling if scaling is not None else d ** -0.5
+    layer = pending_append(key)
+    if q == 1 and attention_mask is None and b == 1 and layer is not None:
+        # the cache's newest row is still pending (GrowingLayer with fused append): write it and
+        # attend over the whole cache in one launch
+        k_new, v_new, stable = layer.take_pending()
+        out = decode_attention_append(query.reshape(hkv, g, d), key[0], value[0], k_new, v_new, scaling,
+                                      stable_rows=stable).reshape(1, hq, 1, d)
+        return out.transpose(1, 2).contiguous(), None
+    if layer is not None:
+        layer._flush()
     if q == 1 and attention_mask is None:
         if b == 1:
             out = decode_attention(query.reshape(hkv, g, d), key[0], value[0], scaling).reshape(1, hq, 1, d)

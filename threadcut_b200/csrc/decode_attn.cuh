@@ -84,6 +84,12 @@ struct DecodeParams {
   int out_f32;             // 1: `out` is fp32 (unrounded partial for a cross-GPU merge), else T
   int64_t stable_rows;     // uniform lengths only: rows [0, stable_rows) of K/V are written by no
                            // kernel that can still be running when this one starts (0: none)
+  // fused append (single sequence, tensor-core kernel): row n-1 of K/V is k_app/v_app ([hkv][d],
+  // head strides sa_k/sa_v); the CTA whose tile holds that row takes it from there and writes it to
+  // the cache. Null: no append.
+  const void* k_app;
+  const void* v_app;
+  int64_t sa_k, sa_v;
 };
 
 // Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
@@ -628,6 +634,27 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       const uint32_t vst = kst + G::kTileBytes;
       const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
       const int valid = rem < kTile ? (int)rem : kTile;
+      const int64_t app_r = p.k_app != nullptr ? (n - 1) - (t0 + (int64_t)j * kTile) : -1;
+      const bool patch = app_r >= 0 && app_r < kTile;
+      if (patch) {
+        // the appended row: the cache still holds stale data there, so replace the staged copy with
+        // k_app/v_app (16-byte chunks into the swizzled row) and write the row to the cache
+        const int r = (int)app_r;
+        constexpr int CH = D / 8;  // 16-byte chunks per row
+        const uint4* ka = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + h * p.sa_k);
+        const uint4* va = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_app) + h * p.sa_v);
+        uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + h * p.sk_h + (n - 1) * p.sk_n);
+        uint4* vc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + h * p.sv_h + (n - 1) * p.sv_n);
+        for (int idx = lane; idx < 2 * CH; idx += 32) {
+          const bool isv = idx >= CH;
+          const int c = isv ? idx - CH : idx;
+          const uint4 x = isv ? va[c] : ka[c];
+          *reinterpret_cast<uint4*>(stage + (isv ? G::kTileBytes : 0) + (c >> 3) * G::kBoxBytes + r * 128 +
+                                    (((c & 7) ^ (r & 7)) << 4)) = x;
+          (isv ? vc : kc)[c] = x;
+        }
+        __syncwarp();
+      }
       if (valid < kTile) {
         // rows past this slice may hold another sequence's or uninitialised data (ragged caches
         // are mapped to their capacity): zero those V rows so a masked p = 0 never meets a NaN
@@ -732,7 +759,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
           }
         }
       }
-      if (valid < kTile) fence_proxy_async_smem();  // the zeroing above precedes the next TMA write
+      if (valid < kTile || patch) fence_proxy_async_smem();  // generic writes above precede the next TMA write
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }

@@ -239,6 +239,17 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
               encode_kv_map(&p.tmv, p.v, dtype, d, max_n, p.hkv, p.batch, p.sv_n, p.sv_h, p.sv_b);
   }
   if (!use_mma && !gen_dim(d)) return mma_dim(d) ? TC_ERR_ALIGN : TC_ERR_INVALID;
+  if (p.k_app != nullptr && !use_mma) {
+    // fused append needs the tensor-core kernel: write the row with two strided copies, then decode
+    const size_t es = esize(dtype);
+    const int64_t row = max_n - 1;
+    if (cudaMemcpy2DAsync(const_cast<char*>(static_cast<const char*>(p.k)) + (p.sk_n * row) * es, p.sk_h * es,
+                          p.k_app, p.sa_k * es, d * es, p.hkv, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpy2DAsync(const_cast<char*>(static_cast<const char*>(p.v)) + (p.sv_n * row) * es, p.sv_h * es,
+                          p.v_app, p.sa_v * es, d * es, p.hkv, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return TC_ERR_CUDA;
+    p.k_app = p.v_app = nullptr;
+  }
   const int dev = current_device();
   const DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
                                     use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
@@ -421,11 +432,16 @@ int decode_single(const void* q, const void* k, const void* v, void* out, float*
                   int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h, int64_t k_stride_n,
                   int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g, float scale,
                   int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream,
-                  int64_t stable_rows = 0) {
+                  int64_t stable_rows = 0, const void* k_app = nullptr, const void* v_app = nullptr,
+                  int64_t sa_k = 0, int64_t sa_v = 0) {
   if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
   if (stable_rows < 0) return TC_ERR_INVALID;
   DecodeParams p = base_params();
   p.stable_rows = stable_rows < n ? stable_rows : n;
+  p.k_app = k_app;
+  p.v_app = v_app;
+  p.sa_k = sa_k;
+  p.sa_v = sa_v;
   p.q = q;
   p.out = out;
   p.lse = lse;
@@ -460,6 +476,35 @@ int tc_decode_attention_stable(const void* q, const void* k, const void* v, void
   return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
                        v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
                        workspace_bytes, stream, stable_rows);
+}
+
+int tc_decode_attention_append(const void* q, const void* k_new, const void* v_new, void* k, void* v, void* out,
+                               int hkv, int g, int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g,
+                               int64_t k_new_stride_h, int64_t v_new_stride_h, int64_t k_stride_h,
+                               int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                               int64_t out_stride_g, float scale, int splits, int dtype, int64_t stable_rows,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (n < 1 || k_new == nullptr || v_new == nullptr) return TC_ERR_INVALID;
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  // the appended row is copied as 16-byte chunks by the tensor-core kernel; a misaligned one makes
+  // the host fall back to strided copies (decided in run_decode through the K/V alignment)
+  const bool row_al = aligned16(k_new) && aligned16(v_new) && stride16(k_new_stride_h, dtype) &&
+                      stride16(v_new_stride_h, dtype);
+  if (!row_al) {
+    const size_t es = esize(dtype);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpy2DAsync(static_cast<char*>(k) + (k_stride_n * (n - 1)) * es, k_stride_h * es, k_new,
+                          k_new_stride_h * es, d * es, hkv, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+        cudaMemcpy2DAsync(static_cast<char*>(v) + (v_stride_n * (n - 1)) * es, v_stride_h * es, v_new,
+                          v_new_stride_h * es, d * es, hkv, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return TC_ERR_CUDA;
+    return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h,
+                         k_stride_n, v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype,
+                         workspace, workspace_bytes, stream, 0);
+  }
+  return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream, stable_rows, k_new, v_new, k_new_stride_h, v_new_stride_h);
 }
 
 int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,

@@ -19,7 +19,7 @@ import torch
 from . import _lib
 from ._lib import check, dtype_code, lib, require_cuda, stream_ptr, workspaces
 
-__all__ = ["decode_attention", "decode_attention_lse", "decode_attention_partial", "decode_attention_batched",
+__all__ = ["decode_attention", "decode_attention_append", "decode_attention_lse", "decode_attention_partial", "decode_attention_batched",
            "decode_attention_ragged", "merge_partials", "RaggedKV"]
 
 
@@ -110,6 +110,44 @@ def decode_attention(q, k, v, scale, split=256, block=16, *, splits=None, stable
     if out is not None:
         return out
     return _decode(q, k, v, scale, splits, False, stable_rows=stable_rows)
+
+
+def decode_attention_append(q, k, v, k_new, v_new, scale, *, splits=None, stable_rows=0):
+    """GrowingLayer.update of one token fused with decode_attention: writes k_new / v_new [hkv, d]
+    as the LAST row of the cache views k / v [hkv, n, d] and returns attention of q [hkv, g, d] over
+    all n rows ([hkv, g, d]) — one launch instead of two copies and a decode. The last row of k/v
+    is an output here: its previous contents are never read. stable_rows as for decode_attention."""
+    what = "decode_attention_append"
+    require_cuda(q, k, v, k_new, v_new, what=what)
+    _check_same_dtype(what, q, k, v, k_new, v_new)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3 or k_new.dim() != 2 or v_new.dim() != 2:
+        raise ValueError(f"{what}: expected q [hkv, g, d], k/v [hkv, n, d], k_new/v_new [hkv, d]")
+    hkv, g, d = q.shape
+    n = k.shape[1]
+    if (k.shape[0] != hkv or k.shape[2] != d or v.shape != k.shape or tuple(k_new.shape) != (hkv, d)
+            or tuple(v_new.shape) != (hkv, d) or n < 1):
+        raise ValueError(f"{what}: shapes q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}, "
+                         f"k_new {tuple(k_new.shape)}, v_new {tuple(v_new.shape)} do not fit")
+    if k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError(f"{what}: the cache views must have a contiguous last dimension (they are written)")
+    if stable_rows < 0:
+        raise ValueError(f"{what}: stable_rows must be >= 0")
+    q, k_new, v_new = _last_contig(q), _last_contig(k_new), _last_contig(v_new)
+    code = dtype_code(q, what)
+    dev = q.device
+    out = torch.empty((hkv, g, d), dtype=q.dtype, device=dev)
+    L = lib()
+    s = int(splits or 0)
+    stream = stream_ptr(dev)
+    ws = workspaces.get(("decode", hkv), dev, _lib.decode_workspace_bound(1, hkv, g, d, code), stream)
+    with torch.cuda.device(dev):
+        st = L.tc_decode_attention_append(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), hkv, g, d,
+            n, q.stride(0), q.stride(1), k_new.stride(0), v_new.stride(0), k.stride(0), k.stride(1), v.stride(0),
+            v.stride(1), out.stride(0), out.stride(1), float(scale), s, code, int(stable_rows), ws.data_ptr(),
+            ws.numel(), stream)
+    check(what, st)
+    return out
 
 
 def decode_attention_lse(q, k, v, scale, *, splits=None):

@@ -27,6 +27,11 @@ from .match import Split
 
 __all__ = ["rotate_half", "shift_keys", "splice", "GrowingLayer", "new_cache"]
 
+# attention implementation that consumes deferred appends (threadcut_b200.attention.NAME)
+FUSED_ATTENTION = "threadcut"
+# kbuf address -> GrowingLayer whose last appended row is not written yet (the fused decode writes it)
+_PENDING = {}
+
 
 def rotate_half(x):
     """(x1, x2) -> (-x2, x1) over the two halves of the last dim (torch; used by callers' RoPE)."""
@@ -142,11 +147,21 @@ def splice(cache, s: Split, inv_freq):
 class GrowingLayer(DynamicLayer):
     """DynamicLayer backed by a preallocated buffer: appending a token writes in place instead of
     re-copying the whole cache with torch.cat. Grows by max(need, 1.25x, +2048 tokens), the same
-    policy as threadcut/kv.py:53-63."""
+    policy as threadcut/kv.py:53-63.
+
+    Fused append (`fuse_append`, set by new_cache when the model's attention is threadcut_b200's):
+    a one-token update on a CUDA cache does not write the row; it returns the views with the row
+    pending, and the decode branch of threadcut_b200.attention writes it in the same launch that
+    reads the cache (tc_decode_attention_append). Any other use of the cache (another update,
+    crop, splice, a prefill or batched attention call) writes the pending row first."""
+
+    fuse_append = False
 
     def lazy_initialization(self, key_states, value_states, *args, **kwargs):
         super().lazy_initialization(key_states, value_states)
         self.n, self.kbuf, self.vbuf = 0, None, None
+        self._pending = None   # (k [hkv, d], v [hkv, d]) of row n-1, not yet in the buffers
+        self._plain_write = True  # the buffers were last written by a plain copy (not a fused decode)
 
     def _reserve(self, need, like):
         cap = 0 if self.kbuf is None else self.kbuf.shape[-2]
@@ -159,34 +174,87 @@ class GrowingLayer(DynamicLayer):
             kb[..., :self.n, :] = self.kbuf[..., :self.n, :]
             vb[..., :self.n, :] = self.vbuf[..., :self.n, :]
         self.kbuf, self.vbuf = kb, vb
+        self._plain_write = True
 
     def _view(self):
         self.keys, self.values = self.kbuf[..., :self.n, :], self.vbuf[..., :self.n, :]
 
+    def _flush(self):
+        """Write a pending appended row with plain copies (kv.py:71-72)."""
+        pend = getattr(self, "_pending", None)
+        if pend is not None:
+            k, v = pend
+            self._pending = None
+            _PENDING.pop(self.kbuf.data_ptr(), None)
+            self.kbuf[0, :, self.n - 1, :] = k
+            self.vbuf[0, :, self.n - 1, :] = v
+            self._plain_write = True
+
+    def take_pending(self):
+        """For the fused decode: (k_new, v_new, stable_rows) of the pending row, which the caller
+        must write (tc_decode_attention_append). stable_rows is n-1 unless a plain copy wrote the
+        buffers since the last fused decode (that copy may still be in flight), else 0."""
+        k, v = self._pending
+        self._pending = None
+        _PENDING.pop(self.kbuf.data_ptr(), None)
+        stable = 0 if self._plain_write else self.n - 1
+        self._plain_write = False
+        return k, v, stable
+
     def update(self, key_states, value_states, *args, **kwargs):
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
+        self._flush()
         add = key_states.shape[-2]
         self._reserve(self.n + add, key_states)
-        self.kbuf[..., self.n:self.n + add, :] = key_states
-        self.vbuf[..., self.n:self.n + add, :] = value_states
+        if (add == 1 and self.fuse_append and key_states.is_cuda and key_states.shape[0] == 1
+                and key_states.dtype in (torch.bfloat16, torch.float16)):
+            self._pending = (key_states[0, :, 0, :], value_states[0, :, 0, :])
+            _PENDING[self.kbuf.data_ptr()] = self
+        else:
+            self.kbuf[..., self.n:self.n + add, :] = key_states
+            self.vbuf[..., self.n:self.n + add, :] = value_states
+            self._plain_write = True
         self.n += add
         self._view()
         return self.keys, self.values
 
     def crop(self, max_length):
+        self._flush()
         self.n = min(self.n, max_length)
         self._view()
 
     def splice(self, s: Split, inv_freq):
         """In-place A.B.C -> A.C: only C is touched, O(|C|) bytes, one kernel launch."""
+        self._flush()
         if s.c and s.gap:
             _splice_growing([self], s, inv_freq)
+            self._plain_write = True
         self.n = s.a + s.c
         self._view()
+
+
+def pending_append(key):
+    """The GrowingLayer whose keys view `key` ([1, hkv, n, d]) has its last row pending, or None."""
+    if not _PENDING or not key.is_cuda:
+        return None
+    layer = _PENDING.get(key.data_ptr())
+    if layer is None or layer._pending is None or key.shape[-2] != layer.n or key.dim() != 4:
+        return None
+    return layer
+
+
+def flush_pending(key):
+    """Write the pending row behind `key`, if any (for readers other than the fused decode)."""
+    layer = pending_append(key)
+    if layer is not None:
+        layer._flush()
 
 
 def new_cache(config):
     cache = DynamicCache(config=config)
     cache.layers = [GrowingLayer() for _ in cache.layers]
+    if getattr(config, "_attn_implementation", None) == FUSED_ATTENTION:
+        for layer in cache.layers:
+            layer.fuse_append = True  # the decode branch of threadcut_b200.attention writes the row
     return cache
