@@ -329,6 +329,34 @@ def time_append_16k(qs, ks, vs, steps, warmup, dist):
     return out[0], out[1]
 
 
+def time_split_128k(dev, reps=20):
+    """split() of a config-5-like request (128k cached tokens, a 32k span pruned mid-context, a
+    300-token fresh tail) on the device (tokens already on the GPU, result read back) and with the
+    host rule on Python lists (the reference's path). Returns (device us, host us)."""
+    import time
+    import numpy as np
+    from threadcut_b200.match import split, split_device
+    rng = np.random.default_rng(0)
+    cached = rng.integers(0, 151936, workloads.CFG5_CTX)
+    new = np.concatenate([cached[:49152], cached[81920:], rng.integers(0, 151936, 300)])
+    cd = torch.as_tensor(cached, device=dev, dtype=torch.int32)
+    nd = torch.as_tensor(new, device=dev, dtype=torch.int32)
+    want = split(cached.tolist(), new.tolist())
+    for _ in range(3):
+        assert split_device(cd, nd) == want
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        split_device(cd, nd)
+    dev_us = (time.perf_counter() - t) / reps * 1e6
+    cl, nl = cached.tolist(), new.tolist()
+    t = time.perf_counter()
+    for _ in range(3):
+        split(cl, nl)
+    host_us = (time.perf_counter() - t) / 3 * 1e6
+    return dev_us, host_us
+
+
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
     """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
     cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
@@ -472,6 +500,7 @@ def run_ours(args, rank, local, world, dist):
             "frac": round(c4_bytes / (c4_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4), "bytes_per_layer": c4_bytes,
             "workload": "cfg4: 64 ragged sequences, lengths uniform in [1024,16384] (seeded), per-sequence bf16 "
                         "K/V caches, 32 q / 8 kv heads, d 128, 36 launches per step over 2 distinct layer caches"}
+    split_dev_us, split_host_us = time_split_128k(dev)
     strong_ms = max_over_ranks(time_strong_128k(args.steps, args.warmup, dev, dist, rank, world), dist)
     strong = {"us_per_layer": round(strong_ms * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
               "kv_heads_per_rank": workloads.HKV // world,
@@ -519,6 +548,9 @@ def run_ours(args, rank, local, world, dist):
                        "copy_then_decode_us_per_layer": round(unfused_ms * 1000.0 / LAYERS, 3),
                        "what": "a decode step's K/V append + attention per 16k layer: decode_attention_append "
                                "(one launch) vs two row copies then decode_attention (the reference's order)"},
+        "split_128k": {"device_us": round(split_dev_us, 1), "host_numpy_us": round(split_host_us, 1),
+                       "what": "match.split of a 128k cached / 97k new request: tc_split (tokens on the GPU, "
+                               "result read back, wall clock) vs the host rule on Python lists"},
         "no_stable_rows": {"us_per_layer": round(plain_ms * 1000.0 / LAYERS, 3),
                            "frac": round(BYTES_PER_LAYER / (plain_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
                            "what": "the same 36-layer step through plain tc_decode_attention (nothing declared "

@@ -122,6 +122,16 @@ int tc_decode_attention_append(const void* q, const void* k_new, const void* v_n
                                float scale, int splits, int dtype, int64_t stable_rows,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* split(cached, new, min_suffix, suffix) of threadcut/match.py:33-48 on the device: token ids as
+ * int32 device arrays (n_new >= 1). Writes (a, c0, c) of the resulting Split as three int64 to the
+ * device pointer out3; identical to the host rule, ties included (the first start with the longest
+ * match). Workspace: tc_split_workspace_size(n_cached) bytes, 8-byte aligned, no initial contents.
+ * (No counterpart in the reference: it splits on the host with numpy.) */
+size_t tc_split_workspace_size(int64_t n_cached);
+int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens, int64_t n_new,
+             int min_suffix, int suffix, int64_t* out3, void* workspace, size_t workspace_bytes,
+             void* stream);
+
 /* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
  * example a plugin running inside another runtime that owns every device allocation and forbids
  * allocating in its execute hook, a loop where the implicit synchronisation of cudaMalloc is not

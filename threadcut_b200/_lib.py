@@ -42,6 +42,8 @@ SIGNATURES = {
     "tc_decode_attention_ragged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64, _i64]
                                    + [_i64] * 6 + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_ragged_tensormaps_size": (_sz, [_i]),
+    "tc_split_workspace_size": (_sz, [_i64]),
+    "tc_split": (_i, [_vp, _i64, _vp, _i64, _i, _i, _vp, _vp, _sz, _vp]),
     "tc_ragged_encode_tensormaps": (_i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_i64),
                                          ctypes.POINTER(_i64), _i64, _i, _i, _i, _i]),
     "tc_shift_keys": (_i, [_vp, _vp, _i64, _i64, _i] + [_i64] * 4 + [_fp, _i, _vp]),

@@ -10,6 +10,7 @@
 
 #include "decode_attn.cuh"
 #include "rope_splice.cuh"
+#include "split.cuh"
 
 using namespace tc;
 
@@ -793,6 +794,40 @@ int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, voi
   return tc_decode_attention(q, k, v, out, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n, v_stride_h,
                              v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, scratch,
                              kNoAllocScratchBytes, stream);
+}
+
+size_t tc_split_workspace_size(int64_t n_cached) {
+  if (n_cached < 0) return 0;
+  return sizeof(SplitWs) + sizeof(int64_t) * (size_t)(n_cached > 0 ? n_cached : 1);
+}
+
+int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens, int64_t n_new, int min_suffix,
+             int suffix, int64_t* out3, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_new < 1 || n_cached < 0 || n_cached >= (int64_t)0xffffffffLL || min_suffix < 1 || out3 == nullptr ||
+      new_tokens == nullptr || (n_cached > 0 && cached == nullptr))
+    return TC_ERR_INVALID;
+  if (workspace == nullptr || workspace_bytes < tc_split_workspace_size(n_cached) ||
+      reinterpret_cast<uintptr_t>(workspace) % 8 != 0)
+    return TC_ERR_WORKSPACE;
+  SplitParams p;
+  p.cached = cached;
+  p.fresh = new_tokens;
+  p.n_cached = n_cached;
+  p.n_new = n_new;
+  p.min_suffix = min_suffix;
+  p.suffix = suffix ? 1 : 0;
+  p.cap = n_cached > 0 ? n_cached : 1;
+  p.ws = static_cast<SplitWs*>(workspace);
+  p.out = out3;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = sm_count(current_device());
+  const int64_t m = n_cached < n_new ? n_cached : n_new;
+  split_init_kernel<<<1, 32, 0, st>>>(p);
+  split_lcp_kernel<<<grid_for(m > 0 ? m : 1, kSplitThreads, sms, 8), kSplitThreads, 0, st>>>(p);
+  split_window_kernel<<<grid_for(n_cached > 0 ? n_cached : 1, kSplitThreads, sms, 8), kSplitThreads, 0, st>>>(p);
+  split_extend_kernel<<<sms * 2, kExtendThreads, 0, st>>>(p);
+  split_finish_kernel<<<1, 32, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
 }  // extern "C"

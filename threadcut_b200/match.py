@@ -12,7 +12,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-__all__ = ["Split", "lcp", "split"]
+__all__ = ["Split", "lcp", "split", "split_device"]
 
 
 @dataclass(frozen=True)
@@ -63,3 +63,39 @@ def split(cached, new, min_suffix=32, suffix=True):
         if c > best.c:
             best = Split(a, j, c)
     return best
+
+
+def split_device(cached, new, min_suffix=32, suffix=True, device=None):
+    """split() computed on the GPU (tc_split): same rule and tie-breaking, integer-exact. `cached`
+    and `new` are token-id sequences (lists, numpy arrays or int tensors; ids must fit int32);
+    host sequences are copied to `device` (default: the current CUDA device). Returns a Split
+    (reading it back synchronises the stream). `new` must be non-empty."""
+    import torch
+
+    from ._lib import check, lib, stream_ptr, workspaces
+
+    if len(new) == 0:
+        raise ValueError("split_device: `new` must hold at least one token")
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.type != "cuda":
+        raise RuntimeError("split_device: needs a CUDA device (the host rule is split())")
+
+    def as_dev(x):
+        if isinstance(x, torch.Tensor) and x.dtype == torch.int32:
+            return x.to(device=dev).contiguous()
+        t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x, dtype=np.int64))
+        if t.numel() and (int(t.max()) > 2**31 - 1 or int(t.min()) < -2**31):
+            raise ValueError("split_device: token ids must fit int32")
+        return t.to(device=dev, dtype=torch.int32).contiguous()
+
+    c, n = as_dev(cached), as_dev(new)
+    L = lib()
+    ws = workspaces.get(("split",), dev, L.tc_split_workspace_size(c.numel()))
+    out = torch.empty(3, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        check("tc_split", L.tc_split(c.data_ptr() if c.numel() else None, c.numel(), n.data_ptr(), n.numel(),
+                                     int(min_suffix), 1 if suffix else 0, out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     stream_ptr(dev)))
+    a, c0, cl = out.tolist()
+    return Split(int(a), int(c0), int(cl))
+
