@@ -19,6 +19,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 
@@ -64,8 +65,10 @@ class ClockSampler:
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.join(HERE, "gpurun_out"), exist_ok=True)
-            self.path = os.path.join(HERE, "gpurun_out", f"clocks_gpu{self.index}.csv")
+            # raw samples go to BENCH_CLOCKS_DIR when set (kept for inspection), else a temp folder
+            out_dir = os.environ.get("BENCH_CLOCKS_DIR") or tempfile.mkdtemp(prefix="bench_clocks_")
+            os.makedirs(out_dir, exist_ok=True)
+            self.path = os.path.join(out_dir, f"clocks_gpu{self.index}.csv")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
