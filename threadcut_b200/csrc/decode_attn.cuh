@@ -25,13 +25,16 @@
 //     spare, the point is to take the per-token FMA/shuffle work off the issue slots so the CTA
 //     stays a pure HBM stream.
 //   * epilogue: the warps' (m, l, o) are combined in shared memory; with one split the CTA writes
-//     the output, otherwise it publishes an unnormalised partial to the workspace (red.release on
-//     the head's counter). The CTAs that took the head's last min(g, splits) start tickets are its
-//     mergers: each waits for all partials and merges one query head's columns by log-sum-exp,
-//     every thread folding one column of a share of the splits in a single L2 round trip
-//     (see finish_cta).
-//   * launched with programmatic dependent launch: the prologue overlaps the previous kernel's
-//     tail, and nothing the previous kernel may write is read before griddepcontrol.wait.
+//     the output, otherwise it publishes an unnormalised partial to the workspace. Heads with few
+//     splits (<= 3 per warp) are merged by the CTA that arrives last on the head's acq_rel count;
+//     heads with more splits by up to 16 CTAs chosen by start ticket, each owning a slice of the
+//     output columns, after a bounded wait on the head's release count (see finish_cta).
+//   * launched with programmatic dependent launch: the prologue (barrier init, tensor-map and L2
+//     prefetches, and the TMA loads of rows the caller declared stable) overlaps the previous
+//     kernel's tail; q, lengths, the workspace and everything else that kernel may write are read
+//     after griddepcontrol.wait.
+//   * fused append (k_app/v_app): the consumer whose tile holds row n-1 patches that row into the
+//     staged tile from k_app/v_app and stores it to the cache.
 // fp32, d < 64, or K/V whose strides break the 16-byte TMA rule use decode_generic_kernel: the same
 // partition and epilogue with plain loads and FMA math.
 #pragma once
