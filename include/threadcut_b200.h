@@ -132,6 +132,20 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
              int min_suffix, int suffix, int64_t* out3, void* workspace, size_t workspace_bytes,
              void* stream);
 
+/* GQA prefill attention on the tcgen05 tensor cores (threadcut/attention.py:43-46 without the
+ * repeat_kv expansion): q [hq, lq, d] (strides q_stride_h, q_stride_p), k/v [hkv, lk, d], out
+ * [lq, hq, d] (strides out_stride_p, out_stride_h); query position p attends to keys
+ * [0, lk - lq + p] (a prefill of lq new tokens over an lk-token cache that ends with them).
+ * bf16/f16, d = 128, hq = 4*hkv, 1 <= lq <= lk; 16-byte aligned bases and strides. Other shapes
+ * return TC_ERR_INVALID / TC_ERR_ALIGN. */
+int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
+                         int hq, int hkv, int lq, int lk, int d,
+                         int64_t q_stride_h, int64_t q_stride_p,
+                         int64_t k_stride_h, int64_t k_stride_n,
+                         int64_t v_stride_h, int64_t v_stride_n,
+                         int64_t out_stride_p, int64_t out_stride_h,
+                         float scale, int dtype, void* stream);
+
 /* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
  * example a plugin running inside another runtime that owns every device allocation and forbids
  * allocating in its execute hook, a loop where the implicit synchronisation of cudaMalloc is not

@@ -1,0 +1,54 @@
+"""tcgen05 GQA prefill attention against the fp32 SDPA math with the causal-offset mask (needs a
+B200). P enters the second MMA in 16 bits (as in flash attention), so the bar is 1e-2."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from threadcut_b200 import _lib
+from threadcut_b200.prefill import causal_offset_mask, prefill_attention
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def reference(q, k, v, scale):
+    hq, hkv = q.shape[1], k.shape[1]
+    lq, lk = q.shape[2], k.shape[2]
+    kk = k.float().repeat_interleave(hq // hkv, 1)
+    vv = v.float().repeat_interleave(hq // hkv, 1)
+    mask = causal_offset_mask(lq, lk, q.device)
+    return F.scaled_dot_product_attention(q.float(), kk, vv, attn_mask=mask, scale=scale).transpose(1, 2)
+
+
+@pytest.mark.parametrize("lq,lk", [(1, 1), (5, 5), (1, 300), (32, 32), (33, 100), (128, 128), (129, 700),
+                                   (300, 1000), (512, 4096), (100, 5000)])
+@pytest.mark.parametrize("hkv", [8, 2])
+def test_prefill_matches_sdpa(lq, lk, hkv):
+    g = torch.Generator(device=DEV).manual_seed(lq * 7 + lk + hkv)
+    q = torch.randn(1, 4 * hkv, lq, 128, generator=g, device=DEV).to(torch.bfloat16)
+    k = torch.randn(1, hkv, lk, 128, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(1, hkv, lk, 128, generator=g, device=DEV).to(torch.bfloat16)
+    out = prefill_attention(q, k, v, 0.0883)
+    torch.cuda.synchronize()
+    ref = reference(q, k, v, 0.0883)
+    err = (out.float() - ref).abs().max().item()
+    assert out.shape == (1, lq, 4 * hkv, 128) and err <= 1e-2, (lq, lk, hkv, err)
+    assert _lib.device_errors(clear=True) == 0
+
+
+def test_prefill_fp16_strided_and_peaked():
+    g = torch.Generator(device=DEV).manual_seed(3)
+    # HF layout: query [1, hq, lq, d] as a transposed view of [1, lq, hq, d]
+    q = torch.randn(1, 200, 32, 128, generator=g, device=DEV).to(torch.float16).transpose(1, 2)
+    kb = torch.randn(1, 8, 1000, 128, generator=g, device=DEV).to(torch.float16)
+    k, v = kb[:, :, :900], kb[:, :, 100:]  # cache views with a head stride larger than the length
+    out = prefill_attention(q, k, v, 0.5)  # large scale: peaked softmax, exercises the O rescale
+    ref = reference(q, k, v, 0.5)
+    assert (out.float() - ref).abs().max().item() <= 1e-2
+    assert _lib.device_errors(clear=True) == 0
+
+
+def test_prefill_rejects_unsupported_shapes():
+    q = torch.randn(1, 32, 4, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        prefill_attention(q, q[:, :8], q[:, :8], 0.1)

@@ -12,8 +12,8 @@ the unexpanded cache, b == 1 through decode_attention and b > 1 through decode_a
 pending (fused append, set up by new_cache for this attention), that row is written by the same
 launch (decode_attention_append) instead of a separate copy before attention (kv.py:71-72).
 Decode on a non-CUDA tensor raises: there is no CPU path.
-Prefill (q > 1 or a mask) is outside the decode hot path and keeps the reference's branch:
-expand KV once and call torch SDPA (attention.py:43-46).
+Prefill (q > 1 or a mask) is outside the decode hot path and keeps the reference's torch SDPA
+branch (attention.py:43-46), with SDPA's GQA mode instead of an explicit repeat_kv expansion.
 """
 import torch.nn.functional as F
 from transformers import AttentionInterface
@@ -56,9 +56,11 @@ def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=No
         else:
             out = decode_attention_batched(query.reshape(b, hkv, g, d), key, value, scaling).reshape(b, hq, 1, d)
     else:
+        # the reference expands K/V with repeat_kv first (attention.py:43-46); SDPA's own GQA mode
+        # computes the same attention without materialising the expansion (4x the cache per layer)
         is_causal = attention_mask is None and q > 1 and q == key.shape[2]
-        out = F.scaled_dot_product_attention(query, repeat_kv(key, g), repeat_kv(value, g),
-                                             attn_mask=attention_mask, scale=scaling, is_causal=is_causal)
+        out = F.scaled_dot_product_attention(query, key, value, attn_mask=attention_mask, scale=scaling,
+                                             is_causal=is_causal, enable_gqa=g > 1)
     return out.transpose(1, 2).contiguous(), None
 
 

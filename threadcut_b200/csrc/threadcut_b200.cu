@@ -11,6 +11,7 @@
 #include "decode_attn.cuh"
 #include "rope_splice.cuh"
 #include "split.cuh"
+#include "prefill_attn.cuh"
 
 using namespace tc;
 
@@ -95,6 +96,21 @@ bool encode_kv_map(CUtensorMap* m, const void* base, int dtype, int d, int64_t r
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// 4-D 16-bit tensor map (128-byte swizzle, zero fill): dims innermost first, strides in elements of
+// dims 1..3, box in elements.
+bool encode_map4(CUtensorMap* m, const void* base, int dtype, const int64_t (&dims)[4], const int64_t (&strides)[3],
+                 const uint32_t (&box)[4]) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (fn == nullptr || base == nullptr) return false;
+  const cuuint64_t gd[4] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2], (cuuint64_t)dims[3]};
+  const cuuint64_t gs[3] = {(cuuint64_t)strides[0] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[2] * 2};
+  const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, dtype == TC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+            const_cast<void*>(base), gd, gs, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // ------------------------------------------------------------------------------- decode planning
@@ -827,6 +843,52 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
   split_window_kernel<<<grid_for(n_cached > 0 ? n_cached : 1, kSplitThreads, sms, 8), kSplitThreads, 0, st>>>(p);
   split_extend_kernel<<<sms * 2, kExtendThreads, 0, st>>>(p);
   split_finish_kernel<<<1, 32, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_prefill_attention(const void* q, const void* k, const void* v, void* out, int hq, int hkv, int lq, int lk,
+                         int d, int64_t q_stride_h, int64_t q_stride_p, int64_t k_stride_h, int64_t k_stride_n,
+                         int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_p, int64_t out_stride_h,
+                         float scale, int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (d != 128 || hkv < 1 || hkv > 65535 || hq != kPfGroup * hkv || lq < 1 || lk < lq || q == nullptr ||
+      k == nullptr || v == nullptr || out == nullptr)
+    return TC_ERR_INVALID;
+  if (!(scale == scale) || scale == INFINITY || scale == -INFINITY) return TC_ERR_INVALID;
+  const int64_t st[8] = {q_stride_h, q_stride_p, k_stride_h, k_stride_n, v_stride_h, v_stride_n, out_stride_p,
+                         out_stride_h};
+  for (int64_t x : st)
+    if (!stride16(x, dtype)) return TC_ERR_ALIGN;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return TC_ERR_ALIGN;
+  PrefillParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int64_t qd[4] = {128, lq, hq, 1}, qs[3] = {q_stride_p, q_stride_h, q_stride_h * hq};
+  const int64_t kd[4] = {128, lk, hkv, 1}, ks[3] = {k_stride_n, k_stride_h, k_stride_h * hkv};
+  const int64_t vs[3] = {v_stride_n, v_stride_h, v_stride_h * hkv};
+  const uint32_t qbox[4] = {64, (uint32_t)kPfQ, (uint32_t)kPfGroup, 1}, kbox[4] = {64, (uint32_t)kPfKeys, 1, 1};
+  if (!encode_map4(&p.tmq, q, dtype, qd, qs, qbox) || !encode_map4(&p.tmk, k, dtype, kd, ks, kbox) ||
+      !encode_map4(&p.tmv, v, dtype, kd, vs, kbox))
+    return TC_ERR_INVALID;
+  p.out = out;
+  p.so_p = out_stride_p;
+  p.so_h = out_stride_h;
+  p.lq = lq;
+  p.lk = lk;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.c = scale * kLog2e;
+  const int dev = current_device();
+  const dim3 grid((unsigned)((lq + kPfQ - 1) / kPfQ), (unsigned)hkv);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dtype == TC_BF16) {
+    e = set_smem(reinterpret_cast<const void*>(prefill_kernel<__nv_bfloat16>), kPfSmem, dev);
+    if (e == cudaSuccess) prefill_kernel<__nv_bfloat16><<<grid, kPfThreads, kPfSmem, s>>>(p);
+  } else {
+    e = set_smem(reinterpret_cast<const void*>(prefill_kernel<__half>), kPfSmem, dev);
+    if (e == cudaSuccess) prefill_kernel<__half><<<grid, kPfThreads, kPfSmem, s>>>(p);
+  }
+  if (e != cudaSuccess) return TC_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
