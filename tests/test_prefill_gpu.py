@@ -52,3 +52,27 @@ def test_prefill_rejects_unsupported_shapes():
     q = torch.randn(1, 32, 4, 64, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         prefill_attention(q, q[:, :8], q[:, :8], 0.1)
+
+
+def test_plugin_prefill_branch_uses_the_kernel_for_causal_masks():
+    """The plugin's prefill branch: the HF causal-over-cache mask and the plain causal case (no mask,
+    lq == lk) take the tcgen05 kernel; any other mask keeps SDPA; both agree with the reference."""
+    from threadcut_b200 import attention as plug
+    g = torch.Generator(device=DEV).manual_seed(9)
+    q = torch.randn(1, 32, 64, 128, generator=g, device=DEV).to(torch.bfloat16)
+    k = torch.randn(1, 8, 640, 128, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(1, 8, 640, 128, generator=g, device=DEV).to(torch.bfloat16)
+    mask = causal_offset_mask(64, 640, q.device)[None, None]
+    assert plug._is_causal_offset(mask, 64, 640) and plug._is_causal_offset(mask, 64, 640)  # second: cached
+    out, _ = plug.attention(None, q, k, v, mask, scaling=0.0883)
+    assert torch.equal(out, prefill_attention(q, k, v, 0.0883))
+    assert (out.float() - reference(q, k, v, 0.0883)).abs().max().item() <= 1e-2
+    other = mask.clone()
+    other[..., 0] = False  # not the causal-offset pattern: SDPA path
+    assert not plug._is_causal_offset(other, 64, 640)
+    out2, _ = plug.attention(None, q, k, v, other, scaling=0.0883)
+    assert out2.shape == out.shape
+    qc = q[:, :, :, :]
+    kc, vc = k[:, :, :64], v[:, :, :64]
+    out3, _ = plug.attention(None, qc, kc, vc, None, scaling=0.0883)  # plain causal, lq == lk
+    assert (out3.float() - reference(qc, kc, vc, 0.0883)).abs().max().item() <= 1e-2

@@ -12,15 +12,21 @@ the unexpanded cache, b == 1 through decode_attention and b > 1 through decode_a
 pending (fused append, set up by new_cache for this attention), that row is written by the same
 launch (decode_attention_append) instead of a separate copy before attention (kv.py:71-72).
 Decode on a non-CUDA tensor raises: there is no CPU path.
-Prefill (q > 1 or a mask) is outside the decode hot path and keeps the reference's torch SDPA
+Prefill (q > 1 or a mask): a causal prefill over the cache (query p sees keys up to lk - lq + p;
+b == 1, 4 query heads per KV head, head_dim 128, 16-bit) runs the tcgen05 kernel of
+threadcut_b200.prefill over the unexpanded cache; anything else keeps the reference's torch SDPA
 branch (attention.py:43-46), with SDPA's GQA mode instead of an explicit repeat_kv expansion.
 """
+import weakref
+
+import torch
 import torch.nn.functional as F
 from transformers import AttentionInterface
 from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
 
 from .flash_decode import decode_attention, decode_attention_append, decode_attention_batched
 from .kv import FUSED_ATTENTION, pending_append
+from . import prefill as _prefill
 
 NAME = FUSED_ATTENTION  # "threadcut", as threadcut/attention.py:22
 
@@ -33,6 +39,26 @@ def repeat_kv(x, n):
         return x
     b, h, s, d = x.shape
     return x.unsqueeze(2).expand(b, h, n, s, d).reshape(b, h * n, s, d)
+
+
+_mask_seen = {}  # the last mask tensor found to be the causal-offset mask (weak reference) + version
+
+
+def _is_causal_offset(mask, lq, lk):
+    """True when `mask` means query p sees keys [0, lk - lq + p]: None with lq == lk (HF drops the
+    mask of a plain causal prefill), or the boolean [1, 1, lq, lk] mask HF builds for a prefill over
+    a cache. The comparison runs once per mask tensor (HF passes one mask to every layer)."""
+    if mask is None:
+        return lq == lk
+    if mask.dtype != torch.bool or tuple(mask.shape) != (1, 1, lq, lk):
+        return False
+    hit = _mask_seen.get("last")
+    if hit is not None and hit[0]() is mask and hit[1] == mask._version:
+        return True
+    ok = bool(torch.equal(mask[0, 0], _prefill.causal_offset_mask(lq, lk, mask.device)))
+    if ok:
+        _mask_seen["last"] = (weakref.ref(mask), mask._version)
+    return ok
 
 
 def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, **kwargs):
@@ -55,6 +81,9 @@ def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=No
             out = decode_attention(query.reshape(hkv, g, d), key[0], value[0], scaling).reshape(1, hq, 1, d)
         else:
             out = decode_attention_batched(query.reshape(b, hkv, g, d), key, value, scaling).reshape(b, hq, 1, d)
+    elif _prefill.supported(query, key, value) and _is_causal_offset(attention_mask, q, key.shape[2]):
+        # causal prefill over the cache (the engine's D chunk): tcgen05 kernel, K/V never expanded
+        return _prefill.prefill_attention(query, key, value, scaling), None
     else:
         # the reference expands K/V with repeat_kv first (attention.py:43-46); SDPA's own GQA mode
         # computes the same attention without materialising the expansion (4x the cache per layer)
