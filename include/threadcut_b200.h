@@ -137,14 +137,20 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
  * [lq, hq, d] (strides out_stride_p, out_stride_h); query position p attends to keys
  * [0, lk - lq + p] (a prefill of lq new tokens over an lk-token cache that ends with them).
  * bf16/f16, d = 128, hq = 4*hkv, 1 <= lq <= lk; 16-byte aligned bases and strides. Other shapes
- * return TC_ERR_INVALID / TC_ERR_ALIGN. */
+ * return TC_ERR_INVALID / TC_ERR_ALIGN. splits = 0 picks the number of KV splits from the SM count
+ * (tc_prefill_splits); with more than one, fp32 partials are merged by log-sum-exp (out must then be
+ * contiguous [lq, hq, d], else one split is used) in `workspace` of tc_prefill_workspace_size()
+ * bytes (no initial contents). */
+int tc_prefill_splits(int hkv, int lq, int lk);
+size_t tc_prefill_workspace_size(int hq, int hkv, int lq, int lk, int splits);
 int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
                          int hq, int hkv, int lq, int lk, int d,
                          int64_t q_stride_h, int64_t q_stride_p,
                          int64_t k_stride_h, int64_t k_stride_n,
                          int64_t v_stride_h, int64_t v_stride_n,
                          int64_t out_stride_p, int64_t out_stride_h,
-                         float scale, int dtype, void* stream);
+                         float scale, int splits, int dtype,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Decode attention that allocates nothing, for callers that cannot hand us device memory: for
  * example a plugin running inside another runtime that owns every device allocation and forbids

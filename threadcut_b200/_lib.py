@@ -42,7 +42,10 @@ SIGNATURES = {
     "tc_decode_attention_ragged": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _i64, _i64]
                                    + [_i64] * 6 + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_ragged_tensormaps_size": (_sz, [_i]),
-    "tc_prefill_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i] + [_i64] * 8 + [_f, _i, _vp]),
+    "tc_prefill_splits": (_i, [_i, _i, _i]),
+    "tc_prefill_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "tc_prefill_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i] + [_i64] * 8
+                             + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_split_workspace_size": (_sz, [_i64]),
     "tc_split": (_i, [_vp, _i64, _vp, _i64, _i, _i, _vp, _vp, _sz, _vp]),
     "tc_ragged_encode_tensormaps": (_i, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_i64),

@@ -846,13 +846,50 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
   return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
+// KV splits of the prefill kernel: 1 when (query blocks x KV heads) already fill two waves of SMs,
+// else the smallest count (<= 16, >= 2 tiles per split) that keeps the last wave at least 85 % full.
+int prefill_splits(int hkv, int lq, int lk, int sms) {
+  const int64_t base = (int64_t)((lq + kPfQ - 1) / kPfQ) * hkv;
+  if (base >= 2 * (int64_t)sms) return 1;
+  const int64_t tiles = ((int64_t)lk + kPfKeys - 1) / kPfKeys;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 16 && tiles / s >= 2; ++s) {
+    const int64_t ctas = base * s;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const double eff = (double)ctas / (double)(waves * sms);
+    if (ctas >= sms && eff >= 0.85) return s;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+size_t prefill_ws_bytes(int hq, int lq, int splits) {
+  if (splits <= 1) return 0;
+  return sizeof(float) * (size_t)splits * (size_t)lq * (size_t)hq * (128 + 1);
+}
+
+int tc_prefill_splits(int hkv, int lq, int lk) {
+  if (hkv < 1 || lq < 1 || lk < lq) return 0;
+  return prefill_splits(hkv, lq, lk, sm_count(current_device()));
+}
+
+size_t tc_prefill_workspace_size(int hq, int hkv, int lq, int lk, int splits) {
+  if (hkv < 1 || lq < 1 || lk < lq) return 0;
+  const int s = splits > 0 ? (splits > 16 ? 16 : splits) : prefill_splits(hkv, lq, lk, sm_count(current_device()));
+  return prefill_ws_bytes(hq, lq, s);
+}
+
 int tc_prefill_attention(const void* q, const void* k, const void* v, void* out, int hq, int hkv, int lq, int lk,
                          int d, int64_t q_stride_h, int64_t q_stride_p, int64_t k_stride_h, int64_t k_stride_n,
                          int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_p, int64_t out_stride_h,
-                         float scale, int dtype, void* stream) {
+                         float scale, int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
   if (d != 128 || hkv < 1 || hkv > 65535 || hq != kPfGroup * hkv || lq < 1 || lk < lq || q == nullptr ||
-      k == nullptr || v == nullptr || out == nullptr)
+      k == nullptr || v == nullptr || out == nullptr || splits < 0)
     return TC_ERR_INVALID;
   if (!(scale == scale) || scale == INFINITY || scale == -INFINITY) return TC_ERR_INVALID;
   const int64_t st[8] = {q_stride_h, q_stride_p, k_stride_h, k_stride_n, v_stride_h, v_stride_n, out_stride_p,
@@ -860,6 +897,12 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
   for (int64_t x : st)
     if (!stride16(x, dtype)) return TC_ERR_ALIGN;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return TC_ERR_ALIGN;
+  const int dev = current_device();
+  int ns = splits > 0 ? (splits > 16 ? 16 : splits) : prefill_splits(hkv, lq, lk, sm_count(dev));
+  // split partials are merged into rows of d contiguous elements: needs the [lq, hq, d] layout
+  if (ns > 1 && !(out_stride_h == 128 && out_stride_p == (int64_t)hq * 128)) ns = 1;
+  const size_t need = prefill_ws_bytes(hq, lq, ns);
+  if (ns > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return TC_ERR_WORKSPACE;
   PrefillParams p;
   std::memset(&p, 0, sizeof(p));
   const int64_t qd[4] = {128, lq, hq, 1}, qs[3] = {q_stride_p, q_stride_h, q_stride_h * hq};
@@ -877,8 +920,13 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
   p.hq = hq;
   p.hkv = hkv;
   p.c = scale * kLog2e;
-  const int dev = current_device();
-  const dim3 grid((unsigned)((lq + kPfQ - 1) / kPfQ), (unsigned)hkv);
+  p.nsplit = ns;
+  const int64_t rows = (int64_t)lq * hq;
+  if (ns > 1) {
+    p.o_part = static_cast<float*>(workspace);
+    p.lse_part = p.o_part + (size_t)ns * rows * 128;
+  }
+  const dim3 grid((unsigned)((lq + kPfQ - 1) / kPfQ), (unsigned)hkv, (unsigned)ns);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (dtype == TC_BF16) {
@@ -888,8 +936,9 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
     e = set_smem(reinterpret_cast<const void*>(prefill_kernel<__half>), kPfSmem, dev);
     if (e == cudaSuccess) prefill_kernel<__half><<<grid, kPfThreads, kPfSmem, s>>>(p);
   }
-  if (e != cudaSuccess) return TC_ERR_CUDA;
-  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  if (e != cudaSuccess || cudaGetLastError() != cudaSuccess) return TC_ERR_CUDA;
+  if (ns > 1) return tc_merge_partials(p.o_part, p.lse_part, out, nullptr, ns, rows, 128, 128, dtype, stream);
+  return TC_OK;
 }
 
 }  // extern "C"

@@ -10,7 +10,7 @@ whether the kernel takes the inputs; the plugin keeps torch SDPA for everything 
 import torch
 
 from . import _lib
-from ._lib import check, lib, require_cuda, stream_ptr
+from ._lib import check, lib, require_cuda, stream_ptr, workspaces
 
 __all__ = ["prefill_attention", "supported", "causal_offset_mask"]
 
@@ -30,7 +30,7 @@ def causal_offset_mask(lq, lk, device):
     return j <= (lk - lq) + p
 
 
-def prefill_attention(query, key, value, scale):
+def prefill_attention(query, key, value, scale, *, splits=None):
     what = "prefill_attention"
     require_cuda(query, key, value, what=what)
     if not supported(query, key, value):
@@ -46,10 +46,14 @@ def prefill_attention(query, key, value, scale):
     if v.stride(-1) != 1:
         v = v.contiguous()
     out = torch.empty((1, lq, hq, d), dtype=query.dtype, device=query.device)
+    L = lib()
+    s = int(splits or 0)
     with torch.cuda.device(query.device):
-        st = lib().tc_prefill_attention(
+        nb = L.tc_prefill_workspace_size(hq, hkv, lq, lk, s)
+        ws = workspaces.get("prefill", query.device, nb) if nb else None
+        st = L.tc_prefill_attention(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), hq, hkv, lq, lk, d, q.stride(0), q.stride(1),
-            k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(1), out.stride(2), float(scale),
-            _lib.DTYPE_CODE[query.dtype], stream_ptr(query.device))
+            k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(1), out.stride(2), float(scale), s,
+            _lib.DTYPE_CODE[query.dtype], ws.data_ptr() if ws is not None else None, nb, stream_ptr(query.device))
     check(what, st)
     return out
