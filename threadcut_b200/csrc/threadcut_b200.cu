@@ -846,20 +846,21 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
   return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
-// KV splits of the prefill kernel: 1 when (query blocks x KV heads) already fill two waves of SMs,
-// else the smallest count (<= 16, >= 2 tiles per split) that keeps the last wave at least 85 % full.
+// KV splits of the prefill kernel (one CTA per SM): none when (query blocks x KV heads) already make
+// two waves; else the smallest count (<= 16, >= 8 tiles per split) whose CTAs fill their waves of
+// SMs at least 95 %, else the count with the fullest waves.
 int prefill_splits(int hkv, int lq, int lk, int sms) {
   const int64_t base = (int64_t)((lq + kPfQ - 1) / kPfQ) * hkv;
   if (base >= 2 * (int64_t)sms) return 1;
   const int64_t tiles = ((int64_t)lk + kPfKeys - 1) / kPfKeys;
   int best = 1;
   double best_eff = 0.0;
-  for (int s = 1; s <= 16 && tiles / s >= 2; ++s) {
+  for (int s = 1; s <= 16 && (s == 1 || tiles / s >= 8); ++s) {
     const int64_t ctas = base * s;
     const int64_t waves = (ctas + sms - 1) / sms;
     const double eff = (double)ctas / (double)(waves * sms);
-    if (ctas >= sms && eff >= 0.85) return s;
-    if (eff > best_eff + 1e-9) {
+    if (eff >= 0.95) return s;
+    if (eff > best_eff + 0.02) {
       best_eff = eff;
       best = s;
     }
