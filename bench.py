@@ -360,6 +360,49 @@ def time_split_128k(dev, reps=20):
     return dev_us, host_us
 
 
+def bf16_peak():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def time_prefill(steps, warmup, dev, lq=512, lk=98304):
+    """The engine's prefill after a splice (config-5-like: a 512-token chunk over a 98k-token cache,
+    32 q / 8 kv heads, d 128): the tcgen05 GQA prefill kernel, SDPA's GQA mode, and the reference's
+    own path (repeat_kv + SDPA with the explicit mask, threadcut/attention.py:43-46). Returns ms of
+    each and the useful FLOPs (visible query-key pairs only)."""
+    import torch.nn.functional as F
+    from threadcut_b200.attention import repeat_kv
+    from threadcut_b200.prefill import causal_offset_mask, prefill_attention
+    g = torch.Generator(device=dev).manual_seed(88)
+    q = torch.randn(1, 32, lq, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, 8, lk, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, 8, lk, 128, generator=g, device=dev).to(torch.bfloat16)
+    mask = causal_offset_mask(lq, lk, dev)[None, None]
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ours = timed(lambda: prefill_attention(q, k, v, workloads.SCALE))
+    gqa = timed(lambda: F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=workloads.SCALE,
+                                                       enable_gqa=True))
+    ref = timed(lambda: F.scaled_dot_product_attention(q, repeat_kv(k, 4), repeat_kv(v, 4), attn_mask=mask,
+                                                       scale=workloads.SCALE))
+    pairs = lq * (lk - lq) + lq * (lq + 1) // 2
+    return ours, gqa, ref, 4.0 * 32 * pairs * 128
+
+
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
     """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
     cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
@@ -504,6 +547,8 @@ def run_ours(args, rank, local, world, dist):
             "workload": "cfg4: 64 ragged sequences, lengths uniform in [1024,16384] (seeded), per-sequence bf16 "
                         "K/V caches, 32 q / 8 kv heads, d 128, 36 launches per step over 2 distinct layer caches"}
     split_dev_us, split_host_us = time_split_128k(dev)
+    pf_ms, pf_gqa_ms, pf_ref_ms, pf_flops = time_prefill(min(args.steps, 10), args.warmup, dev)
+    tc_peak, tc_peak_kind = bf16_peak()
     strong_ms = max_over_ranks(time_strong_128k(args.steps, args.warmup, dev, dist, rank, world), dist)
     strong = {"us_per_layer": round(strong_ms * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
               "kv_heads_per_rank": workloads.HKV // world,
@@ -551,6 +596,14 @@ def run_ours(args, rank, local, world, dist):
                        "copy_then_decode_us_per_layer": round(unfused_ms * 1000.0 / LAYERS, 3),
                        "what": "a decode step's K/V append + attention per 16k layer: decode_attention_append "
                                "(one launch) vs two row copies then decode_attention (the reference's order)"},
+        "prefill_512x98k": {
+            "tcgen05_ms": round(pf_ms, 4), "sdpa_gqa_ms": round(pf_gqa_ms, 4), "reference_path_ms": round(pf_ref_ms, 4),
+            "tflops": round(pf_flops / (pf_ms * 1e-3) / 1e12, 1),
+            "roofline": {"bound": "tensor", "achieved": round(pf_flops / (pf_ms * 1e-3) / 1e12, 1), "peak": tc_peak,
+                         "unit": "TFLOP/s", "frac": round(pf_flops / (pf_ms * 1e-3) / 1e12 / tc_peak, 4),
+                         "peak_kind": tc_peak_kind},
+            "what": "prefill of a 512-token chunk over a 98,304-token cache (32 q / 8 kv heads, d 128, causal with "
+                    "the cache offset): tc_prefill_attention vs SDPA GQA mode vs the reference's repeat_kv + SDPA"},
         "split_128k": {"device_us": round(split_dev_us, 1), "host_numpy_us": round(split_host_us, 1),
                        "what": "match.split of a 128k cached / 97k new request: tc_split (tokens on the GPU, "
                                "result read back, wall clock) vs the host rule on Python lists"},
