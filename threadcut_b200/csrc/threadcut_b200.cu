@@ -850,7 +850,7 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
 // two waves; else the smallest count (<= 16, >= 8 tiles per split) whose CTAs fill their waves of
 // SMs at least 95 %, else the count with the fullest waves.
 int prefill_splits(int hkv, int lq, int lk, int sms) {
-  const int64_t base = (int64_t)((lq + kPfQ - 1) / kPfQ) * hkv;
+  const int64_t base = (int64_t)((lq + kPfQ * kPfTiles - 1) / (kPfQ * kPfTiles)) * hkv;
   if (base >= 2 * (int64_t)sms) return 1;
   const int64_t tiles = ((int64_t)lk + kPfKeys - 1) / kPfKeys;
   int best = 1;
@@ -927,7 +927,7 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
     p.o_part = static_cast<float*>(workspace);
     p.lse_part = p.o_part + (size_t)ns * rows * 128;
   }
-  const dim3 grid((unsigned)((lq + kPfQ - 1) / kPfQ), (unsigned)hkv, (unsigned)ns);
+  const dim3 grid((unsigned)((lq + kPfQ * kPfTiles - 1) / (kPfQ * kPfTiles)), (unsigned)hkv, (unsigned)ns);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (dtype == TC_BF16) {
