@@ -81,7 +81,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  // heaviest causal Q blocks first (blocks are dispatched in blockIdx.x order): longest-first
+  // scheduling shortens the tail when the grid is more than one wave
+  const int qb = gridDim.x - 1 - blockIdx.x, h = blockIdx.y, split = blockIdx.z;
   const int p0 = qb * kPfQ * kPfTiles;  // first position of Q tile 0; tile x starts at p0 + 32x
   const int off = p.lk - p.lq;          // key j is visible to position pos iff j <= off + pos
   const int kend = p.lk < off + p0 + kPfQ * kPfTiles ? p.lk : off + p0 + kPfQ * kPfTiles;
@@ -217,40 +219,51 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
       for (int cch = 0; cch < 4; ++cch) tmem_ld32(tS + lb + cch * 32, v[cch]);
       tmem_wait_ld();
-      // scores in the exp2 domain, masked past this row's last visible key
+      // raw scores, masked (-inf) past this row's last visible key; row max over 8 partial chains
       const int ja = t_lo + j;
       const bool masked_tile = (ja + 1) * kPfKeys - 1 > limit_min;
-      float mt = -INFINITY;
+      float mx[8];
 #pragma unroll
-      for (int cch = 0; cch < 4; ++cch)
+      for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
+      if (masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float xv = __uint_as_float(v[cch][e]) * p.c;
-          if (masked_tile && ja * kPfKeys + cch * 32 + e > limit) xv = -INFINITY;
-          v[cch][e] = __float_as_uint(xv);
-          mt = fmaxf(mt, xv);
-        }
+        for (int cch = 0; cch < 4; ++cch)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (ja * kPfKeys + cch * 32 + e > limit) v[cch][e] = __float_as_uint(-INFINITY);
+            mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[cch][e]));
+          }
+      } else {
+#pragma unroll
+        for (int cch = 0; cch < 4; ++cch)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[cch][e]));
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.c;  // exp2 domain (c > 0)
       // lazy max: keep m unless this tile's max passes it by more than kPfLazyMax
       const bool bump = mt > m + kPfLazyMax;
       const float mn = bump ? mt : m;
       const float alpha = !bump ? 1.f : (m == -INFINITY ? 0.f : fast_exp2(m - mn));
       const float mref = mn == -INFINITY ? 0.f : mn;  // no visible key yet (a later KV split): p = 0
-      float rs = 0.f;
-      // P over the first 64 columns of this tile's S (all of S is in registers already), one half of
-      // the keys at a time so the scores and the packed words are not live together
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = 2^(s c - mref) over the first 64 columns of this tile's S (all of S is in registers
+      // already), one half of the keys at a time so the scores and the packed words are not live
+      // together.
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t w[32];  // 16-bit pairs: keys 2e, 2e+1 of this half
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int cch = half * 2 + (e >> 4), k2 = 2 * (e & 15);
-          const float a = fast_exp2(__uint_as_float(v[cch][k2]) - mref);
-          const float bb = fast_exp2(__uint_as_float(v[cch][k2 + 1]) - mref);
-          rs += a + bb;
+          const float a = fast_exp2(fmaf(__uint_as_float(v[cch][k2]), p.c, -mref));
+          const float bb = fast_exp2(fmaf(__uint_as_float(v[cch][k2 + 1]), p.c, -mref));
+          rs4[e & 3] += a + bb;
           w[e] = Mma<T>::pack(a, bb);
         }
         tmem_st32(tS + lb + half * 32, w);
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l = l * alpha + rs;
       m = mn;
       // s_full's commit covers P V of tile j-1 (issued before S of tile j), so O is current here
