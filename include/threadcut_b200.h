@@ -14,6 +14,11 @@
  *                             threadcut/kv.py:28-33             splice(cache, s, inv_freq), all layers
  *   tc_splice_copy            threadcut/kv.py:34-41             splice(...) copy path (non-growing caches)
  *   tc_merge_partials         threadcut/flash_decode.py:68-69   softmax(lse) merge of split partials
+ *   tc_decode_attention_paged, tc_paged_rotate_keys, tc_paged_write
+ *                             threadcut/README.md:141-144       the paged KV layout named there as the next
+ *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
+ *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
+ *                             append into page slots (kv.py:64-77 GrowingLayer.update semantics)
  */
 #ifndef THREADCUT_B200_H
 #define THREADCUT_B200_H
@@ -217,6 +222,46 @@ size_t tc_ragged_tensormaps_size(int batch);
 int tc_ragged_encode_tensormaps(void* host_out, const void* const* k_ptrs, const void* const* v_ptrs,
                                 const int64_t* caps, const int64_t* head_strides, int64_t kv_stride_n,
                                 int batch, int hkv, int d, int dtype);
+
+/* ======================================================================================
+ * Paged K/V cache. A layer's K and V pools are [pages][hkv][page_rows][d] (element strides
+ * pool_stride_page/_h/_row, last dim contiguous, 16-byte aligned rows); one sequence is an ordered
+ * list of row runs inside pages. Tile tables are DEVICE int32 arrays [n_tiles][3] = (page, first
+ * row, rows) with 1 <= rows <= 32 and first row + rows <= page_rows; every kernel bounds-checks
+ * them against the pool (a bad entry is skipped or clamped, never accessed out of the pool).
+ *
+ * tc_decode_attention_paged: decode attention (as tc_decode_attention) of q [hkv][g][d] over the
+ * n_tokens rows the tile table lists, in any order (decode has no mask beyond the rows listed).
+ * 16-bit dtypes, d in {64, 128, 256}, page_rows >= 32. k_new/v_new (both or neither): the step's
+ * new row [hkv][d] (head strides k_new_stride_h/v_new_stride_h) is the last row of the last tile;
+ * the cache still holds stale data there and the launch writes the row into the pools while it
+ * decodes (fused append). Workspace: tc_decode_attention_workspace_size(1, hkv, g, d,
+ * 32 * n_tiles, 0, splits, dtype) bytes, first 16*hkv bytes ZERO before the first call.
+ * ====================================================================================== */
+int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out,
+                              int hkv, int g, int d, int64_t page_rows, int64_t num_pages,
+                              int64_t pool_stride_page, int64_t pool_stride_h, int64_t pool_stride_row,
+                              const int32_t* tiles, int64_t n_tiles, int64_t n_tokens,
+                              const void* k_new, const void* v_new, int64_t k_new_stride_h,
+                              int64_t v_new_stride_h,
+                              int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_h, int64_t out_stride_g,
+                              float scale, int splits, int dtype,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Re-rotates, in place, the keys of the rows the tile table lists in every layer's K pool
+ * (k_pools: HOST array of `layers` device pointers, layers <= 128) by one RoPE delta (cos_sin as
+ * in tc_shift_keys): the splice of C in a paged cache, where B's pages are dropped by the caller
+ * and no row moves. Values are not touched. Each row is read and written by one thread. */
+int tc_paged_rotate_keys(void* const* k_pools, int layers, int hkv, int d, int64_t page_rows, int64_t num_pages,
+                         int64_t pool_stride_page, int64_t pool_stride_h, int64_t pool_stride_row,
+                         const int32_t* tiles, int64_t n_tiles, const float* cos_sin, int dtype, void* stream);
+
+/* Writes t new rows per head (K and V sources [hkv][t][d] with the given strides) of one layer to
+ * their slots: DEVICE int32 array [t][2] = (page, row). */
+int tc_paged_write(const void* k_src, const void* v_src, void* k_pool, void* v_pool, int hkv, int d, int64_t t,
+                   int64_t src_stride_h, int64_t src_stride_t, int64_t vsrc_stride_h, int64_t vsrc_stride_t,
+                   int64_t page_rows, int64_t num_pages, int64_t pool_stride_page, int64_t pool_stride_h,
+                   int64_t pool_stride_row, const int32_t* slots, int dtype, void* stream);
 
 /* ======================================================================================
  * RoPE key shift: out = k*cos(delta*theta) + rotate_half(k)*sin(delta*theta), in fp32 with the

@@ -13,4 +13,6 @@ build container and records its outputs).
                 threadcut/flash_decode.py:21-69), LSE merge (flash_decode.py:68-69)
   rope.py       rotate_half / shift_keys (threadcut/kv.py:15-25), bf16 round-to-nearest-even
   splice.py     GrowingLayer.splice and the copy splice (threadcut/kv.py:28-41, 83-92)
+  paged.py      the reference's contiguous cache model (appends, splices) and a gather of a paged
+                pool in run order, the checker of the paged layout (threadcut README.md:141-144)
 """

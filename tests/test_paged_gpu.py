@@ -1,0 +1,145 @@
+"""Paged K/V cache on the GPU (needs a B200) against the reference's contiguous cache model.
+
+* after appends and splices the pools, read in run order, equal the reference cache bit for bit
+  (keys re-rotated by the same fp32 expression as threadcut/kv.py:25, values untouched);
+* paged decode is within the decode tolerance of the fp32 oracle on the gathered cache, and
+  bit-identical to the contiguous kernel when the pages hold the sequence in order (same tiles,
+  same split);
+* the fused append (one-token step written by the decode launch) is bit-identical to writing the
+  row first and decoding.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import ATTN_ATOL, attn_error, ref_cos_sin
+from oracle.attention import decode_attention_ref
+from oracle.paged import ListCache, gather_ref
+from oracle.rope import inv_freq_default
+from threadcut_b200 import _lib
+from threadcut_b200.flash_decode import decode_attention
+from threadcut_b200.match import Split
+from threadcut_b200.paged import PagedKV
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_device_errors():
+    _lib.device_errors(clear=True)
+    yield
+    assert _lib.device_errors(clear=True) == 0
+
+
+def f32(t):
+    return t.float().cpu().numpy()
+
+
+def drive(seed, layers=2, hkv=8, d=128, dtype=torch.bfloat16, page_rows=64, ops=14, max_tokens=3000):
+    """Random engine-like traffic on a PagedKV and on the reference's list model side by side."""
+    rng = np.random.default_rng(seed)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    inv_freq = torch.as_tensor(inv_freq_default(d, 1e6), dtype=torch.float32)
+    kv = PagedKV(layers, hkv, d, max_tokens=max_tokens, page_rows=page_rows, dtype=dtype, device=DEV)
+    ref = ListCache(layers, hkv, d)
+    for i in range(ops):
+        if i % 3 != 2 or kv.n == 0:
+            t = int(rng.choice([1, 1, 7, 40, 64, 130, 300]))
+            if kv.n + t > max_tokens - 2 * page_rows:
+                t = 1
+            kv.reserve(t)
+            for l in range(layers):
+                k = torch.randn(hkv, t, d, generator=g, device=DEV).to(dtype)
+                v = torch.randn(hkv, t, d, generator=g, device=DEV).to(dtype)
+                kv.write(l, k, v)
+                ref.append(l, f32(k), f32(v))
+        else:
+            n = kv.n
+            a = int(rng.integers(0, n + 1))
+            c0 = int(rng.integers(a, n + 1))
+            c = int(rng.integers(0, n - c0 + 1))
+            kv.splice(Split(a, c0, c), inv_freq)
+            ref.splice(a, c0, c, dtype="bf16" if dtype == torch.bfloat16 else "f16",
+                       cos_sin=ref_cos_sin(-(c0 - a), inv_freq))
+    torch.cuda.synchronize()
+    return kv, ref, g
+
+
+@pytest.mark.parametrize("seed,page_rows,d", [(0, 64, 128), (1, 32, 128), (2, 96, 128), (3, 64, 64), (4, 128, 256)])
+def test_pools_match_the_reference_cache_bit_for_bit(seed, page_rows, d):
+    kv, ref, _ = drive(seed, d=d, page_rows=page_rows)
+    for l in range(kv.layers):
+        k = gather_ref(f32(kv.k[l]), kv.table.runs)
+        v = gather_ref(f32(kv.v[l]), kv.table.runs)
+        assert k.shape == ref.k[l].shape
+        assert np.array_equal(k.view(np.uint32), ref.k[l].view(np.uint32)), (seed, l)
+        assert np.array_equal(v.view(np.uint32), ref.v[l].view(np.uint32)), (seed, l)
+        gk, gv = kv.gather(l)
+        assert np.array_equal(f32(gk), k) and np.array_equal(f32(gv), v)
+
+
+@pytest.mark.parametrize("seed,page_rows,d,dtype", [(5, 64, 128, torch.bfloat16), (6, 32, 128, torch.float16),
+                                                    (7, 64, 64, torch.bfloat16), (8, 128, 256, torch.bfloat16)])
+@pytest.mark.parametrize("splits", [None, 1, 7])
+def test_paged_decode_matches_the_oracle(seed, page_rows, d, dtype, splits):
+    kv, ref, g = drive(seed, d=d, dtype=dtype, page_rows=page_rows)
+    q = torch.randn(kv.hkv, 4, d, generator=g, device=DEV).to(dtype)
+    for l in range(kv.layers):
+        out = kv.decode(l, q, 0.088, splits=splits)
+        torch.cuda.synchronize()
+        want = decode_attention_ref(f32(q), ref.k[l], ref.v[l], 0.088)
+        assert attn_error(f32(out), want, dtype) <= ATTN_ATOL, (seed, l, splits)
+
+
+@pytest.mark.parametrize("n", [1, 31, 32, 100, 4096, 16384])
+def test_in_order_pages_are_bit_identical_to_the_contiguous_kernel(n):
+    """One append of n rows fills pages 0, 1, 2, ... in order: the paged tiles are the contiguous
+    kernel's tiles, so the split and every partial sum are the same."""
+    g = torch.Generator(device=DEV).manual_seed(n)
+    kv = PagedKV(1, 8, 128, max_tokens=n, page_rows=64, device=DEV)
+    k = torch.randn(8, n, 128, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(8, n, 128, generator=g, device=DEV).to(torch.bfloat16)
+    kv.reserve(n)
+    kv.write(0, k, v)
+    q = torch.randn(8, 4, 128, generator=g, device=DEV).to(torch.bfloat16)
+    got = kv.decode(0, q, 0.0883)
+    want = decode_attention(q, k, v, 0.0883)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), n
+
+
+@pytest.mark.parametrize("seed,page_rows", [(9, 64), (10, 32)])
+def test_fused_append_is_write_then_decode(seed, page_rows):
+    kv_a, _, g = drive(seed, page_rows=page_rows)
+    kv_b, _, _ = drive(seed, page_rows=page_rows)
+    for step in range(5):
+        q = torch.randn(kv_a.hkv, 4, 128, generator=g, device=DEV).to(torch.bfloat16)
+        kn = torch.randn(kv_a.hkv, 128, generator=g, device=DEV).to(torch.bfloat16)
+        vn = torch.randn(kv_a.hkv, 128, generator=g, device=DEV).to(torch.bfloat16)
+        kv_a.reserve(1)
+        kv_b.reserve(1)
+        for l in range(kv_a.layers):
+            kv_a.write(l, kn[:, None], vn[:, None])
+            want = kv_a.decode(l, q, 0.09)
+            got = kv_b.decode(l, q, 0.09, k_new=kn, v_new=vn)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (step, l)
+    for l in range(kv_a.layers):
+        assert torch.equal(kv_a.k[l], kv_b.k[l]) and torch.equal(kv_a.v[l], kv_b.v[l])
+
+
+def test_empty_and_rejected_cases():
+    kv = PagedKV(1, 8, 128, max_tokens=256, device=DEV)
+    q = torch.randn(8, 4, 128, device=DEV).to(torch.bfloat16)
+    assert torch.count_nonzero(kv.decode(0, q, 0.1)) == 0
+    with pytest.raises(ValueError):
+        PagedKV(1, 8, 128, max_tokens=256, page_rows=16, device=DEV)
+    with pytest.raises(ValueError):
+        kv.write(0, torch.zeros(8, 3, 128, device=DEV, dtype=torch.bfloat16),
+                 torch.zeros(8, 3, 128, device=DEV, dtype=torch.bfloat16))  # nothing reserved
+    kv32 = PagedKV(1, 8, 128, max_tokens=256, dtype=torch.float32, device=DEV)
+    kv32.reserve(4)
+    kv32.write(0, torch.randn(8, 4, 128, device=DEV), torch.randn(8, 4, 128, device=DEV))
+    with pytest.raises(_lib.TCError):
+        kv32.decode(0, torch.randn(8, 4, 128, device=DEV), 0.1)  # decode over pages: 16-bit only

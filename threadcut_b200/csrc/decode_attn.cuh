@@ -93,6 +93,13 @@ struct DecodeParams {
   const void* k_app;
   const void* v_app;
   int64_t sa_k, sa_v;
+  // paged mode (single sequence, tensor-core kernel): K and V live in pages of a pool and the
+  // sequence is n_tiles tiles, tile t being rows [tiles[3t+1], tiles[3t+1] + tiles[3t+2]) of page
+  // tiles[3t] (at most kTile rows, inside the page); tmk/tmv are (d, page rows, heads, pages) maps,
+  // k/v the pool bases and sk_b/sk_h/sk_n (sv_*) the page, head and row strides. A fused append
+  // (k_app) is the last row of the last tile. Null: contiguous rows.
+  const int32_t* tiles;
+  int64_t n_tiles;
 };
 
 // Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
@@ -511,7 +518,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   }
   __syncthreads();  // barriers initialised before the producer may arm them below
   int staged = 0;   // producer lane: leading tiles already issued before pdl_wait()
-  if (warp == kCWarps && lane == 0) {
+  if (warp == kCWarps && lane == 0 && p.tiles == nullptr) {
     // Before waiting for the previous kernel (it may still be running):
     //  * tiles whose rows the caller declared stable (p.stable_rows, uniform lengths, where n and
     //    the partition come from kernel parameters) are loaded into the pipeline right away;
@@ -556,8 +563,8 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   pdl_launch();
   pdl_wait();  // everything below may read what the previous kernel in the stream wrote
   const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
-  const int64_t seq_tiles = (n + kTile - 1) / kTile;
-  const int nsplit = n > 0 ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
+  const int64_t seq_tiles = p.tiles ? p.n_tiles : (n + kTile - 1) / kTile;
+  const int nsplit = seq_tiles > 0 ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
   if (split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
   int64_t tt0, tt1;
   split_range(seq_tiles, split, nsplit, tt0, tt1);
@@ -584,11 +591,17 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
         mbar_arrive_expect_tx(&full[s], (uint32_t)G::kStageBytes);
         uint8_t* st = smem + s * G::kStageBytes;
-        const int tok = (int)(t0 + (int64_t)j * kTile);  // rows past the tensor end arrive as zeros
+        // rows past the tensor end (or, paged, past the page end) arrive as zeros
+        int tok = (int)(t0 + (int64_t)j * kTile), cbj = cb;
+        if (p.tiles) {
+          const int32_t* tt = p.tiles + 3 * (tt0 + j);
+          cbj = tt[0];
+          tok = tt[1];
+        }
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx) {
-          tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, h, cb, &full[s], pol);
-          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, h, cb, &full[s], pol);
+          tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, h, cbj, &full[s], pol);
+          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, h, cbj, &full[s], pol);
         }
       }
     }
@@ -635,9 +648,26 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       uint8_t* stage = smem + s * G::kStageBytes;
       const uint32_t kst = smem_u32(stage);
       const uint32_t vst = kst + G::kTileBytes;
-      const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
-      const int valid = rem < kTile ? (int)rem : kTile;
-      const int64_t app_r = p.k_app != nullptr ? (n - 1) - (t0 + (int64_t)j * kTile) : -1;
+      int valid;
+      if (p.tiles) {
+        const int vt = p.tiles[3 * (tt0 + j) + 2];  // device table: clamp into [0, kTile]
+        valid = vt < 0 ? 0 : (vt > kTile ? kTile : vt);
+      } else {
+        const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
+        valid = rem < kTile ? (int)rem : kTile;
+      }
+      int64_t app_r = -1, app_row = n - 1, app_pg = 0;  // row in the tile, row and page in the cache
+      if (p.k_app != nullptr) {
+        if (p.tiles) {
+          if (tt0 + j == p.n_tiles - 1 && valid > 0) {
+            app_r = valid - 1;
+            app_pg = p.tiles[3 * (tt0 + j)];
+            app_row = p.tiles[3 * (tt0 + j) + 1] + app_r;
+          }
+        } else {
+          app_r = (n - 1) - (t0 + (int64_t)j * kTile);
+        }
+      }
       const bool patch = app_r >= 0 && app_r < kTile;
       if (patch) {
         // the appended row: the cache still holds stale data there, so replace the staged copy with
@@ -646,8 +676,10 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         constexpr int CH = D / 8;  // 16-byte chunks per row
         const uint4* ka = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + h * p.sa_k);
         const uint4* va = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_app) + h * p.sa_v);
-        uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + h * p.sk_h + (n - 1) * p.sk_n);
-        uint4* vc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + h * p.sv_h + (n - 1) * p.sv_n);
+        uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + app_pg * p.sk_b + h * p.sk_h +
+                                             app_row * p.sk_n);
+        uint4* vc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + app_pg * p.sv_b + h * p.sv_h +
+                                             app_row * p.sv_n);
         for (int idx = lane; idx < 2 * CH; idx += 32) {
           const bool isv = idx >= CH;
           const int c = isv ? idx - CH : idx;

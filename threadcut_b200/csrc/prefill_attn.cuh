@@ -229,16 +229,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
         for (int cch = 0; cch < 4; ++cch)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
+          for (int e = 0; e < 32; ++e)
             if (ja * kPfKeys + cch * 32 + e > limit) v[cch][e] = __float_as_uint(-INFINITY);
-            mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[cch][e]));
-          }
-      } else {
-#pragma unroll
-        for (int cch = 0; cch < 4; ++cch)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[cch][e]));
       }
+#pragma unroll
+      for (int cch = 0; cch < 4; ++cch)
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          mx[e & 7] = fmax3(mx[e & 7], __uint_as_float(v[cch][2 * e]), __uint_as_float(v[cch][2 * e + 1]));
       const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                              fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * p.c;  // exp2 domain (c > 0)
       // lazy max: keep m unless this tile's max passes it by more than kPfLazyMax
@@ -256,9 +254,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int cch = half * 2 + (e >> 4), k2 = 2 * (e & 15);
-          const float a = fast_exp2(fmaf(__uint_as_float(v[cch][k2]), p.c, -mref));
-          const float bb = fast_exp2(fmaf(__uint_as_float(v[cch][k2 + 1]), p.c, -mref));
-          rs4[e & 3] += a + bb;
+          const float2 xy = ffma2(make_float2(__uint_as_float(v[cch][k2]), __uint_as_float(v[cch][k2 + 1])),
+                                  make_float2(p.c, p.c), make_float2(-mref, -mref));
+          const float a = fast_exp2(xy.x);
+          const float bb = fast_exp2(xy.y);
+          const float2 r2 = fadd2(make_float2(rs4[2 * (e & 1)], rs4[2 * (e & 1) + 1]), make_float2(a, bb));
+          rs4[2 * (e & 1)] = r2.x;
+          rs4[2 * (e & 1) + 1] = r2.y;
           w[e] = Mma<T>::pack(a, bb);
         }
         tmem_st32(tS + lb + half * 32, w);

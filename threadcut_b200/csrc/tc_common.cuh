@@ -338,6 +338,28 @@ __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2hal
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
+// Packed fp32 pairs (one f32x2 instruction for two lanes of work) and a three-input max.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ta, tb, tc, td;\n\tmov.b64 ta, {%2, %3};\n\tmov.b64 tb, {%4, %5};\n\t"
+      "mov.b64 tc, {%6, %7};\n\tfma.rn.f32x2 td, ta, tb, tc;\n\tmov.b64 {%0, %1}, td;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ta, tb, td;\n\tmov.b64 ta, {%2, %3};\n\tmov.b64 tb, {%4, %5};\n\t"
+      "add.rn.f32x2 td, ta, tb;\n\tmov.b64 {%0, %1}, td;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

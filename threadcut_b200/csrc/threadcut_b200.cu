@@ -10,6 +10,7 @@
 
 #include "decode_attn.cuh"
 #include "rope_splice.cuh"
+#include "paged.cuh"
 #include "split.cuh"
 #include "prefill_attn.cuh"
 
@@ -251,6 +252,8 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
   bool use_mma = dtype != TC_F32 && kv_aligned && mma_dim(d);
   if (use_mma && p.k_ptrs != nullptr) {
     use_mma = p.tm_ragged != nullptr;  // ragged caches need their pre-encoded maps
+  } else if (p.tiles != nullptr) {
+    if (!use_mma) return TC_ERR_INVALID;  // paged: the caller encoded the pool maps
   } else if (use_mma) {
     use_mma = encode_kv_map(&p.tmk, p.k, dtype, d, max_n, p.hkv, p.batch, p.sk_n, p.sk_h, p.sk_b) &&
               encode_kv_map(&p.tmv, p.v, dtype, d, max_n, p.hkv, p.batch, p.sv_n, p.sv_h, p.sv_b);
@@ -322,6 +325,16 @@ cudaError_t launch_shift(const ShiftParams& p, int blocks, cudaStream_t st) {
 template <typename T, int VEC>
 cudaError_t launch_splice_copy(const SpliceCopyParams& p, int blocks, cudaStream_t st) {
   splice_copy_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+template <typename T, int VEC>
+cudaError_t launch_paged_rotate(const PagedRotateParams& p, int blocks, cudaStream_t st) {
+  paged_rotate_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+template <typename T, int VEC>
+cudaError_t launch_paged_write(const PagedWriteParams& p, int blocks, cudaStream_t st) {
+  paged_write_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
   return cudaGetLastError();
 }
 template <typename T, int VEC>
@@ -687,6 +700,137 @@ int tc_shift_keys(const void* keys, void* out, int64_t outer, int64_t n, int d, 
   const int64_t tasks = outer * n * ((d / 2) / vec);
   const int blocks = grid_for(tasks, 256, sm_count(current_device()), 16);
   const cudaError_t e = TC_ROPE_DISPATCH(launch_shift, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------------------- paged cache
+int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out, int hkv, int g,
+                              int d, int64_t page_rows, int64_t num_pages, int64_t pool_stride_page,
+                              int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* tiles, int64_t n_tiles,
+                              int64_t n_tokens, const void* k_new, const void* v_new, int64_t k_new_stride_h,
+                              int64_t v_new_stride_h, int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_h,
+                              int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (!mma_dim(d) || hkv < 1 || g < 1 || page_rows < kTile || page_rows > (1 << 30) || num_pages < 1 ||
+      num_pages > (1 << 30) || n_tiles < 0 || n_tiles > ((int64_t)1 << 31) / kTile || n_tokens < 0)
+    return TC_ERR_INVALID;
+  if (k_pool == nullptr || v_pool == nullptr || (n_tiles > 0 && tiles == nullptr)) return TC_ERR_INVALID;
+  if ((k_new == nullptr) != (v_new == nullptr)) return TC_ERR_INVALID;
+  if (!aligned16(k_pool) || !aligned16(v_pool) || !stride16(pool_stride_page, dtype) ||
+      !stride16(pool_stride_h, dtype) || !stride16(pool_stride_row, dtype))
+    return TC_ERR_ALIGN;
+  if (k_new != nullptr && (!aligned16(k_new) || !aligned16(v_new) || !stride16(k_new_stride_h, dtype) ||
+                           !stride16(v_new_stride_h, dtype)))
+    return TC_ERR_ALIGN;
+  DecodeParams p = base_params();
+  if (!encode_kv_map(&p.tmk, k_pool, dtype, d, page_rows, hkv, num_pages, pool_stride_row, pool_stride_h,
+                     pool_stride_page) ||
+      !encode_kv_map(&p.tmv, v_pool, dtype, d, page_rows, hkv, num_pages, pool_stride_row, pool_stride_h,
+                     pool_stride_page))
+    return TC_ERR_INVALID;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  p.q = q;
+  p.out = out;
+  p.lse_b = (int64_t)hkv * g;
+  p.k = k_pool;
+  p.v = v_pool;
+  p.n = n_tokens;
+  p.sq_h = q_stride_h;
+  p.sq_g = q_stride_g;
+  p.so_h = out_stride_h;
+  p.so_g = out_stride_g;
+  p.sk_b = pool_stride_page;
+  p.sk_h = pool_stride_h;
+  p.sk_n = pool_stride_row;
+  p.sv_b = pool_stride_page;
+  p.sv_h = pool_stride_h;
+  p.sv_n = pool_stride_row;
+  p.hkv = hkv;
+  p.g = g;
+  p.batch = 1;
+  p.k_app = n_tiles > 0 ? k_new : nullptr;
+  p.v_app = n_tiles > 0 ? v_new : nullptr;
+  p.sa_k = k_new_stride_h;
+  p.sa_v = v_new_stride_h;
+  return run_decode(p, dtype, d, false, n_tiles * kTile, n_tiles * kTile, splits, true, scale, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tc_paged_rotate_keys(void* const* k_pools, int layers, int hkv, int d, int64_t page_rows, int64_t num_pages,
+                         int64_t pool_stride_page, int64_t pool_stride_h, int64_t pool_stride_row,
+                         const int32_t* tiles, int64_t n_tiles, const float* cos_sin, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (layers < 1 || layers > kMaxLayers || hkv < 1 || d < 2 || d % 2 || d > kMaxRopeDim || page_rows < 1 ||
+      num_pages < 1 || n_tiles < 0 || k_pools == nullptr || cos_sin == nullptr)
+    return TC_ERR_INVALID;
+  if (n_tiles == 0) return TC_OK;
+  if (tiles == nullptr) return TC_ERR_INVALID;
+  PagedRotateParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int l = 0; l < layers; ++l) {
+    if (k_pools[l] == nullptr) return TC_ERR_INVALID;
+    p.kp[l] = k_pools[l];
+  }
+  p.layers = layers;
+  p.hkv = hkv;
+  p.d = d;
+  p.page_rows = page_rows;
+  p.num_pages = num_pages;
+  p.s_page = pool_stride_page;
+  p.s_h = pool_stride_h;
+  p.s_row = pool_stride_row;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  load_cos_sin(p.cs, cos_sin, d);
+  const int64_t strides[3] = {pool_stride_page, pool_stride_h, pool_stride_row};
+  const int vec = rope_vec(dtype, d / 2, k_pools, layers, strides, 3);
+  const int64_t tasks = (int64_t)layers * n_tiles * hkv * kPagedTileRows * ((d / 2) / vec);
+  const int blocks = grid_for(tasks, 256, sm_count(current_device()), 8);
+  const cudaError_t e =
+      TC_ROPE_DISPATCH(launch_paged_rotate, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_paged_write(const void* k_src, const void* v_src, void* k_pool, void* v_pool, int hkv, int d, int64_t t,
+                   int64_t src_stride_h, int64_t src_stride_t, int64_t vsrc_stride_h, int64_t vsrc_stride_t,
+                   int64_t page_rows, int64_t num_pages, int64_t pool_stride_page, int64_t pool_stride_h,
+                   int64_t pool_stride_row, const int32_t* slots, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (hkv < 1 || d < 1 || t < 0 || page_rows < 1 || num_pages < 1) return TC_ERR_INVALID;
+  if (t == 0) return TC_OK;
+  if (k_src == nullptr || v_src == nullptr || k_pool == nullptr || v_pool == nullptr || slots == nullptr)
+    return TC_ERR_INVALID;
+  PagedWriteParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.k_src = k_src;
+  p.v_src = v_src;
+  p.kp = k_pool;
+  p.vp = v_pool;
+  p.hkv = hkv;
+  p.d = d;
+  p.t = t;
+  p.src_sh = src_stride_h;
+  p.src_st = src_stride_t;
+  p.vsrc_sh = vsrc_stride_h;
+  p.vsrc_st = vsrc_stride_t;
+  p.page_rows = page_rows;
+  p.num_pages = num_pages;
+  p.s_page = pool_stride_page;
+  p.s_h = pool_stride_h;
+  p.s_row = pool_stride_row;
+  p.slots = slots;
+  const void* ptrs[4] = {k_src, v_src, k_pool, v_pool};
+  const int64_t strides[7] = {src_stride_h, src_stride_t, vsrc_stride_h, vsrc_stride_t,
+                              pool_stride_page, pool_stride_h, pool_stride_row};
+  // whole rows move as 16-byte chunks when d allows it (rope_vec checks d/2; check d itself here)
+  int vec = rope_vec(dtype, d / 2, ptrs, 4, strides, 7);
+  if (d % vec != 0) vec = 1;
+  const int64_t tasks = 2 * t * hkv * (d / vec);
+  const int blocks = grid_for(tasks, 256, sm_count(current_device()), 8);
+  const cudaError_t e =
+      TC_ROPE_DISPATCH(launch_paged_write, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
