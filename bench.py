@@ -332,6 +332,89 @@ def time_append_16k(qs, ks, vs, steps, warmup, dist):
     return out[0], out[1]
 
 
+def time_paged(steps, warmup, dev, dist, layers=LAYERS):
+    """Paged cache (threadcut_b200.paged): (1) a 36-layer decode step over 16,384 live tokens held
+    in 64-row pages after a splice whose cut points fall inside pages (ragged runs), replayed from a
+    CUDA graph; (2) the config-2 splice as a paged splice: B's pages dropped on the host and C's
+    keys re-rotated in place (tc_paged_rotate_keys, all layers in one launch, the same C rows every
+    step). Returns (decode ms per step, rotate ms per launch, rotate bytes per layer, host table
+    splice us, tiles)."""
+    import ctypes
+    from threadcut_b200._lib import TC_BF16, check, cos_sin_table, lib
+    from threadcut_b200.match import Split
+    from threadcut_b200.paged import PagedKV, PageTable
+    g = torch.Generator(device=dev).manual_seed(99)
+    kv = PagedKV(layers, 8, 128, max_tokens=20000, page_rows=64, device=dev)
+    kv.reserve(20000)
+    for l in range(layers):
+        kv.write(l, torch.randn(8, 20000, 128, generator=g, device=dev).to(torch.bfloat16),
+                 torch.randn(8, 20000, 128, generator=g, device=dev).to(torch.bfloat16))
+    kv.splice(Split(4010, 7626, 12374), workloads.inv_freq())  # n = 16384, runs start/end inside pages
+    assert kv.n == N_CTX
+    qs = [torch.randn(8, 4, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+
+    def launch_all():
+        for l in range(layers):
+            kv.decode(l, qs[l], workloads.SCALE)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    dec_ms = time_graph(graph, steps, warmup, dist)
+    tiles = kv._tiles()[1]
+    del graph, kv, qs
+    torch.cuda.empty_cache()
+    # (2) config-2 splice on a fresh 8192-token paged cache
+    n = workloads.CFG2_N
+    a, c0, c = workloads.CFG2_SPLIT
+    kv = PagedKV(layers, 8, 128, max_tokens=n, page_rows=64, device=dev)
+    kv.reserve(n)
+    reps = 200
+    tabs = []
+    for _ in range(reps):
+        tabs.append(PageTable(kv.table.num_pages, 64))
+        tabs[-1].reserve(n)
+    tabs[0].splice(Split(a, c0, c))  # first call pays numpy's lazy imports
+    t0 = time.perf_counter()
+    for tab in tabs[1:]:
+        tab.splice(Split(a, c0, c))
+    host_us = (time.perf_counter() - t0) / (reps - 1) * 1e6
+    runs_c = kv.table._cut(c0, c0 + c)
+    ct = PageTable.tiles_of(runs_c)
+    ctiles = torch.from_numpy(ct).to(dev)
+    cs, cs_ptr = cos_sin_table(a - c0, workloads.inv_freq())
+    kp = (ctypes.c_void_p * layers)(*[t.data_ptr() for t in kv.k])
+    L = lib()
+    sp, sh, sr = kv._strides()
+
+    def run():
+        check("tc_paged_rotate_keys", L.tc_paged_rotate_keys(kp, layers, 8, 128, 64, kv.table.num_pages, sp, sh, sr,
+                                                             ctiles.data_ptr(), ct.shape[0], cs_ptr, TC_BF16,
+                                                             torch.cuda.current_stream(dev).cuda_stream))
+    for _ in range(warmup):
+        run()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    e1.synchronize()
+    barrier(dist)
+    rot_ms = e0.elapsed_time(e1) / steps
+    del kv, cs
+    torch.cuda.empty_cache()
+    return dec_ms, rot_ms, 2 * c * 8 * 128 * 2, host_us, tiles
+
+
 def time_split_128k(dev, reps=20):
     """split() of a config-5-like request (128k cached tokens, a 32k span pruned mid-context, a
     300-token fresh tail) on the device (tokens already on the GPU, result read back) and with the
@@ -546,6 +629,8 @@ def run_ours(args, rank, local, world, dist):
             "frac": round(c4_bytes / (c4_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4), "bytes_per_layer": c4_bytes,
             "workload": "cfg4: 64 ragged sequences, lengths uniform in [1024,16384] (seeded), per-sequence bf16 "
                         "K/V caches, 32 q / 8 kv heads, d 128, 36 launches per step over 2 distinct layer caches"}
+    pg_dec_ms, pg_rot_ms, pg_rot_bytes, pg_host_us, pg_tiles = time_paged(args.steps, args.warmup, dev, dist)
+    pg_dec_ms, pg_rot_ms = max_over_ranks(pg_dec_ms, dist), max_over_ranks(pg_rot_ms, dist)
     split_dev_us, split_host_us = time_split_128k(dev)
     pf_ms, pf_gqa_ms, pf_ref_ms, pf_flops = time_prefill(min(args.steps, 10), args.warmup, dev)
     tc_peak, tc_peak_kind = bf16_peak()
@@ -604,6 +689,19 @@ def run_ours(args, rank, local, world, dist):
                          "peak_kind": tc_peak_kind},
             "what": "prefill of a 512-token chunk over a 98,304-token cache (32 q / 8 kv heads, d 128, causal with "
                     "the cache offset): tc_prefill_attention vs SDPA GQA mode vs the reference's repeat_kv + SDPA"},
+        "paged": {
+            "decode_16k_us_per_layer": round(pg_dec_ms * 1000.0 / LAYERS, 3),
+            "decode_16k_frac": round(BYTES_PER_LAYER / (pg_dec_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
+            "decode_tiles": pg_tiles,
+            "splice_cfg2_us_per_layer": round(pg_rot_ms * 1000.0 / LAYERS, 3),
+            "splice_cfg2_gbs": round(pg_rot_bytes * LAYERS / (pg_rot_ms * 1e-3) / 1e9, 1),
+            "splice_cfg2_frac": round(pg_rot_bytes * LAYERS / (pg_rot_ms * 1e-3) / 1e9 / hbm, 4),
+            "splice_cfg2_bytes_per_layer": pg_rot_bytes,
+            "splice_cfg2_host_table_us": round(pg_host_us, 2),
+            "what": "paged K/V cache (64-row pages): decode of the 36-layer 16k step over ragged runs (a splice "
+                    "cut inside pages), and the cfg2 splice Split(2048,4096,4096) as B's pages dropped on the "
+                    "host + C's keys re-rotated in place (values never move: half the contiguous splice's bytes); "
+                    "compare decode with the headline value and the splice with shift.us_per_layer"},
         "split_128k": {"device_us": round(split_dev_us, 1), "host_numpy_us": round(split_host_us, 1),
                        "what": "match.split of a 128k cached / 97k new request: tc_split (tokens on the GPU, "
                                "result read back, wall clock) vs the host rule on Python lists"},

@@ -16,7 +16,7 @@ from .splice import copy_splice_ref
 def gather_ref(pool, runs):
     """pool [pages, hkv, page_rows, d]; runs [(page, first row, rows), ...] -> [hkv, n, d]."""
     pool = np.asarray(pool)
-    if not runs:
+    if len(runs) == 0:
         return np.zeros((pool.shape[1], 0, pool.shape[3]), dtype=pool.dtype)
     return np.concatenate([pool[p, :, r0:r0 + c, :] for p, r0, c in runs], axis=1)
 

@@ -70,7 +70,7 @@ def test_whole_pages_of_b_and_the_tail_are_freed():
     tab = PageTable(16, 64)
     tab.reserve(64 * 10)                                      # pages 0..9, full
     runs_c, freed = tab.splice(Split(70, 300, 200))           # A = pages 0-1, B = rest of 1..4, C = 4..7
-    assert runs_c[0] == [4, 300 - 256, 64 - (300 - 256)]      # C starts inside page 4
+    assert runs_c[0].tolist() == [4, 300 - 256, 64 - (300 - 256)]      # C starts inside page 4
     assert freed == [2, 3, 8, 9]                              # wholly inside B, and the stale tail
     assert tab.n == 270
     assert {r[0] for r in tab.runs} == {0, 1, 4, 5, 6, 7}

@@ -35,7 +35,12 @@ TILE_ROWS = 32  # rows per tile-table entry (the decode kernel's tile height)
 
 class PageTable:
     """Host bookkeeping of one paged sequence: free pages, the run list, slot allocation, splice and
-    the decode tile table. No device work; PagedKV drives the kernels with what this returns."""
+    the decode tile table. No device work; PagedKV drives the kernels with what this returns.
+
+    Runs are an int64 array [R, 3] (page, first row, rows) and the tile table an int32 array
+    [T, 3] kept in step with them in a growable buffer: an append touches only the tail of the
+    table (tiles from `dirty` on changed; a one-token append is O(1)), and a splice keeps the tiles
+    of every run it does not cut and re-tiles only the runs cut at a, c0 and c0 + c."""
 
     def __init__(self, num_pages, page_rows):
         if page_rows < TILE_ROWS:
@@ -43,66 +48,142 @@ class PageTable:
         self.num_pages = int(num_pages)
         self.page_rows = int(page_rows)
         self.free = list(range(self.num_pages - 1, -1, -1))  # stack: page 0 is taken first
-        self.runs = []  # [page, first row, rows] in logical order
+        self._runs = np.zeros((0, 3), np.int64)
+        self._tbuf = np.zeros((64, 3), np.int32)
+        self._nt = 0
         self.n = 0
         self.version = 0  # bumped whenever the run list changes
+        self.dirty = 0    # tiles [dirty, T) changed since the last mark_clean()
+
+    @property
+    def runs(self):
+        return self._runs.tolist()
+
+    def tiles(self):
+        return self._tbuf[:self._nt]
+
+    def mark_clean(self):
+        self.dirty = self._nt
+
+    def _set_tiles(self, keep, tail):
+        """Tile table = the first `keep` tiles + `tail`."""
+        need = keep + tail.shape[0]
+        if need > self._tbuf.shape[0]:
+            buf = np.zeros((max(need, 2 * self._tbuf.shape[0]), 3), np.int32)
+            buf[:keep] = self._tbuf[:keep]
+            self._tbuf = buf
+        self._tbuf[keep:need] = tail
+        self._nt = need
+        self.dirty = min(self.dirty, keep)
 
     # ---------------------------------------------------------------- allocation
-    def _take_page(self):
-        if not self.free:
-            raise MemoryError("PagedKV: no free page left in the pool")
-        return self.free.pop()
-
     def reserve(self, t):
         """Slots (page, row) for t new tokens at the end of the sequence, in order: first the rows
         after the last run in its page, then fresh pages. Returns an int32 array [t, 2]."""
         t = int(t)
+        P = self.page_rows
         out = np.empty((t, 2), dtype=np.int32)
-        i = 0
-        while i < t:
-            if self.runs:
-                last = self.runs[-1]
-                room = self.page_rows - (last[1] + last[2])
+        if t == 0:
+            return out
+        runs = self._runs
+        room = P - int(runs[-1, 1] + runs[-1, 2]) if runs.shape[0] else 0
+        if t == 1 and room >= 1:
+            # one-token step inside the last page: extend the last run and its last tile
+            page, r = int(runs[-1, 0]), int(runs[-1, 1] + runs[-1, 2])
+            out[0, 0], out[0, 1] = page, r
+            runs[-1, 2] += 1
+            last = self._tbuf[self._nt - 1]
+            if int(last[2]) < TILE_ROWS and int(last[0]) == page and int(last[1] + last[2]) == r:
+                last[2] += 1
+                self.dirty = min(self.dirty, self._nt - 1)
             else:
-                room = 0
-            if room <= 0:
-                self.runs.append([self._take_page(), 0, 0])
-                continue
-            take = min(room, t - i)
-            r0 = last[1] + last[2]
-            out[i:i + take, 0] = last[0]
-            out[i:i + take, 1] = np.arange(r0, r0 + take, dtype=np.int32)
-            last[2] += take
-            i += take
+                self._set_tiles(self._nt, np.asarray([[page, r, 1]], np.int32))
+            self.n += 1
+            self.version += 1
+            return out
+        first = min(room, t)
+        n_new = -(-(t - first) // P)
+        if n_new > len(self.free):
+            raise MemoryError("PagedKV: no free page left in the pool")
+        retile_run = runs.shape[0]  # runs from this index on are (re)tiled below
+        keep = self._nt             # tiles before this index stay as they are
+        if first > 0:
+            page, r0 = int(runs[-1, 0]), int(runs[-1, 1] + runs[-1, 2])
+            out[:first, 0] = page
+            out[:first, 1] = np.arange(r0, r0 + first, dtype=np.int32)
+            keep = self._nt - int(-(-runs[-1, 2] // TILE_ROWS))  # the last run's tiles are redone
+            retile_run = runs.shape[0] - 1
+            runs[-1, 2] += first
+        if n_new:
+            pages = [self.free.pop() for _ in range(n_new)]
+            counts = np.full(n_new, P, np.int64)
+            counts[-1] = (t - first) - P * (n_new - 1)
+            new = np.stack([np.asarray(pages, np.int64), np.zeros(n_new, np.int64), counts], axis=1)
+            out[first:, 0] = np.repeat(np.asarray(pages, np.int32), P)[:t - first]
+            out[first:, 1] = np.tile(np.arange(P, dtype=np.int32), n_new)[:t - first]
+            self._runs = np.concatenate((runs, new))
+        self._set_tiles(keep, self.tiles_of(self._runs[retile_run:]))
         self.n += t
         self.version += 1
         return out
 
     # ---------------------------------------------------------------- splice
+    def _index(self):
+        cnt = self._runs[:, 2]
+        end = np.cumsum(cnt)
+        nt = (cnt + TILE_ROWS - 1) // TILE_ROWS
+        tile0 = np.concatenate(([0], np.cumsum(nt)))
+        return end, end - cnt, tile0
+
+    def _span(self, lo, hi, end, start, tile0):
+        """Runs covering logical tokens [lo, hi) cut at the ends, and their tiles: the tiles of runs
+        kept whole are copied from the current table, cut runs are re-tiled."""
+        if hi <= lo or self._runs.shape[0] == 0:
+            return np.zeros((0, 3), np.int64), np.zeros((0, 3), np.int32)
+        i0 = int(np.searchsorted(end, lo, side="right"))
+        i1 = int(np.searchsorted(start, hi, side="left"))
+        sel = self._runs[i0:i1].copy()
+        cut_lo = lo - int(start[i0])
+        cut_hi = int(end[i1 - 1]) - hi
+        if cut_lo > 0:
+            sel[0, 1] += cut_lo
+            sel[0, 2] -= cut_lo
+        if cut_hi > 0:
+            sel[-1, 2] -= cut_hi
+        k = sel.shape[0]
+        a = 1 if cut_lo > 0 else 0                 # runs [a, b) of sel keep their old tiles
+        b = k - 1 if (cut_hi > 0 and k - 1 >= a) else k
+        parts = []
+        if a:
+            parts.append(self.tiles_of(sel[:1]))
+        if b > a:
+            parts.append(self._tbuf[tile0[i0 + a]:tile0[i0 + b]])
+        if b < k:
+            parts.append(self.tiles_of(sel[b:]))
+        return sel, np.concatenate(parts) if parts else np.zeros((0, 3), np.int32)
+
     def _cut(self, lo, hi):
-        """Runs covering logical tokens [lo, hi), split at the ends."""
-        out, pos = [], 0
-        for page, r0, cnt in self.runs:
-            a, b = max(lo, pos), min(hi, pos + cnt)
-            if a < b:
-                out.append([page, r0 + (a - pos), b - a])
-            pos += cnt
-            if pos >= hi:
-                break
-        return out
+        """Runs covering logical tokens [lo, hi), split at the ends (int64 [k, 3])."""
+        end, start, tile0 = self._index()
+        return self._span(lo, hi, end, start, tile0)[0]
 
     def splice(self, s: Split):
         """Keep A = [0, a) and C = [c0, c0 + c) (threadcut/kv.py:28-33 semantics, everything after C
-        dropped). Returns (C's runs in the new list, pages freed)."""
+        dropped). Returns (C's runs in the new list as [k, 3] int64, pages freed)."""
         a, c0, c = int(s.a), int(s.c0), int(s.c)
         if not (0 <= a <= c0 and c >= 0 and c0 + c <= self.n):
             raise ValueError(f"splice {s} outside a sequence of {self.n} tokens")
-        runs_a = self._cut(0, a)
-        runs_c = self._cut(c0, c0 + c)
-        kept = {r[0] for r in runs_a} | {r[0] for r in runs_c}
-        dropped = sorted({r[0] for r in self.runs} - kept)
+        end, start, tile0 = self._index()
+        runs_a, tiles_a = self._span(0, a, end, start, tile0)
+        runs_c, tiles_c = self._span(c0, c0 + c, end, start, tile0)
+        new = np.concatenate((runs_a, runs_c))
+        old_used = np.zeros(self.num_pages, bool)
+        old_used[self._runs[:, 0]] = True
+        old_used[new[:, 0]] = False
+        dropped = np.flatnonzero(old_used).tolist()
         self.free.extend(reversed(dropped))
-        self.runs = runs_a + runs_c
+        self._runs = new
+        self._set_tiles(0, np.concatenate((tiles_a, tiles_c)))
         self.n = a + c
         self.version += 1
         return runs_c, dropped
@@ -117,25 +198,29 @@ class PageTable:
     # ---------------------------------------------------------------- tables
     @staticmethod
     def tiles_of(runs):
-        """Tile table [n_tiles, 3] (page, first row, rows <= TILE_ROWS) covering `runs` in order."""
-        rows = []
-        for page, r0, cnt in runs:
-            for off in range(0, cnt, TILE_ROWS):
-                rows.append((page, r0 + off, min(TILE_ROWS, cnt - off)))
-        return np.asarray(rows, dtype=np.int32).reshape(-1, 3)
-
-    def tiles(self):
-        return self.tiles_of(self.runs)
+        """Tile table [n_tiles, 3] int32 (page, first row, rows <= TILE_ROWS) covering `runs`."""
+        runs = np.asarray(runs, np.int64).reshape(-1, 3)
+        if runs.shape[0] == 0:
+            return np.zeros((0, 3), np.int32)
+        nt = (runs[:, 2] + TILE_ROWS - 1) // TILE_ROWS
+        idx = np.repeat(np.arange(runs.shape[0]), nt)
+        off = (np.arange(idx.shape[0]) - np.repeat(np.cumsum(nt) - nt, nt)) * TILE_ROWS
+        sel = runs[idx]
+        out = np.empty((idx.shape[0], 3), np.int32)
+        out[:, 0] = sel[:, 0]
+        out[:, 1] = sel[:, 1] + off
+        out[:, 2] = np.minimum(TILE_ROWS, sel[:, 2] - off)
+        return out
 
     def positions(self):
         """(page, row) of every logical token, int64 [n, 2] (for gathers and checks)."""
-        out = np.empty((self.n, 2), dtype=np.int64)
-        i = 0
-        for page, r0, cnt in self.runs:
-            out[i:i + cnt, 0] = page
-            out[i:i + cnt, 1] = np.arange(r0, r0 + cnt)
-            i += cnt
-        return out
+        runs = self._runs
+        if runs.shape[0] == 0:
+            return np.zeros((0, 2), np.int64)
+        cnt = runs[:, 2]
+        idx = np.repeat(np.arange(runs.shape[0]), cnt)
+        k = np.arange(idx.shape[0]) - np.repeat(np.cumsum(cnt) - cnt, cnt)
+        return np.stack((runs[idx, 0], runs[idx, 1] + k), axis=1)
 
 
 class PagedKV:
@@ -161,9 +246,8 @@ class PagedKV:
         self.v = [torch.zeros(shape, dtype=dtype, device=dev) for _ in range(self.layers)]
         self._kptrs = (ctypes.c_void_p * self.layers)(*[t.data_ptr() for t in self.k])
         self._slots = None       # device int32 [t, 2] of the step reserved last
-        self._tiles_dev = None   # device int32 [n_tiles, 3] of table version _tiles_ver
-        self._tiles_n = 0
-        self._tiles_ver = -1
+        self._tiles_dev = None   # device int32 [capacity, 3]: the tile table, rows [0, n) valid
+        self._tiles_ver = -1     # table version the device copy reflects
 
     @property
     def n(self):
@@ -174,12 +258,21 @@ class PagedKV:
         return s[0], s[1], s[2]
 
     def _tiles(self):
+        """Device tile table and its length, brought up to date by copying only the rows that
+        changed since the last call (an append changes the tail; a splice everything)."""
+        tab = self.table.tiles()
+        nt = tab.shape[0]
         if self._tiles_ver != self.table.version:
-            tab = self.table.tiles()
-            self._tiles_n = tab.shape[0]
-            self._tiles_dev = torch.from_numpy(tab).to(self.device) if tab.size else None
+            lo = self.table.dirty
+            if self._tiles_dev is None or self._tiles_dev.shape[0] < nt:
+                cap = max(nt, 2 * (self._tiles_dev.shape[0] if self._tiles_dev is not None else 0), 64)
+                self._tiles_dev = torch.empty((cap, 3), dtype=torch.int32, device=self.device)
+                lo = 0
+            if lo < nt:
+                self._tiles_dev[lo:nt].copy_(torch.from_numpy(np.ascontiguousarray(tab[lo:nt])))
+            self.table.mark_clean()
             self._tiles_ver = self.table.version
-        return self._tiles_dev, self._tiles_n
+        return (self._tiles_dev if nt else None), nt
 
     # ---------------------------------------------------------------- step
     def reserve(self, t):
@@ -249,7 +342,7 @@ class PagedKV:
         the pool, C's keys are re-rotated by -(c0 - a) positions where they lie, nothing moves."""
         runs_c, _ = self.table.splice(s)
         gap = int(s.c0) - int(s.a)
-        if gap == 0 or not runs_c:
+        if gap == 0 or runs_c.shape[0] == 0:
             return  # the reference clones C onto itself: nothing to rotate
         tab = PageTable.tiles_of(runs_c)
         tiles = torch.from_numpy(tab).to(self.device)
