@@ -56,6 +56,7 @@ constexpr int kMergeLoads = 8;   // partials one merger thread loads per L2 roun
 constexpr int kLastSplitsPerWarp = 3;  // last-arrival merge: partials per warp (one round trip)
 constexpr int kMaxMergers = 16;        // start-ticket mergers per (sequence, head), column slices
 constexpr int kMmaCtasPerSm = 1; // resident CTAs per SM of the tensor-core kernel
+constexpr int kTabTiles = 256;   // paged mode: tile-table entries of a slice staged in shared memory
 constexpr int kGenCtasPerSm = 4; // same for the generic kernel
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -489,7 +490,9 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {
 // ------------------------------------------------------------------------------------------------
 // Tensor-core path: T in {bf16, f16}, D in {64, 128, 256}, NG = number of 8-head column tiles
 // (g <= 8*NG). K/V tiles arrive by tensor-map TMA: one cp.async.bulk.tensor per 64-column box.
-template <typename T, int D, int NG>
+// kPaged: K/V rows come through the tile table (p.tiles); a separate instantiation, so the
+// contiguous kernel carries none of it.
+template <typename T, int D, int NG, bool kPaged>
 __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     decode_mma_kernel(const __grid_constant__ DecodeParams p) {
   using G = MmaGeom<D>;
@@ -505,6 +508,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kPipeBytes);
   uint64_t* empty = full + kStages;
   __shared__ int s_mi;  // merger index of this CTA (-1: not a merger)
+  __shared__ int4 s_tab[kPaged ? kTabTiles : 1];  // paged: this CTA's first kTabTiles table entries
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -518,7 +522,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   }
   __syncthreads();  // barriers initialised before the producer may arm them below
   int staged = 0;   // producer lane: leading tiles already issued before pdl_wait()
-  if (warp == kCWarps && lane == 0 && p.tiles == nullptr) {
+  if (!kPaged && warp == kCWarps && lane == 0) {
     // Before waiting for the previous kernel (it may still be running):
     //  * tiles whose rows the caller declared stable (p.stable_rows, uniform lengths, where n and
     //    the partition come from kernel parameters) are loaded into the pipeline right away;
@@ -563,8 +567,8 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   pdl_launch();
   pdl_wait();  // everything below may read what the previous kernel in the stream wrote
   const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
-  const int64_t seq_tiles = p.tiles ? p.n_tiles : (n + kTile - 1) / kTile;
-  const int nsplit = seq_tiles > 0 ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
+  const int64_t seq_tiles = kPaged ? p.n_tiles : (n + kTile - 1) / kTile;
+  const int nsplit = (kPaged ? seq_tiles > 0 : n > 0) ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
   if (split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
   int64_t tt0, tt1;
   split_range(seq_tiles, split, nsplit, tt0, tt1);
@@ -572,7 +576,22 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
   const int ntiles = (int)(tt1 - tt0);
   if (threadIdx.x == 0) s_mi = -1;
+  if constexpr (kPaged) {
+    // the slice's table entries, loaded once by the whole CTA instead of a dependent global load
+    // in front of every TMA issue and every consumer tile
+    const int nt = ntiles < kTabTiles ? ntiles : kTabTiles;
+    for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+      const int32_t* tt = p.tiles + 3 * (tt0 + i);
+      s_tab[i] = make_int4(tt[0], tt[1], tt[2], 0);
+    }
+  }
   __syncthreads();
+  // (page, first row, rows) of tile j of this slice in paged mode
+  auto tab_entry = [&](int j) -> int4 {
+    if (j < kTabTiles) return s_tab[j];
+    const int32_t* tt = p.tiles + 3 * (tt0 + j);
+    return make_int4(tt[0], tt[1], tt[2], 0);
+  };
 
   if (warp == kCWarps) {
     // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
@@ -593,10 +612,10 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         uint8_t* st = smem + s * G::kStageBytes;
         // rows past the tensor end (or, paged, past the page end) arrive as zeros
         int tok = (int)(t0 + (int64_t)j * kTile), cbj = cb;
-        if (p.tiles) {
-          const int32_t* tt = p.tiles + 3 * (tt0 + j);
-          cbj = tt[0];
-          tok = tt[1];
+        if constexpr (kPaged) {
+          const int4 te = tab_entry(j);
+          cbj = te.x;
+          tok = te.y;
         }
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx) {
@@ -649,8 +668,8 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       const uint32_t kst = smem_u32(stage);
       const uint32_t vst = kst + G::kTileBytes;
       int valid;
-      if (p.tiles) {
-        const int vt = p.tiles[3 * (tt0 + j) + 2];  // device table: clamp into [0, kTile]
+      if constexpr (kPaged) {
+        const int vt = tab_entry(j).z;  // device table: clamp into [0, kTile]
         valid = vt < 0 ? 0 : (vt > kTile ? kTile : vt);
       } else {
         const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
@@ -658,11 +677,12 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       }
       int64_t app_r = -1, app_row = n - 1, app_pg = 0;  // row in the tile, row and page in the cache
       if (p.k_app != nullptr) {
-        if (p.tiles) {
+        if constexpr (kPaged) {
           if (tt0 + j == p.n_tiles - 1 && valid > 0) {
             app_r = valid - 1;
-            app_pg = p.tiles[3 * (tt0 + j)];
-            app_row = p.tiles[3 * (tt0 + j) + 1] + app_r;
+            const int4 te = tab_entry(j);
+            app_pg = te.x;
+            app_row = te.y + app_r;
           }
         } else {
           app_r = (n - 1) - (t0 + (int64_t)j * kTile);

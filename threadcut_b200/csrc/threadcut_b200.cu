@@ -201,7 +201,7 @@ cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st,
 
 template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
-  auto fn = decode_mma_kernel<T, D, NG>;
+  auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true> : decode_mma_kernel<T, D, NG, false>;
   const int smem = MmaGeom<D>::kSmem;
   const int threads = 32 * (kCWarps + 1);
   cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
