@@ -235,8 +235,13 @@ int tc_ragged_encode_tensormaps(void* host_out, const void* const* k_ptrs, const
  * 16-bit dtypes, d in {64, 128, 256}, page_rows >= 32. k_new/v_new (both or neither): the step's
  * new row [hkv][d] (head strides k_new_stride_h/v_new_stride_h) is the last row of the last tile;
  * the cache still holds stale data there and the launch writes the row into the pools while it
- * decodes (fused append). Workspace: tc_decode_attention_workspace_size(1, hkv, g, d,
- * 32 * n_tiles, 0, splits, dtype) bytes, first 16*hkv bytes ZERO before the first call.
+ * decodes (fused append). stable_tiles (as stable_rows of tc_decode_attention_stable): tiles
+ * [0, stable_tiles) of the table, and the rows they list, are written by no kernel that can still
+ * be running when this launch starts, so it may load them before the previous kernel in the stream
+ * has finished; 0 is the plain call. In a decode step over several layers every tile qualifies
+ * except those holding rows the previous launch wrote. Workspace:
+ * tc_decode_attention_workspace_size(1, hkv, g, d, 32 * n_tiles, 0, splits, dtype) bytes, first
+ * 16*hkv bytes ZERO before the first call.
  * ====================================================================================== */
 int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out,
                               int hkv, int g, int d, int64_t page_rows, int64_t num_pages,
@@ -245,7 +250,7 @@ int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_p
                               const void* k_new, const void* v_new, int64_t k_new_stride_h,
                               int64_t v_new_stride_h,
                               int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_h, int64_t out_stride_g,
-                              float scale, int splits, int dtype,
+                              float scale, int splits, int dtype, int64_t stable_tiles,
                               void* workspace, size_t workspace_bytes, void* stream);
 
 /* Re-rotates, in place, the keys of the rows the tile table lists in every layer's K pool

@@ -143,3 +143,26 @@ def test_empty_and_rejected_cases():
     kv32.write(0, torch.randn(8, 4, 128, device=DEV), torch.randn(8, 4, 128, device=DEV))
     with pytest.raises(_lib.TCError):
         kv32.decode(0, torch.randn(8, 4, 128, device=DEV), 0.1)  # decode over pages: 16-bit only
+
+
+@pytest.mark.parametrize("seed,page_rows", [(11, 64), (12, 32)])
+def test_stable_tiles_back_to_back_matches_plain(seed, page_rows):
+    """Layer-by-layer one-token steps with the fused append, launched back to back with every tile
+    but the last declared stable (loaded before the previous launch ends), give the same outputs
+    and pools as the plain calls."""
+    kv_a, _, g = drive(seed, layers=4, page_rows=page_rows)
+    kv_b, _, _ = drive(seed, layers=4, page_rows=page_rows)
+    for step in range(4):
+        qs = [torch.randn(8, 4, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(4)]
+        kn = [torch.randn(8, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(4)]
+        vn = [torch.randn(8, 128, generator=g, device=DEV).to(torch.bfloat16) for _ in range(4)]
+        kv_a.reserve(1)
+        kv_b.reserve(1)
+        want = [kv_a.decode(l, qs[l], 0.09, k_new=kn[l], v_new=vn[l]) for l in range(4)]
+        got = [kv_b.decode(l, qs[l], 0.09, k_new=kn[l], v_new=vn[l], stable_tiles=kv_b.n_tiles - 1)
+               for l in range(4)]
+        torch.cuda.synchronize()
+        for l in range(4):
+            assert torch.equal(got[l], want[l]), (step, l)
+    for l in range(4):
+        assert torch.equal(kv_a.k[l], kv_b.k[l]) and torch.equal(kv_a.v[l], kv_b.v[l])

@@ -57,7 +57,7 @@ SIGNATURES = {
     "tc_splice_copy": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i64, _i64, _i64] + [_i64] * 4 + [_fp, _i, _vp]),
     "tc_merge_partials": (_i, [_vp, _vp, _vp, _vp, _i, _i64, _i, _i64, _i, _vp]),
     "tc_decode_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64,
-                                       _i64, _vp, _vp, _i64, _i64] + [_i64] * 4 + [_f, _i, _i, _vp, _sz, _vp]),
+                                       _i64, _vp, _vp, _i64, _i64] + [_i64] * 4 + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_paged_rotate_keys": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _fp,
                                   _i, _vp]),
     "tc_paged_write": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i64] + [_i64] * 4 + [_i64] * 5 + [_vp, _i, _vp]),

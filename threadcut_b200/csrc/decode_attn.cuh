@@ -101,6 +101,8 @@ struct DecodeParams {
   // (k_app) is the last row of the last tile. Null: contiguous rows.
   const int32_t* tiles;
   int64_t n_tiles;
+  int64_t stable_tiles;  // paged: tiles [0, stable_tiles) and their rows are written by no kernel
+                         // that can still be running when this one starts (0: none)
 };
 
 // Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
@@ -564,6 +566,25 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         }
     }
   }
+  int tab_pre = 0;  // paged: leading slice entries already in s_tab before pdl_wait()
+  if constexpr (kPaged) {
+    // paged: the split comes from kernel parameters, so the slice's leading entries that the caller
+    // declared stable (p.stable_tiles) are loaded into s_tab by the whole CTA before waiting for the
+    // previous kernel. (Starting their K/V copies here too, as the contiguous path does for its
+    // stable rows, measured slower for paged decode, so the copies wait for the producer loop.)
+    const int64_t nt = p.n_tiles;
+    const int ns = nt > 0 ? (int)((nt + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
+    if (nt > 0 && split < ns && p.stable_tiles > 0) {
+      int64_t a0, a1;
+      split_range(nt, split, ns, a0, a1);
+      const int64_t lim = (a1 < p.stable_tiles ? a1 : p.stable_tiles) - a0;
+      tab_pre = lim <= 0 ? 0 : (lim < kTabTiles ? (int)lim : kTabTiles);
+      for (int i = threadIdx.x; i < tab_pre; i += blockDim.x) {
+        const int32_t* tt = p.tiles + 3 * (a0 + i);
+        s_tab[i] = make_int4(tt[0], tt[1], tt[2], 0);
+      }
+    }
+  }
   pdl_launch();
   pdl_wait();  // everything below may read what the previous kernel in the stream wrote
   const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
@@ -580,7 +601,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     // the slice's table entries, loaded once by the whole CTA instead of a dependent global load
     // in front of every TMA issue and every consumer tile
     const int nt = ntiles < kTabTiles ? ntiles : kTabTiles;
-    for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+    for (int i = tab_pre + threadIdx.x; i < nt; i += blockDim.x) {
       const int32_t* tt = p.tiles + 3 * (tt0 + i);
       s_tab[i] = make_int4(tt[0], tt[1], tt[2], 0);
     }

@@ -709,9 +709,10 @@ int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_p
                               int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* tiles, int64_t n_tiles,
                               int64_t n_tokens, const void* k_new, const void* v_new, int64_t k_new_stride_h,
                               int64_t v_new_stride_h, int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_h,
-                              int64_t out_stride_g, float scale, int splits, int dtype, void* workspace,
-                              size_t workspace_bytes, void* stream) {
+                              int64_t out_stride_g, float scale, int splits, int dtype, int64_t stable_tiles,
+                              void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (stable_tiles < 0) return TC_ERR_INVALID;
   if (!mma_dim(d) || hkv < 1 || g < 1 || page_rows < kTile || page_rows > (1 << 30) || num_pages < 1 ||
       num_pages > (1 << 30) || n_tiles < 0 || n_tiles > ((int64_t)1 << 31) / kTile || n_tokens < 0)
     return TC_ERR_INVALID;
@@ -731,6 +732,7 @@ int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_p
     return TC_ERR_INVALID;
   p.tiles = tiles;
   p.n_tiles = n_tiles;
+  p.stable_tiles = stable_tiles < n_tiles ? stable_tiles : n_tiles;
   p.q = q;
   p.out = out;
   p.lse_b = (int64_t)hkv * g;

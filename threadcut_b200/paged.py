@@ -253,6 +253,10 @@ class PagedKV:
     def n(self):
         return self.table.n
 
+    @property
+    def n_tiles(self):
+        return self.table.tiles().shape[0]
+
     def _strides(self):
         s = self.k[0].stride()
         return s[0], s[1], s[2]
@@ -300,10 +304,13 @@ class PagedKV:
                 k.stride(0), k.stride(1), v.stride(0), v.stride(1), self.page_rows, self.table.num_pages,
                 sp, sh, sr, self._slots.data_ptr(), dtype_code(k, "PagedKV.write"), stream_ptr(self.device)))
 
-    def decode(self, layer, q, scale, *, k_new=None, v_new=None, splits=None):
+    def decode(self, layer, q, scale, *, k_new=None, v_new=None, splits=None, stable_tiles=0):
         """Decode attention of q [hkv, g, d] over the whole sequence (threadcut/flash_decode.py:57-69
         semantics). With k_new/v_new [hkv, d] the last reserved row (a one-token step) is written by
-        the same launch (fused append)."""
+        the same launch (fused append). stable_tiles: the leading tiles of the table (see
+        `n_tiles`) whose rows no kernel still running writes, which the launch may load before the
+        previous one ends (0: none; n_tiles - 1 in a layer-by-layer decode step with fused append,
+        where each launch writes only the last row of its own layer)."""
         require_cuda(q, what="PagedKV.decode")
         hkv, g, d = q.shape
         if hkv != self.hkv or d != self.d or q.dtype != self.dtype:
@@ -333,7 +340,8 @@ class PagedKV:
                 nt, self.table.n, k_new.data_ptr() if k_new is not None else None,
                 v_new.data_ptr() if v_new is not None else None, k_new.stride(0) if k_new is not None else 0,
                 v_new.stride(0) if v_new is not None else 0, q.stride(0), q.stride(1), out.stride(0), out.stride(1),
-                float(scale), int(splits or 0), code, ws.data_ptr(), ws.numel(), stream_ptr(q.device)))
+                float(scale), int(splits or 0), code, int(stable_tiles), ws.data_ptr(), ws.numel(),
+                stream_ptr(q.device)))
         return out
 
     # ---------------------------------------------------------------- splice
