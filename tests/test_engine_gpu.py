@@ -163,3 +163,36 @@ def test_cfg5_full_model_128k_spliced_top1_matches_sdpa():
     assert int(ours.argmax()) == int(ref.argmax())
     # bf16 logits through 36 layers differ by rounding noise; the distributions must still agree
     assert torch.corrcoef(torch.stack([ours, ref]))[0, 1].item() > 0.999
+
+
+def small_bf16_engine(paged):
+    """bf16, head_dim 128, 4 query heads per KV head: the paged decode and the tcgen05 prefill run."""
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME).to(DEV)
+    return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=64,
+                  max_ctx=4096, paged=paged)
+
+
+def test_paged_engine_matches_the_contiguous_engine():
+    """The engine on a paged cache (splice = page drop + in-place key rotation, decode over pages with
+    the fused append) against the same engine on the reference's contiguous layout: identical
+    tokens while the pages hold the sequence in order, and after a splice turn the same reuse and
+    last logits within the bf16 tolerance of T2."""
+    from threadcut_b200.kv import PagedLayer
+    eng_p, eng_c = small_bf16_engine(True), small_bf16_engine(False)
+    p1 = rand_ids(150, 11)
+    out_p, st_p = eng_p.generate(p1, max_new_tokens=20)
+    out_c, st_c = eng_c.generate(p1, max_new_tokens=20)
+    assert isinstance(eng_p.cache.layers[0], PagedLayer)
+    assert out_p == out_c and st_p["kv_tokens"] == st_c["kv_tokens"] and st_p["kv_mb"] == st_c["kv_mb"]
+    A, B, C, D = p1[:40], p1[40:97], p1[97:] + out_p, rand_ids(9, 12)
+    with torch.no_grad():
+        lp, sp = eng_p.load(A + C + D)
+        lc, sc = eng_c.load(A + C + D)
+    assert (sp["reused_prefix"], sp["reused_suffix"]) == (sc["reused_prefix"], sc["reused_suffix"]) == (40, len(C))
+    assert eng_p.cache.get_seq_length() == len(A + C + D)
+    assert torch.allclose(lp.float(), lc.float(), atol=3e-2, rtol=0)
+    out_p2, _ = eng_p.generate(A + C + D + rand_ids(3, 13), max_new_tokens=8)
+    assert len(out_p2) > 0

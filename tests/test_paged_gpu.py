@@ -166,3 +166,18 @@ def test_stable_tiles_back_to_back_matches_plain(seed, page_rows):
             assert torch.equal(got[l], want[l]), (step, l)
     for l in range(4):
         assert torch.equal(kv_a.k[l], kv_b.k[l]) and torch.equal(kv_a.v[l], kv_b.v[l])
+
+
+def test_compact_repacks_in_order_and_keeps_the_contents():
+    kv, ref, g = drive(13, page_rows=64)
+    before = [kv.gather(l) for l in range(kv.layers)]
+    kv.compact()
+    runs = kv.table.runs
+    assert [r[0] for r in runs] == list(range(len(runs))) and all(r[1] == 0 for r in runs)
+    for l in range(kv.layers):
+        k, v = kv.gather(l)
+        assert torch.equal(k, before[l][0]) and torch.equal(v, before[l][1])
+    q = torch.randn(kv.hkv, 4, 128, generator=g, device=DEV).to(torch.bfloat16)
+    out = kv.decode(0, q, 0.088)
+    torch.cuda.synchronize()
+    assert attn_error(f32(out), decode_attention_ref(f32(q), ref.k[0], ref.v[0], 0.088), torch.bfloat16) <= ATTN_ATOL

@@ -11,7 +11,7 @@ import torch
 from transformers import AutoModelForCausalLM, AutoTokenizer
 
 from . import attention
-from .kv import new_cache, splice
+from .kv import cache_bytes, new_cache, splice
 from .match import split
 
 __all__ = ["Engine", "sync"]
@@ -24,7 +24,7 @@ def sync(device):
 
 class Engine:
     def __init__(self, model_path, device="cuda", dtype=torch.float16, suffix=True, min_suffix=32,
-                 max_ctx=32768, prefill_chunk=2048, model=None, tokenizer=None):
+                 max_ctx=32768, prefill_chunk=2048, model=None, tokenizer=None, paged=False):
         self.device = torch.device(device)
         self.tok = tokenizer or AutoTokenizer.from_pretrained(model_path)
         self.model = model or AutoModelForCausalLM.from_pretrained(
@@ -39,6 +39,7 @@ class Engine:
         self.inv_freq = self.model.model.rotary_emb.inv_freq
         self.suffix, self.min_suffix = suffix, min_suffix
         self.max_ctx, self.prefill_chunk = max_ctx, prefill_chunk
+        self.paged = paged  # K/V in pages: a splice frees B's pages and rotates C's keys in place
         self.stop_ids = {self.tok.eos_token_id, self.tok.convert_tokens_to_ids("<|im_end|>")}
         self.reset()
 
@@ -58,7 +59,7 @@ class Engine:
         """Bring the cache to `new_ids` with as little compute as possible. Returns (last logits, stats)."""
         s = split(self.ids, new_ids, self.min_suffix, self.suffix) if self.cache is not None else None
         if s is None or (s.a == 0 and s.c == 0):
-            self.cache, reused = new_cache(self.model.config), 0
+            self.cache, reused = new_cache(self.model.config, paged=self.paged, max_tokens=self.max_ctx), 0
         else:
             splice(self.cache, s, self.inv_freq)
             reused = s.a + s.c
@@ -103,8 +104,7 @@ class Engine:
         t2 = time.perf_counter()
         self.ids += out
         kv_tokens = self.cache.get_seq_length()
-        layer = self.cache.layers[0]
-        kv_bytes = 2 * kv_tokens * layer.keys[0, :, 0].numel() * layer.keys.element_size() * len(self.cache.layers)
+        kv_bytes = cache_bytes(self.cache)
         stats.update(completion_tokens=len(out), finish=finish, ttft_s=t1 - t0, decode_s=t2 - t1,
                      kv_tokens=kv_tokens, kv_mb=kv_bytes / 2**20)
         return out, stats

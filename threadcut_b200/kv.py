@@ -107,6 +107,12 @@ def _same_geometry(layers):
 def splice(cache, s: Split, inv_freq):
     """Rewrite every layer of a DynamicCache from A.B.C.(tail) to A.C."""
     layers = cache.layers
+    if layers and all(isinstance(layer, PagedLayer) for layer in layers):
+        state = layers[0].state
+        state.flush_all()
+        if state.kv is not None:
+            state.kv.splice(s, inv_freq)  # B's pages freed, C's keys re-rotated in place
+        return
     if all(isinstance(layer, GrowingLayer) for layer in layers):
         live = [ly for ly in layers if ly.kbuf is not None]
         if s.c and s.gap and live:
@@ -251,10 +257,140 @@ def flush_pending(key):
         layer._flush()
 
 
-def new_cache(config):
+_PAGED_PENDING = {}  # data_ptr of a step's key_states -> the PagedLayer whose row is pending
+
+
+class _PagedState:
+    """The PagedKV shared by the PagedLayers of one cache, created at the first update (when the
+    head count, head size, dtype and device are known)."""
+
+    def __init__(self, layers, max_tokens, page_rows, fuse):
+        self.kv = None
+        self.layers, self.max_tokens, self.page_rows, self.fuse = layers, max_tokens, page_rows, fuse
+        self.members = []
+
+    def ensure(self, key_states):
+        if self.kv is None:
+            from .paged import PagedKV
+            _, hkv, _, d = key_states.shape
+            pages = -(-self.max_tokens // self.page_rows)
+            self.kv = PagedKV(self.layers, hkv, d, max_tokens=self.max_tokens, page_rows=self.page_rows,
+                              dtype=key_states.dtype, device=key_states.device, spare_pages=max(64, pages // 4))
+            self.fuse = (self.fuse and key_states.is_cuda and key_states.dtype in (torch.bfloat16, torch.float16)
+                         and d in (64, 128, 256))
+
+    def flush_all(self):
+        for ly in self.members:
+            ly._flush()
+
+
+class PagedLayer(DynamicLayer):
+    """Cache layer over a paged K/V store (threadcut_b200.paged.PagedKV, the layout threadcut's
+    README.md:141-144 names as the next step); all layers of a cache share one PagedKV. Appends go
+    into page slots (layer 0 reserves them for every layer of the step), a splice drops B's pages
+    and re-rotates C's keys in place (kv.splice), and a one-token step with the threadcut attention
+    leaves the new row pending: the plugin's decode branch writes it in the launch that attends over
+    the pages. Prefill chunks (and any other reader) get a contiguous copy of the layer's K/V."""
+
+    def __init__(self, state, index):
+        super().__init__()
+        self.state, self.index = state, index
+        self._pending = None
+        state.members.append(self)
+
+    def lazy_initialization(self, key_states, value_states, *args, **kwargs):
+        super().lazy_initialization(key_states, value_states)
+        self.state.ensure(key_states)
+
+    def get_seq_length(self):
+        return self.state.kv.n if self.state.kv is not None else 0
+
+    def _flush(self):
+        pend = self._pending
+        if pend is not None:
+            self._pending = None
+            _PAGED_PENDING.pop(pend[2], None)
+            self.state.kv.write(self.index, pend[0][:, None], pend[1][:, None])
+
+    def update(self, key_states, value_states, *args, **kwargs):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        if key_states.shape[0] != 1:
+            raise ValueError("PagedLayer: one sequence per cache (batch 1)")
+        kv = self.state.kv
+        t = key_states.shape[-2]
+        if self.index == 0:
+            self.state.flush_all()
+            try:
+                kv.reserve(t)
+            except MemoryError:
+                kv.compact()
+                kv.reserve(t)
+        if t == 1 and self.state.fuse:
+            self._pending = (key_states[0, :, 0, :], value_states[0, :, 0, :], key_states.data_ptr())
+            _PAGED_PENDING[key_states.data_ptr()] = self
+            return key_states, value_states  # stand-ins: the plugin's decode branch reads the pages
+        kv.write(self.index, key_states[0], value_states[0])
+        k, v = kv.gather(self.index)
+        return k[None], v[None]
+
+    def decode(self, q, scale):
+        """The step's attention for the threadcut plugin: q [hkv, g, d] over the pages with the
+        pending row written by the same launch."""
+        k, v, ptr = self._pending
+        self._pending = None
+        _PAGED_PENDING.pop(ptr, None)
+        kv = self.state.kv
+        return kv.decode(self.index, q, scale, k_new=k, v_new=v, stable_tiles=kv.n_tiles - 1)
+
+    def materialize(self):
+        """Writes the pending row and returns contiguous (K, V) [1, hkv, n, d] (other readers)."""
+        self._flush()
+        k, v = self.state.kv.gather(self.index)
+        return k[None], v[None]
+
+    def crop(self, max_length):
+        self.state.flush_all()
+        n = self.get_seq_length()
+        if max_length < 0:
+            max_length = n - abs(max_length)
+        if self.state.kv is not None and n > max_length:
+            self.state.kv.truncate(max_length)
+
+
+def paged_pending(key):
+    """The PagedLayer whose step row stands behind `key` (a stand-in returned by update), or None."""
+    if not _PAGED_PENDING or not key.is_cuda:
+        return None
+    layer = _PAGED_PENDING.get(key.data_ptr())
+    if layer is None or layer._pending is None:
+        return None
+    return layer
+
+
+def new_cache(config, paged=False, max_tokens=32768, page_rows=64):
+    """A DynamicCache of GrowingLayers (the reference's layout, threadcut/kv.py:44-98) or, with
+    paged=True, of PagedLayers over one PagedKV sized for max_tokens (plus spare pages for the
+    partly used pages splices leave; a full pool is re-packed by PagedKV.compact)."""
     cache = DynamicCache(config=config)
+    fused = getattr(config, "_attn_implementation", None) == FUSED_ATTENTION
+    if paged:
+        state = _PagedState(len(cache.layers), int(max_tokens), int(page_rows), fused)
+        cache.layers = [PagedLayer(state, i) for i in range(len(cache.layers))]
+        return cache
     cache.layers = [GrowingLayer() for _ in cache.layers]
-    if getattr(config, "_attn_implementation", None) == FUSED_ATTENTION:
+    if fused:
         for layer in cache.layers:
             layer.fuse_append = True  # the decode branch of threadcut_b200.attention writes the row
     return cache
+
+
+def cache_bytes(cache):
+    """Bytes of the live K and V of every layer (paged or contiguous)."""
+    layers = cache.layers
+    if layers and isinstance(layers[0], PagedLayer):
+        kv = layers[0].state.kv
+        return 0 if kv is None else 2 * kv.n * kv.hkv * kv.d * kv.k[0].element_size() * kv.layers
+    n = cache.get_seq_length()
+    layer = layers[0]
+    return 2 * n * layer.keys[0, :, 0].numel() * layer.keys.element_size() * len(layers)

@@ -365,6 +365,21 @@ class PagedKV:
     def truncate(self, n):
         self.table.truncate(n)
 
+    def compact(self):
+        """Re-packs the sequence into pages in logical order (one copy of every layer's K and V into
+        fresh pools), for when splices have left so many partly used pages that an append finds no
+        free page. Peak memory: the old and the new pools."""
+        new = PagedKV(self.layers, self.hkv, self.d, max_tokens=self.table.num_pages * self.page_rows,
+                      page_rows=self.page_rows, dtype=self.dtype, device=self.device, spare_pages=0)
+        n = self.n
+        if n:
+            new.reserve(n)
+            for l in range(self.layers):
+                k, v = self.gather(l)
+                new.write(l, k, v)
+                self.k[l] = self.v[l] = None  # free the old pools layer by layer
+        self.__dict__.update(new.__dict__)
+
     # ---------------------------------------------------------------- views
     def gather(self, layer):
         """Contiguous copies (K, V) [hkv, n, d] of one layer in logical order (torch indexing; for
