@@ -414,7 +414,38 @@ def time_paged(steps, warmup, dev, dist, layers=LAYERS):
     rot_ms = e0.elapsed_time(e1) / steps
     del kv, cs
     torch.cuda.empty_cache()
-    return dec_ms, rot_ms, 2 * c * 8 * 128 * 2, host_us, tiles
+    # (3) prefill of a 512-token chunk over a spliced 98k-token paged cache: straight over the pages
+    # vs gather-then-contiguous-kernel (the gather is what a paged cache without it would pay)
+    from threadcut_b200.prefill import prefill_attention
+    kv = PagedKV(1, 8, 128, max_tokens=100000, page_rows=64, device=dev)
+    kv.reserve(99000)
+    kv.write(0, torch.randn(8, 99000, 128, generator=g, device=dev).to(torch.bfloat16),
+             torch.randn(8, 99000, 128, generator=g, device=dev).to(torch.bfloat16))
+    kv.splice(Split(1000, 1726, 97274), workloads.inv_freq())  # 98,274 tokens, runs cut inside pages
+    kv.reserve(512)
+    kv.write(0, torch.randn(8, 512, 128, generator=g, device=dev).to(torch.bfloat16),
+             torch.randn(8, 512, 128, generator=g, device=dev).to(torch.bfloat16))
+    q = torch.randn(1, 32, 512, 128, generator=g, device=dev).to(torch.bfloat16)
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / reps
+    pf_paged = timed(lambda: kv.prefill(0, q, workloads.SCALE))
+    kc, vc = kv.gather(0)
+    pf_contig = timed(lambda: prefill_attention(q, kc[None], vc[None], workloads.SCALE))
+    pf_gather = timed(lambda: kv.gather(0))
+    n_pf = kv.n
+    del kv, kc, vc, q
+    torch.cuda.empty_cache()
+    return dec_ms, rot_ms, 2 * c * 8 * 128 * 2, host_us, tiles, (pf_paged, pf_contig, pf_gather, n_pf)
 
 
 def time_split_128k(dev, reps=20):
@@ -631,7 +662,7 @@ def run_ours(args, rank, local, world, dist):
             "frac": round(c4_bytes / (c4_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4), "bytes_per_layer": c4_bytes,
             "workload": "cfg4: 64 ragged sequences, lengths uniform in [1024,16384] (seeded), per-sequence bf16 "
                         "K/V caches, 32 q / 8 kv heads, d 128, 36 launches per step over 2 distinct layer caches"}
-    pg_dec_ms, pg_rot_ms, pg_rot_bytes, pg_host_us, pg_tiles = time_paged(args.steps, args.warmup, dev, dist)
+    pg_dec_ms, pg_rot_ms, pg_rot_bytes, pg_host_us, pg_tiles, pg_pf = time_paged(args.steps, args.warmup, dev, dist)
     pg_dec_ms, pg_rot_ms = max_over_ranks(pg_dec_ms, dist), max_over_ranks(pg_rot_ms, dist)
     split_dev_us, split_host_us = time_split_128k(dev)
     pf_ms, pf_gqa_ms, pf_ref_ms, pf_flops = time_prefill(min(args.steps, 10), args.warmup, dev)
@@ -700,10 +731,14 @@ def run_ours(args, rank, local, world, dist):
             "splice_cfg2_frac": round(pg_rot_bytes * LAYERS / (pg_rot_ms * 1e-3) / 1e9 / hbm, 4),
             "splice_cfg2_bytes_per_layer": pg_rot_bytes,
             "splice_cfg2_host_table_us": round(pg_host_us, 2),
+            "prefill_512_ms": round(pg_pf[0], 4), "prefill_512_contiguous_ms": round(pg_pf[1], 4),
+            "gather_ms": round(pg_pf[2], 4), "prefill_cache_tokens": pg_pf[3],
             "what": "paged K/V cache (64-row pages): decode of the 36-layer 16k step over ragged runs (a splice "
                     "cut inside pages), and the cfg2 splice Split(2048,4096,4096) as B's pages dropped on the "
                     "host + C's keys re-rotated in place (values never move: half the contiguous splice's bytes); "
-                    "compare decode with the headline value and the splice with shift.us_per_layer"},
+                    "compare decode with the headline value and the splice with shift.us_per_layer; prefill: a 512-token "
+                    "chunk over a spliced ~98k-token paged cache straight over the pages vs the contiguous kernel on "
+                    "a gathered copy (gather_ms = that copy)"},
         "split_128k": {"device_us": round(split_dev_us, 1), "host_numpy_us": round(split_host_us, 1),
                        "what": "match.split of a 128k cached / 97k new request: tc_split (tokens on the GPU, "
                                "result read back, wall clock) vs the host rule on Python lists"},

@@ -14,7 +14,7 @@
  *                             threadcut/kv.py:28-33             splice(cache, s, inv_freq), all layers
  *   tc_splice_copy            threadcut/kv.py:34-41             splice(...) copy path (non-growing caches)
  *   tc_merge_partials         threadcut/flash_decode.py:68-69   softmax(lse) merge of split partials
- *   tc_decode_attention_paged, tc_paged_rotate_keys, tc_paged_write
+ *   tc_decode_attention_paged, tc_prefill_attention_paged, tc_paged_rotate_keys, tc_paged_write
  *                             threadcut/README.md:141-144       the paged KV layout named there as the next
  *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
  *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
@@ -252,6 +252,21 @@ int tc_decode_attention_paged(const void* q, const void* k_pool, const void* v_p
                               int64_t q_stride_h, int64_t q_stride_g, int64_t out_stride_h, int64_t out_stride_g,
                               float scale, int splits, int dtype, int64_t stable_tiles,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Causal prefill over a paged cache (as tc_prefill_attention, the causal-over-cache mask: query p
+ * sees logical keys [0, lk - lq + p]): the lk logical keys are the rows of a sub-tile table
+ * `ktab` (DEVICE int32 [n_sub][4] = page, first row, rows <= 32, logical position of the first
+ * row; consecutive in logical order, 16-byte aligned), key tile j being sub-tiles [4j, 4j + 4);
+ * qb_tiles (DEVICE int32, one per 64-query block) = the key tiles with a logical start below
+ * min(lk, lk - lq + 64 * (block + 1)), at least 1. Pool rows that no sub-tile lists must hold
+ * finite values (masked slots meet them with a zero weight). hq = 4 * hkv, d = 128, 16-bit.
+ * Workspace as tc_prefill_workspace_size(hq, hkv, lq, 128 * ceil(n_sub / 4), splits). */
+int tc_prefill_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out, int hq, int hkv,
+                               int lq, int lk, int d, int64_t page_rows, int64_t num_pages, int64_t pool_stride_page,
+                               int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* ktab, int64_t n_sub,
+                               const int32_t* qb_tiles, int64_t q_stride_h, int64_t q_stride_p,
+                               int64_t out_stride_p, int64_t out_stride_h, float scale, int splits, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
 
 /* Re-rotates, in place, the keys of the rows the tile table lists in every layer's K pool
  * (k_pools: HOST array of `layers` device pointers, layers <= 128) by one RoPE delta (cos_sin as

@@ -181,3 +181,59 @@ def test_compact_repacks_in_order_and_keeps_the_contents():
     out = kv.decode(0, q, 0.088)
     torch.cuda.synchronize()
     assert attn_error(f32(out), decode_attention_ref(f32(q), ref.k[0], ref.v[0], 0.088), torch.bfloat16) <= ATTN_ATOL
+
+
+def prefill_reference(q, k, v, scale):
+    """fp32 SDPA with the causal-over-cache mask on the gathered (contiguous) cache."""
+    from threadcut_b200.prefill import causal_offset_mask
+    hq, hkv = q.shape[1], k.shape[1]
+    kk = k.float().repeat_interleave(hq // hkv, 1)
+    vv = v.float().repeat_interleave(hq // hkv, 1)
+    mask = causal_offset_mask(q.shape[2], k.shape[2], q.device)
+    return torch.nn.functional.scaled_dot_product_attention(q.float(), kk, vv, attn_mask=mask,
+                                                            scale=scale).transpose(1, 2)
+
+
+@pytest.mark.parametrize("seed,page_rows,hkv,lq", [(14, 64, 8, 1), (15, 64, 8, 200), (16, 32, 2, 64), (17, 96, 8, 65),
+                                                   (18, 128, 2, 300), (19, 64, 2, 7)])
+@pytest.mark.parametrize("splits", [None, 1, 3])
+def test_paged_prefill_matches_the_reference(seed, page_rows, hkv, lq, splits):
+    """A prefill chunk appended after random appends and splices (ragged runs, runs starting inside
+    pages) attends over the pages directly, within the prefill kernel's 1e-2 of fp32 SDPA on the
+    gathered cache."""
+    kv, _, g = drive(seed, layers=1, hkv=hkv, page_rows=page_rows)
+    kv.reserve(lq)
+    kv.write(0, torch.randn(hkv, lq, 128, generator=g, device=DEV).to(torch.bfloat16),
+             torch.randn(hkv, lq, 128, generator=g, device=DEV).to(torch.bfloat16))
+    q = torch.randn(1, 4 * hkv, lq, 128, generator=g, device=DEV).to(torch.bfloat16)
+    out = kv.prefill(0, q, 0.0883, splits=splits)
+    torch.cuda.synchronize()
+    k, v = kv.gather(0)
+    err = (out.float() - prefill_reference(q, k[None], v[None], 0.0883)).abs().max().item()
+    assert out.shape == (1, lq, 4 * hkv, 128) and err <= 1e-2, (seed, lq, splits, err)
+
+
+def test_paged_prefill_long_cache_and_fresh_sequence():
+    """A 512-token chunk over a 20k-token spliced cache, and a first chunk (cache = the chunk)."""
+    g = torch.Generator(device=DEV).manual_seed(20)
+    inv_freq = torch.as_tensor(inv_freq_default(128, 1e6), dtype=torch.float32)
+    kv = PagedKV(1, 8, 128, max_tokens=24000, device=DEV)
+    kv.reserve(22000)
+    kv.write(0, torch.randn(8, 22000, 128, generator=g, device=DEV).to(torch.bfloat16),
+             torch.randn(8, 22000, 128, generator=g, device=DEV).to(torch.bfloat16))
+    kv.splice(Split(3001, 5077, 16000), inv_freq)
+    kv.reserve(512)
+    kv.write(0, torch.randn(8, 512, 128, generator=g, device=DEV).to(torch.bfloat16),
+             torch.randn(8, 512, 128, generator=g, device=DEV).to(torch.bfloat16))
+    q = torch.randn(1, 32, 512, 128, generator=g, device=DEV).to(torch.bfloat16)
+    out = kv.prefill(0, q, 0.0883)
+    k, v = kv.gather(0)
+    assert (out.float() - prefill_reference(q, k[None], v[None], 0.0883)).abs().max().item() <= 1e-2
+    fresh = PagedKV(1, 8, 128, max_tokens=300, device=DEV)
+    fresh.reserve(300)
+    fresh.write(0, torch.randn(8, 300, 128, generator=g, device=DEV).to(torch.bfloat16),
+                torch.randn(8, 300, 128, generator=g, device=DEV).to(torch.bfloat16))
+    q = torch.randn(1, 32, 300, 128, generator=g, device=DEV).to(torch.bfloat16)
+    out = fresh.prefill(0, q, 0.0883)
+    k, v = fresh.gather(0)
+    assert (out.float() - prefill_reference(q, k[None], v[None], 0.0883)).abs().max().item() <= 1e-2

@@ -11,8 +11,9 @@ the unexpanded cache, b == 1 through decode_attention and b > 1 through decode_a
 (the reference used folded SDPA there). When the cache is a GrowingLayer whose newest row is still
 pending (fused append, set up by new_cache for this attention), that row is written by the same
 launch (decode_attention_append) instead of a separate copy before attention (kv.py:71-72).
-With a paged cache (kv.new_cache(..., paged=True)) the one-token step's key is a stand-in and the
-decode runs over the pages (PagedKV.decode, fused append); other branches get a contiguous copy.
+With a paged cache (kv.new_cache(..., paged=True)) the key is a stand-in: the one-token step decodes
+over the pages (PagedKV.decode, fused append), a causal prefill chunk runs the tcgen05 kernel over
+the pages (PagedKV.prefill), and other branches get a contiguous copy.
 Decode on a non-CUDA tensor raises: there is no CPU path.
 Prefill (q > 1 or a mask): a causal prefill over the cache (query p sees keys up to lk - lq + p;
 b == 1, 4 query heads per KV head, head_dim 128, 16-bit) runs the tcgen05 kernel of
@@ -70,10 +71,13 @@ def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=No
     scaling = scaling if scaling is not None else d ** -0.5
     paged = paged_pending(key)
     if paged is not None:
-        if q == 1 and attention_mask is None and b == 1:
+        if q == 1 and attention_mask is None and b == 1 and paged._pending is not None:
             # paged cache, one-token step: attend over the pages, the step's row written by the launch
             out = paged.decode(query.reshape(hkv, g, d), scaling).reshape(1, hq, 1, d)
             return out.transpose(1, 2).contiguous(), None
+        if paged.can_prefill(query) and _is_causal_offset(attention_mask, q, paged.get_seq_length()):
+            # paged cache, prefill chunk (rows already in the pages): tcgen05 kernel over the pages
+            return paged.prefill(query, scaling), None
         key, value = paged.materialize()
     layer = pending_append(key)
     if q == 1 and attention_mask is None and b == 1 and layer is not None:

@@ -63,13 +63,22 @@ struct PrefillParams {
   int nsplit;       // KV splits (grid.z); > 1: fp32 partials + LSE per split, merged afterwards
   float* o_part;    // [nsplit][lq*hq][128] normalised partial outputs (row = position*hq + head)
   float* lse_part;  // [nsplit][lq*hq] natural-log LSE of each partial
+  // paged (prefill_kernel<T, true>): K and V live in pages; key tile j is the 32-row sub-tiles
+  // [4j, 4j + 4) of ktab (page, first row, rows <= 32, logical position of the first row), loaded
+  // as four boxes (64, 32) of (d, page rows, heads, pages) maps; a sub-tile past n_sub is loaded
+  // from page oob_page (past the pool: zeros) and masked. qb_tiles[qb] = key tiles visible to
+  // query block qb (host-computed from the logical positions).
+  const int4* ktab;
+  int n_sub;
+  int oob_page;
+  const int32_t* qb_tiles;
 };
 
 // TMEM columns (fp32 words) of Q tile x: S (and P over its first 64 columns), then O.
 __device__ __forceinline__ uint32_t pf_col_s(int x) { return (uint32_t)(x * 128); }
 __device__ __forceinline__ uint32_t pf_col_o(int x) { return (uint32_t)(256 + x * 128); }
 
-template <typename T>
+template <typename T, bool kPaged>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -87,7 +96,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   const int p0 = qb * kPfQ * kPfTiles;  // first position of Q tile 0; tile x starts at p0 + 32x
   const int off = p.lk - p.lq;          // key j is visible to position pos iff j <= off + pos
   const int kend = p.lk < off + p0 + kPfQ * kPfTiles ? p.lk : off + p0 + kPfQ * kPfTiles;
-  const int ntot = (kend + kPfKeys - 1) / kPfKeys;  // >= 1: key 0 is visible to every position
+  // >= 1: key 0 is visible to every position
+  const int ntot = kPaged ? p.qb_tiles[qb] : (kend + kPfKeys - 1) / kPfKeys;
   const int t_lo = (int)((int64_t)ntot * split / p.nsplit);
   const int ntile = (int)((int64_t)ntot * (split + 1) / p.nsplit) - t_lo;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -128,8 +138,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         for (int bx = 0; bx < 2; ++bx)
           tma_load_4d(sQ + x * 32768 + bx * 16384, &p.tmq, bx * 64, p0 + kPfQ * x, h * kPfGroup, 0, &q_full, pol);
       int armed = 0;  // K/V tiles whose copies were issued
+      int4 nxt[4];      // paged: the next tile's sub-tile entries, read one tile ahead
+      auto fetch = [&](int j) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int si = 4 * (t_lo + j) + c;
+          nxt[c] = si < p.n_sub ? p.ktab[si] : make_int4(p.oob_page, 0, 0, 0);
+        }
+      };
+      if (kPaged && ntile > 0) fetch(0);
       for (int j = 0; j < ntile; ++j) {
         const int s = j & 1;
+        int4 cur[4];
+        if constexpr (kPaged) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
+          if (j + 1 < ntile) fetch(j + 1);
+        }
         if (s_abort) break;
         if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, TC_DEVERR_PIPE_TIMEOUT, kPfSpin)) {
           s_abort = 1;
@@ -137,9 +162,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         }
         mbar_arrive_expect_tx(&kv_full[s], 65536u);
         uint8_t* st = sKV + s * 65536;
-        for (int bx = 0; bx < 2; ++bx) {
-          tma_load_4d(st + bx * 16384, &p.tmk, bx * 64, (t_lo + j) * kPfKeys, h, 0, &kv_full[s], pol);
-          tma_load_4d(st + 32768 + bx * 16384, &p.tmv, bx * 64, (t_lo + j) * kPfKeys, h, 0, &kv_full[s], pol);
+        if constexpr (kPaged) {
+          // four 32-row boxes per 64 columns, at row offsets 0/32/64/96 of the 128-row swizzled tile
+          // (the 128-byte swizzle repeats every 8 rows, so the tile image is the contiguous one)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            for (int bx = 0; bx < 2; ++bx) {
+              tma_load_4d(st + bx * 16384 + c * 4096, &p.tmk, bx * 64, cur[c].y, h, cur[c].x, &kv_full[s], pol);
+              tma_load_4d(st + 32768 + bx * 16384 + c * 4096, &p.tmv, bx * 64, cur[c].y, h, cur[c].x, &kv_full[s],
+                          pol);
+            }
+        } else {
+          for (int bx = 0; bx < 2; ++bx) {
+            tma_load_4d(st + bx * 16384, &p.tmk, bx * 64, (t_lo + j) * kPfKeys, h, 0, &kv_full[s], pol);
+            tma_load_4d(st + 32768 + bx * 16384, &p.tmv, bx * 64, (t_lo + j) * kPfKeys, h, 0, &kv_full[s], pol);
+          }
         }
         armed = j + 1;
       }
@@ -211,6 +248,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntile; ++j) {
+      int4 te[4];  // paged: this tile's sub-tile entries (read before the wait, which hides the load)
+      if constexpr (kPaged) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int si = 4 * (t_lo + j) + c;
+          te[c] = si < p.n_sub ? p.ktab[si] : make_int4(0, 0, 0, 0);
+        }
+      }
       // warp-uniform: tcgen05.ld/st and the votes below are warp-collective
       ok = __all_sync(0xffffffffu, !s_abort && mbar_wait(&s_full[x], j & 1, TC_DEVERR_PIPE_TIMEOUT, kPfSpin));
       if (!ok) break;
@@ -221,16 +266,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       tmem_wait_ld();
       // raw scores, masked (-inf) past this row's last visible key; row max over 8 partial chains
       const int ja = t_lo + j;
-      const bool masked_tile = (ja + 1) * kPfKeys - 1 > limit_min;
       float mx[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) mx[r] = -INFINITY;
-      if (masked_tile) {
+      if constexpr (kPaged) {
+        // chunk c of the row is sub-tile c: slot e holds logical key te[c].w + e if e < te[c].z
+        const bool full = te[0].z == 32 && te[1].z == 32 && te[2].z == 32 && te[3].z == 32 &&
+                          te[3].w + 31 <= limit_min;
+        if (!full) {
 #pragma unroll
-        for (int cch = 0; cch < 4; ++cch)
+          for (int cch = 0; cch < 4; ++cch)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (ja * kPfKeys + cch * 32 + e > limit) v[cch][e] = __float_as_uint(-INFINITY);
+            for (int e = 0; e < 32; ++e)
+              if (e >= te[cch].z || te[cch].w + e > limit) v[cch][e] = __float_as_uint(-INFINITY);
+        }
+      } else {
+        const bool masked_tile = (ja + 1) * kPfKeys - 1 > limit_min;
+        if (masked_tile) {
+#pragma unroll
+          for (int cch = 0; cch < 4; ++cch)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (ja * kPfKeys + cch * 32 + e > limit) v[cch][e] = __float_as_uint(-INFINITY);
+        }
       }
 #pragma unroll
       for (int cch = 0; cch < 4; ++cch)

@@ -1030,6 +1030,35 @@ size_t tc_prefill_workspace_size(int hq, int hkv, int lq, int lk, int splits) {
   return prefill_ws_bytes(hq, lq, s);
 }
 
+}  // extern "C"
+
+namespace {
+template <typename T, bool kPaged>
+cudaError_t launch_prefill_t(const PrefillParams& p, dim3 grid, int dev, cudaStream_t s) {
+  const cudaError_t e = set_smem(reinterpret_cast<const void*>(prefill_kernel<T, kPaged>), kPfSmem, dev);
+  if (e != cudaSuccess) return e;
+  prefill_kernel<T, kPaged><<<grid, kPfThreads, kPfSmem, s>>>(p);
+  return cudaGetLastError();
+}
+
+// One prefill launch (grid: query blocks x KV heads x splits) and, with splits, the LSE merge.
+int launch_prefill(const PrefillParams& p, int lq, int hkv, int ns, int64_t rows, void* out, int dtype, int dev,
+                   void* stream, bool paged = false) {
+  const dim3 grid((unsigned)((lq + kPfQ * kPfTiles - 1) / (kPfQ * kPfTiles)), (unsigned)hkv, (unsigned)ns);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dtype == TC_BF16)
+    e = paged ? launch_prefill_t<__nv_bfloat16, true>(p, grid, dev, s) : launch_prefill_t<__nv_bfloat16, false>(p, grid, dev, s);
+  else
+    e = paged ? launch_prefill_t<__half, true>(p, grid, dev, s) : launch_prefill_t<__half, false>(p, grid, dev, s);
+  if (e != cudaSuccess) return TC_ERR_CUDA;
+  if (ns > 1) return tc_merge_partials(p.o_part, p.lse_part, out, nullptr, ns, rows, 128, 128, dtype, stream);
+  return TC_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int tc_prefill_attention(const void* q, const void* k, const void* v, void* out, int hq, int hkv, int lq, int lk,
                          int d, int64_t q_stride_h, int64_t q_stride_p, int64_t k_stride_h, int64_t k_stride_n,
                          int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_p, int64_t out_stride_h,
@@ -1073,19 +1102,63 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
     p.o_part = static_cast<float*>(workspace);
     p.lse_part = p.o_part + (size_t)ns * rows * 128;
   }
-  const dim3 grid((unsigned)((lq + kPfQ * kPfTiles - 1) / (kPfQ * kPfTiles)), (unsigned)hkv, (unsigned)ns);
-  const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  if (dtype == TC_BF16) {
-    e = set_smem(reinterpret_cast<const void*>(prefill_kernel<__nv_bfloat16>), kPfSmem, dev);
-    if (e == cudaSuccess) prefill_kernel<__nv_bfloat16><<<grid, kPfThreads, kPfSmem, s>>>(p);
-  } else {
-    e = set_smem(reinterpret_cast<const void*>(prefill_kernel<__half>), kPfSmem, dev);
-    if (e == cudaSuccess) prefill_kernel<__half><<<grid, kPfThreads, kPfSmem, s>>>(p);
+  return launch_prefill(p, lq, hkv, ns, rows, out, dtype, dev, stream);
+}
+
+int tc_prefill_attention_paged(const void* q, const void* k_pool, const void* v_pool, void* out, int hq, int hkv,
+                               int lq, int lk, int d, int64_t page_rows, int64_t num_pages, int64_t pool_stride_page,
+                               int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* ktab, int64_t n_sub,
+                               const int32_t* qb_tiles, int64_t q_stride_h, int64_t q_stride_p,
+                               int64_t out_stride_p, int64_t out_stride_h, float scale, int splits, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (d != 128 || hkv < 1 || hkv > 65535 || hq != kPfGroup * hkv || lq < 1 || lk < lq || q == nullptr ||
+      k_pool == nullptr || v_pool == nullptr || out == nullptr || ktab == nullptr || qb_tiles == nullptr ||
+      splits < 0 || n_sub < 1 || n_sub > (1 << 28) || page_rows < kTile || page_rows > (1 << 30) ||
+      num_pages < 1 || num_pages >= (1 << 30))
+    return TC_ERR_INVALID;
+  if (!(scale == scale) || scale == INFINITY || scale == -INFINITY) return TC_ERR_INVALID;
+  const int64_t st[7] = {q_stride_h, q_stride_p, out_stride_p, out_stride_h, pool_stride_page, pool_stride_h,
+                         pool_stride_row};
+  for (int64_t x : st)
+    if (!stride16(x, dtype)) return TC_ERR_ALIGN;
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) || !aligned16(ktab))
+    return TC_ERR_ALIGN;
+  const int dev = current_device();
+  const int lk_tiles = (int)((n_sub + 3) / 4) * kPfKeys;  // key slots the tiles hold (planning only)
+  int ns = splits > 0 ? (splits > 16 ? 16 : splits) : prefill_splits(hkv, lq, lk_tiles, sm_count(dev));
+  if (ns > 1 && !(out_stride_h == 128 && out_stride_p == (int64_t)hq * 128)) ns = 1;
+  const size_t need = prefill_ws_bytes(hq, lq, ns);
+  if (ns > 1 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return TC_ERR_WORKSPACE;
+  PrefillParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int64_t qd[4] = {128, lq, hq, 1}, qs[3] = {q_stride_p, q_stride_h, q_stride_h * hq};
+  const uint32_t qbox[4] = {64, (uint32_t)kPfQ, (uint32_t)kPfGroup, 1};
+  if (!encode_map4(&p.tmq, q, dtype, qd, qs, qbox) ||
+      !encode_kv_map(&p.tmk, k_pool, dtype, d, page_rows, hkv, num_pages, pool_stride_row, pool_stride_h,
+                     pool_stride_page) ||
+      !encode_kv_map(&p.tmv, v_pool, dtype, d, page_rows, hkv, num_pages, pool_stride_row, pool_stride_h,
+                     pool_stride_page))
+    return TC_ERR_INVALID;
+  p.ktab = reinterpret_cast<const int4*>(ktab);
+  p.n_sub = (int)n_sub;
+  p.oob_page = (int)num_pages;
+  p.qb_tiles = qb_tiles;
+  p.out = out;
+  p.so_p = out_stride_p;
+  p.so_h = out_stride_h;
+  p.lq = lq;
+  p.lk = lk;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.c = scale * kLog2e;
+  p.nsplit = ns;
+  const int64_t rows = (int64_t)lq * hq;
+  if (ns > 1) {
+    p.o_part = static_cast<float*>(workspace);
+    p.lse_part = p.o_part + (size_t)ns * rows * 128;
   }
-  if (e != cudaSuccess || cudaGetLastError() != cudaSuccess) return TC_ERR_CUDA;
-  if (ns > 1) return tc_merge_partials(p.o_part, p.lse_part, out, nullptr, ns, rows, 128, 128, dtype, stream);
-  return TC_OK;
+  return launch_prefill(p, lq, hkv, ns, rows, out, dtype, dev, stream, true);
 }
 
 }  // extern "C"

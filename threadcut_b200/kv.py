@@ -295,7 +295,8 @@ class PagedLayer(DynamicLayer):
     def __init__(self, state, index):
         super().__init__()
         self.state, self.index = state, index
-        self._pending = None
+        self._pending = None   # (k [hkv, d], v [hkv, d]) of a one-token step, not yet in the pages
+        self._standin = None   # data_ptr of the key stand-in update() returned this step
         state.members.append(self)
 
     def lazy_initialization(self, key_states, value_states, *args, **kwargs):
@@ -305,11 +306,16 @@ class PagedLayer(DynamicLayer):
     def get_seq_length(self):
         return self.state.kv.n if self.state.kv is not None else 0
 
+    def _release(self):
+        if self._standin is not None:
+            _PAGED_PENDING.pop(self._standin, None)
+            self._standin = None
+
     def _flush(self):
         pend = self._pending
+        self._release()
         if pend is not None:
             self._pending = None
-            _PAGED_PENDING.pop(pend[2], None)
             self.state.kv.write(self.index, pend[0][:, None], pend[1][:, None])
 
     def update(self, key_states, value_states, *args, **kwargs):
@@ -326,10 +332,15 @@ class PagedLayer(DynamicLayer):
             except MemoryError:
                 kv.compact()
                 kv.reserve(t)
-        if t == 1 and self.state.fuse:
-            self._pending = (key_states[0, :, 0, :], value_states[0, :, 0, :], key_states.data_ptr())
-            _PAGED_PENDING[key_states.data_ptr()] = self
-            return key_states, value_states  # stand-ins: the plugin's decode branch reads the pages
+        if self.state.fuse:
+            # stand-ins: the plugin's decode and prefill branches read the pages themselves
+            if t == 1:
+                self._pending = (key_states[0, :, 0, :], value_states[0, :, 0, :])
+            else:
+                kv.write(self.index, key_states[0], value_states[0])
+            self._standin = key_states.data_ptr()
+            _PAGED_PENDING[self._standin] = self
+            return key_states, value_states
         kv.write(self.index, key_states[0], value_states[0])
         k, v = kv.gather(self.index)
         return k[None], v[None]
@@ -337,11 +348,21 @@ class PagedLayer(DynamicLayer):
     def decode(self, q, scale):
         """The step's attention for the threadcut plugin: q [hkv, g, d] over the pages with the
         pending row written by the same launch."""
-        k, v, ptr = self._pending
+        k, v = self._pending
         self._pending = None
-        _PAGED_PENDING.pop(ptr, None)
+        self._release()
         kv = self.state.kv
         return kv.decode(self.index, q, scale, k_new=k, v_new=v, stable_tiles=kv.n_tiles - 1)
+
+    def can_prefill(self, query):
+        return (self._pending is None and query.shape[0] == 1 and query.shape[-1] == 128
+                and query.shape[1] == 4 * self.state.kv.hkv and query.dtype == self.state.kv.dtype
+                and query.dtype in (torch.bfloat16, torch.float16))
+
+    def prefill(self, query, scale):
+        """The chunk's causal attention for the threadcut plugin, straight over the pages."""
+        self._release()
+        return self.state.kv.prefill(self.index, query, scale)
 
     def materialize(self):
         """Writes the pending row and returns contiguous (K, V) [1, hkv, n, d] (other readers)."""
@@ -359,11 +380,11 @@ class PagedLayer(DynamicLayer):
 
 
 def paged_pending(key):
-    """The PagedLayer whose step row stands behind `key` (a stand-in returned by update), or None."""
+    """The PagedLayer that returned `key` as this step's stand-in from update(), or None."""
     if not _PAGED_PENDING or not key.is_cuda:
         return None
     layer = _PAGED_PENDING.get(key.data_ptr())
-    if layer is None or layer._pending is None:
+    if layer is None or layer._standin != key.data_ptr():
         return None
     return layer
 

@@ -248,6 +248,9 @@ class PagedKV:
         self._slots = None       # device int32 [t, 2] of the step reserved last
         self._tiles_dev = None   # device int32 [capacity, 3]: the tile table, rows [0, n) valid
         self._tiles_ver = -1     # table version the device copy reflects
+        self._ktab = None        # device int32 [T, 4]: tiles + logical start, for prefill
+        self._ktab_starts = None
+        self._ktab_ver = -1
 
     @property
     def n(self):
@@ -342,6 +345,52 @@ class PagedKV:
                 v_new.stride(0) if v_new is not None else 0, q.stride(0), q.stride(1), out.stride(0), out.stride(1),
                 float(scale), int(splits or 0), code, int(stable_tiles), ws.data_ptr(), ws.numel(),
                 stream_ptr(q.device)))
+        return out
+
+    def _prefill_table(self):
+        """Device int32 [T, 4] = (page, first row, rows, logical position of the first row) of the
+        current tile table, and the host copy of the logical starts."""
+        if self._ktab_ver != self.table.version:
+            tab = self.table.tiles()
+            starts = (np.cumsum(tab[:, 2], dtype=np.int64) - tab[:, 2]).astype(np.int32)
+            k4 = np.ascontiguousarray(np.concatenate((tab, starts[:, None]), axis=1))
+            self._ktab = torch.from_numpy(k4).to(self.device)
+            self._ktab_starts = starts
+            self._ktab_ver = self.table.version
+        return self._ktab, self._ktab_starts
+
+    def prefill(self, layer, query, scale, *, splits=None):
+        """Causal attention of a chunk's queries over the whole paged sequence, whose last lq tokens
+        are the chunk (already written): query [1, 4*hkv, lq, 128] (bf16/fp16) -> [1, lq, hq, 128],
+        as threadcut_b200.prefill.prefill_attention on the contiguous cache, with no copy of it."""
+        require_cuda(query, what="PagedKV.prefill")
+        _, hq, lq, d = query.shape
+        n = self.table.n
+        if (query.shape[0] != 1 or d != 128 or d != self.d or hq != 4 * self.hkv or query.dtype != self.dtype
+                or query.dtype not in (torch.bfloat16, torch.float16) or not 1 <= lq <= n):
+            raise ValueError(f"PagedKV.prefill: query {tuple(query.shape)} {query.dtype} does not fit the cache")
+        ktab, starts = self._prefill_table()
+        n_sub = ktab.shape[0]
+        nqb = -(-lq // 64)
+        kend = np.minimum(n, (n - lq) + 64 * (np.arange(nqb, dtype=np.int64) + 1))
+        qbt = np.maximum(np.searchsorted(starts[::4], kend, side="left"), 1).astype(np.int32)
+        qb_tiles = torch.from_numpy(qbt).to(self.device)
+        q = query[0]
+        if q.stride(-1) != 1:
+            q = q.contiguous()
+        out = torch.empty((1, lq, hq, d), dtype=query.dtype, device=query.device)
+        L = lib()
+        sp, sh, sr = self._strides()
+        s = int(splits or 0)
+        with torch.cuda.device(query.device):
+            nb = L.tc_prefill_workspace_size(hq, self.hkv, lq, 128 * (-(-n_sub // 4)), s)
+            ws = workspaces.get("prefill", query.device, nb) if nb else None
+            st = L.tc_prefill_attention_paged(
+                q.data_ptr(), self.k[layer].data_ptr(), self.v[layer].data_ptr(), out.data_ptr(), hq, self.hkv, lq, n,
+                d, self.page_rows, self.table.num_pages, sp, sh, sr, ktab.data_ptr(), n_sub, qb_tiles.data_ptr(),
+                q.stride(0), q.stride(1), out.stride(1), out.stride(2), float(scale), s, _lib.DTYPE_CODE[query.dtype],
+                ws.data_ptr() if ws is not None else None, nb, stream_ptr(query.device))
+        check("tc_prefill_attention_paged", st)
         return out
 
     # ---------------------------------------------------------------- splice
