@@ -196,3 +196,37 @@ def test_paged_engine_matches_the_contiguous_engine():
     assert torch.allclose(lp.float(), lc.float(), atol=3e-2, rtol=0)
     out_p2, _ = eng_p.generate(A + C + D + rand_ids(3, 13), max_new_tokens=8)
     assert len(out_p2) > 0
+
+
+@pytest.mark.parametrize("kind", ["fp32_d16", "bf16_g2"])
+def test_paged_engine_fallbacks_match_the_contiguous_engine(kind):
+    """Paged caches the kernels cannot read directly: fp32 with head_dim 16 (no fused decode: rows are
+    written and the attention sees a gathered copy) and bf16 with 2 query heads per KV head (decode
+    over the pages, prefill on a gathered copy). Same tokens as the contiguous engine, two turns."""
+    def make(paged):
+        torch.manual_seed(0)
+        if kind == "fp32_d16":
+            cfg = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                              num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=4096)
+            dtype = torch.float32
+        else:
+            cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                              num_attention_heads=4, num_key_value_heads=2, head_dim=128, max_position_embeddings=4096)
+            dtype = torch.bfloat16
+        model = AutoModelForCausalLM.from_config(cfg, dtype=dtype, attn_implementation=tc_attention.NAME).to(DEV)
+        return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=16,
+                      max_ctx=2048, paged=paged)
+    eng_p, eng_c = make(True), make(False)
+    p1 = rand_ids(60, 21)
+    out_p, _ = eng_p.generate(p1, max_new_tokens=10)
+    out_c, _ = eng_c.generate(p1, max_new_tokens=10)
+    assert out_p == out_c
+    p2 = p1[:20] + p1[35:] + out_p + rand_ids(5, 22)  # a pruned span: the splice path
+    out_p2, sp = eng_p.generate(p2, max_new_tokens=10)
+    out_c2, sc = eng_c.generate(p2, max_new_tokens=10)
+    assert (sp["reused_prefix"], sp["reused_suffix"]) == (sc["reused_prefix"], sc["reused_suffix"])
+    assert sp["reused_suffix"] > 0
+    if kind == "fp32_d16":
+        assert out_p2 == out_c2
+    else:
+        assert len(out_p2) > 0
