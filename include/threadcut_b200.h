@@ -14,7 +14,8 @@
  *                             threadcut/kv.py:28-33             splice(cache, s, inv_freq), all layers
  *   tc_splice_copy            threadcut/kv.py:34-41             splice(...) copy path (non-growing caches)
  *   tc_merge_partials         threadcut/flash_decode.py:68-69   softmax(lse) merge of split partials
- *   tc_decode_attention_paged, tc_prefill_attention_paged, tc_paged_rotate_keys, tc_paged_write
+ *   tc_decode_attention_paged, tc_prefill_attention_paged, tc_paged_rotate_keys, tc_paged_write,
+ *   tc_paged_gather
  *                             threadcut/README.md:141-144       the paged KV layout named there as the next
  *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
  *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
@@ -282,6 +283,15 @@ int tc_paged_write(const void* k_src, const void* v_src, void* k_pool, void* v_p
                    int64_t src_stride_h, int64_t src_stride_t, int64_t vsrc_stride_h, int64_t vsrc_stride_t,
                    int64_t page_rows, int64_t num_pages, int64_t pool_stride_page, int64_t pool_stride_h,
                    int64_t pool_stride_row, const int32_t* slots, int dtype, void* stream);
+
+/* One layer's sequence copied out of the pools in logical order: k_out/v_out [hkv][n][d] (element
+ * strides out_stride_h/out_stride_n, last dim contiguous); `tiles` is the DEVICE int32 [n_tiles][4]
+ * table of tc_prefill_attention_paged (page, first row, rows, logical position of the first row).
+ * Rows whose logical position falls outside [0, n) are skipped. */
+int tc_paged_gather(const void* k_pool, const void* v_pool, void* k_out, void* v_out, int hkv, int d, int64_t n,
+                    int64_t out_stride_h, int64_t out_stride_n, int64_t page_rows, int64_t num_pages,
+                    int64_t pool_stride_page, int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* tiles,
+                    int64_t n_tiles, int dtype, void* stream);
 
 /* ======================================================================================
  * RoPE key shift: out = k*cos(delta*theta) + rotate_half(k)*sin(delta*theta), in fp32 with the

@@ -60,6 +60,8 @@ SIGNATURES = {
                                        _i64, _vp, _vp, _i64, _i64] + [_i64] * 4 + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_prefill_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp,
                                         _i64, _vp, _i64, _i64, _i64, _i64, _f, _i, _i, _vp, _sz, _vp]),
+    "tc_paged_gather": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64,
+                             _i, _vp]),
     "tc_paged_rotate_keys": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _fp,
                                   _i, _vp]),
     "tc_paged_write": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i64] + [_i64] * 4 + [_i64] * 5 + [_vp, _i, _vp]),

@@ -9,6 +9,8 @@
 //                        one launch; a tile-table entry (page, first row, rows <= 32) per 32-row tile
 //                        of C. Bytes = read + write of C's keys only (values never move).
 //   paged_write_kernel:  writes t new rows per head (K and V of one layer) to their (page, row) slots.
+//   paged_gather_kernel: one layer's K and V copied out in logical order (contiguous views for the
+//                        attention paths that do not read pages).
 #pragma once
 
 #include <stdint.h>
@@ -86,6 +88,45 @@ __global__ void __launch_bounds__(256) paged_write_kernel(const __grid_constant_
     const T* src = static_cast<const T*>(isv ? p.v_src : p.k_src) + h * (isv ? p.vsrc_sh : p.src_sh) +
                    r * (isv ? p.vsrc_st : p.src_st) + ch * VEC;
     T* dst = static_cast<T*>(isv ? p.vp : p.kp) + page * p.s_page + h * p.s_h + pr * p.s_row + ch * VEC;
+    st_chunk<T, VEC>(dst, ld_chunk<T, VEC>(src));
+  }
+}
+
+struct PagedGatherParams {
+  const void* kp;  // one layer's pools
+  const void* vp;
+  void* k_out;     // [hkv][n][d] with element strides (out_sh, out_sn)
+  void* v_out;
+  int hkv, d;
+  int64_t n;
+  int64_t out_sh, out_sn;
+  int64_t page_rows, num_pages;
+  int64_t s_page, s_h, s_row;
+  const int32_t* tiles;  // [n_tiles][4]: page, first row, rows <= 32, logical position of the first row
+  int64_t n_tiles;
+};
+
+// Contiguous copy of one layer's sequence (rows in logical order), K and V: one 16-byte chunk
+// (or element) per task, tasks ordered (tile, head, row, chunk) so a warp reads and writes whole rows.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) paged_gather_kernel(const __grid_constant__ PagedGatherParams p) {
+  const int cpr = p.d / VEC;
+  const int per_tile = kPagedTileRows * cpr;
+  const int64_t per = p.n_tiles * p.hkv * per_tile;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < 2 * per; i += (int64_t)gridDim.x * blockDim.x) {
+    const bool isv = i >= per;
+    const int64_t u = isv ? i - per : i;
+    const int in_tile = (int)(u % per_tile);
+    const int64_t th = u / per_tile;
+    const int h = (int)(th % p.hkv);
+    const int64_t tile = th / p.hkv;
+    const int row = in_tile / cpr, ch = in_tile - row * cpr;
+    const int32_t* tt = p.tiles + 4 * tile;
+    if (row >= tt[2]) continue;
+    const int64_t page = tt[0], pr = (int64_t)tt[1] + row, pos = (int64_t)tt[3] + row;
+    if (page < 0 || page >= p.num_pages || tt[1] < 0 || pr >= p.page_rows || pos < 0 || pos >= p.n) continue;
+    const T* src = static_cast<const T*>(isv ? p.vp : p.kp) + page * p.s_page + h * p.s_h + pr * p.s_row + ch * VEC;
+    T* dst = static_cast<T*>(isv ? p.v_out : p.k_out) + h * p.out_sh + pos * p.out_sn + ch * VEC;
     st_chunk<T, VEC>(dst, ld_chunk<T, VEC>(src));
   }
 }

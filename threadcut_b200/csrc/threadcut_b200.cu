@@ -338,6 +338,11 @@ cudaError_t launch_paged_write(const PagedWriteParams& p, int blocks, cudaStream
   return cudaGetLastError();
 }
 template <typename T, int VEC>
+cudaError_t launch_paged_gather(const PagedGatherParams& p, int blocks, cudaStream_t st) {
+  paged_gather_kernel<T, VEC><<<blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+template <typename T, int VEC>
 cudaError_t launch_splice_inplace(const SpliceParams& p, int blocks, cudaStream_t st) {
   splice_inplace_kernel<T, VEC><<<blocks, kSpliceThreads, 0, st>>>(p);
   return cudaGetLastError();
@@ -833,6 +838,44 @@ int tc_paged_write(const void* k_src, const void* v_src, void* k_pool, void* v_p
   const int blocks = grid_for(tasks, 256, sm_count(current_device()), 8);
   const cudaError_t e =
       TC_ROPE_DISPATCH(launch_paged_write, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_paged_gather(const void* k_pool, const void* v_pool, void* k_out, void* v_out, int hkv, int d, int64_t n,
+                    int64_t out_stride_h, int64_t out_stride_n, int64_t page_rows, int64_t num_pages,
+                    int64_t pool_stride_page, int64_t pool_stride_h, int64_t pool_stride_row, const int32_t* tiles,
+                    int64_t n_tiles, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (hkv < 1 || d < 1 || n < 0 || n_tiles < 0 || page_rows < 1 || num_pages < 1) return TC_ERR_INVALID;
+  if (n == 0 || n_tiles == 0) return TC_OK;
+  if (k_pool == nullptr || v_pool == nullptr || k_out == nullptr || v_out == nullptr || tiles == nullptr)
+    return TC_ERR_INVALID;
+  PagedGatherParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.kp = k_pool;
+  p.vp = v_pool;
+  p.k_out = k_out;
+  p.v_out = v_out;
+  p.hkv = hkv;
+  p.d = d;
+  p.n = n;
+  p.out_sh = out_stride_h;
+  p.out_sn = out_stride_n;
+  p.page_rows = page_rows;
+  p.num_pages = num_pages;
+  p.s_page = pool_stride_page;
+  p.s_h = pool_stride_h;
+  p.s_row = pool_stride_row;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  const void* ptrs[4] = {k_pool, v_pool, k_out, v_out};
+  const int64_t strides[5] = {out_stride_h, out_stride_n, pool_stride_page, pool_stride_h, pool_stride_row};
+  int vec = rope_vec(dtype, d / 2, ptrs, 4, strides, 5);
+  if (d % vec != 0) vec = 1;
+  const int64_t tasks = 2 * n_tiles * hkv * kPagedTileRows * (d / vec);
+  const int blocks = grid_for(tasks, 256, sm_count(current_device()), 8);
+  const cudaError_t e =
+      TC_ROPE_DISPATCH(launch_paged_gather, dtype, vec, p, blocks, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 

@@ -261,7 +261,7 @@ class PagedKV:
         return self.table.tiles().shape[0]
 
     def _strides(self):
-        s = self.k[0].stride()
+        s = next(t for t in self.k if t is not None).stride()  # compact() frees pools layer by layer
         return s[0], s[1], s[2]
 
     def _tiles(self):
@@ -431,9 +431,18 @@ class PagedKV:
 
     # ---------------------------------------------------------------- views
     def gather(self, layer):
-        """Contiguous copies (K, V) [hkv, n, d] of one layer in logical order (torch indexing; for
-        prefill chunks and checks, not the decode path)."""
-        pos = torch.from_numpy(self.table.positions()).to(self.device)
-        k = self.k[layer][pos[:, 0], :, pos[:, 1], :]  # [n, hkv, d]
-        v = self.v[layer][pos[:, 0], :, pos[:, 1], :]
-        return k.transpose(0, 1).contiguous(), v.transpose(0, 1).contiguous()
+        """Contiguous copies (K, V) [hkv, n, d] of one layer in logical order (tc_paged_gather), for
+        the attention paths that do not read pages and for compact()."""
+        n = self.table.n
+        k = torch.empty((self.hkv, n, self.d), dtype=self.dtype, device=self.device)
+        v = torch.empty_like(k)
+        if n == 0:
+            return k, v
+        ktab, _ = self._prefill_table()
+        sp, sh, sr = self._strides()
+        with torch.cuda.device(self.device):
+            check("tc_paged_gather", lib().tc_paged_gather(
+                self.k[layer].data_ptr(), self.v[layer].data_ptr(), k.data_ptr(), v.data_ptr(), self.hkv, self.d, n,
+                k.stride(0), k.stride(1), self.page_rows, self.table.num_pages, sp, sh, sr, ktab.data_ptr(),
+                ktab.shape[0], _lib.DTYPE_CODE[self.dtype], stream_ptr(self.device)))
+        return k, v
