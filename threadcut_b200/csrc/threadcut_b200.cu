@@ -1003,7 +1003,7 @@ int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, voi
 
 size_t tc_split_workspace_size(int64_t n_cached) {
   if (n_cached < 0) return 0;
-  return sizeof(SplitWs) + sizeof(int64_t) * (size_t)(n_cached > 0 ? n_cached : 1);
+  return sizeof(SplitWs) + 2 * sizeof(int64_t) * (size_t)(n_cached > 0 ? n_cached : 1);  // candidates + slots
 }
 
 int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens, int64_t n_new, int min_suffix,
@@ -1030,7 +1030,8 @@ int tc_split(const int32_t* cached, int64_t n_cached, const int32_t* new_tokens,
   split_init_kernel<<<1, 32, 0, st>>>(p);
   split_lcp_kernel<<<grid_for(m > 0 ? m : 1, kSplitThreads, sms, 8), kSplitThreads, 0, st>>>(p);
   split_window_kernel<<<grid_for(n_cached > 0 ? n_cached : 1, kSplitThreads, sms, 8), kSplitThreads, 0, st>>>(p);
-  split_extend_kernel<<<sms * 2, kExtendThreads, 0, st>>>(p);
+  split_extend_kernel<<<sms * 4, kExtendThreads, 0, st>>>(p);
+  split_best_kernel<<<sms, kSplitThreads, 0, st>>>(p);
   split_finish_kernel<<<1, 32, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
