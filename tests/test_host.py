@@ -91,6 +91,45 @@ def test_argument_validation_without_a_gpu():
     assert L.tc_shift_keys(None, None, 0, 5, 8, 0, 0, 0, 0, tab, 2, None) == 0
 
 
+def test_paged_prefill_and_split_argument_validation_without_a_gpu():
+    """The paged, paged-prefill, gather and device-split entry points reject bad arguments (and
+    accept empty work) before touching CUDA."""
+    L = _lib.lib()
+    z = [0] * 4
+    # paged decode: fp32 pools, pages shorter than a tile, a fused row without its value half
+    assert L.tc_decode_attention_paged(None, None, None, None, 8, 4, 128, 64, 10, 0, 0, 0, None, 0, 0, None, None,
+                                       0, 0, *z, 0.1, 0, 0, 0, None, 0, None) == 3
+    assert L.tc_decode_attention_paged(None, None, None, None, 8, 4, 128, 16, 10, 0, 0, 0, None, 0, 0, None, None,
+                                       0, 0, *z, 0.1, 0, 2, 0, None, 0, None) == 1
+    kn = ctypes.c_void_p(16)
+    assert L.tc_decode_attention_paged(kn, kn, kn, kn, 8, 4, 128, 64, 10, 0, 0, 0, kn, 1, 32, kn, None,
+                                       0, 0, *z, 0.1, 0, 2, 0, None, 0, None) == 1
+    # stable_tiles must not be negative
+    assert L.tc_decode_attention_paged(kn, kn, kn, kn, 8, 4, 128, 64, 10, 0, 0, 0, kn, 1, 32, None, None,
+                                       0, 0, *z, 0.1, 0, 2, -1, None, 0, None) == 1
+    # paged prefill: head_dim 64, 2 query heads per KV head, no sub-tile table
+    assert L.tc_prefill_attention_paged(kn, kn, kn, kn, 32, 8, 4, 100, 64, 64, 10, 0, 0, 0, kn, 4, kn, 0, 0, 0, 0,
+                                        0.1, 0, 2, None, 0, None) == 1
+    assert L.tc_prefill_attention_paged(kn, kn, kn, kn, 16, 8, 4, 100, 128, 64, 10, 0, 0, 0, kn, 4, kn, 0, 0, 0, 0,
+                                        0.1, 0, 2, None, 0, None) == 1
+    assert L.tc_prefill_attention_paged(kn, kn, kn, kn, 32, 8, 4, 100, 128, 64, 10, 0, 0, 0, None, 4, kn, 0, 0, 0, 0,
+                                        0.1, 0, 2, None, 0, None) == 1
+    # rotate / write / gather: no layers, no heads, bad dtype; empty work succeeds without a launch
+    tab = (ctypes.c_float * 128)()
+    kp = (ctypes.c_void_p * 1)(16)
+    assert L.tc_paged_rotate_keys(kp, 0, 8, 128, 64, 10, 0, 0, 0, kn, 1, tab, 2, None) == 1
+    assert L.tc_paged_rotate_keys(kp, 1, 8, 128, 64, 10, 0, 0, 0, None, 0, tab, 2, None) == 0
+    assert L.tc_paged_write(kn, kn, kn, kn, 0, 128, 3, 0, 0, 0, 0, 64, 10, 0, 0, 0, kn, 2, None) == 1
+    assert L.tc_paged_write(kn, kn, kn, kn, 8, 128, 0, 0, 0, 0, 0, 64, 10, 0, 0, 0, kn, 2, None) == 0
+    assert L.tc_paged_gather(kn, kn, kn, kn, 8, 128, 10, 0, 0, 64, 10, 0, 0, 0, kn, 1, 7, None) == 3
+    assert L.tc_paged_gather(kn, kn, kn, kn, 8, 128, 0, 0, 0, 64, 10, 0, 0, 0, kn, 1, 2, None) == 0
+    # device split: an empty request, a missing workspace
+    out = (ctypes.c_int64 * 3)()
+    assert L.tc_split(kn, 10, kn, 0, 32, 1, out, kn, 1 << 20, None) == 1
+    assert L.tc_split(kn, 10, kn, 5, 32, 1, out, None, 0, None) == 4
+    assert L.tc_split_workspace_size(1000) >= 16 * 1000
+
+
 def test_splice_workspace_bound():
     L = _lib.lib()
     assert L.tc_splice_workspace_size(36, 8, 4096) >= 16 + 4 * 36 * 8 * (4096 // 64)
