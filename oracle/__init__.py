@@ -6,8 +6,8 @@ CPU-baseline leg of bench.py may import it, and only as the checker or the timed
 never as a product path. The package threadcut_b200 does not import it.
 
 Parity is pinned: tests/test_oracle.py checks every function here against golden vectors produced
-by the reference itself (tests/golden/make_golden.py imports /root/reference/threadcut in the
-build container and records its outputs).
+by the reference itself (tests/golden/make_golden.py imports the reference's threadcut package
+in the build container, where the reference checkout is mounted, and records its outputs).
 
   attention.py  folded-GQA decode attention (threadcut/attention.py:35-42,47 and the math of
                 threadcut/flash_decode.py:21-69), LSE merge (flash_decode.py:68-69)

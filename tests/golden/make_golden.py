@@ -3,7 +3,9 @@
 Run in the build container, where the reference is mounted (it is absent on the GPU box; the
 committed .npz/.json are what travels):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
+
+(or set THREADCUT_REFERENCE to the checkout instead of passing --reference).
 
 It imports threadcut.attention / threadcut.kv / threadcut.match from the reference checkout and
 records their outputs on the CPU (the decode branch there is the folded SDPA of
@@ -45,8 +47,11 @@ def store(t):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("THREADCUT_REFERENCE"),
+                    help="path of the reference checkout (the directory holding threadcut/)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or THREADCUT_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     from threadcut import attention as ref_attn  # noqa: E402
     from threadcut import kv as ref_kv  # noqa: E402
