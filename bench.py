@@ -519,6 +519,107 @@ def time_prefill(steps, warmup, dev, lq=512, lk=98304):
     return ours, gqa, ref, 4.0 * 32 * pairs * 128
 
 
+def time_cfg5_step(steps, warmup, dev):
+    """Config 5 end to end: random-init Qwen3-4B (bf16) whose 36-layer cache holds 131,072 tokens,
+    spliced with Split(49152, 81920, 49152) (the pruned span dropped, the suffix re-rotated by -32768)
+    to 98,304 tokens, then one greedy decode token per step through the HF model with
+    threadcut_b200's attention plugin: forward + argmax read back to the host, as the reference's
+    engine does per token (threadcut/engine.py:66-73). The appended row is cropped after each step
+    so every step decodes at the same length. Timed three ways: eager (the engine's path), the same
+    forward replayed from a CUDA graph, and eager with HF's SDPA attention (the stock torch path).
+    Returns a dict of ms per token, the splice ms and the step's algorithmic bytes."""
+    from transformers import AutoModelForCausalLM
+    from threadcut_b200 import attention as tc_attention
+    from threadcut_b200.kv import new_cache, splice
+    from threadcut_b200.match import Split
+    torch.manual_seed(0)
+    cfg = workloads.qwen3_4b_config()
+    with torch.device(dev):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
+    model.eval()
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    ctx = workloads.CFG5_CTX
+    lo, hi = workloads.CFG5_PRUNE
+    s = Split(lo, hi, ctx - hi)
+    cache = new_cache(cfg)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    for layer in cache.layers:
+        k = torch.randn(1, workloads.HKV, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, workloads.HKV, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        layer.update(k, v)
+        del k, v
+    warm = new_cache(cfg)  # a small splice first: the timed one then pays no first-launch setup
+    for layer in warm.layers:
+        layer.update(*(torch.zeros(1, workloads.HKV, 96, workloads.D, device=dev, dtype=torch.bfloat16),) * 2)
+    splice(warm, Split(16, 48, 48), model.model.rotary_emb.inv_freq)
+    del warm
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    splice(cache, s, model.model.rotary_emb.inv_freq)
+    e1.record()
+    e1.synchronize()
+    splice_ms = e0.elapsed_time(e1)
+    n = s.a + s.c
+    x = torch.tensor([[1234]], device=dev)
+
+    def crop():
+        for layer in cache.layers:
+            layer.crop(n)
+
+    def eager():
+        tok = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].argmax()
+        tok.item()
+        crop()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b) / steps
+
+    def graph_ms(key):
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                tok = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].argmax()
+            crop()
+
+            def replay():
+                graph.replay()
+                tok.item()
+
+            out[key] = timed(replay)
+            del graph
+        except Exception as exc:  # a host op the capture cannot hold: report it, keep the eager number
+            crop()
+            out[key] = None
+            out[key.replace("_ms", "_error")] = f"{type(exc).__name__}: {str(exc)[:160]}"
+
+    out = {"splice_ms": splice_ms, "n": n, "weight_bytes": weight_bytes,
+           "kv_bytes": LAYERS * decode_bytes(n)}
+    with torch.no_grad():
+        out["eager_ms"] = timed(eager)
+        with torch.cuda.nvtx.range("cfg5_step"):  # one eager step, for a profiler's launch list
+            eager()
+        torch.cuda.synchronize(dev)
+        graph_ms("graph_ms")
+        model.set_attn_implementation("sdpa")
+        for layer in cache.layers:
+            layer.fuse_append = False  # SDPA reads the cache itself: appends must be written, not deferred
+        out["sdpa_eager_ms"] = timed(eager)
+        graph_ms("sdpa_graph_ms")
+    del model, cache
+    torch.cuda.empty_cache()
+    return out
+
+
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
     """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
     cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
@@ -674,6 +775,23 @@ def run_ours(args, rank, local, world, dist):
                           "per-layer latency, max over ranks",
               "frac_per_gpu": round(decode_bytes(workloads.CFG5_CTX) / world / (strong_ms * 1e-3 / LAYERS) / 1e9
                                     / hbm, 4)}
+    cfg5 = None
+    if world == 1:
+        c5 = time_cfg5_step(min(args.steps, 10), args.warmup, dev)
+        step_bytes = c5["weight_bytes"] + c5["kv_bytes"]
+        rnd = lambda v: None if v is None else round(v, 3)  # noqa: E731
+        cfg5 = {"eager_ms": rnd(c5["eager_ms"]), "graph_ms": rnd(c5["graph_ms"]),
+                "sdpa_eager_ms": rnd(c5["sdpa_eager_ms"]), "sdpa_graph_ms": rnd(c5["sdpa_graph_ms"]),
+                "splice_ms": rnd(c5["splice_ms"]),
+                "n": c5["n"], "bytes_per_token": step_bytes,
+                "ideal_ms": round(step_bytes / (hbm * 1e9) * 1e3, 3),
+                "what": "one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache "
+                        "(131,072 tokens, Split(49152, 81920, 49152) timed once as splice_ms): HF forward with "
+                        "threadcut_b200's attention + argmax read back, eager and replayed from a CUDA graph, vs "
+                        "the same with HF's SDPA attention (under capture HF passes SDPA an explicit mask); ideal_ms = weights + K/V bytes at the measured HBM peak"}
+        for key in ("graph_error", "sdpa_graph_error"):
+            if key in c5:
+                cfg5[key] = c5[key]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         us, nl, thr = cpu_reference_us_per_layer(args.cpu_seconds)
@@ -751,6 +869,7 @@ def run_ours(args, rank, local, world, dist):
             "frac": round(BYTES_PER_LAYER / (sdpa_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
             "what": "the reference's own torch decode path (folded GQA SDPA) on the same 36 layers, same GPU"}},
         "strong_128k": strong,
+        "cfg5_step": cfg5,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -768,6 +887,9 @@ def run_partial(args, rank, local, world, dist):
         us = ms * 1000 / args.layers
         out.update(us_per_layer=round(us, 3), gbs=round(decode_bytes(args.ctx) / (us * 1e-6) / 1e9, 1))
         del graph
+    elif args.only == "cfg5":
+        c5 = time_cfg5_step(args.steps, args.warmup, dev)
+        out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in c5.items()})
     else:
         ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist, layers=args.layers), dist)
         out.update(us_per_layer=round(ms * 1000 / args.layers, 3),
@@ -811,8 +933,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--only", choices=["all", "decode", "shift"], default="all",
-                    help="profiling runs: time only the decode graph or only the splice (smaller JSON line)")
+    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5"], default="all",
+                    help="profiling runs: time only the decode graph, the splice or the config-5 model step "
+                         "(smaller JSON line)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling runs: layers per step")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="profiling runs: context length")
     args = ap.parse_args()

@@ -124,18 +124,9 @@ def test_T3_no_pruning_matches_hf_generate():
     assert out2 == [t for t in ref2 if t not in engine.stop_ids][:len(out2)]
 
 
-def qwen3_4b_config(layers=36):
-    """Qwen3-4B geometry (BASELINE: hidden 2560, 36 layers, 32/8 heads, head_dim 128, theta 1e6);
-    intermediate 9728, vocab 151936, tied embeddings and eps 1e-6 are the published values."""
-    return Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
-                       num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
-                       tie_word_embeddings=True, max_position_embeddings=262144,
-                       rope_parameters={"rope_type": "default", "rope_theta": 1.0e6})
-
-
 def test_cfg5_full_model_128k_spliced_top1_matches_sdpa():
     torch.manual_seed(0)
-    cfg = qwen3_4b_config()
+    cfg = workloads.qwen3_4b_config()
     with torch.device(DEV):
         model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
     model.eval()
@@ -159,6 +150,8 @@ def test_cfg5_full_model_128k_spliced_top1_matches_sdpa():
         for layer in cache.layers:
             layer.crop(n)  # drop the token the first pass appended
         model.set_attn_implementation("sdpa")
+        for layer in cache.layers:
+            layer.fuse_append = False  # SDPA reads the cache itself: appends must be written, not deferred
         ref = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].float()
     assert int(ours.argmax()) == int(ref.argmax())
     # bf16 logits through 36 layers differ by rounding noise; the distributions must still agree
@@ -230,3 +223,35 @@ def test_paged_engine_fallbacks_match_the_contiguous_engine(kind):
         assert out_p2 == out_c2
     else:
         assert len(out_p2) > 0
+
+
+def test_decode_step_replays_from_a_cuda_graph():
+    """A one-token decode step through the plugin (fused append + decode kernel) can be captured in
+    a CUDA graph: the registered mask builder keeps the capture free of host reads, and each replay
+    gives the eager step's logits."""
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
+    model = model.to(DEV).eval()
+    cache = new_cache(model.config)
+    ids = torch.randint(0, 512, (1, 300), device=DEV)
+    x = torch.tensor([[7]], device=DEV)
+    with torch.no_grad():
+        model(input_ids=ids, past_key_values=cache, use_cache=True)
+        n = cache.get_seq_length()
+        eager = model(input_ids=x, past_key_values=cache, use_cache=True).logits.float()
+        for layer in cache.layers:
+            layer.crop(n)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = model(input_ids=x, past_key_values=cache, use_cache=True).logits
+        for layer in cache.layers:
+            layer.crop(n)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        replayed = out.float().clone()
+        del graph
+    assert int(replayed.argmax()) == int(eager.argmax())
+    torch.testing.assert_close(replayed, eager, atol=2e-2, rtol=0)

@@ -233,3 +233,54 @@ def test_host_binding_first_use_in_a_fresh_process():
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+def test_qwen3_4b_config_geometry_and_size():
+    """The config-5 model: BASELINE geometry, and about 4.0B parameters (8 GB of bf16 weights with the
+    tied embedding stored once), counted on the meta device without allocating them."""
+    from transformers import AutoModelForCausalLM
+
+    import workloads
+    cfg = workloads.qwen3_4b_config()
+    assert (cfg.hidden_size, cfg.num_hidden_layers, cfg.num_attention_heads, cfg.num_key_value_heads,
+            cfg.head_dim) == (2560, 36, 32, 8, 128)
+    assert cfg.rope_parameters["rope_theta"] == 1.0e6 and cfg.max_position_embeddings >= 131072
+    with torch.device("meta"):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16)
+    params = sum(p.numel() for p in model.parameters())
+    assert 3.9e9 < params < 4.1e9, params
+
+
+def _mask_cases():
+    from transformers.masking_utils import causal_mask_function, sliding_window_causal_mask_function
+    pad = torch.ones(1, 9, dtype=torch.bool)
+    pad[0, 2] = False
+    for q_len, kv_len, q_off in ((1, 9, 8), (1, 9, 5), (4, 9, 5), (9, 9, 0), (1, 1, 0)):
+        yield dict(batch_size=1, q_length=q_len, kv_length=kv_len, q_offset=q_off, kv_offset=0)
+        yield dict(batch_size=1, q_length=q_len, kv_length=kv_len, q_offset=q_off, kv_offset=0, attention_mask=pad[:, :kv_len])
+        yield dict(batch_size=1, q_length=q_len, kv_length=kv_len, q_offset=q_off, kv_offset=0, allow_is_causal_skip=False)
+        yield dict(batch_size=1, q_length=q_len, kv_length=kv_len, q_offset=q_off, kv_offset=0, local_size=4,
+                   mask_function=sliding_window_causal_mask_function(4))
+    yield dict(batch_size=2, q_length=1, kv_length=9, q_offset=8, kv_offset=0, mask_function=causal_mask_function)
+
+
+@pytest.mark.parametrize("capturing", [False, True])
+def test_plugin_mask_equals_sdpa_mask(capturing, monkeypatch):
+    """The registered mask builder returns sdpa_mask's mask (reference attention.py:50-51). While a
+    CUDA graph is being captured, sdpa_mask builds the all-True mask of a one-token step, and the
+    plugin's builder returns None there instead; every other case is unchanged."""
+    import transformers.masking_utils as mu
+    from threadcut_b200 import attention as tc_attention
+    if capturing:
+        monkeypatch.setattr(mu, "is_tracing", lambda *a, **k: True)
+    for kw in _mask_cases():
+        ref = mu.sdpa_mask(**kw)
+        ours = tc_attention.attention_mask(**kw)
+        decode_skip = (kw["q_length"] == 1 and kw.get("attention_mask") is None and kw.get("local_size") is None
+                       and kw.get("allow_is_causal_skip", True) and kw["q_offset"] >= kw["kv_length"] - 1)
+        if capturing and decode_skip:
+            assert ours is None and ref is not None and bool(ref.all()), kw
+        elif ref is None:
+            assert ours is None, kw
+        else:
+            assert ours is not None and torch.equal(ours, ref), kw

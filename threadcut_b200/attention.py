@@ -25,7 +25,7 @@ import weakref
 import torch
 import torch.nn.functional as F
 from transformers import AttentionInterface
-from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+from transformers.masking_utils import AttentionMaskInterface, causal_mask_function, sdpa_mask
 
 from .flash_decode import decode_attention, decode_attention_append, decode_attention_batched
 from .kv import FUSED_ATTENTION, paged_pending, pending_append
@@ -33,7 +33,7 @@ from . import prefill as _prefill
 
 NAME = FUSED_ATTENTION  # "threadcut", as threadcut/attention.py:22
 
-__all__ = ["NAME", "attention", "repeat_kv"]
+__all__ = ["NAME", "attention", "attention_mask", "repeat_kv"]
 
 
 def repeat_kv(x, n):
@@ -106,5 +106,23 @@ def attention(module, query, key, value, attention_mask, dropout=0.0, scaling=No
     return out.transpose(1, 2).contiguous(), None
 
 
+def attention_mask(batch_size, q_length, kv_length, q_offset=0, kv_offset=0, mask_function=causal_mask_function,
+                   attention_mask=None, local_size=None, allow_is_causal_skip=True, **kwargs):
+    """The mask builder registered with the attention (the reference registers sdpa_mask,
+    threadcut/attention.py:50-51). It returns sdpa_mask's result, except for one case that sdpa_mask
+    cannot tell apart from an export trace: a one-token step with no padding mask, the plain causal
+    pattern and the query at or after every key. Every key is then visible, so the mask would be all
+    True, and None is returned (sdpa_mask returns None there too, unless a CUDA graph is being
+    captured). The decode branch then needs no mask. Without None, the capture of a decode step
+    would reach the prefill mask check, which reads the mask back to the host."""
+    if (q_length == 1 and attention_mask is None and local_size is None and allow_is_causal_skip
+            and mask_function is causal_mask_function and isinstance(q_offset, int) and isinstance(kv_offset, int)
+            and q_offset >= kv_offset + kv_length - 1):
+        return None
+    return sdpa_mask(batch_size=batch_size, q_length=q_length, kv_length=kv_length, q_offset=q_offset,
+                     kv_offset=kv_offset, mask_function=mask_function, attention_mask=attention_mask,
+                     local_size=local_size, allow_is_causal_skip=allow_is_causal_skip, **kwargs)
+
+
 AttentionInterface.register(NAME, attention)
-AttentionMaskInterface.register(NAME, sdpa_mask)
+AttentionMaskInterface.register(NAME, attention_mask)

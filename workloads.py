@@ -23,6 +23,17 @@ CFG4_BATCH, CFG4_LO, CFG4_HI = 64, 1024, 16384
 CFG5_CTX, CFG5_PRUNE = 131072, (49152, 81920)
 
 
+def qwen3_4b_config(layers=LAYERS):
+    """Qwen3-4B geometry (hidden 2560, 36 layers, 32/8 heads, head_dim 128, RoPE theta 1e6) for the
+    random-init config-5 model; intermediate 9728, vocab 151936, tied embeddings and eps 1e-6 are the
+    published values, and 262144 positions make 128k contexts legal."""
+    from transformers import Qwen3Config
+    return Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728, num_hidden_layers=layers,
+                       num_attention_heads=HQ, num_key_value_heads=HKV, head_dim=D, rms_norm_eps=1e-6,
+                       tie_word_embeddings=True, max_position_embeddings=262144,
+                       rope_parameters={"rope_type": "default", "rope_theta": THETA})
+
+
 def inv_freq(d=D, theta=THETA):
     """Default RoPE frequencies (transformers' rotary init): 1 / theta^(2i/d), fp32 [d/2]."""
     return 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
