@@ -620,6 +620,90 @@ def time_cfg5_step(steps, warmup, dev):
     return out
 
 
+def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
+    """Config 5 over `world` GPUs: threadcut_b200.tp.TPDecoder (rank r holds KV heads
+    head_shard(8, r, world), their query heads, 1/world of the MLP and of the vocabulary; two NCCL
+    all-reduces per layer) decoding one greedy token of random-init Qwen3-4B over the 131,072-token
+    cache spliced to 98,304 (each rank splices its own heads). Each step is the token's forward plus
+    the next token read back to the host; the appended row is cropped after each step so every step
+    decodes at the same length. Eager and replayed from a CUDA graph (the all-reduces inside it).
+    Returns (eager ms, graph ms or None, splice ms, per-rank bytes per token), max over ranks."""
+    from transformers import AutoModelForCausalLM
+    from threadcut_b200.match import Split
+    from threadcut_b200.tp import TPDecoder
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = AutoModelForCausalLM.from_config(workloads.qwen3_4b_config(), dtype=torch.bfloat16)
+    dec = TPDecoder(model, dev, world=world, rank=rank)
+    hr = dec.h1 - dec.h0
+    shard_bytes = sum(t.numel() * t.element_size() for w in dec.layers_w for t in vars(w).values()
+                      if isinstance(t, torch.Tensor)) + dec.lm_head.numel() * dec.lm_head.element_size()
+    inv = model.model.rotary_emb.inv_freq.detach().to(dev)
+    del model
+    torch.cuda.empty_cache()
+    ctx = workloads.CFG5_CTX
+    lo, hi = workloads.CFG5_PRUNE
+    s = Split(lo, hi, ctx - hi)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    for i in range(len(dec.layers)):
+        k = torch.randn(1, hr, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, hr, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        dec.load_local(i, k, v)
+        del k, v
+    from threadcut_b200.kv import GrowingLayer, splice as kv_splice
+    warm = [GrowingLayer() for _ in range(LAYERS)]  # a small splice first: no first-launch setup timed
+    for ly in warm:
+        ly.update(*(torch.zeros(1, hr, 96, workloads.D, device=dev, dtype=torch.bfloat16),) * 2)
+    kv_splice(type("Warm", (), {"layers": warm})(), Split(16, 48, 48), inv)
+    del warm
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dec.splice(s, inv)
+    e1.record()
+    e1.synchronize()
+    splice_ms = max_over_ranks(e0.elapsed_time(e1), dist)
+    n = s.a + s.c
+    tok = torch.tensor([1234], device=dev)
+
+    def eager():
+        int(dec.step(tok, n))
+        dec.crop(n)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        barrier(dist)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        b.synchronize()
+        barrier(dist)
+        return max_over_ranks(a.elapsed_time(b) / steps, dist)
+
+    with torch.no_grad():
+        eager_ms = timed(eager)
+        graph, out, ok = None, None, 1.0
+        try:
+            graph, out = dec.capture(tok, n)
+        except Exception:  # a host op the capture cannot hold: every rank skips the replay
+            ok = 0.0
+        ok = -max_over_ranks(-ok, dist)  # min over ranks: replay only if every rank captured
+        graph_ms = None
+        if ok:
+            def replay():
+                graph.replay()
+                int(out)
+
+            graph_ms = timed(replay)
+        del graph
+    del dec
+    torch.cuda.empty_cache()
+    return eager_ms, graph_ms, splice_ms, shard_bytes + LAYERS * (4096 // world * n + 16384 // world)
+
+
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
     """Config 4: 64 ragged sequences (lengths uniform in [1024, 16384], seeded), one contiguous K/V
     cache per sequence and layer, one query token each. A step is 36 decode_attention_ragged launches
@@ -792,6 +876,15 @@ def run_ours(args, rank, local, world, dist):
         for key in ("graph_error", "sdpa_graph_error"):
             if key in c5:
                 cfg5[key] = c5[key]
+    tp_eager, tp_graph, tp_splice, tp_bytes = time_cfg5_tp(min(args.steps, 10), args.warmup, dev, dist, rank, world)
+    cfg5_tp = {"eager_ms": round(tp_eager, 3), "graph_ms": None if tp_graph is None else round(tp_graph, 3),
+               "splice_ms": round(tp_splice, 3), "bytes_per_rank": tp_bytes,
+               "ideal_ms": round(tp_bytes / (hbm * 1e9) * 1e3, 3),
+               "what": f"one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache, "
+                       f"tensor-parallel over {world} GPU(s) (threadcut_b200.tp.TPDecoder: KV heads, their query "
+                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 NCCL all-reduces per layer), next "
+                       f"token read back each step; eager and CUDA graph; max over ranks; ideal_ms = one rank's "
+                       f"weight + K/V bytes at the measured HBM peak (collectives not counted)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         us, nl, thr = cpu_reference_us_per_layer(args.cpu_seconds)
@@ -870,6 +963,7 @@ def run_ours(args, rank, local, world, dist):
             "what": "the reference's own torch decode path (folded GQA SDPA) on the same 36 layers, same GPU"}},
         "strong_128k": strong,
         "cfg5_step": cfg5,
+        "cfg5_tp": cfg5_tp,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -887,6 +981,10 @@ def run_partial(args, rank, local, world, dist):
         us = ms * 1000 / args.layers
         out.update(us_per_layer=round(us, 3), gbs=round(decode_bytes(args.ctx) / (us * 1e-6) / 1e9, 1))
         del graph
+    elif args.only == "cfg5tp":
+        e, g, sp, b = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world)
+        out.update(eager_ms=round(e, 3), graph_ms=None if g is None else round(g, 3), splice_ms=round(sp, 3),
+                   bytes_per_rank=b, world=world)
     elif args.only == "cfg5":
         c5 = time_cfg5_step(args.steps, args.warmup, dev)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in c5.items()})
@@ -933,9 +1031,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5"], default="all",
-                    help="profiling runs: time only the decode graph, the splice or the config-5 model step "
-                         "(smaller JSON line)")
+    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5", "cfg5tp"], default="all",
+                    help="profiling runs: time only the decode graph, the splice, the config-5 model step or its "
+                         "tensor-parallel form (smaller JSON line)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling runs: layers per step")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="profiling runs: context length")
     args = ap.parse_args()

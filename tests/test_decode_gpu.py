@@ -361,6 +361,30 @@ def test_fused_append_matches_copy_then_decode(n, d, dtype):
     assert _lib.device_errors(clear=True) == 0
 
 
+@pytest.mark.parametrize("hkv,n", [(1, 300), (1, 98305), (2, 4097), (4, 33)])
+def test_fused_append_with_few_kv_heads(hkv, n):
+    """The tensor-parallel decoder's shapes: 1, 2 or 4 KV heads per rank (Qwen3-4B's 8 over 8, 4 or
+    2 GPUs), append fused; bit-identical to copying the row first and decoding."""
+    from threadcut_b200.flash_decode import decode_attention_append
+    g = torch.Generator(device=DEV).manual_seed(hkv * 1000 + n)
+    kb = torch.randn(hkv, n + 8, 128, generator=g, device=DEV).to(torch.bfloat16)
+    vb = torch.randn(hkv, n + 8, 128, generator=g, device=DEV).to(torch.bfloat16)
+    q = torch.randn(hkv, 4, 128, generator=g, device=DEV).to(torch.bfloat16)
+    kn = torch.randn(hkv, 128, generator=g, device=DEV).to(torch.bfloat16)
+    vn = torch.randn(hkv, 128, generator=g, device=DEV).to(torch.bfloat16)
+    kb2, vb2 = kb.clone(), vb.clone()
+    kb2[:, n - 1], vb2[:, n - 1] = kn, vn
+    want = decode_attention(q, kb2[:, :n], vb2[:, :n], 0.0883)
+    check_decode(q, kb2[:, :n], vb2[:, :n], 0.0883, torch.bfloat16)  # the decode itself vs the oracle
+    for stable in (0, n - 1):
+        kb3, vb3 = kb.clone(), vb.clone()
+        got = decode_attention_append(q, kb3[:, :n], vb3[:, :n], kn, vn, 0.0883, stable_rows=stable)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (hkv, n, stable)
+        assert torch.equal(kb3, kb2) and torch.equal(vb3, vb2)
+    assert _lib.device_errors(clear=True) == 0
+
+
 def test_growing_layer_fused_append_through_the_plugin():
     """A GrowingLayer with fused append leaves the decode step's row pending; the plugin's decode
     branch writes it in the fused launch; prefill and explicit reads flush it; results match a cache

@@ -255,3 +255,11 @@ def test_decode_step_replays_from_a_cuda_graph():
         del graph
     assert int(replayed.argmax()) == int(eager.argmax())
     torch.testing.assert_close(replayed, eager, atol=2e-2, rtol=0)
+
+
+def test_tensor_parallel_decoder_on_one_gpu_matches_the_hf_forward():
+    """threadcut_b200.tp.TPDecoder at world 1: the HF forward's top-1 and logits, and a CUDA graph
+    of its step replays the eager token (tests/tp_worker.py)."""
+    from tp_worker import check
+    res = check(torch.device(DEV))
+    assert res["max_abs"] < 0.1, res

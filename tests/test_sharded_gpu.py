@@ -27,3 +27,14 @@ def test_seq_and_head_sharded_decode_match_single_gpu():
     res = subprocess.run(cmd, capture_output=True, text=True)
     print(res.stdout[-3000:], res.stderr[-3000:])
     assert res.returncode == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
+def test_tensor_parallel_decoder_matches_the_hf_forward():
+    world = min(torch.cuda.device_count(), 2)
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.join(HERE, "tp_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    print(res.stdout[-3000:], res.stderr[-3000:])
+    assert res.returncode == 0

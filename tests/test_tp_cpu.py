@@ -1,0 +1,110 @@
+"""Host logic of the tensor-parallel decoder on CPU: weight slicing, the two sums per layer, the
+vocabulary-sliced argmax, and the local-head cache, on one rank and on two `gloo` ranks.
+
+The decode kernel needs a GPU, so these tests replace `tp._attend` (append + attention of one
+step) with a torch restatement on CPU; everything else is the product code. The expected logits
+are the HF model's own fp32 forward over the whole prompt (modeling_qwen3 with eager attention).
+The step also must not read any tensor value back to the host, so that it can be captured in a
+CUDA graph on the GPU."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+from torch.utils._python_dispatch import TorchDispatchMode
+from transformers import AutoModelForCausalLM, Qwen3Config
+
+from threadcut_b200 import tp
+
+
+def _cpu_attend(layer, q, k, v, scale):
+    hr, d = k.shape
+    layer.update(k.view(1, hr, 1, d), v.view(1, hr, 1, d))  # a CPU cache writes the row at once
+    kk, vv = layer.keys[0].float(), layer.values[0].float()
+    p = (torch.einsum("hgd,hnd->hgn", q.float(), kk) * scale).softmax(-1)
+    return torch.einsum("hgn,hnd->hgd", p, vv).to(q.dtype)
+
+
+class _NoHostRead(TorchDispatchMode):
+    """Fails on any op that reads a tensor value back to the host (.item(), int(t), indexing by a
+    0-dim tensor): a CUDA graph capture of the step could not hold it."""
+
+    def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+        if func is torch.ops.aten._local_scalar_dense.default:
+            raise AssertionError("the decode step reads a tensor value back to the host")
+        return func(*args, **(kwargs or {}))
+
+
+def _model():
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=4096)
+    return AutoModelForCausalLM.from_config(cfg, dtype=torch.float32, attn_implementation="eager").eval()
+
+
+def _run(rank, world, n_ctx=20):
+    model = _model()
+    ids = torch.randint(0, 512, (1, n_ctx + 1), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits[0, -1]  # logits after the last token, full context
+        out = model(input_ids=ids[:, :n_ctx], use_cache=True)
+        dec = tp.TPDecoder(model, "cpu", world=world, rank=rank, group=None)
+        for i, layer in enumerate(out.past_key_values.layers):
+            dec.load(i, layer.keys, layer.values)
+        assert dec.get_seq_length() == n_ctx
+        logits = dec.logits(ids[0, n_ctx:], n_ctx)
+        assert dec.get_seq_length() == n_ctx + 1
+        dec.crop(n_ctx)
+        with _NoHostRead():
+            tok = dec.step(ids[0, n_ctx:], n_ctx)
+    return ref, logits, tok
+
+
+def test_one_rank_equals_the_hf_forward(monkeypatch):
+    monkeypatch.setattr(tp, "_attend", _cpu_attend)
+    ref, logits, tok = _run(0, 1)
+    torch.testing.assert_close(logits, ref, atol=1e-4, rtol=0)
+    assert int(tok) == int(ref.argmax())
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tp._attend = _cpu_attend
+        ref, logits, tok = _run(rank, world)
+        err = float((logits - ref).abs().max())
+        q.put((rank, err, int(tok), int(ref.argmax())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_two_gloo_ranks_equal_the_hf_forward(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(world))
+    for rank, err, tok, ref_tok in res:
+        assert err < 1e-4, (rank, err)
+        assert tok == ref_tok
+
+
+def test_uneven_splits_are_rejected():
+    model = _model()
+    with pytest.raises(ValueError):
+        tp.TPDecoder(model, "cpu", world=3, rank=0)  # 2 KV heads over 3 ranks
