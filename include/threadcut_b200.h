@@ -20,6 +20,10 @@
  *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
  *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
  *                             append into page slots (kv.py:64-77 GrowingLayer.update semantics)
+ *   tc_add_rmsnorm, tc_qk_norm_rope, tc_silu_mul
+ *                             threadcut/engine.py:66-73         the per-token model call, run by
+ *                             transformers' Qwen3 layer (RMSNorm, q/k norm + RoPE, SwiGLU) there; here
+ *                             one launch each in the tensor-parallel decode step
  */
 #ifndef THREADCUT_B200_H
 #define THREADCUT_B200_H
@@ -370,6 +374,27 @@ int tc_decode_attention_partial(const void* q, const void* k, const void* v, flo
                                 int64_t out_stride_h, int64_t out_stride_g,
                                 float scale, int splits, int dtype,
                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-token layer ops of the tensor-parallel decode step (threadcut_b200/tp.py), each one launch in
+ * place of a chain of torch ops of transformers' Qwen3 layer (modeling_qwen3.py; threadcut runs
+ * that layer through transformers, threadcut/engine.py:66-73). Row-major contiguous tensors of
+ * `dtype`; rounding to dtype after each torch op they replace.
+ *
+ * tc_add_rmsnorm: for each of `rows` rows of `hidden` elements, h += delta (delta may be NULL:
+ * no add), out = weight * dtype(h * rsqrt(mean(h^2) + eps)) (Qwen3RMSNorm.forward, with the
+ * residual add of Qwen3DecoderLayer.forward before it). h is updated in place. */
+int tc_add_rmsnorm(void* h, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
+                   float eps, int dtype, void* stream);
+
+/* tc_qk_norm_rope: in place on q [q_heads][d] and k [k_heads][d]: per-head RMSNorm with
+ * q_weight / k_weight [d] (q_norm / k_norm), then x*cos + rotate_half(x)*sin with cos, sin [d] of
+ * dtype (apply_rotary_pos_emb). d even, at most 1024. */
+int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight, const void* cos_t,
+                    const void* sin_t, int q_heads, int k_heads, int d, float eps, int dtype, void* stream);
+
+/* tc_silu_mul: out[r][i] = dtype(silu(gate_up[r][i])) * gate_up[r][inter + i] for `rows` rows
+ * (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), gate and up side by side in one row). */
+int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

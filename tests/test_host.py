@@ -284,3 +284,31 @@ def test_plugin_mask_equals_sdpa_mask(capturing, monkeypatch):
             assert ours is None, kw
         else:
             assert ours is not None and torch.equal(ours, ref), kw
+
+
+def test_layer_ops_on_cpu_tensors_fail_loudly():
+    """The tensor-parallel step's launches refuse host tensors (no CPU path, no device call)."""
+    from threadcut_b200 import tp
+    x = torch.zeros(1, 64, dtype=torch.bfloat16)
+    w = torch.ones(64, dtype=torch.bfloat16)
+    with pytest.raises((RuntimeError, ValueError, TypeError)):
+        tp._add_rmsnorm(x, None, w, torch.empty_like(x), 1e-6)
+    with pytest.raises((RuntimeError, ValueError, TypeError)):
+        tp._qk_norm_rope(x, x, w, w, w, w, 1e-6)
+    with pytest.raises((RuntimeError, ValueError, TypeError)):
+        tp._silu_mul(torch.zeros(1, 128, dtype=torch.bfloat16), x)
+
+
+def test_layer_ops_argument_validation_without_a_gpu():
+    L = _lib.lib()
+    assert L.tc_add_rmsnorm(None, None, None, None, 0, 64, 1e-6, 2, None) == 0  # no rows: nothing to do
+    assert L.tc_add_rmsnorm(None, None, None, None, 1, 64, 1e-6, 2, None) != 0
+    assert L.tc_add_rmsnorm(None, None, None, None, 1, 0, 1e-6, 2, None) != 0
+    assert L.tc_add_rmsnorm(None, None, None, None, 1, 64, 1e-6, 7, None) != 0
+    assert L.tc_qk_norm_rope(None, None, None, None, None, None, 0, 0, 128, 1e-6, 2, None) == 0
+    assert L.tc_qk_norm_rope(None, None, None, None, None, None, 1, 0, 127, 1e-6, 2, None) != 0
+    assert L.tc_qk_norm_rope(None, None, None, None, None, None, 1, 0, 2048, 1e-6, 2, None) != 0
+    assert L.tc_qk_norm_rope(None, None, None, None, None, None, 1, 1, 128, 1e-6, 2, None) != 0
+    assert L.tc_silu_mul(None, None, 0, 64, 2, None) == 0
+    assert L.tc_silu_mul(None, None, 1, 64, 2, None) != 0
+    assert L.tc_silu_mul(None, None, 1, 0, 2, None) != 0

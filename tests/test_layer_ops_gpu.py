@@ -1,0 +1,84 @@
+"""The tensor-parallel step's fused layer ops (csrc/layer_ops.cuh) against the torch ops of
+transformers' Qwen3 layer they replace (modeling_qwen3: Qwen3RMSNorm, q_norm/k_norm +
+apply_rotary_pos_emb, act_fn(gate) * up), on the same bf16 inputs.
+
+The sum of squares is reduced in a different order than torch's mean, so an element may round to
+the neighbouring bf16 value: the bar is two bf16 ulps, and nearly all elements bit-identical."""
+import pytest
+import torch
+import torch.nn.functional as F
+from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
+
+from threadcut_b200 import _lib, tp
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_device_errors():
+    _lib.device_errors(clear=True)
+    yield
+    assert _lib.device_errors(clear=True) == 0
+
+
+def close_bf16(got, want, min_equal=0.98, row_scale=False):
+    """Within two bf16 ulps of each element (of the row's largest element when row_scale: RoPE's
+    sum can cancel, and a one-ulp change of a term is then large next to the result), and at least
+    `min_equal` of the elements bit-identical."""
+    got, want = got.float(), want.float()
+    mag = want.abs().amax(-1, keepdim=True) if row_scale else want.abs()
+    tol = torch.clamp(mag, min=2 ** -120) * 2 ** -6
+    assert bool(((got - want).abs() <= tol).all()), float((got - want).abs().max())
+    assert float((got == want).float().mean()) >= min_equal
+
+
+@pytest.mark.parametrize("hidden,rows", [(2560, 1), (256, 3), (100, 2)])
+@pytest.mark.parametrize("add", [False, True])
+def test_add_rmsnorm_matches_residual_add_and_qwen3_rmsnorm(hidden, rows, add):
+    g = torch.Generator(device=DEV).manual_seed(hidden + rows)
+    h = torch.randn(rows, hidden, generator=g, device=DEV).to(torch.bfloat16)
+    delta = torch.randn(rows, hidden, generator=g, device=DEV).to(torch.bfloat16) if add else None
+    norm = Qwen3RMSNorm(hidden, eps=1e-6).to(DEV).to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(hidden, generator=g, device=DEV))
+        want_h = h + delta if add else h.clone()
+        want = norm(want_h)
+    out = torch.empty_like(h)
+    tp._add_rmsnorm(h, delta, norm.weight.detach(), out, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(h, want_h)  # the residual add rounds exactly as torch's
+    close_bf16(out, want)
+
+
+@pytest.mark.parametrize("nq,nk,pos", [(32, 8, 98304), (4, 1, 7), (8, 2, 0)])
+def test_qk_norm_rope_matches_qwen3_attention_prologue(nq, nk, pos):
+    d = 128
+    g = torch.Generator(device=DEV).manual_seed(nq * 7 + pos)
+    q = torch.randn(nq, d, generator=g, device=DEV).to(torch.bfloat16)
+    k = torch.randn(nk, d, generator=g, device=DEV).to(torch.bfloat16)
+    qn, kn = Qwen3RMSNorm(d, 1e-6).to(DEV).to(torch.bfloat16), Qwen3RMSNorm(d, 1e-6).to(DEV).to(torch.bfloat16)
+    with torch.no_grad():
+        qn.weight.copy_(1 + 0.1 * torch.randn(d, generator=g, device=DEV))
+        kn.weight.copy_(1 + 0.1 * torch.randn(d, generator=g, device=DEV))
+        inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device=DEV).float() / d))
+        ang = pos * inv
+        emb = torch.cat((ang, ang))
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        wq, wk = apply_rotary_pos_emb(qn(q)[None, :, None], kn(k)[None, :, None], cos[None, None], sin[None, None])
+    q2, k2 = q.clone(), k.clone()
+    tp._qk_norm_rope(q2, k2, qn.weight.detach(), kn.weight.detach(), cos, sin, 1e-6)
+    torch.cuda.synchronize()
+    close_bf16(q2, wq[0, :, 0], row_scale=True)
+    close_bf16(k2, wk[0, :, 0], row_scale=True)
+
+
+@pytest.mark.parametrize("inter,rows", [(9728, 1), (1216, 1), (33, 3)])
+def test_silu_mul_matches_qwen3_mlp_activation(inter, rows):
+    g = torch.Generator(device=DEV).manual_seed(inter)
+    gu = (3 * torch.randn(rows, 2 * inter, generator=g, device=DEV)).to(torch.bfloat16)
+    want = F.silu(gu[:, :inter]) * gu[:, inter:]
+    out = torch.empty(rows, inter, device=DEV, dtype=torch.bfloat16)
+    tp._silu_mul(gu, out)
+    torch.cuda.synchronize()
+    close_bf16(out, want, min_equal=0.99)

@@ -1,8 +1,9 @@
 """Host logic of the tensor-parallel decoder on CPU: weight slicing, the two sums per layer, the
 vocabulary-sliced argmax, and the local-head cache, on one rank and on two `gloo` ranks.
 
-The decode kernel needs a GPU, so these tests replace `tp._attend` (append + attention of one
-step) with a torch restatement on CPU; everything else is the product code. The expected logits
+The kernels need a GPU, so these tests replace the four launches of the step (`tp._attend`: append
++ attention; `_add_rmsnorm`, `_qk_norm_rope`, `_silu_mul`) with torch restatements of HF's Qwen3
+arithmetic on CPU; everything else is the product code. The expected logits
 are the HF model's own fp32 forward over the whole prompt (modeling_qwen3 with eager attention).
 The step also must not read any tensor value back to the host, so that it can be captured in a
 CUDA graph on the GPU."""
@@ -17,6 +18,34 @@ from torch.utils._python_dispatch import TorchDispatchMode
 from transformers import AutoModelForCausalLM, Qwen3Config
 
 from threadcut_b200 import tp
+
+
+def _cpu_add_rmsnorm(h, delta, w, out, eps):
+    if delta is not None:
+        h += delta
+    hf = h.float()
+    out.copy_(w * (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(h.dtype))
+
+
+def _cpu_qk_norm_rope(q, k, wq, wk, cos, sin, eps):
+    for x, w in ((q, wq), (k, wk)):
+        xf = x.float()
+        y = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+        h = y.shape[-1] // 2
+        x.copy_(y * cos + torch.cat((-y[..., h:], y[..., :h]), -1) * sin)
+
+
+def _cpu_silu_mul(gu, out):
+    i = out.shape[1]
+    out.copy_(torch.nn.functional.silu(gu[:, :i]) * gu[:, i:])
+
+
+def _cpu_ops(target):
+    """Put the CPU stand-ins in place of the GPU launches (attribute setter: monkeypatch or setattr)."""
+    target(tp, "_attend", _cpu_attend)
+    target(tp, "_add_rmsnorm", _cpu_add_rmsnorm)
+    target(tp, "_qk_norm_rope", _cpu_qk_norm_rope)
+    target(tp, "_silu_mul", _cpu_silu_mul)
 
 
 def _cpu_attend(layer, q, k, v, scale):
@@ -63,7 +92,7 @@ def _run(rank, world, n_ctx=20):
 
 
 def test_one_rank_equals_the_hf_forward(monkeypatch):
-    monkeypatch.setattr(tp, "_attend", _cpu_attend)
+    _cpu_ops(monkeypatch.setattr)
     ref, logits, tok = _run(0, 1)
     torch.testing.assert_close(logits, ref, atol=1e-4, rtol=0)
     assert int(tok) == int(ref.argmax())
@@ -79,7 +108,7 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        tp._attend = _cpu_attend
+        _cpu_ops(setattr)
         ref, logits, tok = _run(rank, world)
         err = float((logits - ref).abs().max())
         q.put((rank, err, int(tok), int(ref.argmax())))

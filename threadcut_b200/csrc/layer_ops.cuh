@@ -1,0 +1,101 @@
+// Small per-token ops of the tensor-parallel decode step (threadcut_b200/tp.py), one launch each,
+// in place of the chains of torch ops of transformers' Qwen3 layer (modeling_qwen3.py):
+//   add_rmsnorm_kernel:  h = h + delta (rounded to T), x = Qwen3RMSNorm(h): fp32 mean of squares
+//                        (sum times the host-computed 1/H, as torch's mean), rsqrt, cast to T, times
+//                        the weight (rounded to T). One CTA per row.
+//   qk_norm_rope_kernel: per head (q_norm / k_norm, then apply_rotary_pos_emb): RMSNorm over d, then
+//                        x*cos + rotate_half(x)*sin with each product and the sum rounded to T, as
+//                        the torch ops round. In place; one CTA per head, one thread per element.
+//   silu_mul_kernel:     act(gate) * up for Qwen3MLP, with gate and up side by side in one row
+//                        (the output of the fused gate/up projection); silu rounded to T first.
+// They move a few KB per token: launch latency, not bandwidth, is what they save.
+#pragma once
+
+#include <stdint.h>
+
+namespace tc {
+
+constexpr int kNormThreads = 256;
+
+// Sum of v over the block (blockDim.x a multiple of 32, at most 1024); red holds 32 floats.
+__device__ __forceinline__ float block_sum_f32(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red may still be read by an earlier call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ delta,
+                                                                   const T* __restrict__ w, T* __restrict__ x,
+                                                                   int H, float inv_h, float eps) {
+  __shared__ float red[32];
+  const int64_t off = (int64_t)blockIdx.x * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float v = to_f32(h[off + i]);
+    if (delta != nullptr) {
+      const T s = from_f32<T>(v + to_f32(delta[off + i]));
+      h[off + i] = s;
+      v = to_f32(s);
+    }
+    ss += v * v;
+  }
+  ss = block_sum_f32(ss, red);
+  const float r = rsqrtf(ss * inv_h + eps);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const T y = from_f32<T>(to_f32(h[off + i]) * r);
+    x[off + i] = from_f32<T>(to_f32(w[i]) * to_f32(y));
+  }
+}
+
+template <typename T>
+__global__ void qk_norm_rope_kernel(T* __restrict__ q, T* __restrict__ k, const T* __restrict__ wq,
+                                    const T* __restrict__ wk, const T* __restrict__ cosv,
+                                    const T* __restrict__ sinv, int q_heads, int d, float inv_d, float eps) {
+  __shared__ float red[32];
+  extern __shared__ float z[];  // the normed head, for rotate_half
+  const int head = blockIdx.x;
+  const bool is_q = head < q_heads;
+  T* row = is_q ? q + (int64_t)head * d : k + (int64_t)(head - q_heads) * d;
+  const T* w = is_q ? wq : wk;
+  const int i = threadIdx.x;  // blockDim.x = d rounded up to a warp multiple
+  const float xi = i < d ? to_f32(row[i]) : 0.f;
+  const float ss = block_sum_f32(xi * xi, red);
+  const float r = rsqrtf(ss * inv_d + eps);
+  float zi = 0.f;
+  if (i < d) {
+    const T y = from_f32<T>(xi * r);
+    zi = to_f32(from_f32<T>(to_f32(w[i]) * to_f32(y)));
+    z[i] = zi;
+  }
+  __syncthreads();
+  if (i < d) {
+    const int half = d >> 1;
+    const float rot = i < half ? -z[i + half] : z[i - half];
+    const float t1 = to_f32(from_f32<T>(zi * to_f32(cosv[i])));
+    const float t2 = to_f32(from_f32<T>(rot * to_f32(sinv[i])));
+    row[i] = from_f32<T>(t1 + t2);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out,
+                                                                int64_t rows, int inter) {
+  const int64_t total = rows * inter;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rr = t / inter;
+    const int c = (int)(t - rr * inter);
+    const float g = to_f32(gu[rr * 2 * inter + c]);
+    const float act = to_f32(from_f32<T>(g / (1.0f + expf(-g))));
+    out[t] = from_f32<T>(act * to_f32(gu[rr * 2 * inter + inter + c]));
+  }
+}
+
+}  // namespace tc

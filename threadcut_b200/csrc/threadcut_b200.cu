@@ -13,6 +13,7 @@
 #include "paged.cuh"
 #include "split.cuh"
 #include "prefill_attn.cuh"
+#include "layer_ops.cuh"
 
 using namespace tc;
 
@@ -1203,6 +1204,70 @@ int tc_prefill_attention_paged(const void* q, const void* k_pool, const void* v_
     p.lse_part = p.o_part + (size_t)ns * rows * 128;
   }
   return launch_prefill(p, lq, hkv, ns, rows, out, dtype, dev, stream, true);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- per-token layer ops (tensor-parallel step)
+namespace {
+template <typename T>
+int launch_layer_op_t(int op, void* a, void* b, const void* c, const void* d0, const void* e, const void* f,
+                      int64_t rows, int n0, int n1, int d, float eps, cudaStream_t st) {
+  if (op == 0) {
+    add_rmsnorm_kernel<T><<<(unsigned)rows, kNormThreads, 0, st>>>(static_cast<T*>(a), static_cast<const T*>(c),
+                                                                   static_cast<const T*>(d0), static_cast<T*>(b), n0,
+                                                                   1.0f / (float)n0, eps);
+  } else if (op == 1) {
+    const int threads = ((d + 31) / 32) * 32;
+    qk_norm_rope_kernel<T><<<(unsigned)(n0 + n1), threads, d * sizeof(float), st>>>(
+        static_cast<T*>(a), static_cast<T*>(b), static_cast<const T*>(c), static_cast<const T*>(d0),
+        static_cast<const T*>(e), static_cast<const T*>(f), n0, d, 1.0f / (float)d, eps);
+  } else {
+    const int64_t total = rows * n0;
+    const int64_t blocks = (total + kNormThreads - 1) / kNormThreads;
+    silu_mul_kernel<T><<<(unsigned)(blocks < 4096 ? blocks : 4096), kNormThreads, 0, st>>>(
+        static_cast<const T*>(c), static_cast<T*>(a), rows, n0);
+  }
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int launch_layer_op(int dtype, int op, void* a, void* b, const void* c, const void* d0, const void* e, const void* f,
+                    int64_t rows, int n0, int n1, int d, float eps, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TC_BF16) return launch_layer_op_t<__nv_bfloat16>(op, a, b, c, d0, e, f, rows, n0, n1, d, eps, st);
+  if (dtype == TC_F16) return launch_layer_op_t<__half>(op, a, b, c, d0, e, f, rows, n0, n1, d, eps, st);
+  return launch_layer_op_t<float>(op, a, b, c, d0, e, f, rows, n0, n1, d, eps, st);
+}
+}  // namespace
+
+extern "C" {
+
+int tc_add_rmsnorm(void* h, const void* delta, const void* weight, void* out, int64_t rows, int hidden, float eps,
+                   int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (rows < 0 || rows > 0x7fffffff || hidden < 1 || !(eps >= 0.f)) return TC_ERR_INVALID;
+  if (rows == 0) return TC_OK;
+  if (h == nullptr || weight == nullptr || out == nullptr) return TC_ERR_INVALID;
+  return launch_layer_op(dtype, 0, h, out, delta, weight, nullptr, nullptr, rows, hidden, 0, 0, eps, stream);
+}
+
+int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight, const void* cos_t,
+                    const void* sin_t, int q_heads, int k_heads, int d, float eps, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (q_heads < 0 || k_heads < 0 || d < 2 || d % 2 || d > 1024 || !(eps >= 0.f)) return TC_ERR_INVALID;
+  if (q_heads + k_heads == 0) return TC_OK;
+  if ((q_heads && (q == nullptr || q_weight == nullptr)) || (k_heads && (k == nullptr || k_weight == nullptr)) ||
+      cos_t == nullptr || sin_t == nullptr)
+    return TC_ERR_INVALID;
+  return launch_layer_op(dtype, 1, q, k, q_weight, k_weight, cos_t, sin_t, 1, q_heads, k_heads, d, eps, stream);
+}
+
+int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (rows < 0 || inter < 1 || rows > ((int64_t)1 << 40) / inter) return TC_ERR_INVALID;
+  if (rows == 0) return TC_OK;
+  if (gate_up == nullptr || out == nullptr) return TC_ERR_INVALID;
+  return launch_layer_op(dtype, 2, out, nullptr, gate_up, nullptr, nullptr, nullptr, rows, inter, 0, 0, 0.f, stream);
 }
 
 }  // extern "C"

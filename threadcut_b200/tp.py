@@ -18,30 +18,52 @@ all ranks' vocabulary slices (torch's argmax rule), found from an all-gather of 
 the weights' dtype, q/k RMSNorm per head, RoPE with cos/sin rounded to the model dtype, SwiGLU),
 so at world == 1 the step is the HF forward with threadcut_b200's attention.
 
+The small ops between the projections run as one launch each (csrc/layer_ops.cuh): the residual
+add fused with the next RMSNorm, q/k norm fused with RoPE, and SwiGLU; the q/k/v and the gate/up
+projections are one GEMV each (their rows side by side). That is about 9 launches and 2 all-reduces
+per layer instead of HF's ~50 kernels, and the whole step can be captured in a CUDA graph
+(`capture`): it reads nothing back to the host.
+
 The cache is the rank's heads only, kept as GrowingLayers: a splice (kv.splice) re-rotates and
-moves only the local heads, with no exchange. There is no CPU path: the attention kernel needs CUDA.
+moves only the local heads, with no exchange. There is no CPU path: the kernels need CUDA.
 """
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 from . import kv as _kv
+from ._lib import check, dtype_code, lib, require_cuda, stream_ptr
 from .flash_decode import decode_attention_append
 from .sharded import head_shard
 
 __all__ = ["TPDecoder"]
 
 
-def _rms(x, w, eps):
-    """Qwen3RMSNorm.forward: fp32 mean of squares, rsqrt, cast back, times the weight."""
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return w * xf.to(x.dtype)
+def _add_rmsnorm(h, delta, w, out, eps):
+    """h [rows, H] += delta (None: no add), out = Qwen3RMSNorm(h) with weight w [H]; one launch
+    (tc_add_rmsnorm). All contiguous, one dtype, on one GPU."""
+    require_cuda(h, w, out, *(() if delta is None else (delta,)), what="add_rmsnorm")
+    st = lib().tc_add_rmsnorm(h.data_ptr(), None if delta is None else delta.data_ptr(), w.data_ptr(),
+                              out.data_ptr(), h.shape[0], h.shape[1], float(eps), dtype_code(h, "add_rmsnorm"),
+                              stream_ptr(h.device))
+    check("tc_add_rmsnorm", st)
 
 
-def _rotate_half(x):
-    h = x.shape[-1] // 2
-    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+def _qk_norm_rope(q, k, wq, wk, cos, sin, eps):
+    """In place: q [hq, d], k [hk, d] := RoPE(RMSNorm per head) (q_norm/k_norm weights wq, wk [d],
+    cos/sin [d] of the model dtype); one launch (tc_qk_norm_rope)."""
+    require_cuda(q, k, wq, wk, cos, sin, what="qk_norm_rope")
+    st = lib().tc_qk_norm_rope(q.data_ptr(), k.data_ptr(), wq.data_ptr(), wk.data_ptr(), cos.data_ptr(),
+                               sin.data_ptr(), q.shape[0], k.shape[0], q.shape[1], float(eps),
+                               dtype_code(q, "qk_norm_rope"), stream_ptr(q.device))
+    check("tc_qk_norm_rope", st)
+
+
+def _silu_mul(gu, out):
+    """out [rows, I] = silu(gu[:, :I]) * gu[:, I:] (gate and up side by side); one launch."""
+    require_cuda(gu, out, what="silu_mul")
+    st = lib().tc_silu_mul(gu.data_ptr(), out.data_ptr(), gu.shape[0], out.shape[1], dtype_code(gu, "silu_mul"),
+                           stream_ptr(gu.device))
+    check("tc_silu_mul", st)
 
 
 def _attend(layer, q, k, v, scale):
@@ -65,16 +87,15 @@ class _Shard:
         def cols(w, lo, hi):
             return w.detach()[:, lo:hi].to(dev).contiguous()
 
-        self.wq = rows(at.q_proj.weight, h0 * g * d, h1 * g * d)
-        self.wk = rows(at.k_proj.weight, h0 * d, h1 * d)
-        self.wv = rows(at.v_proj.weight, h0 * d, h1 * d)
+        # q, k and v rows of this rank side by side: one projection per step
+        self.wqkv = torch.cat((rows(at.q_proj.weight, h0 * g * d, h1 * g * d), rows(at.k_proj.weight, h0 * d, h1 * d),
+                               rows(at.v_proj.weight, h0 * d, h1 * d)))
         self.wo = cols(at.o_proj.weight, h0 * g * d, h1 * g * d)
         self.q_norm = at.q_norm.weight.detach().to(dev)
         self.k_norm = at.k_norm.weight.detach().to(dev)
         self.in_norm = layer.input_layernorm.weight.detach().to(dev)
         self.post_norm = layer.post_attention_layernorm.weight.detach().to(dev)
-        self.wg = rows(mlp.gate_proj.weight, i0, i1)
-        self.wu = rows(mlp.up_proj.weight, i0, i1)
+        self.wgu = torch.cat((rows(mlp.gate_proj.weight, i0, i1), rows(mlp.up_proj.weight, i0, i1)))  # gate | up
         self.wd = cols(mlp.down_proj.weight, i0, i1)
         for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
             if getattr(at, name).bias is not None:
@@ -154,25 +175,34 @@ class TPDecoder:
         return x
 
     def _final_hidden(self, token, pos):
-        """The step's arithmetic up to the final norm: [1, hidden] (appends the token's K/V row)."""
+        """The step's arithmetic up to the final norm: [1, hidden] (appends the token's K/V row).
+        Per layer: the q/k/v projection, q/k norm + RoPE (one launch), attention with the fused
+        append, o_proj, sum over ranks, residual add + post-attention norm (one launch), the gate/up
+        projection, SwiGLU (one launch), down_proj, sum over ranks, and the residual add fused with
+        the next layer's input norm (the final norm after the last layer)."""
         hr, d, g = self.h1 - self.h0, self.d, self.g
-        h = self.embed[token]  # [1, hidden]
+        nq, eps = hr * g, self.eps
+        h = self.embed[token]  # [1, hidden], a fresh tensor (advanced indexing copies)
+        x = torch.empty_like(h)
         ang = float(pos) * self.inv_freq
         emb = torch.cat((ang, ang))
         cos = (emb.cos() * self.attn_scaling).to(self.dtype)
         sin = (emb.sin() * self.attn_scaling).to(self.dtype)
-        for w, layer in zip(self.layers_w, self.layers):
-            x = _rms(h, w.in_norm, self.eps)
-            q = _rms((x @ w.wq.t()).view(hr * g, d), w.q_norm, self.eps)
-            k = _rms((x @ w.wk.t()).view(hr, d), w.k_norm, self.eps)
-            v = (x @ w.wv.t()).view(hr, d)
-            q = q * cos + _rotate_half(q) * sin
-            k = k * cos + _rotate_half(k) * sin
+        _add_rmsnorm(h, None, self.layers_w[0].in_norm, x, eps)
+        nxt = [w.in_norm for w in self.layers_w[1:]] + [self.final_norm]
+        for w, layer, norm_next in zip(self.layers_w, self.layers, nxt):
+            qkv = (x @ w.wqkv.t())[0]
+            q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
+            _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
             o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
-            h = h + self._all_reduce(o.reshape(1, hr * g * d) @ w.wo.t())
-            x = _rms(h, w.post_norm, self.eps)
-            h = h + self._all_reduce((F.silu(x @ w.wg.t()) * (x @ w.wu.t())) @ w.wd.t())
-        return _rms(h, self.final_norm, self.eps)
+            a = self._all_reduce(o.reshape(1, nq * d) @ w.wo.t())
+            _add_rmsnorm(h, a, w.post_norm, x, eps)
+            gu = x @ w.wgu.t()
+            act = gu.new_empty((1, gu.shape[1] // 2))
+            _silu_mul(gu, act)
+            m = self._all_reduce(act @ w.wd.t())
+            _add_rmsnorm(h, m, norm_next, x, eps)
+        return x
 
     def step(self, token, pos):
         """Decode `token` (int64 device tensor [1]) at position `pos` (the cache length before the
