@@ -685,6 +685,9 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
 
     with torch.no_grad():
         eager_ms = timed(eager)
+        with torch.cuda.nvtx.range("cfg5_tp_step"):  # one eager step, for a profiler's launch list
+            eager()
+        torch.cuda.synchronize(dev)
         graph, out, ok = None, None, 1.0
         try:
             graph, out = dec.capture(tok, n)
