@@ -20,7 +20,7 @@
  *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
  *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
  *                             append into page slots (kv.py:64-77 GrowingLayer.update semantics)
- *   tc_add_rmsnorm, tc_qk_norm_rope, tc_silu_mul
+ *   tc_add_rmsnorm, tc_qk_norm_rope, tc_silu_mul, tc_gemv
  *                             threadcut/engine.py:66-73         the per-token model call, run by
  *                             transformers' Qwen3 layer (RMSNorm, q/k norm + RoPE, SwiGLU) there; here
  *                             one launch each in the tensor-parallel decode step
@@ -391,6 +391,11 @@ int tc_add_rmsnorm(void* h, const void* delta, const void* weight, void* out, in
  * dtype (apply_rotary_pos_emb). d even, at most 1024. */
 int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight, const void* cos_t,
                     const void* sin_t, int q_heads, int k_heads, int d, float eps, int dtype, void* stream);
+
+/* tc_gemv: out[i] = sum_k x[k] * w[i][k] for i < n (x [k], w [n][k] row-major, out [n]): the one-token
+ * projections of the step (nn.Linear with no bias), fp32 accumulation rounded once to dtype. 16-bit
+ * dtypes, k a multiple of 8 and at most 24576, x and w 16-byte aligned (else TC_ERR_ALIGN). */
+int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream);
 
 /* tc_silu_mul: out[r][i] = dtype(silu(gate_up[r][i])) * gate_up[r][inter + i] for `rows` rows
  * (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), gate and up side by side in one row). */

@@ -312,3 +312,13 @@ def test_layer_ops_argument_validation_without_a_gpu():
     assert L.tc_silu_mul(None, None, 0, 64, 2, None) == 0
     assert L.tc_silu_mul(None, None, 1, 64, 2, None) != 0
     assert L.tc_silu_mul(None, None, 1, 0, 2, None) != 0
+
+
+def test_gemv_argument_validation_without_a_gpu():
+    L = _lib.lib()
+    assert L.tc_gemv(None, None, None, 0, 64, 2, None) == 0  # no rows: nothing to do
+    assert L.tc_gemv(None, None, None, 4, 64, 2, None) != 0  # null operands
+    assert L.tc_gemv(16, 32, 64, 4, 60, 2, None) != 0  # k not a multiple of 8
+    assert L.tc_gemv(16, 32, 64, 4, 64, 0, None) != 0  # fp32: not supported
+    assert L.tc_gemv(8, 32, 64, 4, 64, 2, None) != 0   # x not 16-byte aligned (rejected before any access)
+    assert L.tc_gemv(16, 32, 64, 4, 32768, 2, None) != 0  # x would not fit in shared memory

@@ -82,3 +82,23 @@ def test_silu_mul_matches_qwen3_mlp_activation(inter, rows):
     tp._silu_mul(gu, out)
     torch.cuda.synchronize()
     close_bf16(out, want, min_equal=0.99)
+
+
+@pytest.mark.parametrize("n,k,dtype", [(6144, 2560, torch.bfloat16), (2560, 4096, torch.bfloat16),
+                                       (2560, 9728, torch.bfloat16), (19456, 2560, torch.bfloat16),
+                                       (18992, 2560, torch.bfloat16), (7, 16, torch.bfloat16),
+                                       (1000, 1216, torch.float16)])
+def test_gemv_matches_the_library_projection(n, k, dtype):
+    """tc_gemv against nn.Linear's matmul (cuBLAS) on the same 16-bit operands: both accumulate in
+    fp32 and round once, in different orders, so results agree to a rounding step."""
+    g = torch.Generator(device=DEV).manual_seed(n + k)
+    x = torch.randn(1, k, generator=g, device=DEV).to(dtype)
+    w = (torch.randn(n, k, generator=g, device=DEV) * k ** -0.5).to(dtype)
+    got = tp._gemv(x, w)
+    want = x @ w.t()
+    exact = (x.float() @ w.float().t())
+    torch.cuda.synchronize()
+    assert got.shape == (1, n) and got.dtype == dtype
+    torch.testing.assert_close(got.float(), want.float(), rtol=2 ** -6, atol=1e-3)
+    torch.testing.assert_close(got.float(), exact, rtol=2 ** -7, atol=1e-3)
+    assert float((got == want).float().mean()) >= 0.8

@@ -59,6 +59,7 @@ SIGNATURES = {
     "tc_add_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _f, _i, _vp]),
     "tc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp]),
     "tc_silu_mul": (_i, [_vp, _vp, _i64, _i, _i, _vp]),
+    "tc_gemv": (_i, [_vp, _vp, _vp, _i64, _i, _i, _vp]),
     "tc_decode_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64,
                                        _i64, _vp, _vp, _i64, _i64] + [_i64] * 4 + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_prefill_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp,

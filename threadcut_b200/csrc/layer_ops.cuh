@@ -8,6 +8,7 @@
 //                        the torch ops round. In place; one CTA per head, one thread per element.
 //   silu_mul_kernel:     act(gate) * up for Qwen3MLP, with gate and up side by side in one row
 //                        (the output of the fused gate/up projection); silu rounded to T first.
+//   gemv_kernel:         the step's projections (one token: x [K] times w [N][K]^T), HBM-bound.
 // They move a few KB per token: launch latency, not bandwidth, is what they save.
 #pragma once
 
@@ -52,6 +53,103 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* __restrict
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     const T y = from_f32<T>(to_f32(h[off + i]) * r);
     x[off + i] = from_f32<T>(to_f32(w[i]) * to_f32(y));
+  }
+}
+
+// 16-bit T only: H % 8 == 0 and H / 8 <= kNormThreads * MAXC. Same arithmetic as add_rmsnorm_kernel,
+// with 16-byte loads and the row kept in registers between the two passes.
+template <typename T, int MAXC>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_vec_kernel(T* __restrict__ h,
+                                                                       const T* __restrict__ delta,
+                                                                       const T* __restrict__ w, T* __restrict__ x,
+                                                                       int H, float inv_h, float eps) {
+  __shared__ float red[32];
+  const int64_t off = (int64_t)blockIdx.x * (H / 8);
+  uint4* hr = reinterpret_cast<uint4*>(h) + off;
+  const uint4* dr = delta != nullptr ? reinterpret_cast<const uint4*>(delta) + off : nullptr;
+  const int hc = H / 8;
+  uint4 hv[MAXC];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < hc) {
+      hv[j] = hr[c];
+      T* e = reinterpret_cast<T*>(&hv[j]);
+      if (dr != nullptr) {
+        const uint4 dv = dr[c];
+        const T* de = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) e[t] = from_f32<T>(to_f32(e[t]) + to_f32(de[t]));
+        hr[c] = hv[j];
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float v = to_f32(e[t]);
+        ss += v * v;
+      }
+    }
+  }
+  ss = block_sum_f32(ss, red);
+  const float r = rsqrtf(ss * inv_h + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* xr = reinterpret_cast<uint4*>(x) + off;
+#pragma unroll
+  for (int j = 0; j < MAXC; ++j) {
+    const int c = threadIdx.x + j * kNormThreads;
+    if (c < hc) {
+      const uint4 wv = wr[c];
+      const T* we = reinterpret_cast<const T*>(&wv);
+      const T* e = reinterpret_cast<const T*>(&hv[j]);
+      uint4 ov;
+      T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) oe[t] = from_f32<T>(to_f32(we[t]) * to_f32(from_f32<T>(to_f32(e[t]) * r)));
+      xr[c] = ov;
+    }
+  }
+}
+
+// out[row] = sum_k x[k] * w[row][k] for a one-row x (the decode step's projections): 16-bit T,
+// K % 8 == 0, x and w 16-byte aligned. x is staged in shared memory; each warp streams whole weight
+// rows with 16-byte non-coherent loads (the weights are read once per step) and reduces across
+// lanes; fp32 accumulation, one rounding to T, as a library GEMM does.
+constexpr int kGemvWarps = 8;
+
+__device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc, __nv_bfloat16*) {
+  const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a));
+  const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+  return fmaf(fa.y, fb.y, fmaf(fa.x, fb.x, acc));
+}
+__device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc, __half*) {
+  const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  return fmaf(fa.y, fb.y, fmaf(fa.x, fb.x, acc));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                               T* __restrict__ out, int64_t N, int K) {
+  extern __shared__ uint4 xs[];
+  const int kc = K / 8;
+  for (int i = threadIdx.x; i < kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kGemvWarps + warp; row < N; row += (int64_t)gridDim.x * kGemvWarps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w + row * (int64_t)K);
+    float acc = 0.f;
+#pragma unroll 8
+    for (int c = lane; c < kc; c += 32) {
+      const uint4 a = __ldg(wr + c);
+      const uint4 b = xs[c];
+      acc = dot2(a.x, b.x, acc, (T*)nullptr);
+      acc = dot2(a.y, b.y, acc, (T*)nullptr);
+      acc = dot2(a.z, b.z, acc, (T*)nullptr);
+      acc = dot2(a.w, b.w, acc, (T*)nullptr);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[row] = from_f32<T>(acc);
   }
 }
 

@@ -1214,9 +1214,17 @@ template <typename T>
 int launch_layer_op_t(int op, void* a, void* b, const void* c, const void* d0, const void* e, const void* f,
                       int64_t rows, int n0, int n1, int d, float eps, cudaStream_t st) {
   if (op == 0) {
-    add_rmsnorm_kernel<T><<<(unsigned)rows, kNormThreads, 0, st>>>(static_cast<T*>(a), static_cast<const T*>(c),
-                                                                   static_cast<const T*>(d0), static_cast<T*>(b), n0,
-                                                                   1.0f / (float)n0, eps);
+    const bool vec = sizeof(T) == 2 && n0 % 8 == 0 && n0 / 8 <= kNormThreads * 4 &&
+                     ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                       reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d0)) & 15) == 0;
+    if (vec)
+      add_rmsnorm_vec_kernel<T, 4><<<(unsigned)rows, kNormThreads, 0, st>>>(
+          static_cast<T*>(a), static_cast<const T*>(c), static_cast<const T*>(d0), static_cast<T*>(b), n0,
+          1.0f / (float)n0, eps);
+    else
+      add_rmsnorm_kernel<T><<<(unsigned)rows, kNormThreads, 0, st>>>(static_cast<T*>(a), static_cast<const T*>(c),
+                                                                     static_cast<const T*>(d0), static_cast<T*>(b),
+                                                                     n0, 1.0f / (float)n0, eps);
   } else if (op == 1) {
     const int threads = ((d + 31) / 32) * 32;
     qk_norm_rope_kernel<T><<<(unsigned)(n0 + n1), threads, d * sizeof(float), st>>>(
@@ -1260,6 +1268,28 @@ int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight
       cos_t == nullptr || sin_t == nullptr)
     return TC_ERR_INVALID;
   return launch_layer_op(dtype, 1, q, k, q_weight, k_weight, cos_t, sin_t, 1, q_heads, k_heads, d, eps, stream);
+}
+
+int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (n < 0 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
+  if (n == 0) return TC_OK;
+  if (x == nullptr || w == nullptr || out == nullptr) return TC_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return TC_ERR_CUDA;
+  const int64_t want = (n + kGemvWarps - 1) / kGemvWarps;
+  const unsigned grid = (unsigned)(want < (int64_t)sms * 64 ? want : (int64_t)sms * 64);
+  const size_t smem = (size_t)k * 2;
+  if (dtype == TC_BF16)
+    gemv_kernel<__nv_bfloat16><<<grid, kGemvWarps * 32, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), n, k);
+  else
+    gemv_kernel<__half><<<grid, kGemvWarps * 32, smem, st>>>(static_cast<const __half*>(x), static_cast<const __half*>(w),
+                                                             static_cast<__half*>(out), n, k);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
 int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream) {

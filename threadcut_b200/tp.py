@@ -20,7 +20,7 @@ so at world == 1 the step is the HF forward with threadcut_b200's attention.
 
 The small ops between the projections run as one launch each (csrc/layer_ops.cuh): the residual
 add fused with the next RMSNorm, q/k norm fused with RoPE, and SwiGLU; the q/k/v and the gate/up
-projections are one GEMV each (their rows side by side). That is about 9 launches and 2 all-reduces
+projections are one GEMV each (their rows side by side), and every projection runs tc_gemv. That is about 9 launches and 2 all-reduces
 per layer instead of HF's ~50 kernels, and the whole step can be captured in a CUDA graph
 (`capture`): it reads nothing back to the host.
 
@@ -64,6 +64,21 @@ def _silu_mul(gu, out):
     st = lib().tc_silu_mul(gu.data_ptr(), out.data_ptr(), gu.shape[0], out.shape[1], dtype_code(gu, "silu_mul"),
                            stream_ptr(gu.device))
     check("tc_silu_mul", st)
+
+
+def _gemv(x, w):
+    """x [1, K] @ w[N, K]^T -> [1, N] for the one-token projections: tc_gemv (HBM-bound, fp32
+    accumulation) for contiguous 16-bit operands with K a multiple of 8 and 16-byte aligned; other
+    operands take the GPU library matmul. CPU tensors raise."""
+    require_cuda(x, w, what="gemv")
+    n, k = w.shape
+    if (x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.is_contiguous() and w.is_contiguous()
+            and k % 8 == 0 and k <= 24576 and x.numel() == k and (x.data_ptr() | w.data_ptr()) % 16 == 0):
+        out = x.new_empty((1, n))
+        check("tc_gemv", lib().tc_gemv(x.data_ptr(), w.data_ptr(), out.data_ptr(), n, k, dtype_code(x, "gemv"),
+                                       stream_ptr(x.device)))
+        return out
+    return x @ w.t()
 
 
 def _attend(layer, q, k, v, scale):
@@ -191,23 +206,23 @@ class TPDecoder:
         _add_rmsnorm(h, None, self.layers_w[0].in_norm, x, eps)
         nxt = [w.in_norm for w in self.layers_w[1:]] + [self.final_norm]
         for w, layer, norm_next in zip(self.layers_w, self.layers, nxt):
-            qkv = (x @ w.wqkv.t())[0]
+            qkv = _gemv(x, w.wqkv)[0]
             q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
             _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
             o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
-            a = self._all_reduce(o.reshape(1, nq * d) @ w.wo.t())
+            a = self._all_reduce(_gemv(o.reshape(1, nq * d), w.wo))
             _add_rmsnorm(h, a, w.post_norm, x, eps)
-            gu = x @ w.wgu.t()
+            gu = _gemv(x, w.wgu)
             act = gu.new_empty((1, gu.shape[1] // 2))
             _silu_mul(gu, act)
-            m = self._all_reduce(act @ w.wd.t())
+            m = self._all_reduce(_gemv(act, w.wd))
             _add_rmsnorm(h, m, norm_next, x, eps)
         return x
 
     def step(self, token, pos):
         """Decode `token` (int64 device tensor [1]) at position `pos` (the cache length before the
         step); returns the greedy next token (int64 device tensor [1])."""
-        logits = (self._final_hidden(token, pos) @ self.lm_head.t())[0]  # this rank's vocabulary slice
+        logits = _gemv(self._final_hidden(token, pos), self.lm_head)[0]  # this rank's vocabulary slice
         idx = logits.argmax()  # first index of the slice's maximum
         if self.world == 1:
             return idx.view(1)
@@ -237,7 +252,7 @@ class TPDecoder:
     def logits(self, token, pos):
         """The full next-token logits (fp32 [vocab]) of `token` at `pos`, for checks: the step's
         arithmetic with the vocabulary slices all-gathered. Appends the token's row like step."""
-        part = (self._final_hidden(token, pos) @ self.lm_head.t())[0].float()
+        part = _gemv(self._final_hidden(token, pos), self.lm_head)[0].float()
         if self.world == 1:
             return part
         parts = [torch.empty_like(part) for _ in range(self.world)]
