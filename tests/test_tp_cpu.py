@@ -138,3 +138,14 @@ def test_uneven_splits_are_rejected():
     model = _model()
     with pytest.raises(ValueError):
         tp.TPDecoder(model, "cpu", world=3, rank=0)  # 2 KV heads over 3 ranks
+
+
+def test_unsupported_attention_kinds_are_rejected():
+    model = _model()
+    model.config.use_sliding_window = True
+    with pytest.raises(ValueError):
+        tp.TPDecoder(model, "cpu", world=1, rank=0)
+    model.config.use_sliding_window = False
+    model.config.rope_parameters = {"rope_type": "dynamic", "rope_theta": 1e6, "factor": 2.0}
+    with pytest.raises(ValueError):
+        tp.TPDecoder(model, "cpu", world=1, rank=0)

@@ -159,7 +159,9 @@ class GrowingLayer(DynamicLayer):
     a one-token update on a CUDA cache does not write the row; it returns the views with the row
     pending, and the decode branch of threadcut_b200.attention writes it in the same launch that
     reads the cache (tc_decode_attention_append). Any other use of the cache (another update,
-    crop, splice, a prefill or batched attention call) writes the pending row first."""
+    crop, splice, a prefill or batched attention call) writes the pending row first. A model switched
+    to another attention implementation after new_cache reads the cache itself: set fuse_append to
+    False on its layers, or the step's row is not in the buffer when that attention reads it."""
 
     fuse_append = False
 

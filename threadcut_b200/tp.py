@@ -128,6 +128,12 @@ class TPDecoder:
 
     def __init__(self, model, device, group=None, world=None, rank=None):
         cfg = model.config
+        kinds = set(getattr(cfg, "layer_types", None) or ["full_attention"])
+        if getattr(cfg, "use_sliding_window", False) or kinds != {"full_attention"}:
+            raise ValueError("TPDecoder: sliding-window attention layers are not supported")
+        rope = (getattr(cfg, "rope_parameters", None) or {}).get("rope_type", "default")
+        if rope in ("dynamic", "longrope"):
+            raise ValueError(f"TPDecoder: RoPE type {rope!r} changes its frequencies with the length")
         self.group = group
         self.world = world if world is not None else (dist.get_world_size(group) if dist.is_initialized() else 1)
         self.rank = rank if rank is not None else (dist.get_rank(group) if dist.is_initialized() else 0)
