@@ -4,15 +4,19 @@ peak at 16k context (BASELINE metric), plus the RoPE-shift splice GB/s.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = decode attention for all 36 Qwen3-4B layers (one query token, 32 q / 8 KV heads,
-head_dim 128, bf16) over a 16384-token cache, every layer its own K/V buffer (36 x 67 MB = 2.4 GB
-per step, far above the 126 MB L2, so no flush is needed). `value` is µs per layer (device time,
-CUDA events, the 36 launches replayed from a CUDA graph), max over ranks; with N GPUs every rank
-runs its own 36 layers (weak scaling, no collective on the data path) and value = time / (36*N).
+head_dim 128, bf16) of one sequence, every layer its own K/V buffer. On N GPUs the sequence holds
+16384 x N tokens and its KV heads are sharded over the GPUs (8 / N per GPU), so every GPU streams
+67 MB per layer (36 x 67 MB = 2.4 GB per step, far above the 126 MB L2, so no flush is needed), and
+the step ends with an all-gather of every layer's outputs to every rank. At N = 1 this is the 16k
+decode; at N = 8 the 128k sequence with one KV head per GPU. `value` is µs per layer of the job
+divided by N (µs per layer per 16k tokens of context: device time, CUDA events, the step replayed
+from a CUDA graph, max over ranks), so the driver's v_1 / v_N is the weak-scaling efficiency.
 `e2e` is the same metric through the public API (`threadcut_b200.flash_decode.decode_attention`,
-one Python call per layer) with each step's queries copied host->device from pinned memory and the
-outputs read back device->host inside the timed region.
-`--impl reference` times the reference's CPU path (the numpy restatement in oracle/, fp32, all host
-threads) on the same workload and prints the same line with "impl": "reference".
+one Python call per layer, and the all-gather) with each step's queries copied host->device from
+pinned memory and the gathered outputs read back device->host inside the timed region.
+`--impl reference` times the reference's CPU path (its torch decode expression on CPU tensors,
+oracle/torch_ref.py, bf16, every host core) on the same workload and prints the same line with
+"impl": "reference".
 """
 import argparse
 import json
@@ -30,6 +34,8 @@ sys.path.insert(0, HERE)
 import workloads  # noqa: E402
 
 METRIC = "flash-decode µs/layer & % of HBM peak (Qwen3-4B GQA, 16k ctx); shift GB/s"
+WORKLOAD = ("cfg3-16k: 36-layer split-KV GQA decode of one sequence of 16384 x N tokens over N GPUs, 32 q / 8 kv "
+            "heads, head_dim 128, KV heads sharded over the GPUs, one K/V buffer per layer")
 N_CTX = 16384
 LAYERS = workloads.LAYERS
 
@@ -144,40 +150,48 @@ def barrier(dist):
 
 
 # ------------------------------------------------------------------ our arm
-def build_layers(n, layers, dev, seed):
-    ks, vs = workloads.layer_kv(n, layers, dev, seed=seed)
+def build_layers(n, layers, dev, seed, heads=8):
+    ks, vs = workloads.layer_kv(n, layers, dev, seed=seed, heads=heads)
     g = torch.Generator(device=dev).manual_seed(seed + 1)
-    qs = [torch.randn(8, 4, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
+    qs = [torch.randn(heads, 4, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(layers)]
     return qs, ks, vs
 
 
-def capture_step(qs, ks, vs, outs, dev, stable=True):
+def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None):
     """CUDA graph of one step: the 36 decode launches through the C ABI with preallocated outputs.
     stable: declare rows [0, n-1) stable (tc_decode_attention_stable), as a decode step may: every
-    row but the newest was written before the step; False runs plain tc_decode_attention."""
+    row but the newest was written before the step; False runs plain tc_decode_attention.
+    combine: None, or (dist, local [layers, hl, 4, 128] whose slices are `outs`, full
+    [world * layers * hl * 4 * 128]) to all-gather every rank's outputs of the step into `full`
+    inside the graph (the head-sharded step's output combine)."""
     from threadcut_b200._lib import TC_BF16, check, lib, workspaces
     L = lib()
     n = ks[0].shape[1]
-    ws = workspaces.get(("decode", 8), dev, L.tc_decode_attention_workspace_size(1, 8, 4, 128, n, n, 0, TC_BF16))
+    hl = qs[0].shape[0]
+    ws = workspaces.get(("decode", hl), dev, L.tc_decode_attention_workspace_size(1, hl, 4, 128, n, n, 0, TC_BF16))
 
     stable_rows = n - 1 if stable else 0
 
     def launch_all():
         st = torch.cuda.current_stream(dev).cuda_stream
         for q, k, v, o in zip(qs, ks, vs, outs):
-            rc = L.tc_decode_attention_stable(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 8, 4, 128, n,
+            rc = L.tc_decode_attention_stable(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128, n,
                                               q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0),
                                               v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16,
                                               stable_rows, ws.data_ptr(), ws.numel(), st)
             check("tc_decode_attention_stable", rc)
+        if combine is not None:
+            dist_, local, full = combine
+            dist_.all_gather_into_tensor(full, local.view(-1))
 
-    launch_all()  # eager warm-up (also sets the kernels' shared-memory attributes)
-    torch.cuda.synchronize()
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        launch_all()  # eager warm-up on the capture stream (kernel attributes, workspace, communicator)
+    torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
-        with torch.cuda.graph(graph, stream=s):
+        with torch.cuda.graph(graph, stream=s, capture_error_mode="thread_local"):
             launch_all()
     torch.cuda.current_stream(dev).wait_stream(s)
     torch.cuda.synchronize()
@@ -198,19 +212,26 @@ def time_graph(graph, steps, warmup, dist):
     return e0.elapsed_time(e1) / steps  # ms per step on this rank
 
 
-def time_e2e(qs, ks, vs, steps, warmup, dist, dev):
-    """Public-API path: pinned host queries -> device, 36 decode_attention calls, outputs -> host."""
+def time_e2e(qs, ks, vs, steps, warmup, dist, dev, world=1):
+    """Public-API path: pinned host queries -> device, 36 decode_attention calls over this rank's
+    heads, (N > 1) one all-gather of the step's outputs over the ranks, outputs -> host."""
     from threadcut_b200.flash_decode import decode_attention
     host_q = torch.stack([q.cpu() for q in qs]).pin_memory()
-    host_out = torch.empty_like(host_q).pin_memory()
     dq = torch.empty_like(host_q, device=dev)
+    full = torch.empty((world * host_q.numel(),), dtype=host_q.dtype, device=dev)
+    host_out = torch.empty(full.shape, dtype=full.dtype).pin_memory()
 
     n = ks[0].shape[1]
 
     def step():
         dq.copy_(host_q, non_blocking=True)
-        outs = [decode_attention(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1) for i in range(len(ks))]
-        host_out.copy_(torch.stack(outs), non_blocking=True)
+        outs = torch.stack([decode_attention(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1)
+                            for i in range(len(ks))])
+        if world > 1:
+            dist.all_gather_into_tensor(full, outs.view(-1))
+        else:
+            full.copy_(outs.view(-1))
+        host_out.copy_(full, non_blocking=True)
 
     for _ in range(warmup):
         step()
@@ -622,40 +643,46 @@ def time_cfg5_step(steps, warmup, dev):
 
 def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
     """Config 5 over `world` GPUs: threadcut_b200.tp.TPDecoder (rank r holds KV heads
-    head_shard(8, r, world), their query heads, 1/world of the MLP and of the vocabulary; two NCCL
+    head_shard(8, r, world), their query heads, 1/world of the MLP and of the vocabulary; two
     all-reduces per layer) decoding one greedy token of random-init Qwen3-4B over the 131,072-token
-    cache spliced to 98,304 (each rank splices its own heads). Each step is the token's forward plus
-    the next token read back to the host; the appended row is cropped after each step so every step
-    decodes at the same length. Eager and replayed from a CUDA graph (the all-reduces inside it).
-    Returns (eager ms, graph ms or None, splice ms, per-rank bytes per token), max over ranks."""
+    cache spliced to 98,304 (each rank splices its own heads). Every rank first computes the
+    expected token the torch way: HF's forward with SDPA attention over the full-head cache spliced
+    the same way (the same seeded K/V on every rank), and the decoder's token is compared with it.
+    Each timed step is the token's forward plus the next token read back to the host; the appended
+    row is cropped after each step so every step decodes at the same length. Eager and replayed from
+    a CUDA graph (the all-reduces inside it). Returns a dict (times max over ranks)."""
     from transformers import AutoModelForCausalLM
+    from threadcut_b200.kv import new_cache, splice as kv_splice
     from threadcut_b200.match import Split
     from threadcut_b200.tp import TPDecoder
     torch.manual_seed(0)
+    cfg = workloads.qwen3_4b_config()
     with torch.device(dev):
-        model = AutoModelForCausalLM.from_config(workloads.qwen3_4b_config(), dtype=torch.bfloat16)
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation="sdpa")
+    model.eval()
     dec = TPDecoder(model, dev, world=world, rank=rank)
-    hr = dec.h1 - dec.h0
     shard_bytes = sum(t.numel() * t.element_size() for w in dec.layers_w for t in vars(w).values()
                       if isinstance(t, torch.Tensor)) + dec.lm_head.numel() * dec.lm_head.element_size()
     inv = model.model.rotary_emb.inv_freq.detach().to(dev)
-    del model
-    torch.cuda.empty_cache()
     ctx = workloads.CFG5_CTX
     lo, hi = workloads.CFG5_PRUNE
     s = Split(lo, hi, ctx - hi)
-    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    n = s.a + s.c
+    ref_cache = new_cache(model.config)  # GrowingLayers; no fused append under SDPA attention
+    gen = torch.Generator(device=dev).manual_seed(0)
     for i in range(len(dec.layers)):
-        k = torch.randn(1, hr, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
-        v = torch.randn(1, hr, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
-        dec.load_local(i, k, v)
+        k = torch.randn(1, workloads.HKV, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, workloads.HKV, ctx, workloads.D, generator=gen, device=dev, dtype=torch.bfloat16)
+        dec.load(i, k, v)
+        ref_cache.layers[i].update(k, v)
         del k, v
-    from threadcut_b200.kv import GrowingLayer, splice as kv_splice
-    warm = [GrowingLayer() for _ in range(LAYERS)]  # a small splice first: no first-launch setup timed
-    for ly in warm:
-        ly.update(*(torch.zeros(1, hr, 96, workloads.D, device=dev, dtype=torch.bfloat16),) * 2)
-    kv_splice(type("Warm", (), {"layers": warm})(), Split(16, 48, 48), inv)
-    del warm
+    tok = torch.tensor([1234], device=dev)
+    with torch.no_grad():
+        kv_splice(ref_cache, s, inv)
+        ref_logits = model(input_ids=tok.view(1, 1), past_key_values=ref_cache, use_cache=True).logits[0, -1].float()
+    ref_top1 = int(ref_logits.argmax())
+    del model, ref_cache
+    torch.cuda.empty_cache()
     barrier(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -663,8 +690,6 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
     e1.record()
     e1.synchronize()
     splice_ms = max_over_ranks(e0.elapsed_time(e1), dist)
-    n = s.a + s.c
-    tok = torch.tensor([1234], device=dev)
 
     def eager():
         int(dec.step(tok, n))
@@ -684,27 +709,39 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
         return max_over_ranks(a.elapsed_time(b) / steps, dist)
 
     with torch.no_grad():
+        logits = dec.logits(tok, n)
+        dec.crop(n)
+        step_tok = int(dec.step(tok, n))
+        dec.crop(n)
+        corr = torch.corrcoef(torch.stack([logits, ref_logits]))[0, 1].item()
+        ok = float(step_tok == ref_top1 and int(logits.argmax()) == ref_top1)
+        top1_ok = -max_over_ranks(-ok, dist) == 1.0  # every rank agrees
         eager_ms = timed(eager)
         with torch.cuda.nvtx.range("cfg5_tp_step"):  # one eager step, for a profiler's launch list
             eager()
         torch.cuda.synchronize(dev)
-        graph, out, ok = None, None, 1.0
+        graph, out, cap = None, None, 1.0
         try:
             graph, out = dec.capture(tok, n)
         except Exception:  # a host op the capture cannot hold: every rank skips the replay
-            ok = 0.0
-        ok = -max_over_ranks(-ok, dist)  # min over ranks: replay only if every rank captured
-        graph_ms = None
-        if ok:
+            cap = 0.0
+        cap = -max_over_ranks(-cap, dist)  # min over ranks: replay only if every rank captured
+        graph_ms, graph_tok = None, None
+        if cap:
             def replay():
                 graph.replay()
                 int(out)
 
             graph_ms = timed(replay)
+            graph_tok = int(out)
         del graph
     del dec
     torch.cuda.empty_cache()
-    return eager_ms, graph_ms, splice_ms, shard_bytes + LAYERS * (4096 // world * n + 16384 // world)
+    return {"eager_ms": eager_ms, "graph_ms": graph_ms, "splice_ms": splice_ms,
+            "bytes": shard_bytes + LAYERS * (4096 // world * n + 16384 // world),
+            "top1_ok": bool(top1_ok and (graph_tok is None or graph_tok == ref_top1)), "token": step_tok,
+            "sdpa_token": ref_top1, "logit_corr": round(corr, 6),
+            "logit_max_abs": round(float((logits - ref_logits).abs().max()), 4)}
 
 
 def time_cfg4(steps, warmup, dev, dist, distinct=2):
@@ -782,54 +819,115 @@ def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
     return ms
 
 
-def cpu_reference_us_per_layer(seconds=10.0, layers_in_memory=4, max_layers=None):
-    """The reference's CPU path (oracle/ numpy restatement, fp32, all host threads) on 16k layers.
-    Returns (us per layer, layers timed, threads)."""
-    import numpy as np
-    from oracle.attention import decode_attention_ref
+def cpu_threads():
+    """Host cores this process may run on (its affinity mask), used as the CPU baseline's thread
+    count at every N: torchrun sets OMP_NUM_THREADS=1, which would otherwise leave one core."""
     try:
-        from threadpoolctl import threadpool_info
-        threads = max((i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"),
-                      default=os.cpu_count())
-    except Exception:  # threadpoolctl missing: numpy's BLAS uses every core by default
-        threads = os.cpu_count()
-    rng = np.random.default_rng(0)
-    bufs = [(rng.standard_normal((8, 4, 128), dtype=np.float32), rng.standard_normal((8, N_CTX, 128), dtype=np.float32),
-             rng.standard_normal((8, N_CTX, 128), dtype=np.float32)) for _ in range(layers_in_memory)]
-    decode_attention_ref(*bufs[0], workloads.SCALE, dtype=np.float32)  # warm-up
-    t0 = time.perf_counter()
-    done = 0
-    while True:
-        q, k, v = bufs[done % layers_in_memory]
-        decode_attention_ref(q, k, v, workloads.SCALE, dtype=np.float32)
-        done += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or (max_layers and done >= max_layers):
-            break
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+_CPU_BUFS = {}
+
+
+def cpu_layers(dtype, layers_in_memory=4):
+    """Seeded 16k decode inputs on the host, built once per dtype: [(q, K, V)] x layers_in_memory."""
+    if dtype not in _CPU_BUFS:
+        g = torch.Generator().manual_seed(0)
+        _CPU_BUFS[dtype] = [(torch.randn(1, 32, 1, 128, generator=g).to(dtype),
+                             torch.randn(1, 8, N_CTX, 128, generator=g).to(dtype),
+                             torch.randn(1, 8, N_CTX, 128, generator=g).to(dtype)) for _ in range(layers_in_memory)]
+    return _CPU_BUFS[dtype]
+
+
+def cpu_reference_us_per_layer(seconds=10.0, max_layers=None, dtype=torch.bfloat16):
+    """The reference's CPU decode path (threadcut/attention.py:41-42: query heads folded, SDPA
+    against the unexpanded cache; oracle/torch_ref.py) on 16k layers in `dtype`, with every host
+    core. Returns (us per layer, layers timed, threads)."""
+    from oracle.torch_ref import folded_decode
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    bufs = cpu_layers(dtype)
+    layers_in_memory = len(bufs)
+    with torch.no_grad():
+        folded_decode(*bufs[0], workloads.SCALE)  # warm-up
+        t0 = time.perf_counter()
+        done = 0
+        while True:
+            q, k, v = bufs[done % layers_in_memory]
+            folded_decode(q, k, v, workloads.SCALE)
+            done += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or (max_layers and done >= max_layers):
+                break
     return el / done * 1e6, done, threads
+
+
+def cpu_shift_us_per_layer(reps=20):
+    """The reference's CPU splice (threadcut/kv.py:83-92: shift_keys of C plus the value clone,
+    written back in place) of config 2, Split(2048, 4096, 4096) of an 8192-token bf16 layer, with
+    every host core. Returns (median us per layer, threads)."""
+    from oracle.torch_ref import growing_splice
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    a, c0, c = workloads.CFG2_SPLIT
+    bufs = [(torch.randn(1, 8, workloads.CFG2_N, 128, generator=g).to(torch.bfloat16),
+             torch.randn(1, 8, workloads.CFG2_N, 128, generator=g).to(torch.bfloat16)) for _ in range(4)]
+    inv = workloads.inv_freq()
+    growing_splice(*bufs[0], a, c0, c, inv)  # warm-up
+    times = []
+    for i in range(reps):
+        kb, vb = bufs[i % len(bufs)]
+        t0 = time.perf_counter()
+        growing_splice(kb, vb, a, c0, c, inv)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, threads
 
 
 def run_ours(args, rank, local, world, dist):
     dev = torch.device("cuda", local)
     hbm, peak_kind = peaks()
-    qs, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
-    outs = [torch.empty_like(q) for q in qs]
-    graph = capture_step(qs, ks, vs, outs, dev)
+    if workloads.HKV % world:
+        raise SystemExit(f"bench: {world} GPUs do not divide the {workloads.HKV} KV heads")
+    # the step: one sequence of 16k * world tokens, 36 layers, KV heads sharded over the ranks
+    # (8 / world per rank: every GPU streams the same 67 MB per layer as one GPU at 16k), each
+    # layer's outputs all-gathered to every rank at the end of the step; at 1 GPU, the 16k headline
+    hl = workloads.HKV // world
+    n_job = N_CTX * world
+    rank_bytes = 512 * hl * n_job + 2048 * hl  # K+V + q + o of this rank's heads, one layer
+    qs, ks, vs = build_layers(n_job, LAYERS, dev, seed=1000 + rank, heads=hl)
+    local_out = torch.empty((LAYERS, hl, 4, 128), dtype=torch.bfloat16, device=dev)
+    outs = list(local_out.unbind(0))
+    full_out = torch.empty((world * local_out.numel(),), dtype=torch.bfloat16, device=dev)
+    combine = (dist, local_out, full_out) if world > 1 else None
+    graph = capture_step(qs, ks, vs, outs, dev, combine=combine)
     with ClockSampler(local) as clk:
         ms = time_graph(graph, args.steps, args.warmup, dist)
     ms = max_over_ranks(ms, dist)
-    us_layer_rank = ms * 1000.0 / LAYERS  # one rank's launch duration (incl. back-to-back gaps)
-    value = ms * 1000.0 / (LAYERS * world)
-    achieved = BYTES_PER_LAYER / (us_layer_rank * 1e-6) / 1e9
-    g_plain = capture_step(qs, ks, vs, outs, dev, stable=False)
+    us_layer_rank = ms * 1000.0 / LAYERS  # one rank's time per layer (incl. back-to-back gaps)
+    value = ms * 1000.0 / (LAYERS * world)  # per 16k tokens of context per layer
+    achieved = rank_bytes / (us_layer_rank * 1e-6) / 1e9
+    if world > 1:  # the combine's share: the same decode launches without the all-gather
+        g_nc = capture_step(qs, ks, vs, outs, dev)
+        nocombine_ms = max_over_ranks(time_graph(g_nc, args.steps, args.warmup, dist), dist)
+        del g_nc
+    else:
+        nocombine_ms = ms
+    g_plain = capture_step(qs, ks, vs, outs, dev, stable=False, combine=combine)
     plain_ms = max_over_ranks(time_graph(g_plain, args.steps, args.warmup, dist), dist)
     del g_plain
-    e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev)
+    e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev, world)
     e2e_ms = max_over_ranks(e2e_ms, dist)
+    del graph, qs, ks, vs
+    torch.cuda.empty_cache()
+    # the single-GPU 16k layers (replicated on every rank) for the comparators and the fused append
+    qs, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
     sdpa_ms = max_over_ranks(time_sdpa_16k(qs, ks, vs, args.steps, args.warmup, dist), dist)
     fused_ms, unfused_ms = time_append_16k(qs, ks, vs, args.steps, args.warmup, dist)
     fused_ms, unfused_ms = max_over_ranks(fused_ms, dist), max_over_ranks(unfused_ms, dist)
-    del graph
+    del qs, ks, vs
     # context-length sweep of config 3 (same kernel, 4k and 32k), and the RoPE-shift splice
     sweep = {}
     for n in (4096, 32768):
@@ -840,7 +938,8 @@ def run_ours(args, rank, local, world, dist):
         sweep[str(n)] = {"us_per_layer": round(t * 1000 / LAYERS, 3),
                          "frac": round((4096 * n + 16384) / (t * 1e-3 / LAYERS) / 1e9 / hbm, 4)}
         del g2, q2, k2, v2, o2
-    sweep[str(N_CTX)] = {"us_per_layer": round(us_layer_rank, 3), "frac": round(achieved / hbm, 4)}
+    if world == 1:
+        sweep[str(N_CTX)] = {"us_per_layer": round(us_layer_rank, 3), "frac": round(achieved / hbm, 4)}
     torch.cuda.empty_cache()
     shift_ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist), dist)
     shift_gbs = SHIFT_BYTES_PER_LAYER * LAYERS / (shift_ms * 1e-3) / 1e9
@@ -879,21 +978,35 @@ def run_ours(args, rank, local, world, dist):
         for key in ("graph_error", "sdpa_graph_error"):
             if key in c5:
                 cfg5[key] = c5[key]
-    tp_eager, tp_graph, tp_splice, tp_bytes = time_cfg5_tp(min(args.steps, 10), args.warmup, dev, dist, rank, world)
-    cfg5_tp = {"eager_ms": round(tp_eager, 3), "graph_ms": None if tp_graph is None else round(tp_graph, 3),
-               "splice_ms": round(tp_splice, 3), "bytes_per_rank": tp_bytes,
-               "ideal_ms": round(tp_bytes / (hbm * 1e9) * 1e3, 3),
+    tp = time_cfg5_tp(min(args.steps, 10), args.warmup, dev, dist, rank, world)
+    cfg5_tp = {"eager_ms": round(tp["eager_ms"], 3),
+               "graph_ms": None if tp["graph_ms"] is None else round(tp["graph_ms"], 3),
+               "splice_ms": round(tp["splice_ms"], 3), "bytes_per_rank": tp["bytes"],
+               "ideal_ms": round(tp["bytes"] / (hbm * 1e9) * 1e3, 3),
+               "top1_ok": tp["top1_ok"], "token": tp["token"], "sdpa_token": tp["sdpa_token"],
+               "logit_corr": tp["logit_corr"], "logit_max_abs": tp["logit_max_abs"],
                "what": f"one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache, "
                        f"tensor-parallel over {world} GPU(s) (threadcut_b200.tp.TPDecoder: KV heads, their query "
-                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 NCCL all-reduces per layer), next "
-                       f"token read back each step; eager and CUDA graph; max over ranks; ideal_ms = one rank's "
-                       f"weight + K/V bytes at the measured HBM peak (collectives not counted)"}
+                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 all-reduces per layer), next "
+                       f"token read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
+                       f"graph and gathered-logit tokens equal HF's SDPA forward over the same spliced full cache "
+                       f"(sdpa_token) on every rank; ideal_ms = one rank's weight + K/V bytes at the measured HBM "
+                       f"peak (collectives not counted)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        us, nl, thr = cpu_reference_us_per_layer(args.cpu_seconds)
-        cpu = {"value": round(us, 2), "unit": "us/layer", "cores": thr, "kind": "port",
-               "sample": f"{nl} layers of 16k decode (fp32 numpy restatement of the reference's folded SDPA, "
-                         f"4 distinct layer buffers cycled, ~{args.cpu_seconds:.0f}s)"}
+        us16, nl16, thr = cpu_reference_us_per_layer(args.cpu_seconds / 2, dtype=torch.bfloat16)
+        us32, nl32, _ = cpu_reference_us_per_layer(args.cpu_seconds / 2, dtype=torch.float32)
+        sh_us, _ = cpu_shift_us_per_layer()
+        cpu = {"value": round(min(us16, us32), 2), "unit": "us/layer", "cores": thr, "kind": "port",
+               "bf16_us_per_layer": round(us16, 2), "fp32_us_per_layer": round(us32, 2),
+               "sample": f"{nl16} bf16 + {nl32} fp32 layers of 16k decode through the reference's CPU decode "
+                         f"expression (threadcut/attention.py:41-42: F.scaled_dot_product_attention(q.reshape(1,8,4,128), "
+                         f"K, V, scale) on CPU tensors, oracle/torch_ref.py), 4 distinct layer buffers cycled, "
+                         f"~{args.cpu_seconds:.0f}s; value = the faster dtype",
+               "shift": {"us_per_layer": round(sh_us, 1),
+                         "gbs": round(SHIFT_BYTES_PER_LAYER / (sh_us * 1e-6) / 1e9, 2),
+                         "sample": "config-2 splice of one bf16 layer, median of 20: shift_keys of C + value "
+                                   "clone written back (threadcut/kv.py:20-25,83-92 on CPU tensors)"}}
     traffic = None  # DRAM bytes per launch from the committed ncu capture of this kernel and size
     tpath = os.path.join(HERE, "profiles", "decode_16k_traffic.txt")
     if os.path.exists(tpath):
@@ -904,18 +1017,30 @@ def run_ours(args, rank, local, world, dist):
         "metric": METRIC, "value": round(value, 3), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) K/V and queries",
-        "config": {"workload": "cfg3-16k: 36-layer split-KV GQA decode, n=16384, 32 q / 8 kv heads, head_dim 128, "
-                               "one K/V buffer per layer", "layers": LAYERS, "n": N_CTX, "batch": 1,
-                   "l2": "inputs larger than L2 (36 distinct 67 MB layers = 2.4 GB per step)",
-                   "parallelism": f"weak: every rank decodes its own 36 layers ({world} rank(s))",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "n": n_job, "batch": 1,
+                   "kv_heads_per_gpu": hl,
+                   "l2": f"inputs larger than L2 (36 distinct {rank_bytes / 1e6:.0f} MB layers per GPU = "
+                         f"{LAYERS * rank_bytes / 1e9:.1f} GB per step)",
+                   "parallelism": f"head-sharded over {world} GPU(s): {hl} KV head(s) of the {n_job}-token sequence "
+                                  f"per GPU" + (", each step's outputs all-gathered to every rank (NCCL, in the "
+                                               "graph)" if world > 1 else ""),
+                   "value": "us per layer of the job / world = us per layer per 16k tokens of context (at 1 GPU: "
+                            "the 16k decode; at 8: the 128k sequence with one KV head per GPU)",
                    "stable_rows": "n-1: every row but the newest declared stable, as in a decode step "
                                   "(tc_decode_attention_stable); see no_stable_rows for the plain entry point"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "decode_mma_kernel<bf16,128,1>", "bytes_per_launch": BYTES_PER_LAYER},
+                     "frac": round(achieved / hbm, 4), "traffic": traffic if world == 1 else None,
+                     "peak_kind": peak_kind, "kernel": "decode_mma_kernel<bf16,128,1>", "bytes_per_launch": rank_bytes,
+                     "per": "one GPU's launch (its heads); the job's layer time per GPU includes the combine"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1000.0 / (LAYERS * world), 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "api": "threadcut_b200.flash_decode.decode_attention"},
+                "d2h_bytes_per_step": d2h, "api": "threadcut_b200.flash_decode.decode_attention per layer over the "
+                                                  "rank's heads" + (", torch.distributed all-gather of the step's "
+                                                                    "outputs" if world > 1 else "")},
+        "combine": None if world == 1 else {
+            "us_per_layer_without": round(nocombine_ms * 1000.0 / LAYERS, 3),
+            "us_per_layer_with": round(us_layer_rank, 3),
+            "what": "the step's 36 decode launches with and without the all-gather of their outputs"},
         "gpu_launches": args.steps * LAYERS,
         "clocks": clk.summary(),
         "shift": {"value": round(shift_gbs, 1), "unit": "GB/s", "frac": round(shift_gbs / hbm, 4),
@@ -957,7 +1082,7 @@ def run_ours(args, rank, local, world, dist):
                        "what": "match.split of a 128k cached / 97k new request: tc_split (tokens on the GPU, "
                                "result read back, wall clock) vs the host rule on Python lists"},
         "no_stable_rows": {"us_per_layer": round(plain_ms * 1000.0 / LAYERS, 3),
-                           "frac": round(BYTES_PER_LAYER / (plain_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
+                           "frac": round(rank_bytes / (plain_ms * 1e-3 / LAYERS) / 1e9 / hbm, 4),
                            "what": "the same 36-layer step through plain tc_decode_attention (nothing declared "
                                    "stable: K/V are read only after the preceding launch finished)"},
         "gpu_comparators": {"torch_sdpa_folded_16k": {
@@ -985,9 +1110,8 @@ def run_partial(args, rank, local, world, dist):
         out.update(us_per_layer=round(us, 3), gbs=round(decode_bytes(args.ctx) / (us * 1e-6) / 1e9, 1))
         del graph
     elif args.only == "cfg5tp":
-        e, g, sp, b = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world)
-        out.update(eager_ms=round(e, 3), graph_ms=None if g is None else round(g, 3), splice_ms=round(sp, 3),
-                   bytes_per_rank=b, world=world)
+        tp = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world)
+        out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in tp.items()}, world=world)
     elif args.only == "cfg5":
         c5 = time_cfg5_step(args.steps, args.warmup, dev)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in c5.items()})
@@ -1000,27 +1124,39 @@ def run_partial(args, rank, local, world, dist):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: threadcut's own CPU path for this workload (the torch expressions of
+    oracle/torch_ref.py) on rank 0 with every host core; other ranks exit without work. A step is
+    the 36-layer 16k decode in bf16 (the faster of bf16 and fp32 on CPUs measured so far; fp32 is
+    timed once beside it)."""
     if rank != 0:
         return
     per_step = []
-    threads = os.cpu_count()
+    threads = cpu_threads()
     for i in range(args.warmup + args.steps):
-        us, nl, threads = cpu_reference_us_per_layer(seconds=1e9, max_layers=LAYERS)
+        us, nl, threads = cpu_reference_us_per_layer(seconds=1e9, max_layers=LAYERS, dtype=torch.bfloat16)
         if i >= args.warmup:
             per_step.append(us * LAYERS / 1000.0)  # ms per 36-layer step
+    us32, _, _ = cpu_reference_us_per_layer(seconds=1e9, max_layers=LAYERS, dtype=torch.float32)
+    sh_us, _ = cpu_shift_us_per_layer()
     ms = statistics.mean(per_step)
     value = ms * 1000.0 / LAYERS
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,1) K/V and queries",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) K/V and queries",
         "impl": "reference",
-        "config": {"workload": "cfg3-16k: 36-layer split-KV GQA decode, n=16384, 32 q / 8 kv heads, head_dim 128, "
-                               "one K/V buffer per layer", "layers": LAYERS, "n": N_CTX, "batch": 1,
-                   "parallelism": "rank 0 only (host CPU)"},
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "n": N_CTX, "batch": 1,
+                   "parallelism": "rank 0 only (host CPU, every core of its affinity mask); one 16k-token layer "
+                                  "per unit of the metric (the whole job at N GPUs is N such units per layer)"},
         "cpu_baseline": {"value": round(value, 2), "unit": "us/layer", "cores": threads, "kind": "port",
-                         "sample": "each step: 36 layers of 16k decode through the numpy restatement of the "
-                                   "reference's folded SDPA (fp32), 4 distinct layer buffers cycled"},
+                         "fp32_us_per_layer": round(us32, 2),
+                         "sample": "each step: 36 bf16 layers of 16k decode through the reference's CPU decode "
+                                   "expression (threadcut/attention.py:41-42, F.scaled_dot_product_attention of the "
+                                   "folded query on CPU tensors; oracle/torch_ref.py), 4 distinct layer buffers "
+                                   "cycled",
+                         "shift": {"us_per_layer": round(sh_us, 1),
+                                   "gbs": round(SHIFT_BYTES_PER_LAYER / (sh_us * 1e-6) / 1e9, 2),
+                                   "sample": "config-2 splice of one bf16 layer (threadcut/kv.py:20-25,83-92)"}},
         "e2e": {"value": round(value, 2), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

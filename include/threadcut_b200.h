@@ -173,7 +173,9 @@ int tc_prefill_attention(const void* q, const void* k, const void* v, void* out,
  * with batch 1) exceeds 4 MiB are rejected with TC_ERR_WORKSPACE; Qwen3-4B's geometry (8 KV heads,
  * 4 query heads each, head_dim 128) fits at every context length. The first call on a device looks
  * up the array's device address (with that device current), so make that first call before any
- * stream capture. All calls share the one array and it keeps the last call's contents: each call
+ * stream capture; the address is looked up again after the device's context changed (a
+ * cudaDeviceReset loads the library's device code anew). All calls share the one array and it
+ * keeps the last call's contents: each call
  * clears what must start at zero, but calls that run at the same time on the GPU (different streams,
  * different host threads) race with each other — order them. */
 int tc_decode_attention_noalloc(const void* q, const void* k, const void* v, void* out,

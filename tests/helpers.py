@@ -25,14 +25,31 @@ def half_ulp(ref, dtype):
     return 0.5 * np.exp2(e - MANTISSA[dtype])
 
 
+class AttnError(float):
+    """The error compared with ATTN_ATOL (half-ulp adjusted) that also carries the raw max-abs
+    difference; both appear wherever the value is printed (assertion messages, smoke)."""
+
+    def __new__(cls, adjusted, raw):
+        obj = super().__new__(cls, adjusted)
+        obj.raw = raw
+        return obj
+
+    def __repr__(self):
+        return f"{float(self):.3e} (raw max-abs {self.raw:.3e})"
+
+    __str__ = __repr__
+
+
 def attn_error(out, ref, dtype):
     """Max-abs error of a kernel output against the fp32/fp64 math with the unavoidable output
-    rounding (half an ulp of the output dtype) taken off; it is compared with ATTN_ATOL."""
+    rounding (half an ulp of the output dtype) taken off; it is compared with ATTN_ATOL. The raw
+    max-abs difference rides along as `.raw` and is printed beside it."""
     out = np.asarray(out, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     if ref.size == 0:
-        return 0.0
-    return float(np.max(np.abs(out - ref) - half_ulp(ref, dtype)))
+        return AttnError(0.0, 0.0)
+    diff = np.abs(out - ref)
+    return AttnError(float(np.max(diff - half_ulp(ref, dtype))), float(np.max(diff)))
 
 _gold = None
 _meta = None

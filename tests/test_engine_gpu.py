@@ -1,18 +1,23 @@
-"""End-to-end through the engine and the transformers plugin on the GPU.
+"""End-to-end through the reference engine's calls and the transformers plugin on the GPU.
 
 Mirrors the reference's engine tests (tests/test_core.py): T2 (splice == fresh compute), T3 (greedy
 tokens == stock transformers SDPA generate) on the reference's tiny Qwen3 configuration, and
 config 5: a random-init Qwen3-4B decoding one token over a 128k cache with a 32k span pruned, whose
-next-token logits must have the same top-1 as the torch SDPA path on the same spliced cache.
+next-token logits must have the same top-1 as the torch SDPA path on the same spliced cache. The
+engine's calls (split, splice or new_cache, chunked prefill, greedy decode; threadcut/engine.py:
+41-95) are made by tests/caller.py.
 """
+import numpy as np
 import pytest
 import torch
 from transformers import AutoModelForCausalLM, DynamicCache, Qwen3Config
 
 import workloads
+from caller import Session
+from helpers import ref_cos_sin
+from oracle.rope import shift_keys_ref
 from threadcut_b200 import _lib
 from threadcut_b200 import attention as tc_attention
-from threadcut_b200.engine import Engine
 from threadcut_b200.kv import new_cache, splice
 from threadcut_b200.match import Split
 
@@ -20,20 +25,14 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
-class StubTokenizer:
-    """The engine only needs the stop ids (threadcut/engine.py:36)."""
-    eos_token_id = 511
-
-    def convert_tokens_to_ids(self, tok):
-        return 510
-
-
 def tiny_engine(dtype):
+    """The reference's tiny test model (tests/test_core.py:15-22); stop ids 510/511 stand in for a
+    tokenizer's end-of-turn ids (threadcut/engine.py:36)."""
     torch.manual_seed(0)
     cfg = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
                       num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=4096)
     model = AutoModelForCausalLM.from_config(cfg, dtype=dtype, attn_implementation=tc_attention.NAME).to(DEV)
-    return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=7)
+    return Session(model, min_suffix=4, prefill_chunk=7)
 
 
 @pytest.fixture(autouse=True, scope="module")
@@ -95,7 +94,7 @@ def test_growing_cache_inplace_splice_matches_copy_splice():
             lp.update(lg.keys.clone(), lg.values.clone())
         logits, stats = engine.load(A + C + D)
         splice(plain, Split(len(A), len(A) + len(B), len(C)), engine.inv_freq)
-        ref_logits = engine._forward(D, plain)
+        ref_logits = engine.prefill(D, plain)
     assert (stats["reused_prefix"], stats["reused_suffix"], stats["computed_tokens"]) == (20, 40, 6)
     assert torch.allclose(logits.float(), ref_logits.float(), atol=1e-5, rtol=0)
 
@@ -141,9 +140,17 @@ def test_cfg5_full_model_128k_spliced_top1_matches_sdpa():
         v = torch.randn(1, 8, ctx, 128, generator=gen, device=DEV, dtype=torch.bfloat16)
         layer.update(k, v)
         del k, v
+    # a strided sample of C's source rows in two layers, to check the full-size shift (delta = -32768)
+    rows = torch.arange(s.c0, s.c0 + s.c, 997, device=DEV)
+    picked = (0, len(cache.layers) - 1)
+    src = {i: cache.layers[i].keys[0][:, rows].float().cpu().numpy() for i in picked}
     splice(cache, s, inv)
     n = s.a + s.c
     assert cache.get_seq_length() == n == 98304
+    cos_sin = ref_cos_sin(-s.gap, inv.detach().cpu())
+    for i in picked:
+        got = cache.layers[i].keys[0][:, rows - s.gap].float().cpu().numpy()
+        assert np.array_equal(got, shift_keys_ref(src[i], dtype="bf16", cos_sin=cos_sin)), i
     x = torch.tensor([[1234]], device=DEV)
     with torch.no_grad():
         ours = model(input_ids=x, past_key_values=cache, use_cache=True).logits[0, -1].float()
@@ -164,8 +171,7 @@ def small_bf16_engine(paged):
     cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                       num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
     model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME).to(DEV)
-    return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=64,
-                  max_ctx=4096, paged=paged)
+    return Session(model, min_suffix=4, prefill_chunk=64, max_ctx=4096, layout={"paged": paged, "max_tokens": 4096})
 
 
 def test_paged_engine_matches_the_contiguous_engine():
@@ -207,8 +213,8 @@ def test_paged_engine_fallbacks_match_the_contiguous_engine(kind):
                               num_attention_heads=4, num_key_value_heads=2, head_dim=128, max_position_embeddings=4096)
             dtype = torch.bfloat16
         model = AutoModelForCausalLM.from_config(cfg, dtype=dtype, attn_implementation=tc_attention.NAME).to(DEV)
-        return Engine(None, device=DEV, model=model, tokenizer=StubTokenizer(), min_suffix=4, prefill_chunk=16,
-                      max_ctx=2048, paged=paged)
+        return Session(model, min_suffix=4, prefill_chunk=16, max_ctx=2048,
+                       layout={"paged": paged, "max_tokens": 2048})
     eng_p, eng_c = make(True), make(False)
     p1 = rand_ids(60, 21)
     out_p, _ = eng_p.generate(p1, max_new_tokens=10)

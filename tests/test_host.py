@@ -322,3 +322,62 @@ def test_gemv_argument_validation_without_a_gpu():
     assert L.tc_gemv(16, 32, 64, 4, 64, 0, None) != 0  # fp32: not supported
     assert L.tc_gemv(8, 32, 64, 4, 64, 2, None) != 0   # x not 16-byte aligned (rejected before any access)
     assert L.tc_gemv(16, 32, 64, 4, 32768, 2, None) != 0  # x would not fit in shared memory
+
+
+# ------------------------------------------------------------------ the reference's engine over this package
+REFERENCE = os.environ.get("THREADCUT_REFERENCE", "/root/reference")
+
+
+def test_reference_engine_runs_unchanged_over_this_package(monkeypatch):
+    """threadcut/engine.py, loaded from the reference checkout as it is (no copy in this
+    repository), with its package's attention / kv / match modules resolved to threadcut_b200's:
+    its imports bind to this package, its cache calls build this package's caches (contiguous by
+    default, paged after kv.use_paged_cache()), and a request runs through the plugin (the prefill
+    chunk on the CPU through the reference's torch branch) until the first decode step reaches the
+    CUDA kernels, which refuse CPU tensors: there is no CPU path. Skipped without the checkout
+    (it is not shipped to GPU machines)."""
+    import importlib.util
+    import sys
+    import types
+    from transformers import AutoModelForCausalLM, Qwen3Config
+    from threadcut_b200 import attention, kv, match
+    src = os.path.join(REFERENCE, "threadcut", "engine.py")
+    if not os.path.exists(src):
+        pytest.skip("the reference checkout is not present")
+    pkg = types.ModuleType("threadcut")
+    pkg.__path__ = []
+    pkg.attention, pkg.kv, pkg.match = attention, kv, match
+    for name, mod in (("threadcut", pkg), ("threadcut.attention", attention), ("threadcut.kv", kv),
+                      ("threadcut.match", match)):
+        monkeypatch.setitem(sys.modules, name, mod)
+    spec = importlib.util.spec_from_file_location("threadcut.engine", src)
+    engine = importlib.util.module_from_spec(spec)
+    monkeypatch.setitem(sys.modules, "threadcut.engine", engine)
+    spec.loader.exec_module(engine)
+    assert engine.attention is attention and engine.new_cache is kv.new_cache
+    assert engine.splice is kv.splice and engine.split is match.split
+
+    class Tok:  # the engine only asks the tokenizer for its stop ids (threadcut/engine.py:36)
+        eos_token_id = 511
+
+        def convert_tokens_to_ids(self, tok):
+            return 510
+
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=4096)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.float32, attn_implementation=attention.NAME)
+    eng = engine.Engine(None, device="cpu", model=model, tokenizer=Tok(), min_suffix=4, prefill_chunk=7)
+    cache = engine.new_cache(model.config)
+    assert all(isinstance(ly, kv.GrowingLayer) and ly.fuse_append for ly in cache.layers)
+    try:
+        kv.use_paged_cache(True, max_tokens=1024)
+        assert all(isinstance(ly, kv.PagedLayer) for ly in engine.new_cache(model.config).layers)
+    finally:
+        kv.use_paged_cache(False)
+    ids = torch.randint(10, 500, (20,), generator=torch.Generator().manual_seed(5)).tolist()
+    logits, stats = eng.load(ids)  # fresh cache + chunked prefill: the reference's torch prefill branch
+    assert logits.shape == (1, 512) and stats["computed_tokens"] == 20 and eng.cache.get_seq_length() == 20
+    assert isinstance(eng.cache.layers[0], kv.GrowingLayer)
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        eng.generate(ids + [7, 8], max_new_tokens=2)  # the decode step reaches the kernels

@@ -149,3 +149,36 @@ def test_round_to_matches_torch():
     np.testing.assert_array_equal(ours, ref)
     f = shift_keys_f32(x.reshape(100, 100), 3, workloads.inv_freq(100, 1e4).numpy())
     assert f.dtype == np.float32
+
+
+# ---- oracle/torch_ref.py: the reference's CPU path as torch expressions (the timed CPU baseline)
+@pytest.mark.parametrize("ci", range(7))
+def test_torch_ref_shift_bit_exact_with_reference(ci):
+    from oracle.torch_ref import shift_keys as torch_shift
+    G, M = gold(), meta()["cases"][f"shift{ci}"]
+    dt = storage_dtype(G[f"shift{ci}_in"])
+    keys = torch.from_numpy(values(G[f"shift{ci}_in"])).to({"bf16": torch.bfloat16, "f16": torch.float16,
+                                                            "f32": torch.float32}[dt])
+    out = torch_shift(keys, M["delta"], workloads.inv_freq(M["d"], M["theta"]))
+    np.testing.assert_array_equal(out.float().numpy().view(np.uint32), values(G[f"shift{ci}_out"]).view(np.uint32))
+
+
+def test_torch_ref_cfg2_splice_and_decode_match_reference():
+    from oracle.torch_ref import folded_decode, growing_splice
+    G, Mt = gold(), meta()
+    kc, vc = workloads.cfg2_cache()
+    a, c0, c = workloads.CFG2_SPLIT
+    kb, vb = kc.clone()[None], vc.clone()[None]
+    n = growing_splice(kb, vb, a, c0, c, workloads.inv_freq())
+    assert [sha(kb[0, :, :n]), sha(vb[0, :, :n])] == Mt["cfg2_sha_spliced"]
+    q = workloads.cfg2_query()
+    out = folded_decode(q.float().reshape(1, 32, 1, 128), kb[:, :, :n].float(), vb[:, :, :n].float(), workloads.SCALE)
+    np.testing.assert_allclose(out.numpy(), G["cfg2_out"], atol=ORACLE_ATOL, rtol=0)
+
+
+def test_torch_ref_decode_matches_reference_cfg1():
+    from oracle.torch_ref import folded_decode
+    q, k, v = workloads.cfg1()
+    out = folded_decode(q, k, v, workloads.SCALE)
+    np.testing.assert_allclose(out.numpy().reshape(gold()["cfg1_out_f32"].shape), gold()["cfg1_out_f32"],
+                               atol=ORACLE_ATOL, rtol=0)

@@ -30,8 +30,11 @@ def test_seq_and_head_sharded_decode_match_single_gpu():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
-def test_tensor_parallel_decoder_matches_the_hf_forward():
-    world = min(torch.cuda.device_count(), 2)
+def test_tensor_parallel_decoder_matches_the_sdpa_forward():
+    """TPDecoder on every visible GPU (up to the 8 KV heads' worth) against HF's SDPA forward over the
+    same spliced cache (tests/tp_worker.py)."""
+    world = min(torch.cuda.device_count(), 8)
+    world = max(w for w in (1, 2, 4, 8) if w <= world)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "tp_worker.py")]

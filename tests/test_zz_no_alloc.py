@@ -5,8 +5,9 @@ device memory and forbids allocating while it executes, a loop that cannot affor
 implicit synchronisation, or C code with no allocator at hand. For them the library keeps its
 scratch in one fixed array of its own. These checks call that entry point through the C ABI and
 compare it with tc_decode_attention (the workspace-taking entry point, reached through
-threadcut_b200.flash_decode) on two calls in a row with different problem sizes, so a stale
-workspace state from the first call would show up in the second.
+threadcut_b200.flash_decode) and with the CPU oracle of the reference's decode math on two calls in
+a row with different problem sizes, so a stale workspace state from the first call would show up
+in the second.
 
 This file is collected last on purpose; it needs no state from the other tests.
 """
@@ -15,6 +16,7 @@ import pytest
 import torch
 
 from helpers import ATTN_ATOL, attn_error
+from oracle.attention import decode_attention_ref
 from threadcut_b200 import _lib
 from threadcut_b200.flash_decode import decode_attention
 
@@ -48,9 +50,13 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         assert st == 0, _lib.lib().tc_status_string(st)
         ref = decode_attention(q, k, v, scale)
         torch.cuda.synchronize()
-        err = attn_error(out.float().cpu().numpy(), ref.float().cpu().numpy(), torch.bfloat16)
+        got = out.float().cpu().numpy()
+        err = attn_error(got, ref.float().cpu().numpy(), torch.bfloat16)
         assert err <= ATTN_ATOL, (n, err)
-        assert np.isfinite(out.float().cpu().numpy()).all()
+        math = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), scale)
+        err = attn_error(got, math, torch.bfloat16)
+        assert err <= ATTN_ATOL, (n, err)
+        assert np.isfinite(got).all()
 
 
 def test_noalloc_rejects_problems_larger_than_its_array():

@@ -1,12 +1,15 @@
 """Tensor-parallel decoder check, shared by the one-GPU test (test_engine_gpu.py) and the torchrun
-worker of the multi-GPU test (test_sharded_gpu.py).
+worker of the multi-GPU tests (test_sharded_gpu.py, any number of ranks).
 
-A small bf16 Qwen3 (head_dim 128, 4 query heads per KV head: the decode kernel's fast path) decodes
-one token after a 300-token prompt. Expected: the HF forward with threadcut_b200's attention over
-the whole prompt (same weights, same seed on every rank). Checked: same top-1 and correlated
-logits (the partial sums of the sharded projections round differently in bf16), the step's token
-equals the argmax of the gathered logits, and a CUDA graph of the step (NCCL all-reduces inside)
-replays the eager token."""
+A small bf16 Qwen3 (head_dim 128, 4 query heads per KV head: the decode kernel's fast path) holds a
+2,304-token prompt A.B.C in its cache, computed by stock transformers with SDPA attention. B (256
+tokens) is pruned with kv.splice, leaving 2,048 rows. Expected next token: the same SDPA forward of
+one more token over that spliced cache (the torch path the reference's engine tests compare with,
+threadcut tests/test_core.py:93-101). TPDecoder loads the spliced cache (2,048 rows: every layer's
+buffer exactly full, so the step's append must find room) and is captured in a CUDA graph at once.
+Checked: the replayed token, the eager step's token and the argmax of the gathered logits equal the
+SDPA top-1, and the logits correlate (the partial sums of the sharded projections round differently
+in bf16)."""
 import datetime
 import os
 import sys
@@ -16,10 +19,10 @@ import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
-from transformers import AutoModelForCausalLM, Qwen3Config  # noqa: E402
+from transformers import AutoModelForCausalLM, DynamicCache, Qwen3Config  # noqa: E402
 
-from threadcut_b200 import attention as tc_attention  # noqa: E402
-from threadcut_b200.kv import new_cache  # noqa: E402
+from threadcut_b200.kv import splice  # noqa: E402
+from threadcut_b200.match import Split  # noqa: E402
 from threadcut_b200.tp import TPDecoder  # noqa: E402
 
 
@@ -28,31 +31,36 @@ def check(dev, world=1, rank=0):
     torch.manual_seed(0)
     cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
                       num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
-    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation="sdpa")
     model = model.to(dev).eval()
-    ids = torch.randint(0, 512, (1, 301), generator=torch.Generator().manual_seed(3)).to(dev)
+    ids = torch.randint(0, 512, (1, 2305), generator=torch.Generator().manual_seed(3)).to(dev)
+    s = Split(512, 768, 2304 - 768)
+    n = s.a + s.c
     with torch.no_grad():
-        ref = model(input_ids=ids, past_key_values=new_cache(model.config), use_cache=True).logits[0, -1].float()
-        cache = new_cache(model.config)
-        model(input_ids=ids[:, :300], past_key_values=cache, use_cache=True)
+        cache = DynamicCache(config=model.config)
+        model(input_ids=ids[:, :2304], past_key_values=cache, use_cache=True)
+        splice(cache, s, model.model.rotary_emb.inv_freq)  # the reference's copy splice (kv.py:34-41)
+        assert cache.get_seq_length() == n == 2048
         dec = TPDecoder(model, dev, world=world, rank=rank)
         for i, layer in enumerate(cache.layers):
             dec.load(i, layer.keys, layer.values)
-        tok = ids[0, 300:]
-        logits = dec.logits(tok, 300)
-        dec.crop(300)
-        eager = dec.step(tok, 300)
-        dec.crop(300)
-        graph, out = dec.capture(tok, 300)
+        assert all(ly.kbuf.shape[-2] == n for ly in dec.layers)  # full: the step's row needs a grow
+        tok = ids[0, 2304:]
+        graph, out = dec.capture(tok, n)
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
         replayed = int(out)
         del graph
+        eager = int(dec.step(tok, n))
+        dec.crop(n)
+        logits = dec.logits(tok, n)
+        dec.crop(n)
+        ref = model(input_ids=ids[:, 2304:], past_key_values=cache, use_cache=True).logits[0, -1].float()
     corr = torch.corrcoef(torch.stack([logits, ref]))[0, 1].item()
     res = {"corr": corr, "max_abs": float((logits - ref).abs().max()), "top1": int(logits.argmax()),
-           "ref_top1": int(ref.argmax()), "step": int(eager), "replayed": replayed}
-    assert res["top1"] == res["ref_top1"], res
+           "sdpa_top1": int(ref.argmax()), "step": eager, "replayed": replayed, "world": world}
+    assert res["top1"] == res["sdpa_top1"], res
     assert corr > 0.999, res
     assert res["step"] == res["top1"] and res["replayed"] == res["step"], res
     return res

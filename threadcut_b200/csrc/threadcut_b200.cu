@@ -393,18 +393,49 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 namespace {
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[256] = {};
+unsigned long long g_noalloc_ctx[256] = {};  // id of the context the address above belongs to
 
-// Device address of g_noalloc_scratch on the current device, looked up on the first call for that
-// device (with the device current) and remembered afterwards.
+// Unique id of the calling thread's current CUDA context (ids are never reused, unlike context
+// handles), 0 if there is none or the driver lacks cuCtxGetId. Reached through the runtime's
+// driver entry point, like the tensor-map encoder.
+unsigned long long current_ctx_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_cur = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_cur == nullptr || get_id == nullptr || get_cur(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch on the current device. It is looked up (with the device
+// current) on the first call for that device, and again whenever the device's context changed
+// since (after cudaDeviceReset the module is loaded anew and the array may sit elsewhere).
 int noalloc_scratch(void** addr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return TC_ERR_CUDA;
   if (dev < 0 || dev >= 256) return TC_ERR_INVALID;
+  // 0 before the runtime has made a context current on this thread: the lookup below then runs
+  // (and makes it current), and the next call records the id
+  const unsigned long long ctx = current_ctx_id();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_noalloc_addr[dev] == nullptr || ctx == 0 || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return TC_ERR_CUDA;
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *addr = g_noalloc_addr[dev];
   return TC_OK;

@@ -12,7 +12,7 @@ rotations compose, so moving C left by gap = |B| positions only needs every key 
 * `splice(cache, s, inv_freq)` (kv.py:28-41): when every layer is a GrowingLayer with the same
   buffer geometry, ALL layers are spliced in ONE launch; otherwise the copy path (tc_splice_copy per
   layer, new tensors, as the reference's index_select path).
-* `new_cache(config)` (kv.py:95-98).
+* `new_cache(config)` (kv.py:95-98); `use_paged_cache()` switches what it builds to the paged layout.
 The cos/sin table is built on the host exactly as the reference builds it (fp32 angle
 delta*inv_freq, torch cos/sin) and passed by value into the launch.
 """
@@ -25,7 +25,7 @@ from transformers.cache_utils import DynamicLayer
 from ._lib import check, cos_sin_table, dtype_code, lib, require_cuda, stream_ptr, workspaces
 from .match import Split
 
-__all__ = ["rotate_half", "shift_keys", "splice", "GrowingLayer", "new_cache"]
+__all__ = ["rotate_half", "shift_keys", "splice", "GrowingLayer", "new_cache", "use_paged_cache"]
 
 # attention implementation that consumes deferred appends (threadcut_b200.attention.NAME)
 FUSED_ATTENTION = "threadcut"
@@ -304,6 +304,12 @@ class PagedLayer(DynamicLayer):
     def lazy_initialization(self, key_states, value_states, *args, **kwargs):
         super().lazy_initialization(key_states, value_states)
         self.state.ensure(key_states)
+        # `keys`/`values` carry the layout only ([1, hkv, 1, d] of the cache's dtype and device, not
+        # its rows), for callers that size the cache from them (threadcut/engine.py:99-100); the
+        # rows live in the pages (materialize() gives a contiguous copy)
+        kv = self.state.kv
+        self.keys = torch.zeros((1, kv.hkv, 1, kv.d), dtype=kv.dtype, device=kv.device)
+        self.values = self.keys
 
     def get_seq_length(self):
         return self.state.kv.n if self.state.kv is not None else 0
@@ -391,10 +397,28 @@ def paged_pending(key):
     return layer
 
 
-def new_cache(config, paged=False, max_tokens=32768, page_rows=64):
+# Layout of the caches new_cache(config) builds when the caller does not say: the reference's
+# engine calls new_cache(self.model.config) (threadcut/engine.py:53), so a process that wants the
+# paged layout under that unchanged caller selects it here (use_paged_cache) instead.
+_LAYOUT = {"paged": False, "max_tokens": 32768, "page_rows": 64}
+
+
+def use_paged_cache(enabled=True, max_tokens=32768, page_rows=64):
+    """Make new_cache(config) build paged caches (PagedLayers over one PagedKV of max_tokens rows in
+    page_rows-row pages) from now on, or contiguous GrowingLayer caches again (enabled=False)."""
+    if max_tokens < 1 or page_rows < 1:
+        raise ValueError("use_paged_cache: max_tokens and page_rows must be positive")
+    _LAYOUT.update(paged=bool(enabled), max_tokens=int(max_tokens), page_rows=int(page_rows))
+
+
+def new_cache(config, paged=None, max_tokens=None, page_rows=None):
     """A DynamicCache of GrowingLayers (the reference's layout, threadcut/kv.py:44-98) or, with
     paged=True, of PagedLayers over one PagedKV sized for max_tokens (plus spare pages for the
-    partly used pages splices leave; a full pool is re-packed by PagedKV.compact)."""
+    partly used pages splices leave; a full pool is re-packed by PagedKV.compact). Arguments left
+    None take the process-wide choice of use_paged_cache (default: contiguous, 32768, 64)."""
+    paged = _LAYOUT["paged"] if paged is None else paged
+    max_tokens = _LAYOUT["max_tokens"] if max_tokens is None else max_tokens
+    page_rows = _LAYOUT["page_rows"] if page_rows is None else page_rows
     cache = DynamicCache(config=config)
     fused = getattr(config, "_attn_implementation", None) == FUSED_ATTENTION
     if paged:

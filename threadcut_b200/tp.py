@@ -245,14 +245,33 @@ class TPDecoder:
         """A CUDA graph of step(token, pos) (the all-reduces inside it) and its output tensor; the
         cache is cropped back to `pos` rows, so each replay decodes the same step. The capture is
         thread-local: the process group's watchdog thread polls events meanwhile, which a global
-        capture would count as an illegal call. Every rank must capture at the same point."""
+        capture would count as an illegal call. Every rank must capture at the same point.
+
+        Before capturing, every layer's buffer gets room for row `pos` (a buffer that is exactly
+        full would otherwise grow inside the capture: the new buffer would come from the graph's
+        private pool and the copy of the old rows would only be recorded, leaving the replayed cache
+        uninitialised and reading the freed old buffer), and one eager step runs on the capture
+        stream, so that the decode workspace of that stream is allocated and zeroed outside the
+        graph."""
+        for layer in self.layers:
+            if layer.is_initialized and layer.kbuf is not None:
+                layer._flush()
+                layer._reserve(pos + 1, layer.kbuf)
         torch.cuda.synchronize(self.dev)
         graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
         try:
-            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            with torch.cuda.stream(s):
+                self.step(token, pos)  # eager warm-up on the capture stream
+                self.crop(pos)
+            torch.cuda.synchronize(self.dev)
+            with torch.cuda.graph(graph, stream=s, capture_error_mode="thread_local"):
                 out = self.step(token, pos)
         finally:
             self.crop(pos)
+            torch.cuda.current_stream(self.dev).wait_stream(s)
+            torch.cuda.synchronize(self.dev)
         return graph, out
 
     def logits(self, token, pos):

@@ -79,15 +79,15 @@ def cfg4_lengths(seed=0, batch=CFG4_BATCH, lo=CFG4_LO, hi=CFG4_HI):
     return torch.randint(lo, hi + 1, (batch,), generator=torch.Generator().manual_seed(seed)).tolist()
 
 
-def layer_kv(n, layers, device, dtype=torch.bfloat16, seed=0, cap=None):
-    """`layers` distinct K/V buffers [8, cap, 128] (cap >= n, default n) of N(0,1) data drawn on the
-    device (Philox, deterministic for a seed), as GrowingLayer-style views [8, n, 128]."""
+def layer_kv(n, layers, device, dtype=torch.bfloat16, seed=0, cap=None, heads=HKV):
+    """`layers` distinct K/V buffers [heads, cap, 128] (cap >= n, default n) of N(0,1) data drawn on
+    the device (Philox, deterministic for a seed), as GrowingLayer-style views [heads, n, 128]."""
     cap = n if cap is None else cap
     g = torch.Generator(device=device).manual_seed(seed)
     ks, vs = [], []
     for _ in range(layers):
-        kb = torch.randn(HKV, cap, D, generator=g, device=device, dtype=torch.float32).to(dtype)
-        vb = torch.randn(HKV, cap, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+        kb = torch.randn(heads, cap, D, generator=g, device=device, dtype=torch.float32).to(dtype)
+        vb = torch.randn(heads, cap, D, generator=g, device=device, dtype=torch.float32).to(dtype)
         ks.append(kb[:, :n])
         vs.append(vb[:, :n])
     return ks, vs
