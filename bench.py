@@ -735,9 +735,24 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
             graph_ms = timed(replay)
             graph_tok = int(out)
         del graph
+        nccl_ms = None
+        if dec.use_peer_sums:  # the same graph with the collective library's all-reduce for the sums
+            dec.use_peer_sums = False
+            graph, out = dec.capture(tok, n)
+
+            def replay():
+                graph.replay()
+                int(out)
+
+            nccl_ms = timed(replay)
+            ok = float(int(out) == ref_top1)
+            top1_ok = top1_ok and -max_over_ranks(-ok, dist) == 1.0
+            del graph
+            dec.use_peer_sums = True
+    dec.close()
     del dec
     torch.cuda.empty_cache()
-    return {"eager_ms": eager_ms, "graph_ms": graph_ms, "splice_ms": splice_ms,
+    return {"eager_ms": eager_ms, "graph_ms": graph_ms, "nccl_graph_ms": nccl_ms, "splice_ms": splice_ms,
             "bytes": shard_bytes + LAYERS * (4096 // world * n + 16384 // world),
             "top1_ok": bool(top1_ok and (graph_tok is None or graph_tok == ref_top1)), "token": step_tok,
             "sdpa_token": ref_top1, "logit_corr": round(corr, 6),
@@ -983,12 +998,14 @@ def run_ours(args, rank, local, world, dist):
                "graph_ms": None if tp["graph_ms"] is None else round(tp["graph_ms"], 3),
                "splice_ms": round(tp["splice_ms"], 3), "bytes_per_rank": tp["bytes"],
                "ideal_ms": round(tp["bytes"] / (hbm * 1e9) * 1e3, 3),
+               "nccl_graph_ms": None if tp["nccl_graph_ms"] is None else round(tp["nccl_graph_ms"], 3),
                "top1_ok": tp["top1_ok"], "token": tp["token"], "sdpa_token": tp["sdpa_token"],
                "logit_corr": tp["logit_corr"], "logit_max_abs": tp["logit_max_abs"],
                "what": f"one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache, "
                        f"tensor-parallel over {world} GPU(s) (threadcut_b200.tp.TPDecoder: KV heads, their query "
-                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 all-reduces per layer), next "
-                       f"token read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
+                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 sums over the ranks per layer, through "
+                       f"peer memory fused into the projection and the norm (nccl_graph_ms: the same graph with NCCL "
+                       f"all-reduces instead)), next token read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
                        f"graph and gathered-logit tokens equal HF's SDPA forward over the same spliced full cache "
                        f"(sdpa_token) on every rank; ideal_ms = one rank's weight + K/V bytes at the measured HBM "
                        f"peak (collectives not counted)"}

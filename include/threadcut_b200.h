@@ -51,7 +51,8 @@ enum { TC_F32 = 0, TC_F16 = 1, TC_BF16 = 2 };
 /* ---- device-side error bits (see tc_device_errors) ------------------------------------ */
 enum {
   TC_DEVERR_PIPE_TIMEOUT = 1, /* a K/V staging wait (mbarrier) ran past its poll limit        */
-  TC_DEVERR_FLAG_TIMEOUT = 2  /* an in-place splice wait on another tile ran past its limit  */
+  TC_DEVERR_FLAG_TIMEOUT = 2, /* an in-place splice wait on another tile ran past its limit  */
+  TC_DEVERR_PEER_TIMEOUT = 4  /* a wait for another GPU's rows of a sum ran past its limit    */
 };
 
 /* Human-readable name of a TC_* status. */
@@ -402,6 +403,38 @@ int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype
 /* tc_silu_mul: out[r][i] = dtype(silu(gate_up[r][i])) * gate_up[r][inter + i] for `rows` rows
  * (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), gate and up side by side in one row). */
 int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream);
+
+/* ---- sums over the GPUs of a tensor-parallel step, through peer memory ------------------
+ * No counterpart in the reference (threadcut runs one GPU); they replace the collective library's
+ * all-reduce after the two row-split projections of each layer of threadcut_b200/tp.py.
+ *
+ * Peer regions: every rank allocates one region (tc_peer_alloc, at set-up: cudaMalloc + zero +
+ * cudaIpcGetMemHandle), hands the tc_peer_handle_bytes() handle bytes to the other ranks (any
+ * host transport), and maps theirs (tc_peer_open, cudaIpcOpenMemHandle). Kernels then read and
+ * write peers' regions with plain loads and stores over NVLink; nothing here uses TMA or multicast.
+ * tc_peer_close unmaps a peer's region, tc_peer_free frees the own one. */
+size_t tc_peer_handle_bytes(void);
+int tc_peer_alloc(size_t bytes, void** dev_ptr, void* handle_out);
+int tc_peer_open(const void* handle, void** dev_ptr);
+int tc_peer_close(void* dev_ptr);
+int tc_peer_free(void* dev_ptr);
+
+/* Bytes of the all-reduce region of one rank for `world` ranks summing vectors of `rows` elements
+ * (a control word, then two slots of world x rows 8-byte words). */
+size_t tc_allreduce_region_bytes(int world, int64_t rows);
+
+/* tc_gemv_allreduce: the rows of tc_gemv (x [k] . w[n][k]^T, fp32 accumulation), each sent as an
+ * fp32 word tagged with the sum's number to every rank's region (regions[p]: rank p's region as
+ * mapped in this process, p < world <= 8; regions[rank] is this rank's own). n = the regions'
+ * `rows`. Must be followed, on every rank and in the same order, by tc_allreduce_add_rmsnorm.
+ * tc_allreduce_add_rmsnorm: delta = dtype(sum over ranks of their rows, in rank order, fp32), then
+ * tc_add_rmsnorm with that delta: h += delta (rounded) in place, out = RMSNorm(h) * weight. It waits
+ * (bounded; TC_DEVERR_PEER_TIMEOUT) for every rank's rows of the current sum. hidden = rows <= 8192.
+ * Every rank ends with the same bits in h and out. */
+int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
+                      int dtype, void* stream);
+int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
+                             int world, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -381,3 +381,20 @@ def test_reference_engine_runs_unchanged_over_this_package(monkeypatch):
     assert isinstance(eng.cache.layers[0], kv.GrowingLayer)
     with pytest.raises(RuntimeError, match="CUDA device"):
         eng.generate(ids + [7, 8], max_new_tokens=2)  # the decode step reaches the kernels
+
+
+def test_peer_sum_argument_validation_without_a_gpu():
+    """The peer-memory sums check their arguments before touching the device."""
+    L = _lib.lib()
+    assert L.tc_peer_handle_bytes() == 64
+    assert L.tc_allreduce_region_bytes(8, 2560) == 256 + 2 * 8 * 2560 * 8
+    assert L.tc_allreduce_region_bytes(9, 2560) == 0 and L.tc_allreduce_region_bytes(2, 0) == 0
+    regs = (ctypes.c_void_p * 2)(256, 512)
+    assert L.tc_gemv_allreduce(16, 16, 2560, 512, regs, 2, 0, 0, None) == 3        # fp32: dtype
+    assert L.tc_gemv_allreduce(16, 16, 2560, 512, regs, 2, 2, 2, None) == 1        # rank outside world
+    assert L.tc_gemv_allreduce(16, 16, 2560, 500, regs, 2, 0, 2, None) == 1        # k not a multiple of 8
+    assert L.tc_gemv_allreduce(8, 16, 2560, 512, regs, 2, 0, 2, None) == 2         # x misaligned
+    assert L.tc_gemv_allreduce(16, 16, 2560, 512, None, 2, 0, 2, None) == 1        # no regions
+    assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 9000, 1e-6, 256, 2, 2, None) == 1  # hidden too large
+    assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 2560, 1e-6, 100, 2, 2, None) == 1  # region misaligned
+    assert L.tc_peer_open(None, None) == 1 and L.tc_peer_close(None) == 1 and L.tc_peer_free(None) == 1

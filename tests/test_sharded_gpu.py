@@ -41,3 +41,15 @@ def test_tensor_parallel_decoder_matches_the_sdpa_forward():
     res = subprocess.run(cmd, capture_output=True, text=True)
     print(res.stdout[-3000:], res.stderr[-3000:])
     assert res.returncode == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least 2 GPUs")
+def test_peer_memory_sums_match_the_collective_library():
+    """threadcut_b200.peer.AllReduce (tests/peer_worker.py) on every visible GPU (up to 8)."""
+    world = max(w for w in (2, 4, 8) if w <= min(torch.cuda.device_count(), 8))
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           os.path.join(HERE, "peer_worker.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    print(res.stdout[-3000:], res.stderr[-3000:])
+    assert res.returncode == 0

@@ -69,6 +69,14 @@ SIGNATURES = {
     "tc_paged_rotate_keys": (_i, [ctypes.POINTER(_vp), _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _fp,
                                   _i, _vp]),
     "tc_paged_write": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i64] + [_i64] * 4 + [_i64] * 5 + [_vp, _i, _vp]),
+    "tc_peer_handle_bytes": (_sz, []),
+    "tc_peer_alloc": (_i, [_sz, ctypes.POINTER(_vp), _vp]),
+    "tc_peer_open": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "tc_peer_close": (_i, [_vp]),
+    "tc_peer_free": (_i, [_vp]),
+    "tc_allreduce_region_bytes": (_sz, [_i, _i64]),
+    "tc_gemv_allreduce": (_i, [_vp, _vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _i, _vp]),
+    "tc_allreduce_add_rmsnorm": (_i, [_vp, _vp, _vp, _i, _f, _vp, _i, _i, _vp]),
 }
 
 _lib = None

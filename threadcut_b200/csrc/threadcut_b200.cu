@@ -14,6 +14,7 @@
 #include "split.cuh"
 #include "prefill_attn.cuh"
 #include "layer_ops.cuh"
+#include "peer.cuh"
 
 using namespace tc;
 
@@ -1329,6 +1330,100 @@ int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dty
   if (rows == 0) return TC_OK;
   if (gate_up == nullptr || out == nullptr) return TC_ERR_INVALID;
   return launch_layer_op(dtype, 2, out, nullptr, gate_up, nullptr, nullptr, nullptr, rows, inter, 0, 0, 0.f, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- sums over GPUs through peer memory
+extern "C" {
+
+size_t tc_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int tc_peer_alloc(size_t bytes, void** dev_ptr, void* handle_out) {
+  if (bytes == 0 || dev_ptr == nullptr || handle_out == nullptr) return TC_ERR_INVALID;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return TC_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return TC_ERR_CUDA;
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  *dev_ptr = p;
+  return TC_OK;
+}
+
+int tc_peer_open(const void* handle, void** dev_ptr) {
+  if (handle == nullptr || dev_ptr == nullptr) return TC_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_peer_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) return TC_ERR_INVALID;
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_peer_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return TC_ERR_INVALID;
+  return cudaFree(dev_ptr) == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+size_t tc_allreduce_region_bytes(int world, int64_t rows) {
+  if (world < 1 || world > kArMaxWorld || rows < 1 || rows > 8192) return 0;
+  return (size_t)kArCtrlBytes + (size_t)kArSlots * world * rows * sizeof(uint64_t);
+}
+
+int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
+                      int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world || regions == nullptr) return TC_ERR_INVALID;
+  if (n < 1 || n > 8192 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
+  if (x == nullptr || w == nullptr) return TC_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
+  ArPeers ar;
+  std::memset(&ar, 0, sizeof(ar));
+  for (int p = 0; p < world; ++p) {
+    if (regions[p] == nullptr || (reinterpret_cast<uintptr_t>(regions[p]) & 255)) return TC_ERR_INVALID;
+    ar.data[p] = reinterpret_cast<uint64_t*>(static_cast<char*>(regions[p]) + kArCtrlBytes);
+  }
+  ar.seq = static_cast<const unsigned int*>(regions[rank]);
+  ar.world = world;
+  ar.rank = rank;
+  ar.rows = n;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((n + kArRows - 1) / kArRows);
+  const size_t smem = (size_t)k * 2;
+  if (dtype == TC_BF16)
+    gemv_allreduce_kernel<__nv_bfloat16><<<grid, kArThreads, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), n, k, ar);
+  else
+    gemv_allreduce_kernel<__half><<<grid, kArThreads, smem, st>>>(static_cast<const __half*>(x),
+                                                                  static_cast<const __half*>(w), n, k, ar);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
+                             int world, int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (world < 1 || world > kArMaxWorld || hidden < 1 || hidden > kArNormThreads * kArMaxPerThread || !(eps >= 0.f))
+    return TC_ERR_INVALID;
+  if (h == nullptr || weight == nullptr || out == nullptr || region == nullptr) return TC_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(region) & 255) return TC_ERR_INVALID;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(static_cast<char*>(region) + kArCtrlBytes);
+  unsigned int* seq = static_cast<unsigned int*>(region);
+  if (dtype == TC_BF16)
+    allreduce_add_rmsnorm_kernel<__nv_bfloat16><<<1, kArNormThreads, 0, st>>>(
+        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+        hidden, 1.0f / (float)hidden, eps, mine, seq, world, hidden);
+  else
+    allreduce_add_rmsnorm_kernel<__half><<<1, kArNormThreads, 0, st>>>(
+        static_cast<__half*>(h), static_cast<const __half*>(weight), static_cast<__half*>(out), hidden,
+        1.0f / (float)hidden, eps, mine, seq, world, hidden);
+  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -1,0 +1,104 @@
+"""Device memory shared by the ranks of a process group over NVLink (CUDA IPC), and the sums of the
+tensor-parallel step that run through it.
+
+threadcut runs one GPU (threadcut/engine.py:21-104); the tensor-parallel step of config 5
+(threadcut_b200/tp.py) needs two sums over the ranks per layer. `PeerRegion` gives every rank one
+region of its own memory mapped into every other rank's address space: the library allocates it
+(tc_peer_alloc), the ranks exchange the IPC handles through the process group (an all-gather of the
+handle bytes), and each rank maps the others' (tc_peer_open). `AllReduce` keeps one such region
+per decoder and runs the fused sum: the row-split projection writes its rows into every rank's
+region (tc_gemv_allreduce), and the next kernel adds them up with the residual add and RMSNorm
+(tc_allreduce_add_rmsnorm). No collective library runs on that path; all ranks must make the same
+sequence of calls.
+"""
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from ._lib import check, dtype_code, lib, require_cuda, stream_ptr
+
+__all__ = ["PeerRegion", "AllReduce"]
+
+
+class PeerRegion:
+    """`nbytes` of zeroed device memory on every rank of `group`, each rank's region mapped into
+    every other rank's process. `ptrs[p]` is rank p's region as seen from this process. Collective:
+    every rank of the group constructs it at the same point."""
+
+    def __init__(self, nbytes, device, group=None):
+        self.device = torch.device(device)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        L = lib()
+        hb = L.tc_peer_handle_bytes()
+        handle = (ctypes.c_uint8 * hb)()
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check("tc_peer_alloc", L.tc_peer_alloc(int(nbytes), ctypes.byref(own), handle))
+        self._own = own.value
+        self.ptrs = [None] * self.world
+        self.ptrs[self.rank] = self._own
+        if self.world > 1:
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+            every = torch.empty(self.world * hb, dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy().reshape(self.world, hb)
+            for p in range(self.world):
+                if p == self.rank:
+                    continue
+                buf = (ctypes.c_uint8 * hb).from_buffer_copy(every[p].tobytes())
+                peer = ctypes.c_void_p()
+                with torch.cuda.device(self.device):
+                    check("tc_peer_open", L.tc_peer_open(buf, ctypes.byref(peer)))
+                self.ptrs[p] = peer.value
+        self._arr = (ctypes.c_void_p * self.world)(*self.ptrs)
+
+    def close(self):
+        """Unmaps the peers' regions and frees this rank's (after the device finished using them)."""
+        if self._own is None:
+            return
+        L = lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for p, ptr in enumerate(self.ptrs):
+                if p != self.rank and ptr is not None:
+                    L.tc_peer_close(ctypes.c_void_p(ptr))
+            L.tc_peer_free(ctypes.c_void_p(self._own))
+        self._own = None
+        self.ptrs = [None] * self.world
+
+
+class AllReduce:
+    """The sums of the tensor-parallel step over the ranks of `group`, for vectors of `hidden`
+    elements: gemv(x, w) starts one (w's rows are split over the ranks' columns: each rank holds a
+    partial product), add_rmsnorm(h, weight, out, eps) finishes it."""
+
+    def __init__(self, hidden, device, group=None):
+        self.hidden = int(hidden)
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        nbytes = lib().tc_allreduce_region_bytes(world, self.hidden)
+        if nbytes == 0:
+            raise ValueError(f"AllReduce: {world} ranks x {hidden} elements is outside the supported range")
+        self.region = PeerRegion(nbytes, device, group)
+
+    def gemv(self, x, w):
+        require_cuda(x, w, what="gemv_allreduce")
+        n, k = w.shape
+        if n != self.hidden or x.numel() != k or not (x.is_contiguous() and w.is_contiguous()):
+            raise ValueError("gemv_allreduce: w must be [hidden, k] and x [k], both contiguous")
+        r = self.region
+        check("tc_gemv_allreduce", lib().tc_gemv_allreduce(x.data_ptr(), w.data_ptr(), n, k, r._arr, r.world, r.rank,
+                                                           dtype_code(x, "gemv_allreduce"), stream_ptr(x.device)))
+
+    def add_rmsnorm(self, h, weight, out, eps):
+        require_cuda(h, weight, out, what="allreduce_add_rmsnorm")
+        if h.numel() != self.hidden:
+            raise ValueError("allreduce_add_rmsnorm: h must hold `hidden` elements")
+        r = self.region
+        check("tc_allreduce_add_rmsnorm", lib().tc_allreduce_add_rmsnorm(
+            h.data_ptr(), weight.data_ptr(), out.data_ptr(), self.hidden, float(eps), r.ptrs[r.rank], r.world,
+            dtype_code(h, "allreduce_add_rmsnorm"), stream_ptr(h.device)))
+
+    def close(self):
+        self.region.close()

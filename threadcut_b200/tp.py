@@ -11,8 +11,11 @@ holds, for every layer:
 * 1/world of the MLP's intermediate dimension (gate/up rows, down_proj columns);
 * 1/world of the vocabulary (lm_head rows); norms and the embedding are replicated.
 
-A layer ends in two sums over ranks of [hidden] partials (after o_proj and after down_proj:
-torch.distributed.all_reduce, NCCL). The next token is the first index of the largest logit over
+A layer ends in two sums over ranks of [hidden] partials (after o_proj and after down_proj). On
+more than one rank they run through peer memory (threadcut_b200.peer.AllReduce): the row-split
+projection writes its fp32 rows into every rank's region over NVLink, and the residual add + RMSNorm
+kernel that follows sums them in rank order, so every rank holds the same bits; with
+peer_sums=False, torch.distributed.all_reduce (NCCL) between the projection and the norm. The next token is the first index of the largest logit over
 all ranks' vocabulary slices (torch's argmax rule), found from an all-gather of each rank's
 (best logit, index). The arithmetic is HF's Qwen3 (modeling_qwen3: RMSNorm in fp32 cast back to
 the weights' dtype, q/k RMSNorm per head, RoPE with cos/sin rounded to the model dtype, SwiGLU),
@@ -126,7 +129,7 @@ class TPDecoder:
     load(layer, k, v): fill layer's cache from full-head K/V [1 or -, hkv, n, d] (own heads kept).
     splice(s, inv_freq): kv.splice on the local heads.  crop(n): drop rows past n."""
 
-    def __init__(self, model, device, group=None, world=None, rank=None):
+    def __init__(self, model, device, group=None, world=None, rank=None, peer_sums=True):
         cfg = model.config
         kinds = set(getattr(cfg, "layer_types", None) or ["full_attention"])
         if getattr(cfg, "use_sliding_window", False) or kinds != {"full_attention"}:
@@ -160,6 +163,15 @@ class TPDecoder:
         self.layers = [_kv.GrowingLayer() for _ in base.layers]
         for layer in self.layers:
             layer.fuse_append = True  # the decode launch writes each step's row
+        # the two sums per layer: through peer memory (one-shot, fused into the projection and the
+        # norm after it) on more than one rank unless peer_sums is False, else the collective library
+        self._ar = None
+        self.use_peer_sums = False
+        if (self.world > 1 and peer_sums and self.dev.type == "cuda"
+                and self.dtype in (torch.bfloat16, torch.float16)):
+            from .peer import AllReduce
+            self._ar = AllReduce(cfg.hidden_size, self.dev, group)
+            self.use_peer_sums = True
 
     # ------------------------------------------------------------------ cache
     def load(self, i, k, v):
@@ -216,14 +228,32 @@ class TPDecoder:
             q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
             _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
             o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
-            a = self._all_reduce(_gemv(o.reshape(1, nq * d), w.wo))
-            _add_rmsnorm(h, a, w.post_norm, x, eps)
+            self._sum_add_norm(o.reshape(1, nq * d), w.wo, h, w.post_norm, x)
             gu = _gemv(x, w.wgu)
             act = gu.new_empty((1, gu.shape[1] // 2))
             _silu_mul(gu, act)
-            m = self._all_reduce(_gemv(act, w.wd))
-            _add_rmsnorm(h, m, norm_next, x, eps)
+            self._sum_add_norm(act, w.wd, h, norm_next, x)
         return x
+
+    def _sum_add_norm(self, a, w, h, norm, x):
+        """h += sum over ranks of a @ w^T (w: this rank's columns of a row-split projection), then
+        x = RMSNorm(h) * norm: through peer memory (tc_gemv_allreduce + tc_allreduce_add_rmsnorm)
+        or a collective all-reduce between tc_gemv and tc_add_rmsnorm."""
+        if self.use_peer_sums:
+            self._ar.gemv(a, w)
+            self._ar.add_rmsnorm(h, norm, x, self.eps)
+        else:
+            _add_rmsnorm(h, self._all_reduce(_gemv(a, w)), norm, x, self.eps)
+
+    def close(self):
+        """Releases the peer-memory region of the sums (collective: every rank calls it, after the
+        device finished every step that uses it)."""
+        if self._ar is not None:
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._ar.close()
+            self._ar = None
+            self.use_peer_sums = False
 
     def step(self, token, pos):
         """Decode `token` (int64 device tensor [1]) at position `pos` (the cache length before the
