@@ -1119,13 +1119,17 @@ def run_partial(args, rank, local, world, dist):
     dev = torch.device("cuda", local)
     out = {"only": args.only, "layers": args.layers, "ctx": args.ctx, "steps": args.steps}
     if args.only == "decode":
-        qs, ks, vs = build_layers(args.ctx, args.layers, dev, seed=1000 + rank)
+        qs, ks, vs = build_layers(args.ctx, args.layers, dev, seed=1000 + rank, heads=args.heads)
         outs = [torch.empty_like(q) for q in qs]
-        graph = capture_step(qs, ks, vs, outs, dev)
-        ms = max_over_ranks(time_graph(graph, args.steps, args.warmup, dist), dist)
-        us = ms * 1000 / args.layers
-        out.update(us_per_layer=round(us, 3), gbs=round(decode_bytes(args.ctx) / (us * 1e-6) / 1e9, 1))
-        del graph
+        res = {}
+        for name, stable in (("stable", True), ("plain", False)):
+            graph = capture_step(qs, ks, vs, outs, dev, stable=stable)
+            ms = max_over_ranks(time_graph(graph, args.steps, args.warmup, dist), dist)
+            us = ms * 1000 / args.layers
+            nbytes = 512 * args.heads * args.ctx + 2048 * args.heads
+            res[name] = {"us_per_layer": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+            del graph
+        out.update(heads=args.heads, **res)
     elif args.only == "cfg5tp":
         tp = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in tp.items()}, world=world)
@@ -1192,6 +1196,7 @@ def main():
                          "tensor-parallel form (smaller JSON line)")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling runs: layers per step")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="profiling runs: context length")
+    ap.add_argument("--heads", type=int, default=8, help="profiling runs (decode): KV heads per layer")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -5,8 +5,8 @@ Drop-in replacement for threadcut's hot path, module for module:
   threadcut.attention    -> threadcut_b200.attention      ("threadcut" transformers plugin)
   threadcut.kv           -> threadcut_b200.kv             (RoPE shift, splice, GrowingLayer)
   threadcut.match        -> threadcut_b200.match          (Split bookkeeping, host)
-  threadcut.engine       -> threadcut_b200.engine         (Engine, unchanged behaviour)
-The device code lives in csrc/ and is reached only through the C ABI of include/threadcut_b200.h
+threadcut's engine (threadcut/engine.py) is the caller of these modules and runs over them unchanged;
+it is not part of this package. The device code lives in csrc/ and is reached only through the C ABI of include/threadcut_b200.h
 (libthreadcut_b200.so, built by `python -m threadcut_b200.build`).
 """
 from .match import Split, lcp, split  # noqa: F401  (host only; importable without a GPU)

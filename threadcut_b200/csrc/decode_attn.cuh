@@ -467,7 +467,7 @@ __device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
   return (uint32_t)a | ((uint32_t)b << 16);
 }
 
-template <int D>
+template <int D, int RES = 1>
 struct MmaGeom {
   static_assert(D % 64 == 0, "the tensor-core kernel stages 64-column (128-byte) swizzled boxes");
   static constexpr int kBoxBytes = kTile * 128;      // one TMA box: 32 rows x 64 columns of 16-bit data
@@ -475,7 +475,9 @@ struct MmaGeom {
   static constexpr int kStageBytes = 2 * kTileBytes; // K tile then V tile
   // ~192 KB of K/V in flight per CTA (one CTA per SM): 12 stages at d <= 128, 6 at d = 256.
   // A multiple of kCWarps, so tile j always goes to consumer warp j % kCWarps and stage j % kStages.
-  static constexpr int kStages = D <= 128 ? 12 : 6;
+  // RES CTAs resident per SM share the ring's ~192 KB (RES = 2: 6 stages each, so that the next
+  // launch's CTAs fit beside this one's and start loading while it runs)
+  static constexpr int kStages = (D <= 128 ? 12 : 6) / RES;
   static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
   static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
@@ -494,10 +496,10 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {
 // (g <= 8*NG). K/V tiles arrive by tensor-map TMA: one cp.async.bulk.tensor per 64-column box.
 // kPaged: K/V rows come through the tile table (p.tiles); a separate instantiation, so the
 // contiguous kernel carries none of it.
-template <typename T, int D, int NG, bool kPaged>
-__global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
+template <typename T, int D, int NG, bool kPaged, int RES = 1>
+__global__ void __launch_bounds__(32 * (kCWarps + 1), RES)
     decode_mma_kernel(const __grid_constant__ DecodeParams p) {
-  using G = MmaGeom<D>;
+  using G = MmaGeom<D, RES>;
   constexpr int HP = 8 * NG;
   constexpr int KS = D / 16;
   constexpr int NBOX = D / 64;

@@ -201,8 +201,29 @@ cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st,
   return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
+// CTAs of the tensor-core decode kernel resident per SM (1: a 12-stage ring per CTA; 2: 6 stages,
+// so that the next launch's CTAs can load beside this one's), from TC_DECODE_RESIDENT (default 1).
+int decode_resident() {
+  static const int r = [] {
+    const char* e = std::getenv("TC_DECODE_RESIDENT");
+    return (e != nullptr && e[0] == '2') ? 2 : 1;
+  }();
+  return r;
+}
+
+template <typename T, int D, int NG, int RES>
+cudaError_t launch_mma_res(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
+  auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true, RES> : decode_mma_kernel<T, D, NG, false, RES>;
+  const int smem = MmaGeom<D, RES>::kSmem;
+  const int threads = 32 * (kCWarps + 1);
+  cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  if (e != cudaSuccess) return e;
+  return launch_ex(fn, grid, dim3(threads), smem, st, p);
+}
+
 template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
+  if (D == 128 && NG == 1 && decode_resident() == 2) return launch_mma_res<T, 128, 1, 2>(p, grid, st, dev);
   auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true> : decode_mma_kernel<T, D, NG, false>;
   const int smem = MmaGeom<D>::kSmem;
   const int threads = 32 * (kCWarps + 1);
