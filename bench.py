@@ -157,13 +157,14 @@ def build_layers(n, layers, dev, seed, heads=8):
     return qs, ks, vs
 
 
-def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None):
+def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None, lses=None):
     """CUDA graph of one step: the 36 decode launches through the C ABI with preallocated outputs.
     stable: declare rows [0, n-1) stable (tc_decode_attention_stable), as a decode step may: every
     row but the newest was written before the step; False runs plain tc_decode_attention.
-    combine: None, or (dist, local [layers, hl, 4, 128] whose slices are `outs`, full
-    [world * layers * hl * 4 * 128]) to all-gather every rank's outputs of the step into `full`
-    inside the graph (the head-sharded step's output combine)."""
+    lses: None, or one fp32 [hl, 4] tensor per layer: then each launch computes the fp32 partial and
+    its log-sum-exp (tc_decode_attention_partial_stable; outs fp32), a sequence shard's part.
+    combine: None, or a function run after the launches inside the graph (the sharded step's
+    combine: collectives and the merge)."""
     from threadcut_b200._lib import TC_BF16, check, lib, workspaces
     L = lib()
     n = ks[0].shape[1]
@@ -174,15 +175,20 @@ def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None):
 
     def launch_all():
         st = torch.cuda.current_stream(dev).cuda_stream
-        for q, k, v, o in zip(qs, ks, vs, outs):
-            rc = L.tc_decode_attention_stable(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128, n,
-                                              q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0),
-                                              v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16,
-                                              stable_rows, ws.data_ptr(), ws.numel(), st)
-            check("tc_decode_attention_stable", rc)
+        for i, (q, k, v, o) in enumerate(zip(qs, ks, vs, outs)):
+            if lses is None:
+                rc = L.tc_decode_attention_stable(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128,
+                                                  n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0),
+                                                  v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0, TC_BF16,
+                                                  stable_rows, ws.data_ptr(), ws.numel(), st)
+            else:
+                rc = L.tc_decode_attention_partial_stable(
+                    q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lses[i].data_ptr(), hl, 4, 128, n,
+                    q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1), o.stride(0),
+                    o.stride(1), workloads.SCALE, 0, TC_BF16, stable_rows, ws.data_ptr(), ws.numel(), st)
+            check("tc_decode_attention", rc)
         if combine is not None:
-            dist_, local, full = combine
-            dist_.all_gather_into_tensor(full, local.view(-1))
+            combine()
 
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream(dev))
@@ -196,6 +202,34 @@ def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None):
     torch.cuda.current_stream(dev).wait_stream(s)
     torch.cuda.synchronize()
     return graph
+
+
+class SeqShardedStep:
+    """Buffers and combine of a sequence-sharded decode step over `world` ranks: every rank holds a
+    token slice of all 8 KV heads of every layer and computes per layer the fp32 partial and LSE of
+    its slice (tc_decode_attention_partial_stable); the combine all-gathers the step's partials
+    (two NCCL all-gathers for the 36 layers) and merges them by log-sum-exp in one launch
+    (tc_merge_partials, the merge of threadcut/flash_decode.py:68-69 over ranks) into the bf16
+    outputs of every layer on every rank."""
+
+    def __init__(self, layers, dev, dist, world, hl=8):
+        self.rows = layers * hl * 4
+        self.po = torch.empty((layers, hl, 4, 128), dtype=torch.float32, device=dev)
+        self.pl = torch.empty((layers, hl, 4), dtype=torch.float32, device=dev)
+        self.go = torch.empty((world * self.po.numel(),), dtype=torch.float32, device=dev)
+        self.gl = torch.empty((world * self.pl.numel(),), dtype=torch.float32, device=dev)
+        self.out = torch.empty((self.rows, 128), dtype=torch.bfloat16, device=dev)
+        self.lse = torch.empty((self.rows,), dtype=torch.float32, device=dev)
+        self.outs, self.lses = list(self.po.unbind(0)), list(self.pl.unbind(0))
+        self.dist, self.world, self.dev = dist, world, dev
+
+    def combine(self):
+        from threadcut_b200._lib import TC_BF16, check, lib
+        self.dist.all_gather_into_tensor(self.go, self.po.view(-1))
+        self.dist.all_gather_into_tensor(self.gl, self.pl.view(-1))
+        check("tc_merge_partials", lib().tc_merge_partials(
+            self.go.data_ptr(), self.gl.data_ptr(), self.out.data_ptr(), self.lse.data_ptr(), self.world, self.rows,
+            128, self.out.stride(0), TC_BF16, torch.cuda.current_stream(self.dev).cuda_stream))
 
 
 def time_graph(graph, steps, warmup, dist):
@@ -213,25 +247,32 @@ def time_graph(graph, steps, warmup, dist):
 
 
 def time_e2e(qs, ks, vs, steps, warmup, dist, dev, world=1):
-    """Public-API path: pinned host queries -> device, 36 decode_attention calls over this rank's
-    heads, (N > 1) one all-gather of the step's outputs over the ranks, outputs -> host."""
-    from threadcut_b200.flash_decode import decode_attention
+    """Public-API path: pinned host queries -> device, 36 decode calls, outputs -> host. One GPU:
+    decode_attention per layer. N GPUs (sequence shards): decode_attention_partial per layer over
+    the rank's token slice, the step's partials all-gathered over the ranks and merged by
+    merge_partials, the merged outputs read back."""
+    from threadcut_b200.flash_decode import decode_attention, decode_attention_partial, merge_partials
     host_q = torch.stack([q.cpu() for q in qs]).pin_memory()
     dq = torch.empty_like(host_q, device=dev)
-    full = torch.empty((world * host_q.numel(),), dtype=host_q.dtype, device=dev)
-    host_out = torch.empty(full.shape, dtype=full.dtype).pin_memory()
+    host_out = torch.empty(host_q.shape, dtype=host_q.dtype).pin_memory()
+    layers, hl = host_q.shape[0], host_q.shape[1]
+    go = torch.empty((world, layers * hl * 4, 128), dtype=torch.float32, device=dev)
+    gl = torch.empty((world, layers * hl * 4), dtype=torch.float32, device=dev)
 
     n = ks[0].shape[1]
 
     def step():
         dq.copy_(host_q, non_blocking=True)
-        outs = torch.stack([decode_attention(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1)
-                            for i in range(len(ks))])
-        if world > 1:
-            dist.all_gather_into_tensor(full, outs.view(-1))
+        if world == 1:
+            outs = torch.stack([decode_attention(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1)
+                                for i in range(layers)])
         else:
-            full.copy_(outs.view(-1))
-        host_out.copy_(full, non_blocking=True)
+            parts = [decode_attention_partial(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1)
+                     for i in range(layers)]
+            dist.all_gather_into_tensor(go, torch.stack([o for o, _ in parts]).view(-1))
+            dist.all_gather_into_tensor(gl, torch.stack([lse for _, lse in parts]).view(-1))
+            outs, _ = merge_partials(go, gl, torch.bfloat16)
+        host_out.copy_(outs.view(host_out.shape), non_blocking=True)
 
     for _ in range(warmup):
         step()
@@ -796,11 +837,13 @@ def time_cfg4(steps, warmup, dev, dist, distinct=2):
 
 
 def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
-    """Strong scaling of one long sequence (config 5's 128k context, attention only): the 8 KV heads
-    are sharded over the ranks (head_shard), each rank decodes its heads for all layers, no
-    collective on the data path. Returns ms per 36-layer step on this rank."""
+    """Strong scaling of one long sequence (config 5's 128k context, attention only), two ways.
+    Head-sharded: the 8 KV heads are split over the ranks (head_shard), each rank decodes its heads
+    for all layers, no collective. Sequence-sharded (N > 1): each rank holds all heads of a
+    128k / N-token slice, computes each layer's partial, and the step ends with the combine
+    (SeqShardedStep: all-gathers + one LSE merge). Returns (head ms, sequence ms or None) per
+    36-layer step on this rank."""
     from threadcut_b200.sharded import head_shard
-    from threadcut_b200._lib import TC_BF16, check, lib, workspaces
     n = workloads.CFG5_CTX
     h0, h1 = head_shard(workloads.HKV, rank, world)
     hl = h1 - h0
@@ -809,29 +852,23 @@ def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
     vs = [torch.randn(hl, n, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
     qs = [torch.randn(hl, 4, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
     outs = [torch.empty_like(q) for q in qs]
-    L = lib()
-    ws = workspaces.get(("decode", hl), dev, L.tc_decode_attention_workspace_size(1, hl, 4, 128, n, n, 0, TC_BF16))
-
-    def launch_all():
-        st = torch.cuda.current_stream(dev).cuda_stream
-        for q, k, v, o in zip(qs, ks, vs, outs):
-            check("tc_decode_attention_stable", L.tc_decode_attention_stable(
-                q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), hl, 4, 128, n, q.stride(0), q.stride(1),
-                k.stride(0), k.stride(1), v.stride(0), v.stride(1), o.stride(0), o.stride(1), workloads.SCALE, 0,
-                TC_BF16, n - 1, ws.data_ptr(), ws.numel(), st))
-    launch_all()
-    torch.cuda.synchronize()
-    s = torch.cuda.Stream(device=dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(graph, stream=s):
-            launch_all()
-    torch.cuda.current_stream(dev).wait_stream(s)
-    ms = time_graph(graph, steps, warmup, dist)
-    del graph, ks, vs
+    graph = capture_step(qs, ks, vs, outs, dev)
+    head_ms = time_graph(graph, steps, warmup, dist)
+    del graph, ks, vs, qs
     torch.cuda.empty_cache()
-    return ms
+    seq_ms = None
+    if world > 1:
+        nl = n // world
+        ks = [torch.randn(8, nl, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+        vs = [torch.randn(8, nl, 128, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+        gq = torch.Generator(device=dev).manual_seed(5999)
+        qs = [torch.randn(8, 4, 128, generator=gq, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+        seq = SeqShardedStep(layers, dev, dist, world)
+        graph = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses, combine=seq.combine)
+        seq_ms = time_graph(graph, steps, warmup, dist)
+        del graph, ks, vs, qs, seq
+        torch.cuda.empty_cache()
+    return head_ms, seq_ms
 
 
 def cpu_threads():
@@ -904,38 +941,42 @@ def cpu_shift_us_per_layer(reps=20):
 def run_ours(args, rank, local, world, dist):
     dev = torch.device("cuda", local)
     hbm, peak_kind = peaks()
-    if workloads.HKV % world:
-        raise SystemExit(f"bench: {world} GPUs do not divide the {workloads.HKV} KV heads")
-    # the step: one sequence of 16k * world tokens, 36 layers, KV heads sharded over the ranks
-    # (8 / world per rank: every GPU streams the same 67 MB per layer as one GPU at 16k), each
-    # layer's outputs all-gathered to every rank at the end of the step; at 1 GPU, the 16k headline
-    hl = workloads.HKV // world
+    # the step: one sequence of 16k * world tokens, 36 layers, sharded by token range over the
+    # ranks: every rank holds all 8 KV heads of its own 16k-token slice (the same 67 MB per layer as
+    # one GPU at 16k) and computes each layer's fp32 partial and LSE; the step ends with the combine
+    # (all-gather of the step's partials + one LSE merge launch). At 1 GPU: the 16k headline.
+    hl = workloads.HKV
     n_job = N_CTX * world
-    rank_bytes = 512 * hl * n_job + 2048 * hl  # K+V + q + o of this rank's heads, one layer
-    qs, ks, vs = build_layers(n_job, LAYERS, dev, seed=1000 + rank, heads=hl)
-    local_out = torch.empty((LAYERS, hl, 4, 128), dtype=torch.bfloat16, device=dev)
-    outs = list(local_out.unbind(0))
-    full_out = torch.empty((world * local_out.numel(),), dtype=torch.bfloat16, device=dev)
-    combine = (dist, local_out, full_out) if world > 1 else None
-    graph = capture_step(qs, ks, vs, outs, dev, combine=combine)
+    rank_bytes = 512 * hl * N_CTX + 2048 * hl  # K+V of the rank's slice + q + o, one layer
+    gq = torch.Generator(device=dev).manual_seed(1001)  # the sequence's queries: the same on every rank
+    qs = [torch.randn(hl, 4, 128, generator=gq, device=dev).to(torch.bfloat16) for _ in range(LAYERS)]
+    _, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
+    if world == 1:
+        seq = None
+        outs = [torch.empty_like(q) for q in qs]
+        graph = capture_step(qs, ks, vs, outs, dev)
+    else:
+        seq = SeqShardedStep(LAYERS, dev, dist, world)
+        graph = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses, combine=seq.combine)
     with ClockSampler(local) as clk:
         ms = time_graph(graph, args.steps, args.warmup, dist)
     ms = max_over_ranks(ms, dist)
     us_layer_rank = ms * 1000.0 / LAYERS  # one rank's time per layer (incl. back-to-back gaps)
     value = ms * 1000.0 / (LAYERS * world)  # per 16k tokens of context per layer
     achieved = rank_bytes / (us_layer_rank * 1e-6) / 1e9
-    if world > 1:  # the combine's share: the same decode launches without the all-gather
-        g_nc = capture_step(qs, ks, vs, outs, dev)
+    if world > 1:  # the combine's share: the same decode launches without it
+        g_nc = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses)
         nocombine_ms = max_over_ranks(time_graph(g_nc, args.steps, args.warmup, dist), dist)
         del g_nc
+        g_plain = capture_step(qs, ks, vs, seq.outs, dev, stable=False, lses=seq.lses, combine=seq.combine)
     else:
         nocombine_ms = ms
-    g_plain = capture_step(qs, ks, vs, outs, dev, stable=False, combine=combine)
+        g_plain = capture_step(qs, ks, vs, outs, dev, stable=False)
     plain_ms = max_over_ranks(time_graph(g_plain, args.steps, args.warmup, dist), dist)
     del g_plain
     e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev, world)
     e2e_ms = max_over_ranks(e2e_ms, dist)
-    del graph, qs, ks, vs
+    del graph, qs, ks, vs, seq
     torch.cuda.empty_cache()
     # the single-GPU 16k layers (replicated on every rank) for the comparators and the fused append
     qs, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
@@ -969,12 +1010,19 @@ def run_ours(args, rank, local, world, dist):
     split_dev_us, split_host_us = time_split_128k(dev)
     pf_ms, pf_gqa_ms, pf_ref_ms, pf_flops = time_prefill(min(args.steps, 10), args.warmup, dev)
     tc_peak, tc_peak_kind = bf16_peak()
-    strong_ms = max_over_ranks(time_strong_128k(args.steps, args.warmup, dev, dist, rank, world), dist)
-    strong = {"us_per_layer": round(strong_ms * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
-              "kv_heads_per_rank": workloads.HKV // world,
-              "workload": "one 128k-token sequence, 36 layers, KV heads sharded over the ranks (no collective); "
-                          "per-layer latency, max over ranks",
-              "frac_per_gpu": round(decode_bytes(workloads.CFG5_CTX) / world / (strong_ms * 1e-3 / LAYERS) / 1e9
+    st_head, st_seq = time_strong_128k(args.steps, args.warmup, dev, dist, rank, world)
+    st_head = max_over_ranks(st_head, dist)
+    st_seq = max_over_ranks(st_seq, dist) if st_seq is not None else None
+    best = min(st_head, st_seq) if st_seq is not None else st_head
+    strong = {"us_per_layer": round(best * 1000 / LAYERS, 3), "n": workloads.CFG5_CTX,
+              "head_sharded_us_per_layer": round(st_head * 1000 / LAYERS, 3),
+              "seq_sharded_us_per_layer": None if st_seq is None else round(st_seq * 1000 / LAYERS, 3),
+              "kv_heads_per_rank_head_sharded": workloads.HKV // world,
+              "workload": "one 128k-token sequence, 36 layers, attention only, on N GPUs: head-sharded (8/N KV "
+                          "heads per GPU, no collective) and sequence-sharded (all heads of a 128k/N-token slice per "
+                          "GPU, partials all-gathered and LSE-merged once per step inside the graph); us_per_layer = "
+                          "the faster; per-layer latency, max over ranks; speedup = the 1-GPU value / this",
+              "frac_per_gpu": round(decode_bytes(workloads.CFG5_CTX) / world / (best * 1e-3 / LAYERS) / 1e9
                                     / hbm, 4)}
     cfg5 = None
     if world == 1:
@@ -1035,29 +1083,32 @@ def run_ours(args, rank, local, world, dist):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic: seeded N(0,1) K/V and queries",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "n": n_job, "batch": 1,
-                   "kv_heads_per_gpu": hl,
+                   "tokens_per_gpu": N_CTX,
                    "l2": f"inputs larger than L2 (36 distinct {rank_bytes / 1e6:.0f} MB layers per GPU = "
                          f"{LAYERS * rank_bytes / 1e9:.1f} GB per step)",
-                   "parallelism": f"head-sharded over {world} GPU(s): {hl} KV head(s) of the {n_job}-token sequence "
-                                  f"per GPU" + (", each step's outputs all-gathered to every rank (NCCL, in the "
-                                               "graph)" if world > 1 else ""),
+                   "parallelism": f"sequence-sharded over {world} GPU(s): each GPU holds all 8 KV heads of its own "
+                                  f"{N_CTX}-token slice of the {n_job}-token sequence" +
+                                  (" and computes each layer's fp32 partial + LSE; the step ends with the combine "
+                                   "(NCCL all-gather of the 36 layers' partials and one LSE-merge launch, "
+                                   "tc_merge_partials, inside the graph)" if world > 1 else ""),
                    "value": "us per layer of the job / world = us per layer per 16k tokens of context (at 1 GPU: "
-                            "the 16k decode; at 8: the 128k sequence with one KV head per GPU)",
+                            "the 16k decode; at 8: the 128k sequence, 16k tokens per GPU)",
                    "stable_rows": "n-1: every row but the newest declared stable, as in a decode step "
                                   "(tc_decode_attention_stable); see no_stable_rows for the plain entry point"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic if world == 1 else None,
                      "peak_kind": peak_kind, "kernel": "decode_mma_kernel<bf16,128,1>", "bytes_per_launch": rank_bytes,
-                     "per": "one GPU's launch (its heads); the job's layer time per GPU includes the combine"},
+                     "per": "one GPU's launch (its token slice); the job's layer time per GPU includes the combine"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1000.0 / (LAYERS * world), 3), "unit": "us/layer", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "api": "threadcut_b200.flash_decode.decode_attention per layer over the "
-                                                  "rank's heads" + (", torch.distributed all-gather of the step's "
-                                                                    "outputs" if world > 1 else "")},
+                "d2h_bytes_per_step": d2h,
+                "api": "threadcut_b200.flash_decode.decode_attention per layer" if world == 1 else
+                       "threadcut_b200.flash_decode.decode_attention_partial per layer over the rank's token slice, "
+                       "torch.distributed all-gathers of the step's partials, flash_decode.merge_partials"},
         "combine": None if world == 1 else {
             "us_per_layer_without": round(nocombine_ms * 1000.0 / LAYERS, 3),
             "us_per_layer_with": round(us_layer_rank, 3),
-            "what": "the step's 36 decode launches with and without the all-gather of their outputs"},
+            "what": "the step's 36 partial-decode launches with and without the combine (all-gathers + merge)"},
         "gpu_launches": args.steps * LAYERS,
         "clocks": clk.summary(),
         "shift": {"value": round(shift_gbs, 1), "unit": "GB/s", "frac": round(shift_gbs / hbm, 4),

@@ -378,6 +378,18 @@ int tc_decode_attention_partial(const void* q, const void* k, const void* v, flo
                                 float scale, int splits, int dtype,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* tc_decode_attention_partial with the stable-rows declaration of tc_decode_attention_stable (the
+ * per-rank step of a sequence-sharded decode, where every row of the rank's slice but the newest
+ * is stable). No counterpart in the reference beyond tc_decode_attention_partial's. */
+int tc_decode_attention_partial_stable(const void* q, const void* k, const void* v, float* out_f32, float* lse,
+                                       int hkv, int g, int d, int64_t n,
+                                       int64_t q_stride_h, int64_t q_stride_g,
+                                       int64_t k_stride_h, int64_t k_stride_n,
+                                       int64_t v_stride_h, int64_t v_stride_n,
+                                       int64_t out_stride_h, int64_t out_stride_g,
+                                       float scale, int splits, int dtype, int64_t stable_rows,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* Per-token layer ops of the tensor-parallel decode step (threadcut_b200/tp.py), each one launch in
  * place of a chain of torch ops of transformers' Qwen3 layer (modeling_qwen3.py; threadcut runs
  * that layer through transformers, threadcut/engine.py:66-73). Row-major contiguous tensors of

@@ -95,7 +95,9 @@ def test_paged_decode_matches_the_oracle(seed, page_rows, d, dtype, splits):
 @pytest.mark.parametrize("n", [1, 31, 32, 100, 4096, 16384])
 def test_in_order_pages_are_bit_identical_to_the_contiguous_kernel(n):
     """One append of n rows fills pages 0, 1, 2, ... in order: the paged tiles are the contiguous
-    kernel's tiles, so the split and every partial sum are the same."""
+    kernel's tiles, so with the same per-head split (the planner's one wave of SM-count / heads
+    slices per head, which the contiguous kernel runs when the split count is given) every partial
+    sum is the same."""
     g = torch.Generator(device=DEV).manual_seed(n)
     kv = PagedKV(1, 8, 128, max_tokens=n, page_rows=64, device=DEV)
     k = torch.randn(8, n, 128, generator=g, device=DEV).to(torch.bfloat16)
@@ -104,7 +106,8 @@ def test_in_order_pages_are_bit_identical_to_the_contiguous_kernel(n):
     kv.write(0, k, v)
     q = torch.randn(8, 4, 128, generator=g, device=DEV).to(torch.bfloat16)
     got = kv.decode(0, q, 0.0883)
-    want = decode_attention(q, k, v, 0.0883)
+    per_head = torch.cuda.get_device_properties(DEV).multi_processor_count // 8
+    want = decode_attention(q, k, v, 0.0883, splits=per_head)
     torch.cuda.synchronize()
     assert torch.equal(got, want), n
 

@@ -35,6 +35,8 @@ SIGNATURES = {
                                    + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_decode_attention_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                                     + [_f, _i, _i, _vp, _sz, _vp]),
+    "tc_decode_attention_partial_stable": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
+                                           + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_decode_attention_lse": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                                 + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_decode_attention_batched": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i64, _vp] + [_i64] * 12

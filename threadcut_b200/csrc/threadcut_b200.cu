@@ -154,6 +154,28 @@ DecodePlan plan_decode(int batch, int hkv, int64_t max_n, int64_t total_tokens, 
   return pl;
 }
 
+// Flat partition of a single-sequence decode (DecodeParams::flat_ctas): the CTA count for `tiles`
+// tiles over `hkv` heads, or 0 where it does not apply: fewer CTAs than heads, or more segments per
+// head than the last-arrival merge folds in one round trip. TC_DECODE_FLAT=0 turns it off.
+bool flat_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TC_DECODE_FLAT");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+int64_t flat_ctas(int hkv, int64_t max_n, int sms) {
+  if (!flat_enabled() || max_n <= 0 || hkv < 1) return 0;
+  const int64_t tt = (int64_t)hkv * cdiv(max_n, kTile);
+  const int64_t c = sms < tt ? sms : tt;
+  if (c < hkv || !last_arrival_merge((int)(cdiv(c, hkv) + 1), 32 * (kCWarps + 1))) return 0;
+  return c;
+}
+
+// Segments of one head in a flat partition of c CTAs (the workspace's partial slots per head).
+int64_t flat_max_segments(int hkv, int64_t c) { return cdiv(c, hkv) + 1; }
+
 struct WsLayout {
   size_t counters = 0, ml = 0, o = 0, total = 0;
 };
@@ -201,29 +223,17 @@ cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st,
   return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
-// CTAs of the tensor-core decode kernel resident per SM (1: a 12-stage ring per CTA; 2: 6 stages,
-// so that the next launch's CTAs can load beside this one's), from TC_DECODE_RESIDENT (default 1).
-int decode_resident() {
-  static const int r = [] {
-    const char* e = std::getenv("TC_DECODE_RESIDENT");
-    return (e != nullptr && e[0] == '2') ? 2 : 1;
-  }();
-  return r;
-}
-
-template <typename T, int D, int NG, int RES>
-cudaError_t launch_mma_res(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
-  auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true, RES> : decode_mma_kernel<T, D, NG, false, RES>;
-  const int smem = MmaGeom<D, RES>::kSmem;
-  const int threads = 32 * (kCWarps + 1);
-  cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
-  if (e != cudaSuccess) return e;
-  return launch_ex(fn, grid, dim3(threads), smem, st, p);
-}
-
 template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
-  if (D == 128 && NG == 1 && decode_resident() == 2) return launch_mma_res<T, 128, 1, 2>(p, grid, st, dev);
+  if constexpr (NG == 1 && D <= 128) {
+    if (p.flat_ctas > 0) {  // one sequence, tiles of all heads cut evenly over the CTAs
+      auto fn = decode_mma_kernel<T, D, 1, false, true>;
+      const int smem = MmaGeom<D>::kFlatSmem;
+      cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+      if (e != cudaSuccess) return e;
+      return launch_ex(fn, grid, dim3(32 * (kCWarps + 1)), smem, st, p);
+    }
+  }
   auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true> : decode_mma_kernel<T, D, NG, false>;
   const int smem = MmaGeom<D>::kSmem;
   const int threads = 32 * (kCWarps + 1);
@@ -294,8 +304,17 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
     p.k_app = p.v_app = nullptr;
   }
   const int dev = current_device();
-  const DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
-                                    use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
+  DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
+                              use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
+  // one sequence of uniform length in contiguous rows on the tensor-core kernel, planner's choice of
+  // the partition: the flat partition (all heads' tiles cut evenly over one CTA per SM)
+  const bool flat_ok = use_mma && splits_req == 0 && !ragged && p.batch == 1 && p.lengths == nullptr &&
+                       p.k_ptrs == nullptr && p.tiles == nullptr && (d == 64 || d == 128) && p.g <= 8;
+  const int64_t fc = flat_ok ? flat_ctas(p.hkv, max_n, sm_count(dev)) : 0;
+  if (fc > 0) {
+    pl.tps = cdiv(max_n, kTile);  // one "split" per head: the kernel's per-head split count is 1
+    pl.max_splits = flat_max_segments(p.hkv, fc);
+  }
   const WsLayout w = decode_ws_layout(p.batch, p.hkv, p.g, d, pl.max_splits);
   if (ws == nullptr || ws_bytes < w.total) return TC_ERR_WORKSPACE;
   uint8_t* wb = static_cast<uint8_t*>(ws);
@@ -305,7 +324,10 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
   p.tiles_per_split = (int)pl.tps;
   p.max_splits = (int)pl.max_splits;
   p.c = scale * kLog2e;
-  const dim3 grid((unsigned)pl.max_splits, (unsigned)p.hkv, (unsigned)p.batch);
+  p.flat_ctas = (int)fc;
+  p.tiles_per_head = fc > 0 ? cdiv(max_n, kTile) : 0;
+  const dim3 grid(fc > 0 ? (unsigned)fc : (unsigned)pl.max_splits, fc > 0 ? 1u : (unsigned)p.hkv,
+                  (unsigned)p.batch);
   cudaError_t e;
   if (use_mma) {
     e = dtype == TC_BF16 ? dispatch_mma<__nv_bfloat16>(p, d, grid, st, dev) : dispatch_mma<__half>(p, d, grid, st, dev);
@@ -504,6 +526,8 @@ size_t tc_decode_attention_workspace_size(int batch, int hkv, int g, int d, int6
       const DecodePlan pl = plan_decode(batch, hkv, max_n, total_tokens, ragged != 0, splits, cps, sms);
       if (pl.max_splits > ms) ms = pl.max_splits;
     }
+  const int64_t fc = flat_ctas(hkv, max_n, sms);  // the flat partition's segments per head
+  if (fc > 0 && flat_max_segments(hkv, fc) > ms) ms = flat_max_segments(hkv, fc);
   return decode_ws_layout(batch, hkv, g, d, ms).total;
 }
 
@@ -615,6 +639,18 @@ int tc_decode_attention_partial(const void* q, const void* k, const void* v, flo
   return decode_single(q, k, v, out_f32, lse, true, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
                        v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
                        workspace_bytes, stream);
+}
+
+int tc_decode_attention_partial_stable(const void* q, const void* k, const void* v, float* out_f32, float* lse,
+                                       int hkv, int g, int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g,
+                                       int64_t k_stride_h, int64_t k_stride_n, int64_t v_stride_h,
+                                       int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g, float scale,
+                                       int splits, int dtype, int64_t stable_rows, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  if (lse == nullptr) return TC_ERR_INVALID;
+  return decode_single(q, k, v, out_f32, lse, true, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream, stable_rows);
 }
 
 int tc_decode_attention_batched(const void* q, const void* k, const void* v, void* out, int batch, int hkv, int g,

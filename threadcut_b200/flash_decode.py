@@ -80,6 +80,11 @@ def _decode(q, k, v, scale, splits, want_lse, partial=False, stable_rows=0):
                 k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(0), out.stride(1), float(scale), s,
                 code, int(stable_rows), ws.data_ptr(), ws.numel(), stream)
         fn = L.tc_decode_attention_stable
+    elif stable_rows and partial:
+        args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(), hkv, g, d, n, q.stride(0),
+                q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1), out.stride(0), out.stride(1),
+                float(scale), s, code, int(stable_rows), ws.data_ptr(), ws.numel(), stream)
+        fn = L.tc_decode_attention_partial_stable
     else:
         args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr() if want_lse else None,
                 hkv, g, d, n, q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
@@ -155,10 +160,13 @@ def decode_attention_lse(q, k, v, scale, *, splits=None):
     return _decode(q, k, v, scale, splits, True)
 
 
-def decode_attention_partial(q, k, v, scale, *, splits=None):
+def decode_attention_partial(q, k, v, scale, *, splits=None, stable_rows=0):
     """Partial result of a KV slice for sequence-sharded decode: (o fp32 [hkv, g, d], natural-log
-    lse fp32 [hkv, g]). Partials of disjoint token ranges merge exactly with merge_partials."""
-    return _decode(q, k, v, scale, splits, True, partial=True)
+    lse fp32 [hkv, g]). Partials of disjoint token ranges merge exactly with merge_partials.
+    `stable_rows` as for decode_attention."""
+    if stable_rows < 0:
+        raise ValueError("decode_attention_partial: stable_rows must be >= 0")
+    return _decode(q, k, v, scale, splits, True, partial=True, stable_rows=stable_rows)
 
 
 def decode_attention_batched(q, k, v, scale, lengths=None, *, splits=None):
