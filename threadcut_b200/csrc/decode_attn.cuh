@@ -489,8 +489,12 @@ struct MmaGeom {
   static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
   static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
-  // flat mode adds one combine region per consumer warp (its state for the CTA's first head)
-  static constexpr int kFlatSmem = kSmem + kCWarps * Region<D, 8>::kFloats * 4;
+  // flat mode adds one combine region per consumer warp (its state for the CTA's first head); the
+  // same area is the merge scratch of that head, so it is at least merge_scratch_bytes large
+  static constexpr int kFlatRegionBytes = kCWarps * Region<D, 8>::kFloats * 4 > merge_scratch_bytes(32 * (kCWarps + 1))
+                                              ? kCWarps * Region<D, 8>::kFloats * 4
+                                              : merge_scratch_bytes(32 * (kCWarps + 1));
+  static constexpr int kFlatSmem = kSmem + kFlatRegionBytes;
 };
 
 // Byte offset of element (row, col) of a staged tile: 64-column boxes of 32 rows x 128 bytes, each
@@ -511,6 +515,9 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     decode_mma_kernel(const __grid_constant__ DecodeParams p) {
   static_assert(!(kPaged && kFlat), "flat mode is for contiguous rows");
   using G = MmaGeom<D>;
+  static_assert(!kFlat || (NG == 1 && G::kFlatRegionBytes >= kCWarps * Region<D, 8>::kFloats * 4 &&
+                           G::kFlatRegionBytes >= merge_scratch_bytes(32 * (kCWarps + 1))),
+                "flat mode: the first head's regions and its merge scratch must fit the extra area");
   constexpr int HP = 8 * NG;
   constexpr int KS = D / 16;
   constexpr int NBOX = D / 64;
