@@ -20,7 +20,7 @@
  *                             step (no reference code): decode over pages (flash_decode.py:57-69 semantics),
  *                             splice as page drop + in-place key rotation (kv.py:28-41,83-92 semantics),
  *                             append into page slots (kv.py:64-77 GrowingLayer.update semantics)
- *   tc_add_rmsnorm, tc_qk_norm_rope, tc_silu_mul, tc_gemv
+ *   tc_add_rmsnorm, tc_qk_norm_rope, tc_silu_mul, tc_gemv, tc_gemv_swiglu
  *                             threadcut/engine.py:66-73         the per-token model call, run by
  *                             transformers' Qwen3 layer (RMSNorm, q/k norm + RoPE, SwiGLU) there; here
  *                             one launch each in the tensor-parallel decode step
@@ -412,6 +412,11 @@ int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight
  * dtypes, k a multiple of 8 and at most 24576, x and w 16-byte aligned (else TC_ERR_ALIGN). */
 int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream);
 
+/* tc_gemv_swiglu: tc_gemv of x = dtype(dtype(silu(gate)) * up) computed from gate_up [2k] (gate and
+ * up side by side: the fused gate/up projection's output), i.e. tc_silu_mul followed by tc_gemv in
+ * one launch (Qwen3MLP's down_proj(act_fn(gate_proj(x)) * up_proj(x))), bit-identical to the two. */
+int tc_gemv_swiglu(const void* gate_up, const void* w, void* out, int64_t n, int k, int dtype, void* stream);
+
 /* tc_silu_mul: out[r][i] = dtype(silu(gate_up[r][i])) * gate_up[r][inter + i] for `rows` rows
  * (Qwen3MLP: act_fn(gate_proj(x)) * up_proj(x), gate and up side by side in one row). */
 int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream);
@@ -445,6 +450,9 @@ size_t tc_allreduce_region_bytes(int world, int64_t rows);
  * Every rank ends with the same bits in h and out. */
 int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
                       int dtype, void* stream);
+/* tc_gemv_allreduce of the SwiGLU activation of gate_up [2k], as tc_gemv_swiglu. */
+int tc_gemv_allreduce_swiglu(const void* gate_up, const void* w, int64_t n, int k, void* const* regions, int world,
+                             int rank, int dtype, void* stream);
 int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
                              int world, int dtype, void* stream);
 

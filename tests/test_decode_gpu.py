@@ -430,38 +430,38 @@ def test_growing_layer_fused_append_through_the_plugin():
 
 
 
-# ---- the flat partition: one sequence's tiles of all heads cut evenly over one CTA per SM, a CTA
-# ending one head and starting the next, each head merged over the CTAs that touched it
+# ---- more head counts and lengths: the planner's split of every head against a forced split and
+# the oracle, and the LSE entry point's output equal to the plain one
 @pytest.mark.parametrize("hkv,g,d,n", [(8, 4, 128, 1), (8, 4, 128, 33), (8, 4, 128, 100), (8, 4, 128, 4097),
                                        (8, 4, 128, 16391), (12, 2, 64, 777), (16, 8, 128, 5000), (32, 1, 64, 9000),
                                        (8, 3, 128, 2048), (10, 4, 128, 70000)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_flat_partition_against_oracle_and_split_partition(hkv, g, d, n, dtype):
+def test_head_counts_against_oracle_and_forced_split(hkv, g, d, n, dtype):
     gen = torch.Generator(device=DEV).manual_seed(hkv * 1000 + n)
     q = torch.randn(hkv, g, d, generator=gen, device=DEV).to(dtype)
     cap = n + 17  # GrowingLayer-style views: head stride past the view
     kb = torch.randn(hkv, cap, d, generator=gen, device=DEV).to(dtype)
     vb = torch.randn(hkv, cap, d, generator=gen, device=DEV).to(dtype)
     k, v = kb[:, :n], vb[:, :n]
-    flat = decode_attention(q, k, v, 0.09)
+    planned = decode_attention(q, k, v, 0.09)
     split = decode_attention(q, k, v, 0.09, splits=7)
     ref = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), 0.09)
     torch.cuda.synchronize()
-    assert attn_error(flat.float().cpu().numpy(), ref, dtype) <= ATTN_ATOL, (hkv, n)
+    assert attn_error(planned.float().cpu().numpy(), ref, dtype) <= ATTN_ATOL, (hkv, n)
     assert attn_error(split.float().cpu().numpy(), ref, dtype) <= ATTN_ATOL, (hkv, n)
     o, lse = decode_attention_lse(q, k, v, 0.09)
     _, rl = decode_attention_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), 0.09,
                                  return_lse=True)
     assert np.abs(lse.cpu().numpy() - rl).max() <= 1e-4
-    assert torch.equal(o, flat)
+    assert torch.equal(o, planned)
     assert _lib.device_errors(clear=True) == 0
 
 
 @pytest.mark.parametrize("n", [1, 32, 33, 2049, 16384])
-def test_flat_partition_fused_append_and_partial(n):
-    """Fused append and the fp32 partial (sequence shard) on the flat partition: the appended row
-    lands in the cache of every head and the result equals copy-then-decode bit for bit; the partial
-    and its LSE match the oracle."""
+def test_fused_append_and_stable_partial(n):
+    """Fused append over 8 heads: the appended row lands in the cache of every head and the result
+    equals copy-then-decode bit for bit; the fp32 partial of a sequence shard with stable rows
+    declared (tc_decode_attention_partial_stable) and its LSE match the oracle."""
     gen = torch.Generator(device=DEV).manual_seed(n + 5)
     q = torch.randn(8, 4, 128, generator=gen, device=DEV).to(torch.bfloat16)
     kb = torch.randn(8, n + 40, 128, generator=gen, device=DEV).to(torch.bfloat16)

@@ -102,3 +102,21 @@ def test_gemv_matches_the_library_projection(n, k, dtype):
     torch.testing.assert_close(got.float(), want.float(), rtol=2 ** -6, atol=1e-3)
     torch.testing.assert_close(got.float(), exact, rtol=2 ** -7, atol=1e-3)
     assert float((got == want).float().mean()) >= 0.8
+
+
+@pytest.mark.parametrize("n,k,dtype", [(2560, 9728, torch.bfloat16), (2560, 1216, torch.bfloat16),
+                                       (300, 64, torch.float16)])
+def test_gemv_swiglu_equals_silu_mul_then_gemv(n, k, dtype):
+    """tc_gemv_swiglu computes the SwiGLU activation while staging its input: the same bits as
+    tc_silu_mul followed by tc_gemv (same rounding of the activation, same accumulation order)."""
+    g = torch.Generator(device=DEV).manual_seed(n * 7 + k)
+    gu = (torch.randn(1, 2 * k, generator=g, device=DEV) * 2).to(dtype)
+    w = (torch.randn(n, k, generator=g, device=DEV) * k ** -0.5).to(dtype)
+    act = gu.new_empty((1, k))
+    tp._silu_mul(gu, act)
+    want = tp._gemv(act, w)
+    got = tp._gemv_swiglu(gu, w)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    ref = (F.silu(gu[:, :k].float()).to(dtype).float() * gu[:, k:].float()).to(dtype).float() @ w.float().t()
+    torch.testing.assert_close(got.float(), ref, rtol=2 ** -7, atol=1e-3)

@@ -2,7 +2,7 @@
 vocabulary-sliced argmax, and the local-head cache, on one rank and on two `gloo` ranks.
 
 The kernels need a GPU, so these tests replace the launches of the step (`tp._attend`: append +
-attention; `_add_rmsnorm`, `_qk_norm_rope`, `_silu_mul`, `_gemv`) with torch restatements of HF's Qwen3
+attention; `_add_rmsnorm`, `_qk_norm_rope`, `_silu_mul`, `_gemv`, `_gemv_swiglu`) with torch restatements of HF's Qwen3
 arithmetic on CPU; everything else is the product code. The expected logits
 are the HF model's own fp32 forward over the whole prompt (modeling_qwen3 with eager attention).
 The step also must not read any tensor value back to the host, so that it can be captured in a
@@ -47,6 +47,12 @@ def _cpu_ops(target):
     target(tp, "_qk_norm_rope", _cpu_qk_norm_rope)
     target(tp, "_silu_mul", _cpu_silu_mul)
     target(tp, "_gemv", lambda x, w: x @ w.t())
+    target(tp, "_gemv_swiglu", _cpu_gemv_swiglu)
+
+
+def _cpu_gemv_swiglu(gu, w):
+    i = w.shape[1]
+    return (torch.nn.functional.silu(gu[:, :i]) * gu[:, i:]) @ w.t()
 
 
 def _cpu_attend(layer, q, k, v, scale):

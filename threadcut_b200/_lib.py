@@ -62,6 +62,7 @@ SIGNATURES = {
     "tc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp]),
     "tc_silu_mul": (_i, [_vp, _vp, _i64, _i, _i, _vp]),
     "tc_gemv": (_i, [_vp, _vp, _vp, _i64, _i, _i, _vp]),
+    "tc_gemv_swiglu": (_i, [_vp, _vp, _vp, _i64, _i, _i, _vp]),
     "tc_decode_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp, _i64,
                                        _i64, _vp, _vp, _i64, _i64] + [_i64] * 4 + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_prefill_attention_paged": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i64, _i64, _i64, _i64, _i64, _vp,
@@ -78,6 +79,7 @@ SIGNATURES = {
     "tc_peer_free": (_i, [_vp]),
     "tc_allreduce_region_bytes": (_sz, [_i, _i64]),
     "tc_gemv_allreduce": (_i, [_vp, _vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _i, _vp]),
+    "tc_gemv_allreduce_swiglu": (_i, [_vp, _vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _i, _vp]),
     "tc_allreduce_add_rmsnorm": (_i, [_vp, _vp, _vp, _i, _f, _vp, _i, _i, _vp]),
 }
 

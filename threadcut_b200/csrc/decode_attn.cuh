@@ -103,17 +103,7 @@ struct DecodeParams {
   int64_t n_tiles;
   int64_t stable_tiles;  // paged: tiles [0, stable_tiles) and their rows are written by no kernel
                          // that can still be running when this one starts (0: none)
-  // flat mode (one sequence, uniform length, contiguous rows): the hkv * tiles_per_head tiles of all
-  // heads, in head-major order, are cut into flat_ctas equal ranges, one per CTA (grid.x), so a CTA
-  // may end one head and begin the next; each head is then merged over the CTAs that touched it.
-  int64_t tiles_per_head;
-  int flat_ctas;
 };
-
-// Flat mode: the CTA whose range holds flat tile x (ranges [T*c/C, T*(c+1)/C) of T tiles).
-__host__ __device__ __forceinline__ int64_t flat_cta_of(int64_t x, int64_t T, int64_t C) {
-  return ((x + 1) * C - 1) / T;
-}
 
 // Stores one output element at element offset `off` of p.out, in T or (partial mode) fp32.
 template <typename T>
@@ -489,12 +479,6 @@ struct MmaGeom {
   static_assert(kStages % kCWarps == 0, "stages must divide evenly among the consumer warps");
   static constexpr int kPipeBytes = kStages * kStageBytes;
   static constexpr int kSmem = 1024 + kPipeBytes + 2 * kStages * 8;  // + 1 KB base alignment slack
-  // flat mode adds one combine region per consumer warp (its state for the CTA's first head); the
-  // same area is the merge scratch of that head, so it is at least merge_scratch_bytes large
-  static constexpr int kFlatRegionBytes = kCWarps * Region<D, 8>::kFloats * 4 > merge_scratch_bytes(32 * (kCWarps + 1))
-                                              ? kCWarps * Region<D, 8>::kFloats * 4
-                                              : merge_scratch_bytes(32 * (kCWarps + 1));
-  static constexpr int kFlatSmem = kSmem + kFlatRegionBytes;
 };
 
 // Byte offset of element (row, col) of a staged tile: 64-column boxes of 32 rows x 128 bytes, each
@@ -510,14 +494,10 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {
 // (g <= 8*NG). K/V tiles arrive by tensor-map TMA: one cp.async.bulk.tensor per 64-column box.
 // kPaged: K/V rows come through the tile table (p.tiles); a separate instantiation, so the
 // contiguous kernel carries none of it.
-template <typename T, int D, int NG, bool kPaged, bool kFlat = false>
+template <typename T, int D, int NG, bool kPaged>
 __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     decode_mma_kernel(const __grid_constant__ DecodeParams p) {
-  static_assert(!(kPaged && kFlat), "flat mode is for contiguous rows");
   using G = MmaGeom<D>;
-  static_assert(!kFlat || (NG == 1 && G::kFlatRegionBytes >= kCWarps * Region<D, 8>::kFloats * 4 &&
-                           G::kFlatRegionBytes >= merge_scratch_bytes(32 * (kCWarps + 1))),
-                "flat mode: the first head's regions and its merge scratch must fit the extra area");
   constexpr int HP = 8 * NG;
   constexpr int KS = D / 16;
   constexpr int NBOX = D / 64;
@@ -531,26 +511,9 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   uint64_t* empty = full + kStages;
   __shared__ int s_mi;  // merger index of this CTA (-1: not a merger)
   __shared__ int4 s_tab[kPaged ? kTabTiles : 1];  // paged: this CTA's first kTabTiles table entries
-  // flat mode: each consumer warp's state for the CTA's first head, after the pipeline's barriers
-  float* regs_a = reinterpret_cast<float*>(empty + kStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  // flat mode: flat tiles [f0, f1) of this CTA; tiles j < jb belong to head ha, the rest to hb
-  int64_t f0 = 0, f1 = 0, tph = 1;
-  int ha = h, hb = h, jb = 0x7fffffff;
-  if constexpr (kFlat) {
-    tph = p.tiles_per_head;
-    const int64_t tt = (int64_t)p.hkv * tph;
-    f0 = tt * blockIdx.x / p.flat_ctas;
-    f1 = tt * (blockIdx.x + 1) / p.flat_ctas;
-    ha = (int)(f0 / tph);
-    hb = (int)((f1 - 1) / tph);
-    jb = (int)((int64_t)(ha + 1) * tph - f0);
-  }
-  // head and first token of tile j of this CTA in flat mode
-  auto flat_head = [&](int j) { return j < jb ? ha : hb; };
-  auto flat_tok = [&](int j) { return (int)((f0 + j - (int64_t)flat_head(j) * tph) * kTile); };
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
@@ -561,35 +524,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   }
   __syncthreads();  // barriers initialised before the producer may arm them below
   int staged = 0;   // producer lane: leading tiles already issued before pdl_wait()
-  if (kFlat && warp == kCWarps && lane == 0) {
-    // as below for the flat partition: stable tiles are loaded, the rest of the first pipeline
-    // depth is prefetched into L2
-    prefetch_tensormap(&p.tmk);
-    prefetch_tensormap(&p.tmv);
-    const int64_t pre = f1 - f0 < kStages ? f1 - f0 : kStages;
-    if (p.stable_rows > 0) {
-      const uint64_t pol = policy_evict_first();
-      while (staged < pre && flat_tok(staged) + kTile <= p.stable_rows) {
-        const int s = staged;  // round 0 of stage s: no empty wait
-        mbar_arrive_expect_tx(&full[s], (uint32_t)G::kStageBytes);
-        uint8_t* st = smem + s * G::kStageBytes;
-        const int tok = flat_tok(staged), hh = flat_head(staged);
-#pragma unroll
-        for (int bx = 0; bx < NBOX; ++bx) {
-          tma_load_4d(st + bx * G::kBoxBytes, &p.tmk, bx * 64, tok, hh, 0, &full[s], pol);
-          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, &p.tmv, bx * 64, tok, hh, 0, &full[s], pol);
-        }
-        ++staged;
-      }
-    }
-    for (int j = staged; j < pre; ++j)
-#pragma unroll
-      for (int bx = 0; bx < NBOX; ++bx) {
-        tma_prefetch_4d(&p.tmk, bx * 64, flat_tok(j), flat_head(j), 0);
-        tma_prefetch_4d(&p.tmv, bx * 64, flat_tok(j), flat_head(j), 0);
-      }
-  }
-  if (!kPaged && !kFlat && warp == kCWarps && lane == 0) {
+  if (!kPaged && warp == kCWarps && lane == 0) {
     // Before waiting for the previous kernel (it may still be running):
     //  * tiles whose rows the caller declared stable (p.stable_rows, uniform lengths, where n and
     //    the partition come from kernel parameters) are loaded into the pipeline right away;
@@ -655,12 +590,12 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   const int64_t n = p.lengths ? (int64_t)p.lengths[b] : p.n;
   const int64_t seq_tiles = kPaged ? p.n_tiles : (n + kTile - 1) / kTile;
   const int nsplit = (kPaged ? seq_tiles > 0 : n > 0) ? (int)((seq_tiles + p.tiles_per_split - 1) / p.tiles_per_split) : 1;
-  if (!kFlat && split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
-  int64_t tt0 = 0, tt1 = 0;
-  if (!kFlat) split_range(seq_tiles, split, nsplit, tt0, tt1);
+  if (split >= nsplit) return;  // whole CTA leaves together; the barriers are never used
+  int64_t tt0, tt1;
+  split_range(seq_tiles, split, nsplit, tt0, tt1);
   const int64_t t0 = tt0 * kTile;
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
-  const int ntiles = kFlat ? (int)(f1 - f0) : (int)(tt1 - tt0);
+  const int ntiles = (int)(tt1 - tt0);
   if (threadIdx.x == 0) s_mi = -1;
   if constexpr (kPaged) {
     // the slice's table entries, loaded once by the whole CTA instead of a dependent global load
@@ -682,7 +617,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   if (warp == kCWarps) {
     // the start ticket (which CTA merges) is taken by an idle producer lane, off the pipeline's path;
     // the result is read only after the final __syncthreads
-    if (!kFlat && lane == 1 && nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x))
+    if (lane == 1 && nsplit > 1 && !last_arrival_merge(nsplit, blockDim.x))
       s_mi = merger_index(p, b, h, nsplit, p.g * (D / 4));
     // ---------------- producer: one elected lane issues 2*D/64 tensor copies per tile
     if (lane == 0 && ntiles > 0) {
@@ -697,20 +632,16 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         mbar_arrive_expect_tx(&full[s], (uint32_t)G::kStageBytes);
         uint8_t* st = smem + s * G::kStageBytes;
         // rows past the tensor end (or, paged, past the page end) arrive as zeros
-        int tok = (int)(t0 + (int64_t)j * kTile), cbj = cb, hh = h;
+        int tok = (int)(t0 + (int64_t)j * kTile), cbj = cb;
         if constexpr (kPaged) {
           const int4 te = tab_entry(j);
           cbj = te.x;
           tok = te.y;
         }
-        if constexpr (kFlat) {
-          tok = flat_tok(j);
-          hh = flat_head(j);
-        }
 #pragma unroll
         for (int bx = 0; bx < NBOX; ++bx) {
-          tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, hh, cbj, &full[s], pol);
-          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, hh, cbj, &full[s], pol);
+          tma_load_4d(st + bx * G::kBoxBytes, mk, bx * 64, tok, h, cbj, &full[s], pol);
+          tma_load_4d(st + G::kTileBytes + bx * G::kBoxBytes, mv, bx * 64, tok, h, cbj, &full[s], pol);
         }
       }
     }
@@ -718,9 +649,9 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     // ---------------- consumers
     const int gid = lane >> 2, qd = lane & 3;
     const float c = p.c;
-    // q^T fragments of KV head `hh`: the g query rows of the head (zero-padded to 8 * NG columns)
-    auto load_q = [&](int hh, uint32_t (&dst)[NG][KS][2]) {
-      const T* qb = static_cast<const T*>(p.q) + b * p.sq_b + hh * p.sq_h;
+    uint32_t bq[NG][KS][2];
+    {
+      const T* qb = static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h;
       const T zero = from_f32<T>(0.f);
 #pragma unroll
       for (int nt = 0; nt < NG; ++nt) {
@@ -730,100 +661,39 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           const int d0 = ks * 16 + 2 * qd;
-          dst[nt][ks][0] = pack_raw<T>(ok ? qr[d0] : zero, ok ? qr[d0 + 1] : zero);
-          dst[nt][ks][1] = pack_raw<T>(ok ? qr[d0 + 8] : zero, ok ? qr[d0 + 9] : zero);
+          bq[nt][ks][0] = pack_raw<T>(ok ? qr[d0] : zero, ok ? qr[d0 + 1] : zero);
+          bq[nt][ks][1] = pack_raw<T>(ok ? qr[d0 + 8] : zero, ok ? qr[d0 + 9] : zero);
         }
       }
-    };
-    uint32_t bq[NG][KS][2];
-    uint32_t bq2[kFlat ? NG : 1][kFlat ? KS : 1][2];  // flat mode: the second head's fragments
-    load_q(ha, bq);
-    if constexpr (kFlat) {
-      if (hb != ha) load_q(hb, bq2);
     }
     float m_run[NG][2], l_run[NG][2];
     float oacc[KS][NG][4];
-    auto reset_state = [&]() {
 #pragma unroll
-      for (int nt = 0; nt < NG; ++nt)
+    for (int nt = 0; nt < NG; ++nt)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          m_run[nt][e] = -INFINITY;
-          l_run[nt][e] = 0.f;
-        }
-#pragma unroll
-      for (int md = 0; md < KS; ++md)
-#pragma unroll
-        for (int nt = 0; nt < NG; ++nt)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) oacc[md][nt][r] = 0.f;
-    };
-    using R = Region<D, HP>;
-    // this warp's (m, l, o) -> a combine region in shared memory (l summed over the token lanes)
-    auto write_state = [&](float* reg) {
-#pragma unroll
-      for (int nt = 0; nt < NG; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float l = l_run[nt][e];
-          l += __shfl_xor_sync(0xffffffffu, l, 4);
-          l += __shfl_xor_sync(0xffffffffu, l, 8);
-          l += __shfl_xor_sync(0xffffffffu, l, 16);
-          l_run[nt][e] = l;
-        }
-      if (gid == 0) {
-#pragma unroll
-        for (int nt = 0; nt < NG; ++nt)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int i = nt * 8 + 2 * qd + e;
-            R::m(reg)[i] = m_run[nt][e];
-            R::l(reg)[i] = l_run[nt][e];
-          }
+      for (int e = 0; e < 2; ++e) {
+        m_run[nt][e] = -INFINITY;
+        l_run[nt][e] = 0.f;
       }
 #pragma unroll
-      for (int md = 0; md < KS; ++md)
+    for (int md = 0; md < KS; ++md)
 #pragma unroll
-        for (int nt = 0; nt < NG; ++nt)
+      for (int nt = 0; nt < NG; ++nt)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int dim = md * 16 + gid + (r >> 1) * 8;
-            const int i = nt * 8 + 2 * qd + (r & 1);
-            R::acc(reg, i)[dim] = oacc[md][nt][r];
-          }
-    };
-    reset_state();
-    int cur = 0;  // flat mode: 0 while this warp's tiles belong to head ha, 1 after
+        for (int r = 0; r < 4; ++r) oacc[md][nt][r] = 0.f;
 
     for (int j = warp; j < ntiles; j += kCWarps) {
-      if constexpr (kFlat) {
-        if (cur == 0 && j >= jb) {
-          // first tile of the next head: park this head's state, start the next one's
-          write_state(regs_a + warp * R::kFloats);
-          reset_state();
-#pragma unroll
-          for (int nt = 0; nt < NG; ++nt)
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-              bq[nt][ks][0] = bq2[nt][ks][0];
-              bq[nt][ks][1] = bq2[nt][ks][1];
-            }
-          cur = 1;
-        }
-      }
       const int s = j % kStages;
       if (!mbar_wait(&full[s], (j / kStages) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
       uint8_t* stage = smem + s * G::kStageBytes;
       const uint32_t kst = smem_u32(stage);
       const uint32_t vst = kst + G::kTileBytes;
-      const int hh = kFlat ? flat_head(j) : h;  // KV head of this tile
-      const int64_t tok0 = kFlat ? (int64_t)flat_tok(j) : t0 + (int64_t)j * kTile;  // its first row
       int valid;
       if constexpr (kPaged) {
         const int vt = tab_entry(j).z;  // device table: clamp into [0, kTile]
         valid = vt < 0 ? 0 : (vt > kTile ? kTile : vt);
       } else {
-        const int64_t rem = (kFlat ? n : t1) - tok0;
+        const int64_t rem = t1 - (t0 + (int64_t)j * kTile);
         valid = rem < kTile ? (int)rem : kTile;
       }
       int64_t app_r = -1, app_row = n - 1, app_pg = 0;  // row in the tile, row and page in the cache
@@ -836,7 +706,7 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
             app_row = te.y + app_r;
           }
         } else {
-          app_r = (n - 1) - tok0;
+          app_r = (n - 1) - (t0 + (int64_t)j * kTile);
         }
       }
       const bool patch = app_r >= 0 && app_r < kTile;
@@ -845,11 +715,11 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         // k_app/v_app (16-byte chunks into the swizzled row) and write the row to the cache
         const int r = (int)app_r;
         constexpr int CH = D / 8;  // 16-byte chunks per row
-        const uint4* ka = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + hh * p.sa_k);
-        const uint4* va = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_app) + hh * p.sa_v);
-        uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + app_pg * p.sk_b + hh * p.sk_h +
+        const uint4* ka = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + h * p.sa_k);
+        const uint4* va = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_app) + h * p.sa_v);
+        uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + app_pg * p.sk_b + h * p.sk_h +
                                              app_row * p.sk_n);
-        uint4* vc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + app_pg * p.sv_b + hh * p.sv_h +
+        uint4* vc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.v)) + app_pg * p.sv_b + h * p.sv_h +
                                              app_row * p.sv_n);
         for (int idx = lane; idx < 2 * CH; idx += 32) {
           const bool isv = idx >= CH;
@@ -970,33 +840,42 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
       if (lane == 0) mbar_arrive(&empty[s]);
     }
 
-    // this warp's state -> its own (now idle) stage buffer; flat mode: the first head's state to
-    // regs_a, the second head's (empty if the warp had none of its tiles) to the stage buffer
+    // this warp's state -> its own (now idle) stage buffer
+#pragma unroll
+    for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float l = l_run[nt][e];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_run[nt][e] = l;
+      }
+    using R = Region<D, HP>;
     float* reg = reinterpret_cast<float*>(smem + warp * G::kStageBytes);
-    if (kFlat && cur == 0) {
-      write_state(regs_a + warp * R::kFloats);
-      reset_state();
+    if (gid == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int i = nt * 8 + 2 * qd + e;
+          R::m(reg)[i] = m_run[nt][e];
+          R::l(reg)[i] = l_run[nt][e];
+        }
     }
-    write_state(reg);
+#pragma unroll
+    for (int md = 0; md < KS; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NG; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int dim = md * 16 + gid + (r >> 1) * 8;
+          const int i = nt * 8 + 2 * qd + (r & 1);
+          R::acc(reg, i)[dim] = oacc[md][nt][r];
+        }
   }
   __syncthreads();
-  if constexpr (kFlat) {
-    // each head this CTA touched is finished over the CTAs whose ranges cover it (segments), the
-    // last of them to publish merging it (at most ceil(flat_ctas / hkv) + 1 segments: the host
-    // keeps that within the last-arrival limit)
-    const int64_t tt = (int64_t)p.hkv * tph, cc = p.flat_ctas;
-    const int64_t a_first = flat_cta_of((int64_t)ha * tph, tt, cc);
-    const int nseg_a = (int)(flat_cta_of((int64_t)(ha + 1) * tph - 1, tt, cc) - a_first + 1);
-    finish_cta<T, D, HP>(p, reinterpret_cast<uint8_t*>(regs_a), Region<D, HP>::kFloats * 4, kCWarps, b, ha,
-                         (int)(blockIdx.x - a_first), nseg_a, -1);
-    if (hb != ha) {
-      __syncthreads();
-      const int nseg_b = (int)(flat_cta_of((int64_t)(hb + 1) * tph - 1, tt, cc) - blockIdx.x + 1);
-      finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, b, hb, 0, nseg_b, -1);
-    }
-  } else {
-    finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, b, h, split, nsplit, s_mi);
-  }
+  finish_cta<T, D, HP>(p, smem, G::kStageBytes, kCWarps, b, h, split, nsplit, s_mi);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(T* __restrict
                                                                    const T* __restrict__ w, T* __restrict__ x,
                                                                    int H, float inv_h, float eps) {
   __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
   const int64_t off = (int64_t)blockIdx.x * H;
   float ss = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -64,6 +66,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_vec_kernel(T* __rest
                                                                        const T* __restrict__ w, T* __restrict__ x,
                                                                        int H, float inv_h, float eps) {
   __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
   const int64_t off = (int64_t)blockIdx.x * (H / 8);
   uint4* hr = reinterpret_cast<uint4*>(h) + off;
   const uint4* dr = delta != nullptr ? reinterpret_cast<const uint4*>(delta) + off : nullptr;
@@ -127,14 +131,56 @@ __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc, __half*
   return fmaf(fa.y, fb.y, fmaf(fa.x, fb.x, acc));
 }
 
-template <typename T>
+// L2 prefetch of weight rows (the constant operand of a GEMV) before the wait for the previous
+// kernel: rows row0, row0 + stride, ... below N, one bulk prefetch of K * 2 bytes per row, issued by
+// lane 0 of the calling warp. K * 2 is a multiple of 16 and the rows are 16-byte aligned.
+__device__ __forceinline__ void prefetch_rows_l2(const void* w, int64_t row0, int64_t stride, int64_t N, int K) {
+  if ((threadIdx.x & 31) != 0) return;
+  for (int64_t row = row0; row < N; row += stride) {
+    const char* r = static_cast<const char*>(w) + row * (int64_t)K * 2;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r), "r"((uint32_t)K * 2) : "memory");
+  }
+}
+
+// The GEMV's x staged in shared memory as K/8 16-byte chunks. kSwiGLU: x is Qwen3MLP's activation
+// computed on the fly from gate|up [2K] (the fused gate/up projection's output): chunk i holds
+// T(T(silu(gate)) * up) for its 8 elements, exactly silu_mul_kernel's rounding.
+template <typename T, bool kSwiGLU>
+__device__ __forceinline__ void stage_x(uint4* xs, const T* __restrict__ x, int K) {
+  const int kc = K / 8;
+  for (int i = threadIdx.x; i < kc; i += blockDim.x) {
+    if constexpr (kSwiGLU) {
+      const uint4 gv = reinterpret_cast<const uint4*>(x)[i];
+      const uint4 uv = reinterpret_cast<const uint4*>(x + K)[i];
+      const T* ge = reinterpret_cast<const T*>(&gv);
+      const T* ue = reinterpret_cast<const T*>(&uv);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float g = to_f32(ge[t]);
+        const float act = to_f32(from_f32<T>(g / (1.0f + expf(-g))));
+        oe[t] = from_f32<T>(act * to_f32(ue[t]));
+      }
+      xs[i] = o;
+    } else {
+      xs[i] = reinterpret_cast<const uint4*>(x)[i];
+    }
+  }
+}
+
+template <typename T, bool kSwiGLU = false>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                T* __restrict__ out, int64_t N, int K) {
   extern __shared__ uint4 xs[];
   const int kc = K / 8;
-  for (int i = threadIdx.x; i < kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the weights do not depend on the previous kernel: start pulling this CTA's rows into L2 first
+  prefetch_rows_l2(w, (int64_t)blockIdx.x * kGemvWarps + warp, (int64_t)gridDim.x * kGemvWarps, N, K);
+  pdl_launch();
+  pdl_wait();
+  stage_x<T, kSwiGLU>(xs, x, K);
+  __syncthreads();
   for (int64_t row = (int64_t)blockIdx.x * kGemvWarps + warp; row < N; row += (int64_t)gridDim.x * kGemvWarps) {
     const uint4* wr = reinterpret_cast<const uint4*>(w + row * (int64_t)K);
     float acc = 0.f;
@@ -159,6 +205,8 @@ __global__ void qk_norm_rope_kernel(T* __restrict__ q, T* __restrict__ k, const 
                                     const T* __restrict__ sinv, int q_heads, int d, float inv_d, float eps) {
   __shared__ float red[32];
   extern __shared__ float z[];  // the normed head, for rotate_half
+  pdl_launch();
+  pdl_wait();
   const int head = blockIdx.x;
   const bool is_q = head < q_heads;
   T* row = is_q ? q + (int64_t)head * d : k + (int64_t)(head - q_heads) * d;
@@ -186,6 +234,8 @@ __global__ void qk_norm_rope_kernel(T* __restrict__ q, T* __restrict__ k, const 
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out,
                                                                 int64_t rows, int inter) {
+  pdl_launch();
+  pdl_wait();
   const int64_t total = rows * inter;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t rr = t / inter;

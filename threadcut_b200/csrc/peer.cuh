@@ -47,16 +47,20 @@ __device__ __forceinline__ uint64_t ld_sys_u64(const uint64_t* p) {
 
 // out rows [blockIdx.x * kArRows, +kArRows) of x [K] . w[N][K]^T, each sent to every rank as a
 // (value, epoch) word. 16-bit T, K % 8 == 0, x and w 16-byte aligned. x staged in shared memory.
-template <typename T>
+template <typename T, bool kSwiGLU = false>
 __global__ void __launch_bounds__(kArThreads) gemv_allreduce_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                    int64_t N, int K, const __grid_constant__ ArPeers ar) {
   extern __shared__ uint4 xs[];
   __shared__ float res[kArRows];
   const int kc = K / 8;
-  for (int i = threadIdx.x; i < kc; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row0 = (int64_t)blockIdx.x * kArRows;
+  // this CTA's weight rows into L2 while the previous kernel finishes; x and seq only after the wait
+  prefetch_rows_l2(w, row0 + warp, kArThreads / 32, row0 + kArRows < N ? row0 + kArRows : N, K);
+  pdl_launch();
+  pdl_wait();
+  stage_x<T, kSwiGLU>(xs, x, K);
+  __syncthreads();
   constexpr int kWarps = kArThreads / 32, kRpw = kArRows / kWarps;  // rows per warp, streamed together
   float acc[kRpw];
   const uint4* wr[kRpw];
@@ -105,6 +109,8 @@ __global__ void __launch_bounds__(kArNormThreads) allreduce_add_rmsnorm_kernel(
     T* __restrict__ h, const T* __restrict__ weight, T* __restrict__ out, int H, float inv_h, float eps,
     const uint64_t* __restrict__ mine, unsigned int* seq, int world, int64_t rows) {
   __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
   const unsigned int s = *seq;
   const uint32_t ep = s + 1u;
   const uint64_t* base = mine + (int64_t)(s % kArSlots) * world * rows;

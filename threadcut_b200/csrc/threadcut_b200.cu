@@ -154,28 +154,6 @@ DecodePlan plan_decode(int batch, int hkv, int64_t max_n, int64_t total_tokens, 
   return pl;
 }
 
-// Flat partition of a single-sequence decode (DecodeParams::flat_ctas): the CTA count for `tiles`
-// tiles over `hkv` heads, or 0 where it does not apply: fewer CTAs than heads, or more segments per
-// head than the last-arrival merge folds in one round trip. TC_DECODE_FLAT=0 turns it off.
-bool flat_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("TC_DECODE_FLAT");
-    return !(e != nullptr && e[0] == '0');
-  }();
-  return on;
-}
-
-int64_t flat_ctas(int hkv, int64_t max_n, int sms) {
-  if (!flat_enabled() || max_n <= 0 || hkv < 1) return 0;
-  const int64_t tt = (int64_t)hkv * cdiv(max_n, kTile);
-  const int64_t c = sms < tt ? sms : tt;
-  if (c < hkv || !last_arrival_merge((int)(cdiv(c, hkv) + 1), 32 * (kCWarps + 1))) return 0;
-  return c;
-}
-
-// Segments of one head in a flat partition of c CTAs (the workspace's partial slots per head).
-int64_t flat_max_segments(int hkv, int64_t c) { return cdiv(c, hkv) + 1; }
-
 struct WsLayout {
   size_t counters = 0, ml = 0, o = 0, total = 0;
 };
@@ -223,17 +201,28 @@ cudaError_t launch_ex(Kern fn, dim3 grid, dim3 block, int smem, cudaStream_t st,
   return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
+// Any kernel with programmatic dependent launch (as launch_ex), arguments passed through.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
 template <typename T, int D, int NG>
 cudaError_t launch_mma(const DecodeParams& p, dim3 grid, cudaStream_t st, int dev) {
-  if constexpr (NG == 1 && D <= 128) {
-    if (p.flat_ctas > 0) {  // one sequence, tiles of all heads cut evenly over the CTAs
-      auto fn = decode_mma_kernel<T, D, 1, false, true>;
-      const int smem = MmaGeom<D>::kFlatSmem;
-      cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
-      if (e != cudaSuccess) return e;
-      return launch_ex(fn, grid, dim3(32 * (kCWarps + 1)), smem, st, p);
-    }
-  }
   auto fn = p.tiles != nullptr ? decode_mma_kernel<T, D, NG, true> : decode_mma_kernel<T, D, NG, false>;
   const int smem = MmaGeom<D>::kSmem;
   const int threads = 32 * (kCWarps + 1);
@@ -304,17 +293,8 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
     p.k_app = p.v_app = nullptr;
   }
   const int dev = current_device();
-  DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
-                              use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
-  // one sequence of uniform length in contiguous rows on the tensor-core kernel, planner's choice of
-  // the partition: the flat partition (all heads' tiles cut evenly over one CTA per SM)
-  const bool flat_ok = use_mma && splits_req == 0 && !ragged && p.batch == 1 && p.lengths == nullptr &&
-                       p.k_ptrs == nullptr && p.tiles == nullptr && (d == 64 || d == 128) && p.g <= 8;
-  const int64_t fc = flat_ok ? flat_ctas(p.hkv, max_n, sm_count(dev)) : 0;
-  if (fc > 0) {
-    pl.tps = cdiv(max_n, kTile);  // one "split" per head: the kernel's per-head split count is 1
-    pl.max_splits = flat_max_segments(p.hkv, fc);
-  }
+  const DecodePlan pl = plan_decode(p.batch, p.hkv, max_n, total_tokens, ragged, splits_req,
+                                    use_mma ? kMmaCtasPerSm : kGenCtasPerSm, sm_count(dev));
   const WsLayout w = decode_ws_layout(p.batch, p.hkv, p.g, d, pl.max_splits);
   if (ws == nullptr || ws_bytes < w.total) return TC_ERR_WORKSPACE;
   uint8_t* wb = static_cast<uint8_t*>(ws);
@@ -324,10 +304,7 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
   p.tiles_per_split = (int)pl.tps;
   p.max_splits = (int)pl.max_splits;
   p.c = scale * kLog2e;
-  p.flat_ctas = (int)fc;
-  p.tiles_per_head = fc > 0 ? cdiv(max_n, kTile) : 0;
-  const dim3 grid(fc > 0 ? (unsigned)fc : (unsigned)pl.max_splits, fc > 0 ? 1u : (unsigned)p.hkv,
-                  (unsigned)p.batch);
+  const dim3 grid((unsigned)pl.max_splits, (unsigned)p.hkv, (unsigned)p.batch);
   cudaError_t e;
   if (use_mma) {
     e = dtype == TC_BF16 ? dispatch_mma<__nv_bfloat16>(p, d, grid, st, dev) : dispatch_mma<__half>(p, d, grid, st, dev);
@@ -526,8 +503,6 @@ size_t tc_decode_attention_workspace_size(int batch, int hkv, int g, int d, int6
       const DecodePlan pl = plan_decode(batch, hkv, max_n, total_tokens, ragged != 0, splits, cps, sms);
       if (pl.max_splits > ms) ms = pl.max_splits;
     }
-  const int64_t fc = flat_ctas(hkv, max_n, sms);  // the flat partition's segments per head
-  if (fc > 0 && flat_max_segments(hkv, fc) > ms) ms = flat_max_segments(hkv, fc);
   return decode_ws_layout(batch, hkv, g, d, ms).total;
 }
 
@@ -1302,30 +1277,31 @@ namespace {
 template <typename T>
 int launch_layer_op_t(int op, void* a, void* b, const void* c, const void* d0, const void* e, const void* f,
                       int64_t rows, int n0, int n1, int d, float eps, cudaStream_t st) {
+  const bool vec = op == 0 && sizeof(T) == 2 && n0 % 8 == 0 && n0 / 8 <= kNormThreads * 4 &&
+                   ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                     reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d0)) & 15) == 0;
+  cudaError_t err;
   if (op == 0) {
-    const bool vec = sizeof(T) == 2 && n0 % 8 == 0 && n0 / 8 <= kNormThreads * 4 &&
-                     ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
-                       reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d0)) & 15) == 0;
     if (vec)
-      add_rmsnorm_vec_kernel<T, 4><<<(unsigned)rows, kNormThreads, 0, st>>>(
-          static_cast<T*>(a), static_cast<const T*>(c), static_cast<const T*>(d0), static_cast<T*>(b), n0,
-          1.0f / (float)n0, eps);
+      err = launch_pdl(add_rmsnorm_vec_kernel<T, 4>, dim3((unsigned)rows), dim3(kNormThreads), 0, st,
+                       static_cast<T*>(a), static_cast<const T*>(c), static_cast<const T*>(d0), static_cast<T*>(b),
+                       n0, 1.0f / (float)n0, eps);
     else
-      add_rmsnorm_kernel<T><<<(unsigned)rows, kNormThreads, 0, st>>>(static_cast<T*>(a), static_cast<const T*>(c),
-                                                                     static_cast<const T*>(d0), static_cast<T*>(b),
-                                                                     n0, 1.0f / (float)n0, eps);
+      err = launch_pdl(add_rmsnorm_kernel<T>, dim3((unsigned)rows), dim3(kNormThreads), 0, st, static_cast<T*>(a),
+                       static_cast<const T*>(c), static_cast<const T*>(d0), static_cast<T*>(b), n0,
+                       1.0f / (float)n0, eps);
   } else if (op == 1) {
     const int threads = ((d + 31) / 32) * 32;
-    qk_norm_rope_kernel<T><<<(unsigned)(n0 + n1), threads, d * sizeof(float), st>>>(
-        static_cast<T*>(a), static_cast<T*>(b), static_cast<const T*>(c), static_cast<const T*>(d0),
-        static_cast<const T*>(e), static_cast<const T*>(f), n0, d, 1.0f / (float)d, eps);
+    err = launch_pdl(qk_norm_rope_kernel<T>, dim3((unsigned)(n0 + n1)), dim3(threads), d * sizeof(float), st,
+                     static_cast<T*>(a), static_cast<T*>(b), static_cast<const T*>(c), static_cast<const T*>(d0),
+                     static_cast<const T*>(e), static_cast<const T*>(f), n0, d, 1.0f / (float)d, eps);
   } else {
     const int64_t total = rows * n0;
     const int64_t blocks = (total + kNormThreads - 1) / kNormThreads;
-    silu_mul_kernel<T><<<(unsigned)(blocks < 4096 ? blocks : 4096), kNormThreads, 0, st>>>(
-        static_cast<const T*>(c), static_cast<T*>(a), rows, n0);
+    err = launch_pdl(silu_mul_kernel<T>, dim3((unsigned)(blocks < 4096 ? blocks : 4096)), dim3(kNormThreads), 0, st,
+                     static_cast<const T*>(c), static_cast<T*>(a), rows, n0);
   }
-  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  return err == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
 int launch_layer_op(int dtype, int op, void* a, void* b, const void* c, const void* d0, const void* e, const void* f,
@@ -1359,26 +1335,43 @@ int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight
   return launch_layer_op(dtype, 1, q, k, q_weight, k_weight, cos_t, sin_t, 1, q_heads, k_heads, d, eps, stream);
 }
 
-int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream) {
+namespace {
+int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream, bool swiglu) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
   if (n < 0 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
   if (n == 0) return TC_OK;
   if (x == nullptr || w == nullptr || out == nullptr) return TC_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return TC_ERR_CUDA;
+  const int sms = sm_count(current_device());
+  // at most 8 CTAs per SM (all resident at once: each starts its L2 weight prefetch before the wait)
   const int64_t want = (n + kGemvWarps - 1) / kGemvWarps;
-  const unsigned grid = (unsigned)(want < (int64_t)sms * 64 ? want : (int64_t)sms * 64);
+  const unsigned grid = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
   const size_t smem = (size_t)k * 2;
-  if (dtype == TC_BF16)
-    gemv_kernel<__nv_bfloat16><<<grid, kGemvWarps * 32, smem, st>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(out), n, k);
-  else
-    gemv_kernel<__half><<<grid, kGemvWarps * 32, smem, st>>>(static_cast<const __half*>(x), static_cast<const __half*>(w),
-                                                             static_cast<__half*>(out), n, k);
-  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  cudaError_t e;
+  if (dtype == TC_BF16) {
+    using B = __nv_bfloat16;
+    e = swiglu ? launch_pdl(gemv_kernel<B, true>, dim3(grid), dim3(kGemvWarps * 32), smem, st, static_cast<const B*>(x),
+                            static_cast<const B*>(w), static_cast<B*>(out), n, k)
+               : launch_pdl(gemv_kernel<B, false>, dim3(grid), dim3(kGemvWarps * 32), smem, st,
+                            static_cast<const B*>(x), static_cast<const B*>(w), static_cast<B*>(out), n, k);
+  } else {
+    using H = __half;
+    e = swiglu ? launch_pdl(gemv_kernel<H, true>, dim3(grid), dim3(kGemvWarps * 32), smem, st, static_cast<const H*>(x),
+                            static_cast<const H*>(w), static_cast<H*>(out), n, k)
+               : launch_pdl(gemv_kernel<H, false>, dim3(grid), dim3(kGemvWarps * 32), smem, st,
+                            static_cast<const H*>(x), static_cast<const H*>(w), static_cast<H*>(out), n, k);
+  }
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+}  // namespace
+
+int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream) {
+  return run_gemv(x, w, out, n, k, dtype, stream, false);
+}
+
+int tc_gemv_swiglu(const void* gate_up, const void* w, void* out, int64_t n, int k, int dtype, void* stream) {
+  return run_gemv(gate_up, w, out, n, k, dtype, stream, true);
 }
 
 int tc_silu_mul(const void* gate_up, void* out, int64_t rows, int inter, int dtype, void* stream) {
@@ -1433,8 +1426,9 @@ size_t tc_allreduce_region_bytes(int world, int64_t rows) {
   return (size_t)kArCtrlBytes + (size_t)kArSlots * world * rows * sizeof(uint64_t);
 }
 
-int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
-                      int dtype, void* stream) {
+namespace {
+int run_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
+                       int dtype, void* stream, bool swiglu) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
   if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world || regions == nullptr) return TC_ERR_INVALID;
   if (n < 1 || n > 8192 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
@@ -1451,15 +1445,34 @@ int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* cons
   ar.rank = rank;
   ar.rows = n;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = (unsigned)((n + kArRows - 1) / kArRows);
+  const dim3 grid((unsigned)((n + kArRows - 1) / kArRows));
   const size_t smem = (size_t)k * 2;
-  if (dtype == TC_BF16)
-    gemv_allreduce_kernel<__nv_bfloat16><<<grid, kArThreads, smem, st>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), n, k, ar);
-  else
-    gemv_allreduce_kernel<__half><<<grid, kArThreads, smem, st>>>(static_cast<const __half*>(x),
-                                                                  static_cast<const __half*>(w), n, k, ar);
-  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  cudaError_t e;
+  if (dtype == TC_BF16) {
+    using B = __nv_bfloat16;
+    e = swiglu ? launch_pdl(gemv_allreduce_kernel<B, true>, grid, dim3(kArThreads), smem, st, static_cast<const B*>(x),
+                            static_cast<const B*>(w), n, k, ar)
+               : launch_pdl(gemv_allreduce_kernel<B, false>, grid, dim3(kArThreads), smem, st,
+                            static_cast<const B*>(x), static_cast<const B*>(w), n, k, ar);
+  } else {
+    using H = __half;
+    e = swiglu ? launch_pdl(gemv_allreduce_kernel<H, true>, grid, dim3(kArThreads), smem, st, static_cast<const H*>(x),
+                            static_cast<const H*>(w), n, k, ar)
+               : launch_pdl(gemv_allreduce_kernel<H, false>, grid, dim3(kArThreads), smem, st,
+                            static_cast<const H*>(x), static_cast<const H*>(w), n, k, ar);
+  }
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+}  // namespace
+
+int tc_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
+                      int dtype, void* stream) {
+  return run_gemv_allreduce(x, w, n, k, regions, world, rank, dtype, stream, false);
+}
+
+int tc_gemv_allreduce_swiglu(const void* gate_up, const void* w, int64_t n, int k, void* const* regions, int world,
+                             int rank, int dtype, void* stream) {
+  return run_gemv_allreduce(gate_up, w, n, k, regions, world, rank, dtype, stream, true);
 }
 
 int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
@@ -1472,15 +1485,17 @@ int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(static_cast<char*>(region) + kArCtrlBytes);
   unsigned int* seq = static_cast<unsigned int*>(region);
+  const int64_t rows = hidden;
+  cudaError_t e;
   if (dtype == TC_BF16)
-    allreduce_add_rmsnorm_kernel<__nv_bfloat16><<<1, kArNormThreads, 0, st>>>(
-        static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
-        hidden, 1.0f / (float)hidden, eps, mine, seq, world, hidden);
+    e = launch_pdl(allreduce_add_rmsnorm_kernel<__nv_bfloat16>, dim3(1), dim3(kArNormThreads), 0, st,
+                   static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(weight),
+                   static_cast<__nv_bfloat16*>(out), hidden, 1.0f / (float)hidden, eps, mine, seq, world, rows);
   else
-    allreduce_add_rmsnorm_kernel<__half><<<1, kArNormThreads, 0, st>>>(
-        static_cast<__half*>(h), static_cast<const __half*>(weight), static_cast<__half*>(out), hidden,
-        1.0f / (float)hidden, eps, mine, seq, world, hidden);
-  return cudaGetLastError() == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+    e = launch_pdl(allreduce_add_rmsnorm_kernel<__half>, dim3(1), dim3(kArNormThreads), 0, st,
+                   static_cast<__half*>(h), static_cast<const __half*>(weight), static_cast<__half*>(out), hidden,
+                   1.0f / (float)hidden, eps, mine, seq, world, rows);
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 
 }  // extern "C"

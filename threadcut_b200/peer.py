@@ -82,14 +82,17 @@ class AllReduce:
             raise ValueError(f"AllReduce: {world} ranks x {hidden} elements is outside the supported range")
         self.region = PeerRegion(nbytes, device, group)
 
-    def gemv(self, x, w):
+    def gemv(self, x, w, swiglu=False):
+        """Starts the sum of x @ w^T over the ranks (w [hidden, k], x [k]); swiglu: x is gate|up
+        [2k] and the product is of the SwiGLU activation computed from it (tc_gemv_allreduce_swiglu)."""
         require_cuda(x, w, what="gemv_allreduce")
         n, k = w.shape
-        if n != self.hidden or x.numel() != k or not (x.is_contiguous() and w.is_contiguous()):
-            raise ValueError("gemv_allreduce: w must be [hidden, k] and x [k], both contiguous")
+        if n != self.hidden or x.numel() != (2 * k if swiglu else k) or not (x.is_contiguous() and w.is_contiguous()):
+            raise ValueError("gemv_allreduce: w must be [hidden, k] and x [k] (gate|up [2k]), both contiguous")
         r = self.region
-        check("tc_gemv_allreduce", lib().tc_gemv_allreduce(x.data_ptr(), w.data_ptr(), n, k, r._arr, r.world, r.rank,
-                                                           dtype_code(x, "gemv_allreduce"), stream_ptr(x.device)))
+        fn = lib().tc_gemv_allreduce_swiglu if swiglu else lib().tc_gemv_allreduce
+        check("tc_gemv_allreduce", fn(x.data_ptr(), w.data_ptr(), n, k, r._arr, r.world, r.rank,
+                                      dtype_code(x, "gemv_allreduce"), stream_ptr(x.device)))
 
     def add_rmsnorm(self, h, weight, out, eps):
         require_cuda(h, weight, out, what="allreduce_add_rmsnorm")

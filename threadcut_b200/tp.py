@@ -84,6 +84,23 @@ def _gemv(x, w):
     return x @ w.t()
 
 
+def _gemv_swiglu(gu, w):
+    """silu(gate) * up from gu [1, 2I] (gate | up) times w[N, I]^T -> [1, N]: the SwiGLU activation
+    computed while the GEMV stages its input (tc_gemv_swiglu, one launch)."""
+    require_cuda(gu, w, what="gemv_swiglu")
+    n, k = w.shape
+    if not (gu.dtype == w.dtype and gu.dtype in (torch.bfloat16, torch.float16) and gu.is_contiguous()
+            and w.is_contiguous() and k % 8 == 0 and k <= 24576 and gu.numel() == 2 * k
+            and (gu.data_ptr() | w.data_ptr()) % 16 == 0):
+        act = gu.new_empty((1, k))
+        _silu_mul(gu, act)
+        return _gemv(act, w)
+    out = gu.new_empty((1, n))
+    check("tc_gemv_swiglu", lib().tc_gemv_swiglu(gu.data_ptr(), w.data_ptr(), out.data_ptr(), n, k,
+                                                 dtype_code(gu, "gemv_swiglu"), stream_ptr(gu.device)))
+    return out
+
+
 def _attend(layer, q, k, v, scale):
     """The rank's attention for one step: q [hr, g, d] over the layer's cache plus the step's row
     k, v [hr, d], which the same launch appends (GrowingLayer fused append, decode_attention_append)."""
@@ -211,8 +228,11 @@ class TPDecoder:
         """The step's arithmetic up to the final norm: [1, hidden] (appends the token's K/V row).
         Per layer: the q/k/v projection, q/k norm + RoPE (one launch), attention with the fused
         append, o_proj, sum over ranks, residual add + post-attention norm (one launch), the gate/up
-        projection, SwiGLU (one launch), down_proj, sum over ranks, and the residual add fused with
-        the next layer's input norm (the final norm after the last layer)."""
+        projection, down_proj of the SwiGLU activation (computed by the projection's input staging),
+        sum over ranks, and the residual add fused with the next layer's input norm (the final norm
+        after the last layer). Every kernel launches with programmatic dependent launch: it starts
+        while its predecessor finishes (the projections pulling their weights into L2) and waits for
+        it before reading what it wrote."""
         hr, d, g = self.h1 - self.h0, self.d, self.g
         nq, eps = hr * g, self.eps
         h = self.embed[token]  # [1, hidden], a fresh tensor (advanced indexing copies)
@@ -230,20 +250,20 @@ class TPDecoder:
             o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
             self._sum_add_norm(o.reshape(1, nq * d), w.wo, h, w.post_norm, x)
             gu = _gemv(x, w.wgu)
-            act = gu.new_empty((1, gu.shape[1] // 2))
-            _silu_mul(gu, act)
-            self._sum_add_norm(act, w.wd, h, norm_next, x)
+            self._sum_add_norm(gu, w.wd, h, norm_next, x, swiglu=True)
         return x
 
-    def _sum_add_norm(self, a, w, h, norm, x):
+    def _sum_add_norm(self, a, w, h, norm, x, swiglu=False):
         """h += sum over ranks of a @ w^T (w: this rank's columns of a row-split projection), then
         x = RMSNorm(h) * norm: through peer memory (tc_gemv_allreduce + tc_allreduce_add_rmsnorm)
-        or a collective all-reduce between tc_gemv and tc_add_rmsnorm."""
+        or a collective all-reduce between tc_gemv and tc_add_rmsnorm. swiglu: a is gate|up and the
+        projection's input is its SwiGLU activation, computed by the GEMV as it stages its input."""
         if self.use_peer_sums:
-            self._ar.gemv(a, w)
+            self._ar.gemv(a, w, swiglu=swiglu)
             self._ar.add_rmsnorm(h, norm, x, self.eps)
         else:
-            _add_rmsnorm(h, self._all_reduce(_gemv(a, w)), norm, x, self.eps)
+            part = _gemv_swiglu(a, w) if swiglu else _gemv(a, w)
+            _add_rmsnorm(h, self._all_reduce(part), norm, x, self.eps)
 
     def close(self):
         """Releases the peer-memory region of the sums (collective: every rank calls it, after the
