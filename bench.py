@@ -682,7 +682,7 @@ def time_cfg5_step(steps, warmup, dev):
     return out
 
 
-def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
+def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None):
     """Config 5 over `world` GPUs: threadcut_b200.tp.TPDecoder (rank r holds KV heads
     head_shard(8, r, world), their query heads, 1/world of the MLP and of the vocabulary; two
     all-reduces per layer) decoding one greedy token of random-init Qwen3-4B over the 131,072-token
@@ -775,6 +775,17 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world):
 
             graph_ms = timed(replay)
             graph_tok = int(out)
+            if launches:  # every rank replays (the sums need all ranks); rank 0 records
+                import contextlib
+                from torch.profiler import ProfilerActivity, profile
+                barrier(dist)
+                ctx = profile(activities=[ProfilerActivity.CUDA]) if rank == 0 else contextlib.nullcontext()
+                with ctx as prof:
+                    for _ in range(3):
+                        replay()
+                barrier(dist)
+                if rank == 0:
+                    launch_list(prof, launches, 3)
         del graph
         nccl_ms = None
         if dec.use_peer_sums:  # the same graph with the collective library's all-reduce for the sums
@@ -1165,6 +1176,57 @@ def run_ours(args, rank, local, world, dist):
         print(json.dumps(line), flush=True)
 
 
+def time_gemv(steps, warmup, dev, n, k, layers):
+    """tc_gemv alone: `layers` distinct bf16 weights [n, k] (the gate|up projection of one Qwen3-4B
+    layer at 1 GPU by default, 99.6 MB; together far above L2), one launch per weight per step,
+    replayed from a CUDA graph. The algorithmic bytes of a launch are the weight (x and out are a
+    few KB). Returns µs per launch and GB/s."""
+    from threadcut_b200 import tp
+    g = torch.Generator(device=dev).manual_seed(3)
+    ws = [(torch.randn(n, k, generator=g, device=dev) * k ** -0.5).to(torch.bfloat16) for _ in range(layers)]
+    x = torch.randn(1, k, generator=g, device=dev).to(torch.bfloat16)
+
+    def launch_all():
+        for w in ws:
+            tp._gemv(x, w)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            launch_all()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize()
+    ms = time_graph(graph, steps, warmup, None)
+    us = ms * 1000 / layers
+    hbm, kind = peaks()
+    gbs = n * k * 2 / (us * 1e-6) / 1e9
+    del graph, ws
+    return {"gemv_n": n, "gemv_k": k, "us_per_launch": round(us, 3), "gbs": round(gbs, 1),
+            "frac": round(gbs / hbm, 4), "peak_kind": kind}
+
+
+def launch_list(prof, path, steps):
+    """Kernel launch list of a torch.profiler run: per kernel name, launches, total device µs and
+    share, from the CUDA activity records (the device's own start/end stamps; nothing replayed)."""
+    rows = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time_total > 0:
+            r = rows.setdefault(ev.name, [0, 0.0])
+            r[0] += 1
+            r[1] += ev.device_time_total
+    total = sum(r[1] for r in rows.values()) or 1.0
+    with open(path, "w") as f:
+        f.write(f"# kernel launches of {steps} graph-replayed steps (torch.profiler CUDA activity)\n")
+        f.write("kernel\tlaunches\ttotal_us\tshare\tavg_us\n")
+        for name, (cnt, us) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+            f.write(f"{name}\t{cnt}\t{us:.1f}\t{us / total:.4f}\t{us / cnt:.2f}\n")
+
+
 def run_partial(args, rank, local, world, dist):
     """Profiling helper: one leg at a chosen size, no CPU baseline or e2e (not the bench contract)."""
     dev = torch.device("cuda", local)
@@ -1182,8 +1244,10 @@ def run_partial(args, rank, local, world, dist):
             del graph
         out.update(heads=args.heads, **res)
     elif args.only == "cfg5tp":
-        tp = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world)
+        tp = time_cfg5_tp(args.steps, args.warmup, dev, dist, rank, world, launches=args.launches)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in tp.items()}, world=world)
+    elif args.only == "gemv":
+        out.update(time_gemv(args.steps, args.warmup, dev, args.gemv_n, args.gemv_k, args.layers))
     elif args.only == "cfg5":
         c5 = time_cfg5_step(args.steps, args.warmup, dev)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in c5.items()})
@@ -1242,9 +1306,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5", "cfg5tp"], default="all",
-                    help="profiling runs: time only the decode graph, the splice, the config-5 model step or its "
-                         "tensor-parallel form (smaller JSON line)")
+    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5", "cfg5tp", "gemv"], default="all",
+                    help="profiling runs: time only the decode graph, the splice, the config-5 model step, its "
+                         "tensor-parallel form, or the step's GEMV (smaller JSON line)")
+    ap.add_argument("--launches", default=None,
+                    help="profiling runs (cfg5tp): rank 0 writes the kernel launch list of 3 graph-replayed steps "
+                         "(torch.profiler's CUDA activity records: device time per kernel, no replay) to this file")
+    ap.add_argument("--gemv-n", type=int, default=19456, help="profiling runs (gemv): output rows")
+    ap.add_argument("--gemv-k", type=int, default=2560, help="profiling runs (gemv): input length")
     ap.add_argument("--layers", type=int, default=LAYERS, help="profiling runs: layers per step")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="profiling runs: context length")
     ap.add_argument("--heads", type=int, default=8, help="profiling runs (decode): KV heads per layer")

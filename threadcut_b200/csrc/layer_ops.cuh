@@ -132,11 +132,14 @@ __device__ __forceinline__ float dot2(uint32_t a, uint32_t b, float acc, __half*
 }
 
 // L2 prefetch of weight rows (the constant operand of a GEMV) before the wait for the previous
-// kernel: rows row0, row0 + stride, ... below N, one bulk prefetch of K * 2 bytes per row, issued by
-// lane 0 of the calling warp. K * 2 is a multiple of 16 and the rows are 16-byte aligned.
-__device__ __forceinline__ void prefetch_rows_l2(const void* w, int64_t row0, int64_t stride, int64_t N, int K) {
+// kernel: at most `count` rows row0, row0 + stride, ... below N, one bulk prefetch of K * 2 bytes per
+// row, issued by lane 0 of the calling warp. K * 2 is a multiple of 16 and the rows are 16-byte
+// aligned. Only the first rows of a warp are worth it: the wait is short, and prefetching a whole
+// large projection would only evict what the step reads next.
+__device__ __forceinline__ void prefetch_rows_l2(const void* w, int64_t row0, int64_t stride, int64_t N, int K,
+                                                 int count) {
   if ((threadIdx.x & 31) != 0) return;
-  for (int64_t row = row0; row < N; row += stride) {
+  for (int64_t row = row0; row < N && count > 0; row += stride, --count) {
     const char* r = static_cast<const char*>(w) + row * (int64_t)K * 2;
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r), "r"((uint32_t)K * 2) : "memory");
   }
@@ -176,7 +179,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const T* __restri
   const int kc = K / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the weights do not depend on the previous kernel: start pulling this CTA's rows into L2 first
-  prefetch_rows_l2(w, (int64_t)blockIdx.x * kGemvWarps + warp, (int64_t)gridDim.x * kGemvWarps, N, K);
+  prefetch_rows_l2(w, (int64_t)blockIdx.x * kGemvWarps + warp, (int64_t)gridDim.x * kGemvWarps, N, K, 1);
   pdl_launch();
   pdl_wait();
   stage_x<T, kSwiGLU>(xs, x, K);

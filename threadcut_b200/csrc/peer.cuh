@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kArThreads) gemv_allreduce_kernel(const T* __r
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row0 = (int64_t)blockIdx.x * kArRows;
   // this CTA's weight rows into L2 while the previous kernel finishes; x and seq only after the wait
-  prefetch_rows_l2(w, row0 + warp, kArThreads / 32, row0 + kArRows < N ? row0 + kArRows : N, K);
+  prefetch_rows_l2(w, row0 + warp, kArThreads / 32, row0 + kArRows < N ? row0 + kArRows : N, K, kArRows);
   pdl_launch();
   pdl_wait();
   stage_x<T, kSwiGLU>(xs, x, K);

@@ -1344,9 +1344,8 @@ int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtyp
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int sms = sm_count(current_device());
-  // at most 8 CTAs per SM (all resident at once: each starts its L2 weight prefetch before the wait)
   const int64_t want = (n + kGemvWarps - 1) / kGemvWarps;
-  const unsigned grid = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  const unsigned grid = (unsigned)(want < (int64_t)sms * 64 ? want : (int64_t)sms * 64);
   const size_t smem = (size_t)k * 2;
   cudaError_t e;
   if (dtype == TC_BF16) {
