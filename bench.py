@@ -207,12 +207,13 @@ def capture_step(qs, ks, vs, outs, dev, stable=True, combine=None, lses=None):
 class SeqShardedStep:
     """Buffers and combine of a sequence-sharded decode step over `world` ranks: every rank holds a
     token slice of all 8 KV heads of every layer and computes per layer the fp32 partial and LSE of
-    its slice (tc_decode_attention_partial_stable); the combine all-gathers the step's partials
-    (two NCCL all-gathers for the 36 layers) and merges them by log-sum-exp in one launch
-    (tc_merge_partials, the merge of threadcut/flash_decode.py:68-69 over ranks) into the bf16
-    outputs of every layer on every rank."""
+    its slice (tc_decode_attention_partial_stable); the combine gathers the step's partials from all
+    ranks and merges them by log-sum-exp (the merge of threadcut/flash_decode.py:68-69 over ranks)
+    into the bf16 outputs of every layer on every rank: one tc_peer_gather_merge launch through peer
+    memory (combine), or two NCCL all-gathers and tc_merge_partials (combine_nccl)."""
 
     def __init__(self, layers, dev, dist, world, hl=8):
+        from threadcut_b200.peer import GatherMerge
         self.rows = layers * hl * 4
         self.po = torch.empty((layers, hl, 4, 128), dtype=torch.float32, device=dev)
         self.pl = torch.empty((layers, hl, 4), dtype=torch.float32, device=dev)
@@ -222,14 +223,24 @@ class SeqShardedStep:
         self.lse = torch.empty((self.rows,), dtype=torch.float32, device=dev)
         self.outs, self.lses = list(self.po.unbind(0)), list(self.pl.unbind(0))
         self.dist, self.world, self.dev = dist, world, dev
+        self.gm = GatherMerge(self.rows, 128, dev)
 
     def combine(self):
+        """Through peer memory: one tc_peer_gather_merge launch (push to every rank + merge)."""
+        self.gm(self.po.view(self.rows, 128), self.pl.view(self.rows), self.out, self.lse)
+
+    def combine_nccl(self):
+        """The same through the collective library: two NCCL all-gathers and tc_merge_partials."""
         from threadcut_b200._lib import TC_BF16, check, lib
         self.dist.all_gather_into_tensor(self.go, self.po.view(-1))
         self.dist.all_gather_into_tensor(self.gl, self.pl.view(-1))
         check("tc_merge_partials", lib().tc_merge_partials(
             self.go.data_ptr(), self.gl.data_ptr(), self.out.data_ptr(), self.lse.data_ptr(), self.world, self.rows,
             128, self.out.stride(0), TC_BF16, torch.cuda.current_stream(self.dev).cuda_stream))
+
+    def close(self):
+        self.dist.barrier()
+        self.gm.close()
 
 
 def time_graph(graph, steps, warmup, dist):
@@ -877,7 +888,9 @@ def time_strong_128k(steps, warmup, dev, dist, rank, world, layers=LAYERS):
         seq = SeqShardedStep(layers, dev, dist, world)
         graph = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses, combine=seq.combine)
         seq_ms = time_graph(graph, steps, warmup, dist)
-        del graph, ks, vs, qs, seq
+        del graph, ks, vs, qs
+        seq.close()
+        del seq
         torch.cuda.empty_cache()
     return head_ms, seq_ms
 
@@ -975,9 +988,13 @@ def run_ours(args, rank, local, world, dist):
     us_layer_rank = ms * 1000.0 / LAYERS  # one rank's time per layer (incl. back-to-back gaps)
     value = ms * 1000.0 / (LAYERS * world)  # per 16k tokens of context per layer
     achieved = rank_bytes / (us_layer_rank * 1e-6) / 1e9
-    if world > 1:  # the combine's share: the same decode launches without it
+    nccl_ms = None
+    if world > 1:  # the combine's share: the same decode launches without it, and with NCCL's
         g_nc = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses)
         nocombine_ms = max_over_ranks(time_graph(g_nc, args.steps, args.warmup, dist), dist)
+        del g_nc
+        g_nc = capture_step(qs, ks, vs, seq.outs, dev, lses=seq.lses, combine=seq.combine_nccl)
+        nccl_ms = max_over_ranks(time_graph(g_nc, args.steps, args.warmup, dist), dist)
         del g_nc
         g_plain = capture_step(qs, ks, vs, seq.outs, dev, stable=False, lses=seq.lses, combine=seq.combine)
     else:
@@ -987,7 +1004,10 @@ def run_ours(args, rank, local, world, dist):
     del g_plain
     e2e_ms, h2d, d2h = time_e2e(qs, ks, vs, args.steps, args.warmup, dist, dev, world)
     e2e_ms = max_over_ranks(e2e_ms, dist)
-    del graph, qs, ks, vs, seq
+    del graph, qs, ks, vs
+    if seq is not None:
+        seq.close()
+    del seq
     torch.cuda.empty_cache()
     # the single-GPU 16k layers (replicated on every rank) for the comparators and the fused append
     qs, ks, vs = build_layers(N_CTX, LAYERS, dev, seed=1000 + rank)
@@ -1100,8 +1120,8 @@ def run_ours(args, rank, local, world, dist):
                    "parallelism": f"sequence-sharded over {world} GPU(s): each GPU holds all 8 KV heads of its own "
                                   f"{N_CTX}-token slice of the {n_job}-token sequence" +
                                   (" and computes each layer's fp32 partial + LSE; the step ends with the combine "
-                                   "(NCCL all-gather of the 36 layers' partials and one LSE-merge launch, "
-                                   "tc_merge_partials, inside the graph)" if world > 1 else ""),
+                                   "(one tc_peer_gather_merge launch inside the graph: the 36 layers' partials pushed "
+                                   "to every rank through peer memory and LSE-merged)" if world > 1 else ""),
                    "value": "us per layer of the job / world = us per layer per 16k tokens of context (at 1 GPU: "
                             "the 16k decode; at 8: the 128k sequence, 16k tokens per GPU)",
                    "stable_rows": "n-1: every row but the newest declared stable, as in a decode step "
@@ -1119,7 +1139,10 @@ def run_ours(args, rank, local, world, dist):
         "combine": None if world == 1 else {
             "us_per_layer_without": round(nocombine_ms * 1000.0 / LAYERS, 3),
             "us_per_layer_with": round(us_layer_rank, 3),
-            "what": "the step's 36 partial-decode launches with and without the combine (all-gathers + merge)"},
+            "us_per_layer_with_nccl": round(nccl_ms * 1000.0 / LAYERS, 3),
+            "what": "the step's 36 partial-decode launches without the combine, with it (one tc_peer_gather_merge "
+                    "launch: partials pushed to every rank through peer memory and merged), and with NCCL's "
+                    "all-gathers + tc_merge_partials instead"},
         "gpu_launches": args.steps * LAYERS,
         "clocks": clk.summary(),
         "shift": {"value": round(shift_gbs, 1), "unit": "GB/s", "frac": round(shift_gbs / hbm, 4),

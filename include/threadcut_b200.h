@@ -456,6 +456,19 @@ int tc_gemv_allreduce_swiglu(const void* gate_up, const void* w, int64_t n, int 
 int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
                              int world, int dtype, void* stream);
 
+/* All-gather + log-sum-exp merge of sequence-shard partials through peer memory, one launch: every
+ * rank's fp32 partial o_local [rows][d] (normalised) and natural-log lse_local [rows] of its token
+ * slice (tc_decode_attention_partial*) are pushed into every other rank's region (regions as for
+ * tc_gemv_allreduce, each of tc_gather_region_bytes(world, rows, d) bytes, zeroed), and out [rows][d]
+ * (row stride out_stride_row, dtype) and lse_out (optional) are the merge of all ranks' partials in
+ * rank order: the arithmetic of tc_merge_partials (threadcut/flash_decode.py:68-69 over the ranks),
+ * the same bits on every rank. Waits (bounded; TC_DEVERR_PEER_TIMEOUT) for the other ranks' data.
+ * Every rank calls it in the same order; d % 4 == 0, o_local 16-byte aligned. No counterpart in the
+ * reference (one GPU): it replaces an NCCL all-gather of the partials plus tc_merge_partials. */
+size_t tc_gather_region_bytes(int world, int64_t rows, int d);
+int tc_peer_gather_merge(const float* o_local, const float* lse_local, void* out, float* lse_out, int64_t rows, int d,
+                         int64_t out_stride_row, void* const* regions, int world, int rank, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,5 +1,6 @@
-"""torchrun worker: the peer-memory sums of the tensor-parallel step (threadcut_b200.peer.AllReduce)
-against the same arithmetic through the collective library.
+"""torchrun worker: the peer-memory collectives (threadcut_b200.peer: AllReduce, the sums of the
+tensor-parallel step; GatherMerge, the combine of a sequence-sharded decode) against the same
+arithmetic through the collective library.
 
 Every rank holds its own columns of a row-split projection (x_r [k], w_r [hidden, k]). Expected, as
 torch would compute it: the fp32 partials x_r . w_r^T of all ranks (all-gathered with NCCL) summed in
@@ -62,6 +63,36 @@ def check(dev, world, rank, hidden=2560, k=512, rounds=7):
     return {"rounds": rounds, "worst_h_diff": worst}
 
 
+def check_gather(dev, world, rank, rows=1152, d=128, rounds=5):
+    """GatherMerge (tc_peer_gather_merge) against an NCCL all-gather of the same partials followed by
+    flash_decode.merge_partials: the same bits on every rank, over several gathers (both slots)."""
+    from threadcut_b200.flash_decode import merge_partials
+    from threadcut_b200.peer import GatherMerge
+    gm = GatherMerge(rows, d, dev)
+    g = torch.Generator(device=dev).manual_seed(200 + rank)
+    out = torch.empty(rows, d, dtype=torch.bfloat16, device=dev)
+    lse_out = torch.empty(rows, device=dev)
+    for i in range(rounds):
+        o = torch.randn(rows, d, generator=g, device=dev)
+        lse = torch.randn(rows, generator=g, device=dev) * 3
+        if i == 1:
+            lse[::7] = -float("inf")  # rows this rank's slice did not see
+        gm(o, lse, out, lse_out)
+        go = torch.empty(world * rows * d, device=dev)
+        gl = torch.empty(world * rows, device=dev)
+        dist.all_gather_into_tensor(go, o.view(-1))
+        dist.all_gather_into_tensor(gl, lse)
+        want, want_lse = merge_partials(go.view(world, rows, d), gl.view(world, rows), torch.bfloat16)
+        torch.cuda.synchronize(dev)
+        assert torch.equal(out, want), (i, float((out.float() - want.float()).abs().max()))
+        assert torch.equal(lse_out, want_lse), i
+    errs = _lib.device_errors(clear=True)
+    assert errs == 0, errs
+    dist.barrier()
+    gm.close()
+    return {"gathers": rounds}
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
@@ -70,7 +101,8 @@ def main():
     ok = True
     try:
         try:
-            print(f"rank {rank}/{world}: {check(dev, world, rank)}", flush=True)
+            print(f"rank {rank}/{world}: {check(dev, world, rank)} {check_gather(dev, world, rank)} "
+                  f"{check_gather(dev, world, rank, rows=3, d=128, rounds=3)}", flush=True)
         except AssertionError as exc:
             print(f"rank {rank}/{world}: FAILED {exc}", flush=True)
             ok = False

@@ -398,3 +398,16 @@ def test_peer_sum_argument_validation_without_a_gpu():
     assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 9000, 1e-6, 256, 2, 2, None) == 1  # hidden too large
     assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 2560, 1e-6, 100, 2, 2, None) == 1  # region misaligned
     assert L.tc_peer_open(None, None) == 1 and L.tc_peer_close(None) == 1 and L.tc_peer_free(None) == 1
+
+
+def test_peer_gather_argument_validation_without_a_gpu():
+    L = _lib.lib()
+    # o [rows][d] then lse [rows] per source, padded to a multiple of 4 floats, two slots
+    assert L.tc_gather_region_bytes(8, 1152, 128) == 256 + 2 * 8 * (1152 * 129) * 4
+    assert L.tc_gather_region_bytes(2, 3, 128) == 256 + 2 * 2 * 388 * 4
+    assert L.tc_gather_region_bytes(9, 3, 128) == 0 and L.tc_gather_region_bytes(2, 3, 6) == 0
+    regs = (ctypes.c_void_p * 2)(256, 512)
+    assert L.tc_peer_gather_merge(16, 16, 16, None, 3, 128, 128, regs, 2, 0, 7, None) == 3   # dtype
+    assert L.tc_peer_gather_merge(16, 16, 16, None, 3, 128, 100, regs, 2, 0, 2, None) == 1   # out stride < d
+    assert L.tc_peer_gather_merge(8, 16, 16, None, 3, 128, 128, regs, 2, 0, 2, None) == 2    # o misaligned
+    assert L.tc_peer_gather_merge(16, 16, 16, None, 3, 128, 128, regs, 2, 5, 2, None) == 1   # rank

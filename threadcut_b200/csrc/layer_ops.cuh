@@ -172,33 +172,50 @@ __device__ __forceinline__ void stage_x(uint4* xs, const T* __restrict__ x, int 
   }
 }
 
-template <typename T, bool kSwiGLU = false>
+// RPW rows per warp streamed together (their loads in flight at once; each row keeps the per-lane
+// order of a single-row pass, so the result bits do not depend on RPW); rows of warp-group u are
+// u * RPW .. u * RPW + RPW - 1, warp-groups strided over the grid.
+template <typename T, bool kSwiGLU = false, int RPW = 1>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                T* __restrict__ out, int64_t N, int K) {
   extern __shared__ uint4 xs[];
   const int kc = K / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the weights do not depend on the previous kernel: start pulling this CTA's rows into L2 first
-  prefetch_rows_l2(w, (int64_t)blockIdx.x * kGemvWarps + warp, (int64_t)gridDim.x * kGemvWarps, N, K, 1);
+  const int64_t g0 = (int64_t)blockIdx.x * kGemvWarps + warp, gstride = (int64_t)gridDim.x * kGemvWarps;
+  // the weights do not depend on the previous kernel: start pulling this warp's first rows into L2
+  prefetch_rows_l2(w, g0 * RPW, 1, g0 * RPW + RPW < N ? g0 * RPW + RPW : N, K, RPW);
   pdl_launch();
   pdl_wait();
   stage_x<T, kSwiGLU>(xs, x, K);
   __syncthreads();
-  for (int64_t row = (int64_t)blockIdx.x * kGemvWarps + warp; row < N; row += (int64_t)gridDim.x * kGemvWarps) {
-    const uint4* wr = reinterpret_cast<const uint4*>(w + row * (int64_t)K);
-    float acc = 0.f;
+  for (int64_t grp = g0; grp * RPW < N; grp += gstride) {
+    const uint4* wr[RPW];
+    float acc[RPW];
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) {
+      const int64_t row = grp * RPW + j;
+      wr[j] = reinterpret_cast<const uint4*>(w + (row < N ? row : N - 1) * (int64_t)K);
+      acc[j] = 0.f;
+    }
 #pragma unroll 8
     for (int c = lane; c < kc; c += 32) {
-      const uint4 a = __ldg(wr + c);
       const uint4 b = xs[c];
-      acc = dot2(a.x, b.x, acc, (T*)nullptr);
-      acc = dot2(a.y, b.y, acc, (T*)nullptr);
-      acc = dot2(a.z, b.z, acc, (T*)nullptr);
-      acc = dot2(a.w, b.w, acc, (T*)nullptr);
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) {
+        const uint4 a = __ldg(wr[j] + c);
+        acc[j] = dot2(a.x, b.x, acc[j], (T*)nullptr);
+        acc[j] = dot2(a.y, b.y, acc[j], (T*)nullptr);
+        acc[j] = dot2(a.z, b.z, acc[j], (T*)nullptr);
+        acc[j] = dot2(a.w, b.w, acc[j], (T*)nullptr);
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) out[row] = from_f32<T>(acc);
+    for (int j = 0; j < RPW; ++j) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+      const int64_t row = grp * RPW + j;
+      if (lane == 0 && row < N) out[row] = from_f32<T>(acc[j]);
+    }
   }
 }
 

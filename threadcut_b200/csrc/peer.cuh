@@ -166,3 +166,134 @@ __global__ void __launch_bounds__(kArNormThreads) allreduce_add_rmsnorm_kernel(
 }
 
 }  // namespace tc
+
+namespace tc {
+
+// ---- all-gather + log-sum-exp merge of sequence-shard partials through peer memory.
+// Every rank holds, for `rows` query rows, the fp32 partial output o [rows][d] (normalised) and
+// natural-log LSE [rows] of its token slice. One launch pushes them into every other rank's region
+// and merges all ranks' partials into the output, in rank order, with the arithmetic of
+// merge_partials_kernel (the merge of threadcut/flash_decode.py:68-69 over ranks).
+//
+// Region of each rank (zeroed at creation): [0, 256) control: word 0 `seq` (completed gathers of
+// this rank), word 1 the count of this launch's finished CTAs, words 8 + 8*slot + src: the epoch
+// (gather number + 1) of src's data in slot; then the data, [2 slots][world][gather_src_stride] fp32.
+// Gather s uses slot s % 2: a rank pushes gather s + 2 into slot s % 2 of rank r only after its own
+// gather s + 1 received r's data, which r pushed after it finished gather s (its reads of slot s % 2).
+constexpr int kGmThreads = 256;
+constexpr int kGmMergers = 64;
+
+// Floats per (slot, source) of a gather region: o [rows][d] then lse [rows], rounded up to a
+// multiple of 4 floats so that every source's block starts 16-byte aligned (float4 stores).
+__host__ __device__ __forceinline__ int64_t gather_src_stride(int64_t rows, int d) {
+  return (rows * d + rows + 3) / 4 * 4;
+}
+
+struct GatherPeers {
+  float* data[kArMaxWorld];          // rank p's data area as mapped in this process
+  unsigned int* ctrl[kArMaxWorld];   // rank p's control words as mapped in this process
+  int world, rank;
+  int64_t src_stride;                // floats per (slot, source): gather_src_stride(rows, d)
+  int64_t slot_stride;               // floats per slot: world * src_stride
+};
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// grid.x = (world - 1) pushers + kGmMergers mergers. Pusher i copies this rank's partials to rank
+// (rank + 1 + i) % world and then raises that rank's flag for this rank; merger m waits for every
+// other rank's flag in this rank's region and merges its share of the rows. The last CTA to finish
+// advances seq. rows * d % 4 == 0.
+template <typename T>
+__global__ void __launch_bounds__(kGmThreads) gather_merge_kernel(const float* __restrict__ o_local,
+                                                                  const float* __restrict__ lse_local,
+                                                                  T* __restrict__ out, float* __restrict__ lse_out,
+                                                                  int64_t rows, int d, int64_t out_stride,
+                                                                  const __grid_constant__ GatherPeers gp) {
+  __shared__ int s_ok;
+  pdl_launch();
+  pdl_wait();
+  unsigned int* my_ctrl = gp.ctrl[gp.rank];
+  const unsigned int s = my_ctrl[0];
+  const unsigned int slot = s & 1u, ep = s + 1u;
+  const int pushers = gp.world - 1;
+  if ((int)blockIdx.x < pushers) {
+    const int p = (gp.rank + 1 + (int)blockIdx.x) % gp.world;
+    float* dst = gp.data[p] + slot * gp.slot_stride + (int64_t)gp.rank * gp.src_stride;
+    const int64_t n4 = rows * d / 4;
+    const float4* src4 = reinterpret_cast<const float4*>(o_local);
+    float4* dst4 = reinterpret_cast<float4*>(dst);
+    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) dst4[i] = src4[i];
+    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) dst[rows * d + i] = lse_local[i];
+    __syncthreads();  // every thread's stores precede the flag below
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys_u32(gp.ctrl[p] + 8 + 8 * slot + gp.rank, ep);
+    }
+  } else {
+    const int m = (int)blockIdx.x - pushers, nm = (int)gridDim.x - pushers;
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      for (int r = 0; r < gp.world; ++r) {
+        if (r == gp.rank) continue;
+        uint32_t spin = 0;
+        while (ld_acquire_sys_u32(my_ctrl + 8 + 8 * slot + r) != ep) {
+          if (++spin >= kSpinLimit / 64) {
+            raise_error(TC_DEVERR_PEER_TIMEOUT);
+            ok = 0;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      s_ok = ok;
+    }
+    __syncthreads();
+    const float* mine = gp.data[gp.rank] + slot * gp.slot_stride;
+    const int64_t r0 = rows * m / nm, r1 = rows * (m + 1) / nm;
+    for (int64_t row = r0; row < r1; ++row) {
+      // part r: this rank's own partial from its inputs, the others' from its region
+      float M = -INFINITY;
+      for (int r = 0; r < gp.world; ++r) {
+        const float l = r == gp.rank ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
+        M = fmaxf(M, l);
+      }
+      float L = 0.f;
+      if (M != -INFINITY)
+        for (int r = 0; r < gp.world; ++r) {
+          const float l = r == gp.rank ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
+          L += __expf(l - M);
+        }
+      for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
+        float o = 0.f;
+        if (M != -INFINITY)
+          for (int r = 0; r < gp.world; ++r) {
+            const bool own = r == gp.rank;
+            const float l = own ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
+            const float x = own ? o_local[row * d + dd] : __ldcg(mine + (int64_t)r * gp.src_stride + row * d + dd);
+            o += __expf(l - M) * x;
+          }
+        out[row * out_stride + dd] = from_f32<T>(L > 0.f ? o / L : 0.f);
+      }
+      if (lse_out != nullptr && threadIdx.x == 0) lse_out[row] = L > 0.f ? M + __logf(L) : -INFINITY;
+    }
+    (void)s_ok;
+  }
+  // the last CTA of this launch advances seq (every CTA read it above)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(my_ctrl + 1, 1u) == gridDim.x - 1) {
+      my_ctrl[1] = 0u;
+      my_ctrl[0] = s + 1u;
+    }
+  }
+}
+
+}  // namespace tc

@@ -1335,7 +1335,29 @@ int tc_qk_norm_rope(void* q, void* k, const void* q_weight, const void* k_weight
   return launch_layer_op(dtype, 1, q, k, q_weight, k_weight, cos_t, sin_t, 1, q_heads, k_heads, d, eps, stream);
 }
 
+}  // extern "C"
+
 namespace {
+template <typename T, bool SW, int RPW>
+cudaError_t launch_gemv_r(unsigned grid, size_t smem, cudaStream_t st, const void* x, const void* w, void* out,
+                          int64_t n, int k) {
+  return launch_pdl(gemv_kernel<T, SW, RPW>, dim3(grid), dim3(kGemvWarps * 32), smem, st, static_cast<const T*>(x),
+                    static_cast<const T*>(w), static_cast<T*>(out), n, k);
+}
+
+template <typename T>
+cudaError_t launch_gemv_t(int rpw, bool swiglu, unsigned grid, size_t smem, cudaStream_t st, const void* x,
+                          const void* w, void* out, int64_t n, int k) {
+  if (swiglu) {
+    if (rpw == 4) return launch_gemv_r<T, true, 4>(grid, smem, st, x, w, out, n, k);
+    if (rpw == 2) return launch_gemv_r<T, true, 2>(grid, smem, st, x, w, out, n, k);
+    return launch_gemv_r<T, true, 1>(grid, smem, st, x, w, out, n, k);
+  }
+  if (rpw == 4) return launch_gemv_r<T, false, 4>(grid, smem, st, x, w, out, n, k);
+  if (rpw == 2) return launch_gemv_r<T, false, 2>(grid, smem, st, x, w, out, n, k);
+  return launch_gemv_r<T, false, 1>(grid, smem, st, x, w, out, n, k);
+}
+
 int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream, bool swiglu) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
   if (n < 0 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
@@ -1344,26 +1366,22 @@ int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtyp
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int sms = sm_count(current_device());
-  const int64_t want = (n + kGemvWarps - 1) / kGemvWarps;
+  // rows per warp: 4 when there are enough rows for two CTAs of 4-row warps on every SM, 2 for one,
+  // else 1 (more warps stream, each with fewer rows in flight)
+  const int rpw = n >= (int64_t)sms * 2 * kGemvWarps * 4 ? 4 : (n >= (int64_t)sms * kGemvWarps * 2 ? 2 : 1);
+  const int64_t want = (n + (int64_t)kGemvWarps * rpw - 1) / ((int64_t)kGemvWarps * rpw);
   const unsigned grid = (unsigned)(want < (int64_t)sms * 64 ? want : (int64_t)sms * 64);
   const size_t smem = (size_t)k * 2;
   cudaError_t e;
-  if (dtype == TC_BF16) {
-    using B = __nv_bfloat16;
-    e = swiglu ? launch_pdl(gemv_kernel<B, true>, dim3(grid), dim3(kGemvWarps * 32), smem, st, static_cast<const B*>(x),
-                            static_cast<const B*>(w), static_cast<B*>(out), n, k)
-               : launch_pdl(gemv_kernel<B, false>, dim3(grid), dim3(kGemvWarps * 32), smem, st,
-                            static_cast<const B*>(x), static_cast<const B*>(w), static_cast<B*>(out), n, k);
-  } else {
-    using H = __half;
-    e = swiglu ? launch_pdl(gemv_kernel<H, true>, dim3(grid), dim3(kGemvWarps * 32), smem, st, static_cast<const H*>(x),
-                            static_cast<const H*>(w), static_cast<H*>(out), n, k)
-               : launch_pdl(gemv_kernel<H, false>, dim3(grid), dim3(kGemvWarps * 32), smem, st,
-                            static_cast<const H*>(x), static_cast<const H*>(w), static_cast<H*>(out), n, k);
-  }
+  if (dtype == TC_BF16)
+    e = launch_gemv_t<__nv_bfloat16>(rpw, swiglu, grid, smem, st, x, w, out, n, k);
+  else
+    e = launch_gemv_t<__half>(rpw, swiglu, grid, smem, st, x, w, out, n, k);
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 }  // namespace
+
+extern "C" {
 
 int tc_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream) {
   return run_gemv(x, w, out, n, k, dtype, stream, false);
@@ -1494,6 +1512,49 @@ int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden,
     e = launch_pdl(allreduce_add_rmsnorm_kernel<__half>, dim3(1), dim3(kArNormThreads), 0, st,
                    static_cast<__half*>(h), static_cast<const __half*>(weight), static_cast<__half*>(out), hidden,
                    1.0f / (float)hidden, eps, mine, seq, world, rows);
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t tc_gather_region_bytes(int world, int64_t rows, int d) {
+  if (world < 1 || world > kArMaxWorld || rows < 1 || d < 4 || d % 4 || rows > ((int64_t)1 << 24)) return 0;
+  return (size_t)kArCtrlBytes + 2 * (size_t)world * (size_t)gather_src_stride(rows, d) * sizeof(float);
+}
+
+int tc_peer_gather_merge(const float* o_local, const float* lse_local, void* out, float* lse_out, int64_t rows, int d,
+                         int64_t out_stride_row, void* const* regions, int world, int rank, int dtype, void* stream) {
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (tc_gather_region_bytes(world, rows, d) == 0 || rank < 0 || rank >= world || out_stride_row < d)
+    return TC_ERR_INVALID;
+  if (o_local == nullptr || lse_local == nullptr || out == nullptr || regions == nullptr) return TC_ERR_INVALID;
+  if (!aligned16(o_local)) return TC_ERR_ALIGN;
+  GatherPeers gp;
+  std::memset(&gp, 0, sizeof(gp));
+  for (int p = 0; p < world; ++p) {
+    if (regions[p] == nullptr || (reinterpret_cast<uintptr_t>(regions[p]) & 255)) return TC_ERR_INVALID;
+    gp.ctrl[p] = static_cast<unsigned int*>(regions[p]);
+    gp.data[p] = reinterpret_cast<float*>(static_cast<char*>(regions[p]) + kArCtrlBytes);
+  }
+  gp.world = world;
+  gp.rank = rank;
+  gp.src_stride = gather_src_stride(rows, d);
+  gp.slot_stride = (int64_t)world * gp.src_stride;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int mergers = rows < kGmMergers ? (int)rows : kGmMergers;
+  const dim3 grid((unsigned)(world - 1 + mergers));
+  cudaError_t e;
+  if (dtype == TC_BF16)
+    e = launch_pdl(gather_merge_kernel<__nv_bfloat16>, grid, dim3(kGmThreads), 0, st, o_local, lse_local,
+                   static_cast<__nv_bfloat16*>(out), lse_out, rows, d, out_stride_row, gp);
+  else if (dtype == TC_F16)
+    e = launch_pdl(gather_merge_kernel<__half>, grid, dim3(kGmThreads), 0, st, o_local, lse_local,
+                   static_cast<__half*>(out), lse_out, rows, d, out_stride_row, gp);
+  else
+    e = launch_pdl(gather_merge_kernel<float>, grid, dim3(kGmThreads), 0, st, o_local, lse_local,
+                   static_cast<float*>(out), lse_out, rows, d, out_stride_row, gp);
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 

@@ -18,7 +18,7 @@ import torch.distributed as dist
 
 from ._lib import check, dtype_code, lib, require_cuda, stream_ptr
 
-__all__ = ["PeerRegion", "AllReduce"]
+__all__ = ["PeerRegion", "AllReduce", "GatherMerge"]
 
 
 class PeerRegion:
@@ -102,6 +102,37 @@ class AllReduce:
         check("tc_allreduce_add_rmsnorm", lib().tc_allreduce_add_rmsnorm(
             h.data_ptr(), weight.data_ptr(), out.data_ptr(), self.hidden, float(eps), r.ptrs[r.rank], r.world,
             dtype_code(h, "allreduce_add_rmsnorm"), stream_ptr(h.device)))
+
+    def close(self):
+        self.region.close()
+
+
+class GatherMerge:
+    """The combine of a sequence-sharded decode over the ranks of `group`, through peer memory:
+    __call__(o, lse, out) pushes this rank's fp32 partials o [rows, d] and LSE [rows] into every
+    other rank's region and writes the log-sum-exp merge of all ranks' partials (rank order, the
+    arithmetic of flash_decode.merge_partials) into out [rows, d] — one launch in place of an
+    all-gather and a merge (tc_peer_gather_merge). All ranks call it in the same order."""
+
+    def __init__(self, rows, d, device, group=None):
+        self.rows, self.d = int(rows), int(d)
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        nbytes = lib().tc_gather_region_bytes(world, self.rows, self.d)
+        if nbytes == 0:
+            raise ValueError(f"GatherMerge: {world} ranks x {rows} x {d} is outside the supported range")
+        self.region = PeerRegion(nbytes, device, group)
+
+    def __call__(self, o, lse, out, lse_out=None):
+        require_cuda(o, lse, out, what="peer_gather_merge")
+        if (o.dtype != torch.float32 or lse.dtype != torch.float32 or tuple(o.shape) != (self.rows, self.d)
+                or lse.numel() != self.rows or not o.is_contiguous() or not lse.is_contiguous()
+                or out.shape[-1] != self.d or out.stride(-1) != 1):
+            raise ValueError("peer_gather_merge: o fp32 [rows, d], lse fp32 [rows] (contiguous), out [rows, d]")
+        r = self.region
+        check("tc_peer_gather_merge", lib().tc_peer_gather_merge(
+            o.data_ptr(), lse.data_ptr(), out.data_ptr(), None if lse_out is None else lse_out.data_ptr(), self.rows,
+            self.d, out.stride(-2), r._arr, r.world, r.rank, dtype_code(out, "peer_gather_merge"), stream_ptr(o.device)))
+        return out
 
     def close(self):
         self.region.close()
