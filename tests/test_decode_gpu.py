@@ -333,6 +333,11 @@ def test_host_binding_matches_the_ctypes_path():
     check_decode(qs, k[..., :64].contiguous(), v[..., :64].contiguous(), 0.1, torch.bfloat16)
     with pytest.raises(ValueError):
         decode_attention(q, k[:4], v, 0.1)
+    # the partial (sequence shard) through the binding equals the ctypes path bit for bit
+    assert hasattr(_lib.host(), "partial")
+    po, pl = decode_attention_partial(q, k, v, 0.0883, stable_rows=4999)
+    so, sl = flash_decode._decode(q, k, v, 0.0883, None, True, partial=True, stable_rows=4999)
+    assert torch.equal(po, so) and torch.equal(pl, sl)
 
 
 @pytest.mark.parametrize("n,d,dtype", [(1, 128, torch.bfloat16), (32, 128, torch.bfloat16), (33, 128, torch.bfloat16),

@@ -127,6 +127,8 @@ def host():
                     mod = importlib.util.module_from_spec(spec)
                     spec.loader.exec_module(mod)
                     mod.init(ctypes.cast(handle.tc_decode_attention_stable, ctypes.c_void_p).value)
+                    if hasattr(mod, "init_partial"):
+                        mod.init_partial(ctypes.cast(handle.tc_decode_attention_partial_stable, ctypes.c_void_p).value)
                 _host = mod
     return _host or None
 

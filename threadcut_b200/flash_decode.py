@@ -166,6 +166,15 @@ def decode_attention_partial(q, k, v, scale, *, splits=None, stable_rows=0):
     `stable_rows` as for decode_attention."""
     if stable_rows < 0:
         raise ValueError("decode_attention_partial: stable_rows must be >= 0")
+    hb = _lib.host()
+    if hb is not None and hasattr(hb, "partial") and q.device.type == "cuda" and q.dim() == 3:
+        code = _lib.DTYPE_CODE.get(q.dtype)
+        if code is not None:
+            hkv, g, d = q.shape
+            ws = workspaces.get(("decode", hkv), q.device, _lib.decode_workspace_bound(1, hkv, g, d, code))
+            res = hb.partial(q, k, v, float(scale), int(splits or 0), int(stable_rows), ws)
+            if res is not None:
+                return res
     return _decode(q, k, v, scale, splits, True, partial=True, stable_rows=stable_rows)
 
 
