@@ -683,6 +683,13 @@ def time_cfg5_step(steps, warmup, dev):
             eager()
         torch.cuda.synchronize(dev)
         graph_ms("graph_ms")
+        # the same calls with the one-token step routed through the fused step (tp.accelerate)
+        from threadcut_b200 import tp as tc_tp
+        tc_tp.accelerate(model)
+        out["fused_eager_ms"] = timed(eager)
+        graph_ms("fused_graph_ms")
+        tc_tp.restore(model)
+        torch.cuda.empty_cache()
         model.set_attn_implementation("sdpa")
         for layer in cache.layers:
             layer.fuse_append = False  # SDPA reads the cache itself: appends must be written, not deferred
@@ -1061,15 +1068,18 @@ def run_ours(args, rank, local, world, dist):
         step_bytes = c5["weight_bytes"] + c5["kv_bytes"]
         rnd = lambda v: None if v is None else round(v, 3)  # noqa: E731
         cfg5 = {"eager_ms": rnd(c5["eager_ms"]), "graph_ms": rnd(c5["graph_ms"]),
+                "fused_eager_ms": rnd(c5.get("fused_eager_ms")), "fused_graph_ms": rnd(c5.get("fused_graph_ms")),
                 "sdpa_eager_ms": rnd(c5["sdpa_eager_ms"]), "sdpa_graph_ms": rnd(c5["sdpa_graph_ms"]),
                 "splice_ms": rnd(c5["splice_ms"]),
                 "n": c5["n"], "bytes_per_token": step_bytes,
                 "ideal_ms": round(step_bytes / (hbm * 1e9) * 1e3, 3),
                 "what": "one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache "
                         "(131,072 tokens, Split(49152, 81920, 49152) timed once as splice_ms): HF forward with "
-                        "threadcut_b200's attention + argmax read back, eager and replayed from a CUDA graph, vs "
+                        "threadcut_b200's attention + argmax read back, eager and replayed from a CUDA graph; "
+                        "fused_*: the same model call after tp.accelerate(model) (the one-token step runs the fused "
+                        "TPDecoder step at world 1 over the same cache), the call the reference's engine makes; vs "
                         "the same with HF's SDPA attention (under capture HF passes SDPA an explicit mask); ideal_ms = weights + K/V bytes at the measured HBM peak"}
-        for key in ("graph_error", "sdpa_graph_error"):
+        for key in ("graph_error", "fused_graph_error", "sdpa_graph_error"):
             if key in c5:
                 cfg5[key] = c5[key]
     tp = time_cfg5_tp(min(args.steps, 10), args.warmup, dev, dist, rank, world)

@@ -269,3 +269,43 @@ def test_tensor_parallel_decoder_on_one_gpu_matches_the_hf_forward():
     from tp_worker import check
     res = check(torch.device(DEV))
     assert res["max_abs"] < 0.1, res
+
+
+def test_accelerated_model_matches_the_plugin_forward_and_sdpa():
+    """tp.accelerate(model): the engine's one-token calls (model(input_ids=[[t]],
+    past_key_values=cache, use_cache=True)) run the fused step over the same cache. Teacher-forced
+    over 6 steps after a 300-token prompt, each step's logits have the top-1 of the plugin forward
+    (HF's Qwen3 layer with this attention) and of HF's SDPA forward on copies of the same cache, and
+    correlate; the cache grows by one row per step as the reference's would; a prefill chunk still
+    goes through the model's own forward; restore() undoes it."""
+    from threadcut_b200 import tp
+    torch.manual_seed(0)
+    cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation=tc_attention.NAME)
+    model = model.to(DEV).eval()
+    ids = torch.randint(0, 512, (1, 306), generator=torch.Generator().manual_seed(4)).to(DEV)
+    with torch.no_grad():
+        fast, plain = new_cache(model.config), new_cache(model.config)
+        model(input_ids=ids[:, :300], past_key_values=fast, use_cache=True)
+        model(input_ids=ids[:, :300], past_key_values=plain, use_cache=True)
+        tp.accelerate(model)
+        for i in range(300, 306):
+            x = ids[:, i:i + 1]
+            ref_cache = DynamicCache(config=model.config)
+            for lr, lp in zip(ref_cache.layers, plain.layers):
+                lr.update(lp.keys.clone(), lp.values.clone())
+            got = model(input_ids=x, past_key_values=fast, use_cache=True).logits[0, -1].float()
+            tp.restore(model)
+            want = model(input_ids=x, past_key_values=plain, use_cache=True).logits[0, -1].float()
+            model.set_attn_implementation("sdpa")
+            sdpa = model(input_ids=x, past_key_values=ref_cache, use_cache=True).logits[0, -1].float()
+            model.set_attn_implementation(tc_attention.NAME)
+            tp.accelerate(model)
+            assert fast.get_seq_length() == plain.get_seq_length() == i + 1
+            assert int(got.argmax()) == int(want.argmax()) == int(sdpa.argmax()), i
+            assert torch.corrcoef(torch.stack([got, want]))[0, 1].item() > 0.999
+        chunk = model(input_ids=ids[:, :5], past_key_values=fast, use_cache=True)  # not one token: HF's forward
+        assert chunk.logits.shape[1] == 5 and fast.get_seq_length() == 311
+        tp.restore(model)
+    assert not hasattr(model, "_threadcut_fused_step")

@@ -297,3 +297,79 @@ __global__ void __launch_bounds__(kGmThreads) gather_merge_kernel(const float* _
 }
 
 }  // namespace tc
+
+namespace tc {
+
+// ---- split-K GEMV for long input rows (K >= kSplitKMin): a CTA owns kSkRows output rows and its 8
+// warps split K into 8 contiguous slices, so every lane keeps kSkRows loads per column step in
+// flight however few rows the matrix has (a row per warp over all of K left the 2560 x 9728 down
+// projection at 40 % of HBM). Per row: each lane sums its columns in order, the lanes by xor
+// shuffles, the warps' sums in warp order through shared memory; fp32 throughout, one rounding.
+// kAR: the rows go to every rank's region as (value, epoch) words instead of `out` (as
+// gemv_allreduce_kernel). kSwiGLU: x is gate|up [2K], as stage_x.
+constexpr int kSplitKMin = 2048;
+constexpr int kSkRows = 8;
+
+template <typename T, bool kSwiGLU, bool kAR>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_splitk_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                                      T* __restrict__ out, int64_t N, int K,
+                                                                      const __grid_constant__ ArPeers ar) {
+  extern __shared__ uint4 xs[];
+  __shared__ float part[kGemvWarps][kSkRows];
+  __shared__ float res[kSkRows];
+  const int kc = K / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t)blockIdx.x * kSkRows;
+  pdl_launch();
+  pdl_wait();
+  stage_x<T, kSwiGLU>(xs, x, K);
+  __syncthreads();
+  const int c0 = kc * warp / kGemvWarps, c1 = kc * (warp + 1) / kGemvWarps;
+  const uint4* wr[kSkRows];
+  float acc[kSkRows];
+#pragma unroll
+  for (int j = 0; j < kSkRows; ++j) {
+    const int64_t row = row0 + j;
+    wr[j] = reinterpret_cast<const uint4*>(w + (row < N ? row : N - 1) * (int64_t)K);
+    acc[j] = 0.f;
+  }
+#pragma unroll 2
+  for (int c = c0 + lane; c < c1; c += 32) {
+    const uint4 b = xs[c];
+#pragma unroll
+    for (int j = 0; j < kSkRows; ++j) {
+      const uint4 a = __ldg(wr[j] + c);
+      acc[j] = dot2(a.x, b.x, acc[j], (T*)nullptr);
+      acc[j] = dot2(a.y, b.y, acc[j], (T*)nullptr);
+      acc[j] = dot2(a.z, b.z, acc[j], (T*)nullptr);
+      acc[j] = dot2(a.w, b.w, acc[j], (T*)nullptr);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kSkRows; ++j) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+    if (lane == 0) part[warp][j] = acc[j];
+  }
+  __syncthreads();
+  const int nb = N - row0 < kSkRows ? (int)(N - row0) : kSkRows;
+  if (threadIdx.x < kSkRows) {
+    float sum = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kGemvWarps; ++ww) sum += part[ww][threadIdx.x];
+    if (!kAR && (int)threadIdx.x < nb) out[row0 + threadIdx.x] = from_f32<T>(sum);
+    res[threadIdx.x] = sum;
+  }
+  if constexpr (kAR) {
+    __syncthreads();
+    const unsigned int s = *ar.seq;
+    const uint64_t ep = (uint64_t)(s + 1u) << 32;
+    const int64_t slot_off = (int64_t)(s % kArSlots) * ar.world * ar.rows + (int64_t)ar.rank * ar.rows;
+    for (int idx = threadIdx.x; idx < ar.world * kSkRows; idx += blockDim.x) {
+      const int p = idx / kSkRows, i = idx - p * kSkRows;
+      if (i < nb) st_sys_u64(ar.data[p] + slot_off + row0 + i, ep | __float_as_uint(res[i]));
+    }
+  }
+}
+
+}  // namespace tc

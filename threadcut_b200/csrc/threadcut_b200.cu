@@ -1358,6 +1358,31 @@ cudaError_t launch_gemv_t(int rpw, bool swiglu, unsigned grid, size_t smem, cuda
   return launch_gemv_r<T, false, 1>(grid, smem, st, x, w, out, n, k);
 }
 
+// Input length from which the projections split K over the warps of a CTA; TC_GEMV_SPLITK_MIN
+// overrides the default (a measurement switch).
+int splitk_min() {
+  static const int v = [] {
+    const char* e = std::getenv("TC_GEMV_SPLITK_MIN");
+    return e != nullptr ? std::atoi(e) : kSplitKMin;
+  }();
+  return v;
+}
+
+template <typename T>
+cudaError_t launch_splitk_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
+                            const void* w, void* out, int64_t n, int k) {
+  const dim3 grid((unsigned)((n + kSkRows - 1) / kSkRows));
+  const size_t smem = (size_t)k * 2;
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  T* op = static_cast<T*>(out);
+  if (ar_mode)
+    return swiglu ? launch_pdl(gemv_splitk_kernel<T, true, true>, grid, dim3(kGemvWarps * 32), smem, st, xp, wp, op, n, k, ar)
+                  : launch_pdl(gemv_splitk_kernel<T, false, true>, grid, dim3(kGemvWarps * 32), smem, st, xp, wp, op, n, k, ar);
+  return swiglu ? launch_pdl(gemv_splitk_kernel<T, true, false>, grid, dim3(kGemvWarps * 32), smem, st, xp, wp, op, n, k, ar)
+                : launch_pdl(gemv_splitk_kernel<T, false, false>, grid, dim3(kGemvWarps * 32), smem, st, xp, wp, op, n, k, ar);
+}
+
 int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtype, void* stream, bool swiglu) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
   if (n < 0 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
@@ -1365,6 +1390,13 @@ int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtyp
   if (x == nullptr || w == nullptr || out == nullptr) return TC_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k >= splitk_min()) {  // long rows: K split over the warps of a CTA (see gemv_splitk_kernel)
+    ArPeers none;
+    std::memset(&none, 0, sizeof(none));
+    const cudaError_t e = dtype == TC_BF16 ? launch_splitk_t<__nv_bfloat16>(swiglu, false, none, st, x, w, out, n, k)
+                                           : launch_splitk_t<__half>(swiglu, false, none, st, x, w, out, n, k);
+    return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  }
   const int sms = sm_count(current_device());
   // rows per warp: 4 when there are enough rows for two CTAs of 4-row warps on every SM, 2 for one,
   // else 1 (more warps stream, each with fewer rows in flight)
@@ -1462,6 +1494,11 @@ int run_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* con
   ar.rank = rank;
   ar.rows = n;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k >= splitk_min()) {  // long rows: K split over the warps of a CTA
+    const cudaError_t e = dtype == TC_BF16 ? launch_splitk_t<__nv_bfloat16>(swiglu, true, ar, st, x, w, nullptr, n, k)
+                                           : launch_splitk_t<__half>(swiglu, true, ar, st, x, w, nullptr, n, k);
+    return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  }
   const dim3 grid((unsigned)((n + kArRows - 1) / kArRows));
   const size_t smem = (size_t)k * 2;
   cudaError_t e;

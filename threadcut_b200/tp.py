@@ -38,7 +38,7 @@ from ._lib import check, dtype_code, lib, require_cuda, stream_ptr
 from .flash_decode import decode_attention_append
 from .sharded import head_shard
 
-__all__ = ["TPDecoder"]
+__all__ = ["TPDecoder", "accelerate"]
 
 
 def _add_rmsnorm(h, delta, w, out, eps):
@@ -324,6 +324,16 @@ class TPDecoder:
             torch.cuda.synchronize(self.dev)
         return graph, out
 
+    def step_logits(self, token, pos):
+        """The next-token logits in the model dtype, [1, vocab] (as the HF model's lm_head returns
+        them), of `token` at `pos`; appends the token's row like step."""
+        part = _gemv(self._final_hidden(token, pos), self.lm_head)
+        if self.world == 1:
+            return part
+        parts = [torch.empty_like(part) for _ in range(self.world)]
+        dist.all_gather(parts, part, group=self.group)
+        return torch.cat(parts, dim=1)
+
     def logits(self, token, pos):
         """The full next-token logits (fp32 [vocab]) of `token` at `pos`, for checks: the step's
         arithmetic with the vocabulary slices all-gathered. Appends the token's row like step."""
@@ -333,3 +343,63 @@ class TPDecoder:
         parts = [torch.empty_like(part) for _ in range(self.world)]
         dist.all_gather(parts, part, group=self.group)
         return torch.cat(parts)
+
+
+def _fusable(cache, dec):
+    """True when `cache` is this package's contiguous cache of the model `dec` decodes: every layer a
+    GrowingLayer holding rows, with the fused append on, in the model's dtype, on its device, with
+    the local head count."""
+    layers = getattr(cache, "layers", None)
+    if not layers or len(layers) != len(dec.layers_w):
+        return False
+    for ly in layers:
+        if not (isinstance(ly, _kv.GrowingLayer) and ly.fuse_append and ly.is_initialized
+                and getattr(ly, "kbuf", None) is not None and ly.n > 0):
+            return False
+        kb = ly.kbuf
+        if kb.dtype != dec.dtype or kb.device != dec.dev or kb.shape[0] != 1 or kb.shape[1] != dec.h1 - dec.h0:
+            return False
+    return True
+
+
+def accelerate(model, device=None):
+    """Route the one-token decode steps of a one-GPU Qwen3 model through the fused step of this
+    module, behind the model's own call: after accelerate(model), model(input_ids=[[t]],
+    past_key_values=cache, use_cache=True) over a cache of this package (kv.new_cache with the
+    threadcut attention: GrowingLayers with the fused append, holding rows) returns HF's output type
+    with `.logits` [1, 1, vocab] computed by TPDecoder at world 1 (about 9 launches per layer instead
+    of transformers' ~50), appending the token's K/V row to the same cache. Every other call (a
+    prefill chunk, another cache, extra arguments) goes to the model's own forward. The reference's
+    engine (threadcut/engine.py:66-73, 88-95) makes exactly such calls, so it runs unchanged on the
+    fused step. Returns the TPDecoder doing the work (it shares the model's weights where no copy is
+    needed: the q|k|v and gate|up rows are concatenated copies). bf16/fp16 models only."""
+    from transformers.modeling_outputs import CausalLMOutputWithPast
+    dev = torch.device(device) if device is not None else next(model.parameters()).device
+    dec = TPDecoder(model, dev, world=1, rank=0)
+    if dec.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("accelerate: the fused step needs a bf16 or fp16 model")
+    inner = model.forward
+
+    def forward(*args, **kwargs):
+        ids = kwargs.get("input_ids")
+        cache = kwargs.get("past_key_values")
+        extra = set(kwargs) - {"input_ids", "past_key_values", "use_cache", "logits_to_keep"}
+        if (not args and not extra and ids is not None and ids.dim() == 2 and tuple(ids.shape) == (1, 1)
+                and kwargs.get("use_cache", True) is not False and _fusable(cache, dec)):
+            pos = cache.get_seq_length()
+            dec.layers = cache.layers
+            logits = dec.step_logits(ids.view(1), pos)
+            return CausalLMOutputWithPast(logits=logits.view(1, 1, -1), past_key_values=cache)
+        return inner(*args, **kwargs)
+
+    model.forward = forward
+    model._threadcut_fused_step = (dec, inner)
+    return dec
+
+
+def restore(model):
+    """Undo accelerate(model)."""
+    saved = getattr(model, "_threadcut_fused_step", None)
+    if saved is not None:
+        model.forward = saved[1]
+        del model._threadcut_fused_step
