@@ -302,12 +302,13 @@ namespace tc {
 
 // ---- split-K GEMV for long input rows (K >= kSplitKMin): a CTA owns kSkRows output rows and its 8
 // warps split K into 8 contiguous slices, so every lane keeps kSkRows loads per column step in
-// flight however few rows the matrix has (a row per warp over all of K left the 2560 x 9728 down
-// projection at 40 % of HBM). Per row: each lane sums its columns in order, the lanes by xor
+// flight however few rows the matrix has. Measured (bf16, graph-timed, 4 distinct weights): the
+// 2560 x 9728 down projection 21.8 -> 12.7 us, 2560 x 4096 6.12 -> 5.92 us; at K = 2560 the rows
+// per warp of gemv_kernel are faster (19456 x 2560: 22.4 vs 37.0 us), hence the threshold. Per row: each lane sums its columns in order, the lanes by xor
 // shuffles, the warps' sums in warp order through shared memory; fp32 throughout, one rounding.
 // kAR: the rows go to every rank's region as (value, epoch) words instead of `out` (as
 // gemv_allreduce_kernel). kSwiGLU: x is gate|up [2K], as stage_x.
-constexpr int kSplitKMin = 2048;
+constexpr int kSplitKMin = 4096;
 constexpr int kSkRows = 8;
 
 template <typename T, bool kSwiGLU, bool kAR>
