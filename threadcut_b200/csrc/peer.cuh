@@ -176,12 +176,13 @@ namespace tc {
 // merge_partials_kernel (the merge of threadcut/flash_decode.py:68-69 over ranks).
 //
 // Region of each rank (zeroed at creation): [0, 256) control: word 0 `seq` (completed gathers of
-// this rank), word 1 the count of this launch's finished CTAs, words 8 + 8*slot + src: the epoch
-// (gather number + 1) of src's data in slot; then the data, [2 slots][world][gather_src_stride] fp32.
+// this rank), word 1 the count of this launch's finished CTAs, words 8 + 8*slot + src: arrivals of
+// src's pusher CTAs in slot (kGmPushers per gather, never reset: gather s is complete when the count
+// reaches (s / 2 + 1) * kGmPushers); then the data, [2 slots][world][gather_src_stride] fp32.
 // Gather s uses slot s % 2: a rank pushes gather s + 2 into slot s % 2 of rank r only after its own
 // gather s + 1 received r's data, which r pushed after it finished gather s (its reads of slot s % 2).
 constexpr int kGmThreads = 256;
-constexpr int kGmMergers = 64;
+constexpr int kGmPushers = 8;   // CTAs pushing to one destination rank, each a slice of the data
 
 // Floats per (slot, source) of a gather region: o [rows][d] then lse [rows], rounded up to a
 // multiple of 4 floats so that every source's block starts 16-byte aligned (float4 stores).
@@ -197,93 +198,112 @@ struct GatherPeers {
   int64_t slot_stride;               // floats per slot: world * src_stride
 };
 
-__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void red_release_sys_add_u32(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
-// grid.x = (world - 1) pushers + kGmMergers mergers. Pusher i copies this rank's partials to rank
-// (rank + 1 + i) % world and then raises that rank's flag for this rank; merger m waits for every
-// other rank's flag in this rank's region and merges its share of the rows. The last CTA to finish
-// advances seq. rows * d % 4 == 0.
+// grid.x = (world - 1) * kGmPushers pushers + the mergers. Pusher CTA i copies slice i % kGmPushers
+// of this rank's partials (o, then lse) to rank (rank + 1 + i / kGmPushers) % world and counts
+// itself in there; each merger thread waits until every other rank's pushers have arrived in this
+// rank's region, then merges one float4 of one row (its lse loads for all ranks and o loads in one
+// batch). The last CTA to finish advances seq. rows * d % 4 == 0.
 template <typename T>
 __global__ void __launch_bounds__(kGmThreads) gather_merge_kernel(const float* __restrict__ o_local,
                                                                   const float* __restrict__ lse_local,
                                                                   T* __restrict__ out, float* __restrict__ lse_out,
                                                                   int64_t rows, int d, int64_t out_stride,
                                                                   const __grid_constant__ GatherPeers gp) {
-  __shared__ int s_ok;
   pdl_launch();
   pdl_wait();
   unsigned int* my_ctrl = gp.ctrl[gp.rank];
   const unsigned int s = my_ctrl[0];
-  const unsigned int slot = s & 1u, ep = s + 1u;
-  const int pushers = gp.world - 1;
+  const unsigned int slot = s & 1u;
+  const int pushers = (gp.world - 1) * kGmPushers;
   if ((int)blockIdx.x < pushers) {
-    const int p = (gp.rank + 1 + (int)blockIdx.x) % gp.world;
+    const int p = (gp.rank + 1 + (int)blockIdx.x / kGmPushers) % gp.world;
+    const int part = (int)blockIdx.x % kGmPushers;
     float* dst = gp.data[p] + slot * gp.slot_stride + (int64_t)gp.rank * gp.src_stride;
-    const int64_t n4 = rows * d / 4;
+    // the source block as float4s: o (rows * d / 4), then lse padded to the stride
+    const int64_t n4 = rows * d / 4, nl = rows;
+    const int64_t lo = n4 * part / kGmPushers, hi = n4 * (part + 1) / kGmPushers;
     const float4* src4 = reinterpret_cast<const float4*>(o_local);
     float4* dst4 = reinterpret_cast<float4*>(dst);
-    for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) dst4[i] = src4[i];
-    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) dst[rows * d + i] = lse_local[i];
-    __syncthreads();  // every thread's stores precede the flag below
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst4[i] = src4[i];
+    const int64_t l0 = nl * part / kGmPushers, l1 = nl * (part + 1) / kGmPushers;
+    for (int64_t i = l0 + threadIdx.x; i < l1; i += blockDim.x) dst[rows * d + i] = lse_local[i];
+    __syncthreads();  // every thread's stores precede the arrival below
     if (threadIdx.x == 0) {
       __threadfence_system();
-      st_release_sys_u32(gp.ctrl[p] + 8 + 8 * slot + gp.rank, ep);
+      red_release_sys_add_u32(gp.ctrl[p] + 8 + 8 * slot + gp.rank, 1u);
     }
   } else {
-    const int m = (int)blockIdx.x - pushers, nm = (int)gridDim.x - pushers;
+    const int64_t m = (int64_t)blockIdx.x - pushers;
+    const int64_t t = m * blockDim.x + threadIdx.x;  // (row, float4 column) of this thread
+    const int q4 = d / 4;
+    const unsigned int need = (s / 2u + 1u) * (unsigned int)kGmPushers;
     if (threadIdx.x == 0) {
-      int ok = 1;
       for (int r = 0; r < gp.world; ++r) {
         if (r == gp.rank) continue;
         uint32_t spin = 0;
-        while (ld_acquire_sys_u32(my_ctrl + 8 + 8 * slot + r) != ep) {
+        while (ld_acquire_sys_u32(my_ctrl + 8 + 8 * slot + r) < need) {
           if (++spin >= kSpinLimit / 64) {
             raise_error(TC_DEVERR_PEER_TIMEOUT);
-            ok = 0;
             break;
           }
           __nanosleep(64);
         }
       }
-      s_ok = ok;
     }
     __syncthreads();
-    const float* mine = gp.data[gp.rank] + slot * gp.slot_stride;
-    const int64_t r0 = rows * m / nm, r1 = rows * (m + 1) / nm;
-    for (int64_t row = r0; row < r1; ++row) {
-      // part r: this rank's own partial from its inputs, the others' from its region
-      float M = -INFINITY;
-      for (int r = 0; r < gp.world; ++r) {
-        const float l = r == gp.rank ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
-        M = fmaxf(M, l);
-      }
-      float L = 0.f;
-      if (M != -INFINITY)
-        for (int r = 0; r < gp.world; ++r) {
-          const float l = r == gp.rank ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
-          L += __expf(l - M);
+    if (t < rows * q4) {
+      const int64_t row = t / q4;
+      const int c4 = (int)(t - row * q4);
+      const float* mine = gp.data[gp.rank] + slot * gp.slot_stride;
+      float l[kArMaxWorld];
+      float4 x[kArMaxWorld];
+#pragma unroll
+      for (int r = 0; r < kArMaxWorld; ++r) {
+        if (r < gp.world) {
+          const bool own = r == gp.rank;
+          const float* src = mine + (int64_t)r * gp.src_stride;
+          l[r] = own ? lse_local[row] : __ldcg(src + rows * d + row);
+          x[r] = own ? reinterpret_cast<const float4*>(o_local)[row * q4 + c4]
+                     : __ldcg(reinterpret_cast<const float4*>(src) + row * q4 + c4);
         }
-      for (int dd = threadIdx.x; dd < d; dd += blockDim.x) {
-        float o = 0.f;
-        if (M != -INFINITY)
-          for (int r = 0; r < gp.world; ++r) {
-            const bool own = r == gp.rank;
-            const float l = own ? lse_local[row] : __ldcg(mine + (int64_t)r * gp.src_stride + rows * d + row);
-            const float x = own ? o_local[row * d + dd] : __ldcg(mine + (int64_t)r * gp.src_stride + row * d + dd);
-            o += __expf(l - M) * x;
-          }
-        out[row * out_stride + dd] = from_f32<T>(L > 0.f ? o / L : 0.f);
       }
-      if (lse_out != nullptr && threadIdx.x == 0) lse_out[row] = L > 0.f ? M + __logf(L) : -INFINITY;
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kArMaxWorld; ++r)
+        if (r < gp.world) M = fmaxf(M, l[r]);
+      float L = 0.f;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kArMaxWorld; ++r)
+          if (r < gp.world) L += __expf(l[r] - M);
+#pragma unroll
+        for (int r = 0; r < kArMaxWorld; ++r) {
+          if (r < gp.world) {
+            const float wgt = __expf(l[r] - M);
+            o.x += wgt * x[r].x;
+            o.y += wgt * x[r].y;
+            o.z += wgt * x[r].z;
+            o.w += wgt * x[r].w;
+          }
+        }
+      }
+      T* orow = out + row * out_stride + 4 * c4;
+      orow[0] = from_f32<T>(L > 0.f ? o.x / L : 0.f);
+      orow[1] = from_f32<T>(L > 0.f ? o.y / L : 0.f);
+      orow[2] = from_f32<T>(L > 0.f ? o.z / L : 0.f);
+      orow[3] = from_f32<T>(L > 0.f ? o.w / L : 0.f);
+      if (lse_out != nullptr && c4 == 0) lse_out[row] = L > 0.f ? M + __logf(L) : -INFINITY;
     }
-    (void)s_ok;
   }
   // the last CTA of this launch advances seq (every CTA read it above)
   __syncthreads();

@@ -1580,8 +1580,8 @@ int tc_peer_gather_merge(const float* o_local, const float* lse_local, void* out
   gp.src_stride = gather_src_stride(rows, d);
   gp.slot_stride = (int64_t)world * gp.src_stride;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int mergers = rows < kGmMergers ? (int)rows : kGmMergers;
-  const dim3 grid((unsigned)(world - 1 + mergers));
+  const int64_t mergers = (rows * (d / 4) + kGmThreads - 1) / kGmThreads;  // one thread per float4 of out
+  const dim3 grid((unsigned)((world - 1) * kGmPushers + mergers));
   cudaError_t e;
   if (dtype == TC_BF16)
     e = launch_pdl(gather_merge_kernel<__nv_bfloat16>, grid, dim3(kGmThreads), 0, st, o_local, lse_local,
