@@ -15,6 +15,7 @@
 #include "prefill_attn.cuh"
 #include "layer_ops.cuh"
 #include "peer.cuh"
+#include "gemv_stream.cuh"
 
 using namespace tc;
 
@@ -1368,6 +1369,33 @@ int splitk_min() {
   return v;
 }
 
+// The streaming GEMV (gemv_stream_kernel) unless TC_GEMV_STREAM=0 (a measurement switch: the
+// register-streaming kernels below instead).
+bool gemv_stream_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TC_GEMV_STREAM");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename T>
+cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
+                            const void* w, void* out, int64_t n, int k, int sms, int dev) {
+  const GsPlan g = gs_plan(k);
+  int64_t c = n < sms ? n : sms;
+  if (ar_mode && (n + c - 1) / c > kGsMaxRowsPerCta) c = (n + kGsMaxRowsPerCta - 1) / kGsMaxRowsPerCta;
+  const int smem = g.x_bytes + g.nstages * g.stage_bytes;
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  T* op = static_cast<T*>(out);
+  auto fn = ar_mode ? (swiglu ? gemv_stream_kernel<T, true, true> : gemv_stream_kernel<T, false, true>)
+                    : (swiglu ? gemv_stream_kernel<T, true, false> : gemv_stream_kernel<T, false, false>);
+  const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar);
+}
+
 template <typename T>
 cudaError_t launch_splitk_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
                             const void* w, void* out, int64_t n, int k) {
@@ -1390,6 +1418,15 @@ int run_gemv(const void* x, const void* w, void* out, int64_t n, int k, int dtyp
   if (x == nullptr || w == nullptr || out == nullptr) return TC_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return TC_ERR_ALIGN;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (gemv_stream_enabled()) {
+    ArPeers none;
+    std::memset(&none, 0, sizeof(none));
+    const int dev = current_device();
+    const cudaError_t e =
+        dtype == TC_BF16 ? launch_stream_t<__nv_bfloat16>(swiglu, false, none, st, x, w, out, n, k, sm_count(dev), dev)
+                         : launch_stream_t<__half>(swiglu, false, none, st, x, w, out, n, k, sm_count(dev), dev);
+    return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  }
   if (k >= splitk_min()) {  // long rows: K split over the warps of a CTA (see gemv_splitk_kernel)
     ArPeers none;
     std::memset(&none, 0, sizeof(none));
@@ -1494,6 +1531,13 @@ int run_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* con
   ar.rank = rank;
   ar.rows = n;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (gemv_stream_enabled()) {
+    const int dev = current_device();
+    const cudaError_t e =
+        dtype == TC_BF16 ? launch_stream_t<__nv_bfloat16>(swiglu, true, ar, st, x, w, nullptr, n, k, sm_count(dev), dev)
+                         : launch_stream_t<__half>(swiglu, true, ar, st, x, w, nullptr, n, k, sm_count(dev), dev);
+    return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+  }
   if (k >= splitk_min()) {  // long rows: K split over the warps of a CTA
     const cudaError_t e = dtype == TC_BF16 ? launch_splitk_t<__nv_bfloat16>(swiglu, true, ar, st, x, w, nullptr, n, k)
                                            : launch_splitk_t<__half>(swiglu, true, ar, st, x, w, nullptr, n, k);
