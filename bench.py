@@ -260,15 +260,19 @@ def time_graph(graph, steps, warmup, dist):
 def time_e2e(qs, ks, vs, steps, warmup, dist, dev, world=1):
     """Public-API path: pinned host queries -> device, 36 decode calls, outputs -> host. One GPU:
     decode_attention per layer. N GPUs (sequence shards): decode_attention_partial per layer over
-    the rank's token slice, the step's partials all-gathered over the ranks and merged by
-    merge_partials, the merged outputs read back."""
-    from threadcut_b200.flash_decode import decode_attention, decode_attention_partial, merge_partials
+    the rank's token slice, then peer.GatherMerge (the step's partials pushed to every rank and
+    merged in one launch), the merged outputs read back."""
+    from threadcut_b200.flash_decode import decode_attention, decode_attention_partial
     host_q = torch.stack([q.cpu() for q in qs]).pin_memory()
     dq = torch.empty_like(host_q, device=dev)
     host_out = torch.empty(host_q.shape, dtype=host_q.dtype).pin_memory()
     layers, hl = host_q.shape[0], host_q.shape[1]
-    go = torch.empty((world, layers * hl * 4, 128), dtype=torch.float32, device=dev)
-    gl = torch.empty((world, layers * hl * 4), dtype=torch.float32, device=dev)
+    rows = layers * hl * 4
+    gm = None
+    if world > 1:
+        from threadcut_b200.peer import GatherMerge
+        gm = GatherMerge(rows, 128, dev)
+    merged = torch.empty((rows, 128), dtype=torch.bfloat16, device=dev)
 
     n = ks[0].shape[1]
 
@@ -280,9 +284,8 @@ def time_e2e(qs, ks, vs, steps, warmup, dist, dev, world=1):
         else:
             parts = [decode_attention_partial(dq[i], ks[i], vs[i], workloads.SCALE, stable_rows=n - 1)
                      for i in range(layers)]
-            dist.all_gather_into_tensor(go, torch.stack([o for o, _ in parts]).view(-1))
-            dist.all_gather_into_tensor(gl, torch.stack([lse for _, lse in parts]).view(-1))
-            outs, _ = merge_partials(go, gl, torch.bfloat16)
+            outs = gm(torch.stack([o for o, _ in parts]).view(rows, 128),
+                      torch.stack([lse for _, lse in parts]).view(rows), merged)
         host_out.copy_(outs.view(host_out.shape), non_blocking=True)
 
     for _ in range(warmup):
@@ -295,6 +298,8 @@ def time_e2e(qs, ks, vs, steps, warmup, dist, dev, world=1):
     e1.record()
     e1.synchronize()
     barrier(dist)
+    if gm is not None:
+        gm.close()
     return e0.elapsed_time(e1) / steps, host_q.numel() * host_q.element_size(), host_out.numel() * 2
 
 
@@ -1145,7 +1150,7 @@ def run_ours(args, rank, local, world, dist):
                 "d2h_bytes_per_step": d2h,
                 "api": "threadcut_b200.flash_decode.decode_attention per layer" if world == 1 else
                        "threadcut_b200.flash_decode.decode_attention_partial per layer over the rank's token slice, "
-                       "torch.distributed all-gathers of the step's partials, flash_decode.merge_partials"},
+                       "then threadcut_b200.peer.GatherMerge (the step's partials pushed to every rank and merged)"},
         "combine": None if world == 1 else {
             "us_per_layer_without": round(nocombine_ms * 1000.0 / LAYERS, 3),
             "us_per_layer_with": round(us_layer_rank, 3),

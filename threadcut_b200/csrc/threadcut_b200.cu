@@ -1391,7 +1391,8 @@ cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaSt
   T* op = static_cast<T*>(out);
   auto fn = ar_mode ? (swiglu ? gemv_stream_kernel<T, true, true> : gemv_stream_kernel<T, false, true>)
                     : (swiglu ? gemv_stream_kernel<T, true, false> : gemv_stream_kernel<T, false, false>);
-  const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), smem, dev);
+  // the opt-in is set once per (kernel, device) by set_smem: ask for the budget every plan fits in
+  const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), kGsSmemBudget, dev);
   if (e != cudaSuccess) return e;
   return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar);
 }
