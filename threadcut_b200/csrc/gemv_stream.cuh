@@ -7,9 +7,10 @@
 // whole matrix for the tensor-parallel shards at 8 GPUs) are in shared memory by the time the
 // previous kernel finishes; x (the previous kernel's output) is read after the wait.
 //
-// Rows: each stage holds rs = max(1, 16 KB / row bytes) whole rows; consumer warp j % 8 takes stage
-// chunk j, each of its lanes sums the row's 16-byte columns lane, lane + 32, ... in order and the
-// lanes reduce by xor shuffles: the same order as gemv_kernel with one row per warp, so the result
+// Rows: each stage holds rs = max(1, 16 KB / row bytes) whole rows; every consumer warp waits for
+// every stage and takes the stage's rows whose index in the CTA's block is its warp number modulo 8
+// (so few rows per CTA still spread over all warps), each lane summing the row's 16-byte columns
+// lane, lane + 32, ... in order and the lanes reducing by xor shuffles: the same order as gemv_kernel with one row per warp, so the result
 // bits are those of tc_gemv's single-row pass. Epilogues: the row rounded to T into `out`, or (kAR)
 // the fp32 row as a (value, epoch) word into every rank's region (as gemv_allreduce_kernel).
 // kSwiGLU: x is gate|up [2K] and the staged input is the SwiGLU activation (stage_x).
@@ -32,13 +33,16 @@ struct GsPlan {
   int x_bytes;     // K * 2 rounded up to 128
 };
 
-__host__ __device__ __forceinline__ GsPlan gs_plan(int K) {
+// budget: bytes of shared memory for x and the ring (at most kGsSmemBudget); a smaller budget lets
+// two CTAs of consecutive projections share an SM, the next one loading while this one runs.
+__host__ __device__ __forceinline__ GsPlan gs_plan(int K, int budget = kGsSmemBudget) {
   GsPlan g;
   const int row = K * 2;
   g.rs = row >= 16384 ? 1 : 16384 / row;
   g.stage_bytes = g.rs * row;
   g.x_bytes = (row + 127) / 128 * 128;
-  int ns = (kGsSmemBudget - g.x_bytes - 1024) / g.stage_bytes;
+  int ns = (budget - g.x_bytes - 1024) / g.stage_bytes;
+  if (ns < 1) ns = 1;
   g.nstages = ns > kGsMaxStages ? kGsMaxStages : ns;
   return g;
 }
@@ -51,11 +55,11 @@ __device__ __forceinline__ void consumer_bar() {
 template <typename T, bool kSwiGLU, bool kAR>
 __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                     T* __restrict__ out, int64_t N, int K,
-                                                                    const __grid_constant__ ArPeers ar) {
+                                                                    const __grid_constant__ ArPeers ar,
+                                                                    const GsPlan g) {
   extern __shared__ __align__(128) uint8_t gs_smem[];
   __shared__ uint64_t full[kGsMaxStages], empty[kGsMaxStages];
   __shared__ float res[kAR ? kGsMaxRowsPerCta : 1];
-  const GsPlan g = gs_plan(K);
   uint4* xs = reinterpret_cast<uint4*>(gs_smem);
   uint8_t* ring = gs_smem + g.x_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -66,7 +70,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
   if (threadIdx.x == 0) {
     for (int s = 0; s < g.nstages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kGsConsumers);  // every consumer warp releases every stage
     }
     fence_mbar_init();
   }
@@ -124,12 +128,14 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
     }
     consumer_bar();
     const int kc = K / 8;
-    for (int j = warp; j < nchunks; j += kGsConsumers) {
+    for (int j = 0; j < nchunks; ++j) {
       const int s = j % g.nstages;
       if (!mbar_wait(&full[s], (j / g.nstages) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
       const uint4* st = reinterpret_cast<const uint4*>(ring + s * g.stage_bytes);
       const int rows = nrows - j * g.rs < g.rs ? nrows - j * g.rs : g.rs;
-      for (int rr = 0; rr < rows; ++rr) {
+      // this warp's rows of the stage: block rows j * rs + rr with (j * rs + rr) % 8 == warp
+      const int first = ((warp - (j * g.rs) % kGsConsumers) + kGsConsumers) % kGsConsumers;
+      for (int rr = first; rr < rows; rr += kGsConsumers) {
         const uint4* wr = st + (int64_t)rr * kc;
         float acc = 0.f;
 #pragma unroll 8

@@ -1379,10 +1379,21 @@ bool gemv_stream_enabled() {
   return on;
 }
 
+// Shared memory of one streaming-GEMV CTA in KB (TC_GEMV_STREAM_KB, a measurement switch; default
+// the full budget: one CTA per SM).
+int gemv_stream_budget() {
+  static const int b = [] {
+    const char* e = std::getenv("TC_GEMV_STREAM_KB");
+    const int kb = e != nullptr ? std::atoi(e) : 0;
+    return kb > 0 && kb * 1024 < kGsSmemBudget ? kb * 1024 : kGsSmemBudget;
+  }();
+  return b;
+}
+
 template <typename T>
 cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
                             const void* w, void* out, int64_t n, int k, int sms, int dev) {
-  const GsPlan g = gs_plan(k);
+  const GsPlan g = gs_plan(k, gemv_stream_budget());
   int64_t c = n < sms ? n : sms;
   if (ar_mode && (n + c - 1) / c > kGsMaxRowsPerCta) c = (n + kGsMaxRowsPerCta - 1) / kGsMaxRowsPerCta;
   const int smem = g.x_bytes + g.nstages * g.stage_bytes;
@@ -1394,7 +1405,7 @@ cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaSt
   // the opt-in is set once per (kernel, device) by set_smem: ask for the budget every plan fits in
   const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), kGsSmemBudget, dev);
   if (e != cudaSuccess) return e;
-  return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar);
+  return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar, g);
 }
 
 template <typename T>
