@@ -705,7 +705,66 @@ def time_cfg5_step(steps, warmup, dev):
     return out
 
 
-def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None):
+def kernel_family(name):
+    """Short name of a device activity in a launch list: this library's kernels by name and
+    template flags (the dtype dropped), everything else by its library."""
+    base = name.split("(")[0].replace("void ", "").strip()
+    if base.startswith("tc::"):
+        return base.replace("__nv_bfloat16, ", "").replace("__nv_bfloat16", "").replace("<>", "")
+    if "nccl" in base:
+        return "nccl"
+    if base.startswith("Memcpy") or base.startswith("Memset"):
+        return base.split(" ")[0].lower()
+    return "torch (argmax, embedding, cos/sin)"
+
+
+def serial_launches(dec, tok, n, dev, rank, dist, timed, steps=3):
+    """Launch list of the config-5 step (`dec`) with programmatic dependent launch off
+    (tc_set_pdl(0) while capturing its graph), so each kernel runs alone and the per-kernel device
+    times add up to the step: per kernel family, launches and µs per step and the share, recorded
+    by torch.profiler's CUDA activity on rank 0 (every rank replays: the sums need all of them).
+    Also the replay time of that graph (max over ranks), against which the overlapped graph's time
+    shows what the overlap saves."""
+    from torch.profiler import ProfilerActivity, profile
+    from threadcut_b200._lib import lib
+    prev = lib().tc_set_pdl(0)
+    try:
+        graph, out = dec.capture(tok, n)
+    finally:
+        lib().tc_set_pdl(prev)
+
+    def replay():
+        graph.replay()
+        int(out)
+
+    serial_ms = timed(replay)
+    barrier(dist)
+    prof = None
+    if rank == 0:
+        prof = profile(activities=[ProfilerActivity.CUDA])
+        prof.start()
+    for _ in range(steps):
+        replay()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    res = {"graph_ms": round(serial_ms, 3)}
+    if prof is not None:
+        prof.stop()
+        rows = {}
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time_total > 0:
+                r = rows.setdefault(kernel_family(ev.name), [0, 0.0])
+                r[0] += 1
+                r[1] += ev.device_time_total
+        total = sum(r[1] for r in rows.values()) or 1.0
+        res["kernel_us_per_step"] = round(total / steps, 1)
+        res["kernels"] = [[k, round(c / steps, 1), round(us / steps, 1), round(us / total, 4)]
+                          for k, (c, us) in sorted(rows.items(), key=lambda kv: -kv[1][1])]
+    del graph
+    return res
+
+
+def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None, summary=True):
     """Config 5 over `world` GPUs: threadcut_b200.tp.TPDecoder (rank r holds KV heads
     head_shard(8, r, world), their query heads, 1/world of the MLP and of the vocabulary; two
     all-reduces per layer) decoding one greedy token of random-init Qwen3-4B over the 131,072-token
@@ -714,7 +773,8 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None):
     the same way (the same seeded K/V on every rank), and the decoder's token is compared with it.
     Each timed step is the token's forward plus the next token read back to the host; the appended
     row is cropped after each step so every step decodes at the same length. Eager and replayed from
-    a CUDA graph (the all-reduces inside it). Returns a dict (times max over ranks)."""
+    a CUDA graph (the all-reduces inside it). Returns a dict (times max over ranks), with
+    `launches_serial` (serial_launches) when `summary`."""
     from transformers import AutoModelForCausalLM
     from threadcut_b200.kv import new_cache, splice as kv_splice
     from threadcut_b200.match import Split
@@ -824,10 +884,12 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None):
             top1_ok = top1_ok and -max_over_ranks(-ok, dist) == 1.0
             del graph
             dec.use_peer_sums = True
+        serial = serial_launches(dec, tok, n, dev, rank, dist, timed) if (cap and summary) else None
     dec.close()
     del dec
     torch.cuda.empty_cache()
     return {"eager_ms": eager_ms, "graph_ms": graph_ms, "nccl_graph_ms": nccl_ms, "splice_ms": splice_ms,
+            "launches_serial": serial,
             "bytes": shard_bytes + LAYERS * (4096 // world * n + 16384 // world),
             "top1_ok": bool(top1_ok and (graph_tok is None or graph_tok == ref_top1)), "token": step_tok,
             "sdpa_token": ref_top1, "logit_corr": round(corr, 6),

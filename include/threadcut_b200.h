@@ -65,6 +65,13 @@ int tc_abi_version(void);
  * synchronises the device. Returns the bits, or -1 if the CUDA calls failed. */
 int tc_device_errors(int clear);
 
+/* Programmatic dependent launch for this process's later launches (on by default, or off when
+ * the environment holds TC_PDL=0): on, a kernel starts while its predecessor in the stream ends
+ * and waits for it before reading its results; off, kernels run one after another, so per-kernel
+ * device times add up to a step (for launch lists). A CUDA graph keeps the mode it was captured
+ * with. Returns the previous mode (1 on, 0 off). No reference counterpart (launch tuning). */
+int tc_set_pdl(int on);
+
 /* ======================================================================================
  * Decode attention (one query token per sequence, grouped-query heads folded per KV head).
  *
@@ -132,6 +139,27 @@ int tc_decode_attention_append(const void* q, const void* k_new, const void* v_n
                                int64_t out_stride_h, int64_t out_stride_g,
                                float scale, int splits, int dtype, int64_t stable_rows,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* tc_decode_attention_append with the Qwen3 q/k norm and RoPE in front of it, one launch: q
+ * [hkv, g, d] and k_new [hkv, d] are the raw projections; each query row and each k_new row gets
+ * RMSNorm over d (weights q_norm_weight / k_norm_weight [d], eps) and the rotate-half RoPE with
+ * cos_t/sin_t [d], with exactly tc_qk_norm_rope's arithmetic, and the rotated k_new is the row
+ * written to the cache (v_new as given). Replaces, for one decode token, transformers' Qwen3Attention
+ * steps q_norm, k_norm, apply_rotary_pos_emb and the cache update in front of the plugin call
+ * (threadcut/attention.py:30-42, kv.py:64-77). bf16/fp16, d in {64, 128, 256}, 16-byte aligned K/V
+ * and rows only (TC_ERR_ALIGN / TC_ERR_INVALID otherwise: no other kernel does this fusion); q,
+ * k_new, the weights and cos/sin are read after the previous kernel in the stream completes. */
+int tc_decode_attention_append_rope(const void* q, const void* k_new, const void* v_new, void* k, void* v,
+                                    void* out, int hkv, int g, int d, int64_t n,
+                                    int64_t q_stride_h, int64_t q_stride_g,
+                                    int64_t k_new_stride_h, int64_t v_new_stride_h,
+                                    int64_t k_stride_h, int64_t k_stride_n,
+                                    int64_t v_stride_h, int64_t v_stride_n,
+                                    int64_t out_stride_h, int64_t out_stride_g,
+                                    const void* q_norm_weight, const void* k_norm_weight,
+                                    const void* cos_t, const void* sin_t, float eps,
+                                    float scale, int splits, int dtype, int64_t stable_rows,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* split(cached, new, min_suffix, suffix) of threadcut/match.py:33-48 on the device: token ids as
  * int32 device arrays (n_new >= 1). Writes (a, c0, c) of the resulting Split as three int64 to the

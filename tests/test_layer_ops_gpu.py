@@ -10,6 +10,7 @@ import torch.nn.functional as F
 from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
 
 from threadcut_b200 import _lib, tp
+from threadcut_b200 import flash_decode as fd
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -120,3 +121,51 @@ def test_gemv_swiglu_equals_silu_mul_then_gemv(n, k, dtype):
     assert torch.equal(got, want)
     ref = (F.silu(gu[:, :k].float()).to(dtype).float() * gu[:, k:].float()).to(dtype).float() @ w.float().t()
     torch.testing.assert_close(got.float(), ref, rtol=2 ** -7, atol=1e-3)
+
+
+@pytest.mark.parametrize("hkv,g,d,n,dtype", [(1, 4, 128, 98305, torch.bfloat16), (8, 4, 128, 2049, torch.bfloat16),
+                                             (2, 4, 128, 40, torch.float16), (2, 8, 64, 777, torch.bfloat16),
+                                             (1, 2, 256, 300, torch.float16)])
+def test_attention_with_norm_rope_equals_separate_launches(hkv, g, d, n, dtype):
+    """tc_decode_attention_append_rope (q/k norm + RoPE inside the attention launch) gives the bits
+    of tc_qk_norm_rope followed by tc_decode_attention_append: the same output, the same rotated row
+    n-1 in the cache, and every other cache row untouched; and the rotated q/k it uses are within
+    the Qwen3 prologue's tolerance of the torch ops (checked above for the separate launch)."""
+    gen = torch.Generator(device=DEV).manual_seed(hkv * 1000 + n)
+    k = torch.randn(hkv, n, d, generator=gen, device=DEV).to(dtype)
+    v = torch.randn(hkv, n, d, generator=gen, device=DEV).to(dtype)
+    q = torch.randn(hkv, g, d, generator=gen, device=DEV).to(dtype)
+    kn = torch.randn(hkv, d, generator=gen, device=DEV).to(dtype)
+    vn = torch.randn(hkv, d, generator=gen, device=DEV).to(dtype)
+    wq = (1 + 0.1 * torch.randn(d, generator=gen, device=DEV)).to(dtype)
+    wk = (1 + 0.1 * torch.randn(d, generator=gen, device=DEV)).to(dtype)
+    ang = (n - 1) * (1.0 / (1e6 ** (torch.arange(0, d, 2, device=DEV).float() / d)))
+    emb = torch.cat((ang, ang))
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    scale = d ** -0.5
+    # separate launches
+    q1, k1 = q.clone(), kn.clone()
+    tp._qk_norm_rope(q1.view(hkv * g, d), k1, wq, wk, cos, sin, 1e-6)
+    ka, va = k.clone(), v.clone()
+    want = fd.decode_attention_append(q1, ka, va, k1, vn, scale)
+    # one launch
+    kb, vb = k.clone(), v.clone()
+    q0, kn0 = q.clone(), kn.clone()
+    got = fd.decode_attention_append_rope(q, kb, vb, kn, vn, wq, wk, cos, sin, 1e-6, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(kb, ka) and torch.equal(vb, va)
+    assert torch.equal(kb[:, :n - 1], k[:, :n - 1]) and torch.equal(kb[:, n - 1], k1)
+    assert torch.equal(q, q0) and torch.equal(kn, kn0)  # the raw projections are only read
+
+
+def test_attention_with_norm_rope_rejects_what_it_cannot_fuse():
+    q = torch.randn(1, 4, 128, device=DEV)
+    k = torch.randn(1, 8, 128, device=DEV)
+    row = torch.randn(1, 128, device=DEV)
+    w = torch.ones(128, device=DEV)
+    with pytest.raises(RuntimeError):  # fp32: the tensor-core kernel does not take it
+        fd.decode_attention_append_rope(q, k, k.clone(), row, row, w, w, w, w, 1e-6, 0.1)
+    qb, kb, rb, wb = (t.to(torch.bfloat16) for t in (q, k, row, w))
+    with pytest.raises(ValueError):
+        fd.decode_attention_append_rope(qb, kb, kb.clone(), rb, rb, wb[:64], wb, wb, wb, 1e-6, 0.1)

@@ -25,6 +25,7 @@ SIGNATURES = {
     "tc_status_string": (ctypes.c_char_p, [_i]),
     "tc_abi_version": (_i, []),
     "tc_device_errors": (_i, [_i]),
+    "tc_set_pdl": (_i, [_i]),
     "tc_decode_attention_workspace_size": (_sz, [_i, _i, _i, _i, _i64, _i64, _i, _i]),
     "tc_decode_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                             + [_f, _i, _i, _vp, _sz, _vp]),
@@ -33,6 +34,8 @@ SIGNATURES = {
                                    + [_f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_decode_attention_append": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 10
                                    + [_f, _i, _i, _i64, _vp, _sz, _vp]),
+    "tc_decode_attention_append_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 10
+                                        + [_vp, _vp, _vp, _vp, _f, _f, _i, _i, _i64, _vp, _sz, _vp]),
     "tc_decode_attention_partial": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8
                                     + [_f, _i, _i, _vp, _sz, _vp]),
     "tc_decode_attention_partial_stable": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i64] + [_i64] * 8

@@ -94,6 +94,16 @@ struct DecodeParams {
   const void* k_app;
   const void* v_app;
   int64_t sa_k, sa_v;
+  // q/k norm + RoPE fused in front of the attention (tensor-core kernel, with the fused append):
+  // q and k_app are the raw projections; each CTA normalises and rotates its head's g query rows
+  // and its head's k_app row as qk_norm_rope_kernel does (Qwen3 RMSNorm with weights nq_w / nk_w,
+  // then x*cos + rotate_half(x)*sin with cos/sin [d]) into shared memory, and the rotated k_app is
+  // the row written to the cache. Null nq_w: q and k_app are used as given.
+  const void* nq_w;
+  const void* nk_w;
+  const void* rope_cos;
+  const void* rope_sin;
+  float norm_eps, norm_inv_d;
   // paged mode (single sequence, tensor-core kernel): K and V live in pages of a pool and the
   // sequence is n_tiles tiles, tile t being rows [tiles[3t+1], tiles[3t+1] + tiles[3t+2]) of page
   // tiles[3t] (at most kTile rows, inside the page); tmk/tmv are (d, page rows, heads, pages) maps,
@@ -467,6 +477,44 @@ __device__ __forceinline__ uint32_t pack_raw(T lo, T hi) {
   return (uint32_t)a | ((uint32_t)b << 16);
 }
 
+// One d-vector through Qwen3's q_norm/k_norm and the rotate-half RoPE, by one warp, into dst: the
+// arithmetic of qk_norm_rope_kernel, including its sum order (lane l holds elements l + 32 t; the
+// squares of each group of 32 are summed by a xor butterfly, then the group sums, placed in lanes
+// 0..D/32-1, by another), so the result has the same bits.
+template <typename T, int D>
+__device__ __forceinline__ void norm_rope_row(const T* __restrict__ src, const T* __restrict__ w,
+                                              const T* __restrict__ cosv, const T* __restrict__ sinv,
+                                              float inv_d, float eps, T* dst, int lane) {
+  constexpr int E = D / 32;
+  float x[E], z[E];
+#pragma unroll
+  for (int t = 0; t < E; ++t) x[t] = to_f32(src[lane + 32 * t]);
+  float tot = 0.f;
+#pragma unroll
+  for (int t = 0; t < E; ++t) {
+    float s = x[t] * x[t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == t) tot = s;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float r = rsqrtf(tot * inv_d + eps);
+#pragma unroll
+  for (int t = 0; t < E; ++t) {
+    const T y = from_f32<T>(x[t] * r);
+    z[t] = to_f32(from_f32<T>(to_f32(w[lane + 32 * t]) * to_f32(y)));
+  }
+#pragma unroll
+  for (int t = 0; t < E; ++t) {
+    const int i = lane + 32 * t;
+    const float rot = t < E / 2 ? -z[t + E / 2] : z[t - E / 2];
+    const float t1 = to_f32(from_f32<T>(z[t] * to_f32(cosv[i])));
+    const float t2 = to_f32(from_f32<T>(rot * to_f32(sinv[i])));
+    dst[i] = from_f32<T>(t1 + t2);
+  }
+}
+
 template <int D>
 struct MmaGeom {
   static_assert(D % 64 == 0, "the tensor-core kernel stages 64-column (128-byte) swizzled boxes");
@@ -511,6 +559,8 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   uint64_t* empty = full + kStages;
   __shared__ int s_mi;  // merger index of this CTA (-1: not a merger)
   __shared__ int4 s_tab[kPaged ? kTabTiles : 1];  // paged: this CTA's first kTabTiles table entries
+  // fused q/k norm + RoPE (p.nq_w): the head's g rotated query rows, then its rotated k_app row
+  __shared__ uint4 s_qk[(HP + 1) * D / 8];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -597,6 +647,21 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
   const int64_t t1 = n < tt1 * kTile ? n : tt1 * kTile;
   const int ntiles = (int)(tt1 - tt0);
   if (threadIdx.x == 0) s_mi = -1;
+  const bool rope = p.nq_w != nullptr;
+  if (rope) {
+    // warps 0..g-1: the query rows of head h; warp g: the head's k_app row (the producer warp
+    // included, before it starts issuing: its leading tiles are already in flight)
+    T* sq = reinterpret_cast<T*>(s_qk);
+    const T* cs = static_cast<const T*>(p.rope_cos);
+    const T* sn = static_cast<const T*>(p.rope_sin);
+    for (int r = warp; r <= p.g; r += kCWarps + 1) {
+      const bool isq = r < p.g;
+      const T* src = isq ? static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h + r * p.sq_g
+                         : static_cast<const T*>(p.k_app) + h * p.sa_k;
+      norm_rope_row<T, D>(src, static_cast<const T*>(isq ? p.nq_w : p.nk_w), cs, sn, p.norm_inv_d, p.norm_eps,
+                          sq + (isq ? r : HP) * D, lane);
+    }
+  }
   if constexpr (kPaged) {
     // the slice's table entries, loaded once by the whole CTA instead of a dependent global load
     // in front of every TMA issue and every consumer tile
@@ -651,13 +716,14 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
     const float c = p.c;
     uint32_t bq[NG][KS][2];
     {
-      const T* qb = static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h;
+      const T* qb = rope ? reinterpret_cast<const T*>(s_qk) : static_cast<const T*>(p.q) + b * p.sq_b + h * p.sq_h;
+      const int64_t qg = rope ? (int64_t)D : p.sq_g;
       const T zero = from_f32<T>(0.f);
 #pragma unroll
       for (int nt = 0; nt < NG; ++nt) {
         const int i = nt * 8 + gid;
         const bool ok = i < p.g;
-        const T* qr = qb + (ok ? i : 0) * p.sq_g;
+        const T* qr = qb + (ok ? i : 0) * qg;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           const int d0 = ks * 16 + 2 * qd;
@@ -715,7 +781,8 @@ __global__ void __launch_bounds__(32 * (kCWarps + 1), 1)
         // k_app/v_app (16-byte chunks into the swizzled row) and write the row to the cache
         const int r = (int)app_r;
         constexpr int CH = D / 8;  // 16-byte chunks per row
-        const uint4* ka = reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + h * p.sa_k);
+        const uint4* ka = rope ? s_qk + HP * D / 8
+                               : reinterpret_cast<const uint4*>(static_cast<const T*>(p.k_app) + h * p.sa_k);
         const uint4* va = reinterpret_cast<const uint4*>(static_cast<const T*>(p.v_app) + h * p.sa_v);
         uint4* kc = reinterpret_cast<uint4*>(const_cast<T*>(static_cast<const T*>(p.k)) + app_pg * p.sk_b + h * p.sk_h +
                                              app_row * p.sk_n);

@@ -2,6 +2,7 @@
 // This is the library's only translation unit; it includes every kernel header.
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -174,13 +175,20 @@ WsLayout decode_ws_layout(int batch, int hkv, int g, int d, int64_t max_splits) 
 }
 
 // Programmatic dependent launch (the kernel's prologue overlaps the previous kernel's tail); set
-// TC_PDL=0 in the environment to launch plainly.
+// TC_PDL=0 in the environment, or call tc_set_pdl(0), to launch plainly (each kernel then starts
+// after the previous one ends, so per-kernel device times add up to the step).
+std::atomic<int> g_pdl{-1};
+
 bool pdl_enabled() {
-  static const bool on = [] {
+  int v = g_pdl.load(std::memory_order_relaxed);
+  if (v < 0) {
     const char* e = std::getenv("TC_PDL");
-    return !(e != nullptr && e[0] == '0');
-  }();
-  return on;
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+    int expect = -1;
+    g_pdl.compare_exchange_strong(expect, v, std::memory_order_relaxed);
+    v = g_pdl.load(std::memory_order_relaxed);
+  }
+  return v != 0;
 }
 
 template <typename Kern, typename Params>
@@ -282,6 +290,9 @@ int run_decode(DecodeParams p, int dtype, int d, bool ragged, int64_t max_n, int
               encode_kv_map(&p.tmv, p.v, dtype, d, max_n, p.hkv, p.batch, p.sv_n, p.sv_h, p.sv_b);
   }
   if (!use_mma && !gen_dim(d)) return mma_dim(d) ? TC_ERR_ALIGN : TC_ERR_INVALID;
+  // the fused q/k norm + RoPE exists in the tensor-core kernel only, with the fused append
+  if (p.nq_w != nullptr && (!use_mma || p.k_app == nullptr || p.tiles != nullptr || p.k_ptrs != nullptr))
+    return mma_dim(d) && dtype != TC_F32 ? TC_ERR_ALIGN : TC_ERR_INVALID;
   if (p.k_app != nullptr && !use_mma) {
     // fused append needs the tensor-core kernel: write the row with two strided copies, then decode
     const size_t es = esize(dtype);
@@ -480,6 +491,12 @@ const char* tc_status_string(int status) {
 
 int tc_abi_version(void) { return 1; }
 
+int tc_set_pdl(int on) {
+  const int prev = pdl_enabled() ? 1 : 0;
+  g_pdl.store(on ? 1 : 0, std::memory_order_relaxed);
+  return prev;
+}
+
 int tc_device_errors(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
   unsigned int v = 0;
@@ -517,15 +534,32 @@ int tc_decode_attention(const void* q, const void* k, const void* v, void* out, 
 }
 
 namespace {
+// The fused q/k norm + RoPE of tc_decode_attention_append_rope.
+struct NormRope {
+  const void* q_weight;
+  const void* k_weight;
+  const void* cos_t;
+  const void* sin_t;
+  float eps;
+};
+
 int decode_single(const void* q, const void* k, const void* v, void* out, float* lse, bool out_f32, int hkv, int g,
                   int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g, int64_t k_stride_h, int64_t k_stride_n,
                   int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h, int64_t out_stride_g, float scale,
                   int splits, int dtype, void* workspace, size_t workspace_bytes, void* stream,
                   int64_t stable_rows = 0, const void* k_app = nullptr, const void* v_app = nullptr,
-                  int64_t sa_k = 0, int64_t sa_v = 0) {
+                  int64_t sa_k = 0, int64_t sa_v = 0, const NormRope* nr = nullptr) {
   if (n > 0 && (k == nullptr || v == nullptr)) return TC_ERR_INVALID;
   if (stable_rows < 0) return TC_ERR_INVALID;
   DecodeParams p = base_params();
+  if (nr != nullptr) {
+    p.nq_w = nr->q_weight;
+    p.nk_w = nr->k_weight;
+    p.rope_cos = nr->cos_t;
+    p.rope_sin = nr->sin_t;
+    p.norm_eps = nr->eps;
+    p.norm_inv_d = 1.0f / (float)d;
+  }
   p.stable_rows = stable_rows < n ? stable_rows : n;
   p.k_app = k_app;
   p.v_app = v_app;
@@ -594,6 +628,27 @@ int tc_decode_attention_append(const void* q, const void* k_new, const void* v_n
   return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
                        v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
                        workspace_bytes, stream, stable_rows, k_new, v_new, k_new_stride_h, v_new_stride_h);
+}
+
+int tc_decode_attention_append_rope(const void* q, const void* k_new, const void* v_new, void* k, void* v, void* out,
+                                    int hkv, int g, int d, int64_t n, int64_t q_stride_h, int64_t q_stride_g,
+                                    int64_t k_new_stride_h, int64_t v_new_stride_h, int64_t k_stride_h,
+                                    int64_t k_stride_n, int64_t v_stride_h, int64_t v_stride_n, int64_t out_stride_h,
+                                    int64_t out_stride_g, const void* q_norm_weight, const void* k_norm_weight,
+                                    const void* cos_t, const void* sin_t, float eps, float scale, int splits,
+                                    int dtype, int64_t stable_rows, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  if (n < 1 || q == nullptr || k_new == nullptr || v_new == nullptr || q_norm_weight == nullptr ||
+      k_norm_weight == nullptr || cos_t == nullptr || sin_t == nullptr || !(eps >= 0.f))
+    return TC_ERR_INVALID;
+  if (!valid_dtype(dtype)) return TC_ERR_DTYPE;
+  if (dtype == TC_F32 || !mma_dim(d)) return TC_ERR_INVALID;
+  if (!(aligned16(k_new) && aligned16(v_new) && stride16(k_new_stride_h, dtype) && stride16(v_new_stride_h, dtype)))
+    return TC_ERR_ALIGN;
+  const NormRope nr{q_norm_weight, k_norm_weight, cos_t, sin_t, eps};
+  return decode_single(q, k, v, out, nullptr, false, hkv, g, d, n, q_stride_h, q_stride_g, k_stride_h, k_stride_n,
+                       v_stride_h, v_stride_n, out_stride_h, out_stride_g, scale, splits, dtype, workspace,
+                       workspace_bytes, stream, stable_rows, k_new, v_new, k_new_stride_h, v_new_stride_h, &nr);
 }
 
 int tc_decode_attention_lse(const void* q, const void* k, const void* v, void* out, float* lse, int hkv, int g,

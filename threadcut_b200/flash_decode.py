@@ -155,6 +155,49 @@ def decode_attention_append(q, k, v, k_new, v_new, scale, *, splits=None, stable
     return out
 
 
+def decode_attention_append_rope(q, k, v, k_new, v_new, q_norm, k_norm, cos, sin, eps, scale, *, splits=None,
+                                 stable_rows=0):
+    """decode_attention_append with Qwen3's q/k norm and RoPE in the same launch: q [hkv, g, d] and
+    k_new [hkv, d] are the raw projections; each d-vector gets RMSNorm (weights q_norm / k_norm [d],
+    eps) and x*cos + rotate_half(x)*sin (cos/sin [d]) with the arithmetic of the separate
+    tc_qk_norm_rope launch, and the rotated k_new is the row written to the cache. bf16/fp16, head
+    dim 64/128/256, 16-byte aligned cache rows only (tc_decode_attention_append_rope)."""
+    what = "decode_attention_append_rope"
+    require_cuda(q, k, v, k_new, v_new, q_norm, k_norm, cos, sin, what=what)
+    _check_same_dtype(what, q, k, v, k_new, v_new, q_norm, k_norm, cos, sin)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3 or k_new.dim() != 2 or v_new.dim() != 2:
+        raise ValueError(f"{what}: expected q [hkv, g, d], k/v [hkv, n, d], k_new/v_new [hkv, d]")
+    hkv, g, d = q.shape
+    n = k.shape[1]
+    if (k.shape[0] != hkv or k.shape[2] != d or v.shape != k.shape or tuple(k_new.shape) != (hkv, d)
+            or tuple(v_new.shape) != (hkv, d) or n < 1):
+        raise ValueError(f"{what}: shapes q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}, "
+                         f"k_new {tuple(k_new.shape)}, v_new {tuple(v_new.shape)} do not fit")
+    for name, t in (("q_norm", q_norm), ("k_norm", k_norm), ("cos", cos), ("sin", sin)):
+        if t.numel() != d:
+            raise ValueError(f"{what}: {name} must hold d = {d} values, got {tuple(t.shape)}")
+    if k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError(f"{what}: the cache views must have a contiguous last dimension (they are written)")
+    if stable_rows < 0:
+        raise ValueError(f"{what}: stable_rows must be >= 0")
+    q, k_new, v_new = _last_contig(q), _last_contig(k_new), _last_contig(v_new)
+    q_norm, k_norm, cos, sin = (t.contiguous() for t in (q_norm, k_norm, cos, sin))
+    code = dtype_code(q, what)
+    dev = q.device
+    out = torch.empty((hkv, g, d), dtype=q.dtype, device=dev)
+    stream = stream_ptr(dev)
+    ws = workspaces.get(("decode", hkv), dev, _lib.decode_workspace_bound(1, hkv, g, d, code), stream)
+    with torch.cuda.device(dev):
+        st = lib().tc_decode_attention_append_rope(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), hkv, g, d,
+            n, q.stride(0), q.stride(1), k_new.stride(0), v_new.stride(0), k.stride(0), k.stride(1), v.stride(0),
+            v.stride(1), out.stride(0), out.stride(1), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
+            sin.data_ptr(), float(eps), float(scale), int(splits or 0), code, int(stable_rows), ws.data_ptr(),
+            ws.numel(), stream)
+    check(what, st)
+    return out
+
+
 def decode_attention_lse(q, k, v, scale, *, splits=None):
     """Like decode_attention, plus the natural-log log-sum-exp of the scaled scores, fp32 [hkv, g]."""
     return _decode(q, k, v, scale, splits, True)

@@ -21,11 +21,12 @@ all ranks' vocabulary slices (torch's argmax rule), found from an all-gather of 
 the weights' dtype, q/k RMSNorm per head, RoPE with cos/sin rounded to the model dtype, SwiGLU),
 so at world == 1 the step is the HF forward with threadcut_b200's attention.
 
-The small ops between the projections run as one launch each (csrc/layer_ops.cuh): the residual
-add fused with the next RMSNorm, q/k norm fused with RoPE, and SwiGLU; the q/k/v and the gate/up
-projections are one GEMV each (their rows side by side), and every projection runs tc_gemv. That is about 9 launches and 2 all-reduces
-per layer instead of HF's ~50 kernels, and the whole step can be captured in a CUDA graph
-(`capture`): it reads nothing back to the host.
+The small ops between the projections are fused into their neighbours: the residual add with the
+next RMSNorm (csrc/layer_ops.cuh, or the sum over ranks on more than one rank), q/k norm + RoPE
+with the attention launch, and SwiGLU with the input staging of down_proj; the q/k/v and the
+gate/up projections are one GEMV each (their rows side by side). That is 7 launches per layer
+instead of HF's ~50 kernels, and the whole step can be captured in a CUDA graph (`capture`): it
+reads nothing back to the host.
 
 The cache is the rank's heads only, kept as GrowingLayers: a splice (kv.splice) re-rotates and
 moves only the local heads, with no exchange. There is no CPU path: the kernels need CUDA.
@@ -35,7 +36,7 @@ import torch.distributed as dist
 
 from . import kv as _kv
 from ._lib import check, dtype_code, lib, require_cuda, stream_ptr
-from .flash_decode import decode_attention_append
+from .flash_decode import decode_attention_append, decode_attention_append_rope
 from .sharded import head_shard
 
 __all__ = ["TPDecoder", "accelerate"]
@@ -110,6 +111,16 @@ def _attend(layer, q, k, v, scale):
     return decode_attention_append(q, layer.keys[0], layer.values[0], kp, vp, scale, stable_rows=stable)
 
 
+def _attend_rope(layer, q, k, v, wq, wk, cos, sin, eps, scale):
+    """_attend with the step's q/k norm and RoPE in the same launch: q [hr, g, d] and k [hr, d] are
+    the raw projections (decode_attention_append_rope); the cache receives the rotated k."""
+    hr, d = k.shape
+    layer.update(k.view(1, hr, 1, d), v.view(1, hr, 1, d))
+    kp, vp, stable = layer.take_pending()
+    return decode_attention_append_rope(q, layer.keys[0], layer.values[0], kp, vp, wq, wk, cos, sin, eps, scale,
+                                        stable_rows=stable)
+
+
 class _Shard:
     """One layer's weights on this rank."""
 
@@ -180,6 +191,9 @@ class TPDecoder:
         self.layers = [_kv.GrowingLayer() for _ in base.layers]
         for layer in self.layers:
             layer.fuse_append = True  # the decode launch writes each step's row
+        # q/k norm + RoPE inside the attention launch (the tensor-core decode kernel's shapes)
+        self.fuse_rope = (self.dev.type == "cuda" and self.dtype in (torch.bfloat16, torch.float16)
+                          and self.d in (64, 128, 256))
         # the two sums per layer: through peer memory (one-shot, fused into the projection and the
         # norm after it) on more than one rank unless peer_sums is False, else the collective library
         self._ar = None
@@ -226,8 +240,9 @@ class TPDecoder:
 
     def _final_hidden(self, token, pos):
         """The step's arithmetic up to the final norm: [1, hidden] (appends the token's K/V row).
-        Per layer: the q/k/v projection, q/k norm + RoPE (one launch), attention with the fused
-        append, o_proj, sum over ranks, residual add + post-attention norm (one launch), the gate/up
+        Per layer: the q/k/v projection, attention with the q/k norm + RoPE and the append fused
+        in (or the norm + RoPE as a launch of its own where the decode kernel cannot take it),
+        o_proj, sum over ranks, residual add + post-attention norm (one launch), the gate/up
         projection, down_proj of the SwiGLU activation (computed by the projection's input staging),
         sum over ranks, and the residual add fused with the next layer's input norm (the final norm
         after the last layer). Every kernel launches with programmatic dependent launch: it starts
@@ -246,8 +261,11 @@ class TPDecoder:
         for w, layer, norm_next in zip(self.layers_w, self.layers, nxt):
             qkv = _gemv(x, w.wqkv)[0]
             q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
-            _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
-            o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
+            if self.fuse_rope:
+                o = _attend_rope(layer, q.view(hr, g, d), k, v, w.q_norm, w.k_norm, cos, sin, eps, self.scale)
+            else:
+                _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
+                o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
             self._sum_add_norm(o.reshape(1, nq * d), w.wo, h, w.post_norm, x)
             gu = _gemv(x, w.wgu)
             self._sum_add_norm(gu, w.wd, h, norm_next, x, swiglu=True)
@@ -367,7 +385,7 @@ def accelerate(model, device=None):
     module, behind the model's own call: after accelerate(model), model(input_ids=[[t]],
     past_key_values=cache, use_cache=True) over a cache of this package (kv.new_cache with the
     threadcut attention: GrowingLayers with the fused append, holding rows) returns HF's output type
-    with `.logits` [1, 1, vocab] computed by TPDecoder at world 1 (about 9 launches per layer instead
+    with `.logits` [1, 1, vocab] computed by TPDecoder at world 1 (7 launches per layer instead
     of transformers' ~50), appending the token's K/V row to the same cache. Every other call (a
     prefill chunk, another cache, extra arguments) goes to the model's own forward. The reference's
     engine (threadcut/engine.py:66-73, 88-95) makes exactly such calls, so it runs unchanged on the
