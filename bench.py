@@ -1164,7 +1164,10 @@ def run_ours(args, rank, local, world, dist):
                        f"all-reduces instead)), next token read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
                        f"graph and gathered-logit tokens equal HF's SDPA forward over the same spliced full cache "
                        f"(sdpa_token) on every rank; ideal_ms = one rank's weight + K/V bytes at the measured HBM "
-                       f"peak (collectives not counted)"}
+                       f"peak (collectives not counted); launches_serial: the step's graph captured with programmatic "
+                       f"dependent launch off, its replay time and per-kernel-family launches, µs per step and "
+                       f"shares on rank 0 (torch.profiler CUDA activity)",
+               "launches_serial": tp["launches_serial"]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         us16, nl16, thr = cpu_reference_us_per_layer(args.cpu_seconds / 2, dtype=torch.bfloat16)

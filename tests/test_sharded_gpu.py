@@ -25,7 +25,7 @@ def test_seq_and_head_sharded_decode_match_single_gpu():
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "sharded_worker.py")]
     res = subprocess.run(cmd, capture_output=True, text=True)
-    print(res.stdout[-3000:], res.stderr[-3000:])
+    print(res.stdout[-4000:], res.stderr[:6000], res.stderr[-1500:])
     assert res.returncode == 0
 
 
@@ -39,7 +39,7 @@ def test_tensor_parallel_decoder_matches_the_sdpa_forward():
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "tp_worker.py")]
     res = subprocess.run(cmd, capture_output=True, text=True)
-    print(res.stdout[-3000:], res.stderr[-3000:])
+    print(res.stdout[-4000:], res.stderr[:6000], res.stderr[-1500:])
     assert res.returncode == 0
 
 
@@ -51,5 +51,5 @@ def test_peer_memory_sums_match_the_collective_library():
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(HERE, "peer_worker.py")]
     res = subprocess.run(cmd, capture_output=True, text=True)
-    print(res.stdout[-3000:], res.stderr[-3000:])
+    print(res.stdout[-4000:], res.stderr[:6000], res.stderr[-1500:])
     assert res.returncode == 0

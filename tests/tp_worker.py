@@ -1,7 +1,8 @@
 """Tensor-parallel decoder check, shared by the one-GPU test (test_engine_gpu.py) and the torchrun
 worker of the multi-GPU tests (test_sharded_gpu.py, any number of ranks).
 
-A small bf16 Qwen3 (head_dim 128, 4 query heads per KV head: the decode kernel's fast path) holds a
+A small bf16 Qwen3 (Qwen3-4B's attention shape: 8 KV heads, so 1, 2, 4 and 8 ranks all hold whole
+heads, 4 query heads per KV head, head_dim 128; hidden 256, 2 layers) holds a
 2,304-token prompt A.B.C in its cache, computed by stock transformers with SDPA attention. B (256
 tokens) is pruned with kv.splice, leaving 2,048 rows. Expected next token: the same SDPA forward of
 one more token over that spliced cache (the torch path the reference's engine tests compare with,
@@ -30,7 +31,7 @@ def check(dev, world=1, rank=0):
     """Returns a dict of the measured quantities; raises AssertionError on a mismatch."""
     torch.manual_seed(0)
     cfg = Qwen3Config(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
-                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=8192)
+                      num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192)
     model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16, attn_implementation="sdpa")
     model = model.to(dev).eval()
     ids = torch.randint(0, 512, (1, 2305), generator=torch.Generator().manual_seed(3)).to(dev)

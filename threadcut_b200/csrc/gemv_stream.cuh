@@ -27,6 +27,7 @@ constexpr int kGsThreads = 32 * (kGsConsumers + 1);
 constexpr int kGsMaxStages = 16;
 constexpr int kGsSmemBudget = 200 * 1024;          // x + ring, of the 227 KB a CTA may use
 constexpr int kGsMaxRowsPerCta = 64;               // kAR: rows whose results are kept for the stores
+constexpr int kGsStageBatch = 6;                   // x chunks per thread loaded before use (one batch: K <= 12288)
 
 struct GsPlan {
   int rs;          // rows per stage
@@ -108,24 +109,40 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
     pdl_launch();
     pdl_wait();  // x is the previous kernel's output
     {
+      // each thread issues the loads of up to kGsStageBatch of its 16-byte chunks before using any,
+      // so staging x costs one L2 round trip per batch instead of one per chunk
       const int kc = K / 8;
-      for (int i = threadIdx.x; i < kc; i += 32 * kGsConsumers) {
-        if constexpr (kSwiGLU) {
-          const uint4 gv = reinterpret_cast<const uint4*>(x)[i];
-          const uint4 uv = reinterpret_cast<const uint4*>(x + K)[i];
-          const T* ge = reinterpret_cast<const T*>(&gv);
-          const T* ue = reinterpret_cast<const T*>(&uv);
-          uint4 o;
-          T* oe = reinterpret_cast<T*>(&o);
+      const uint4* xg = reinterpret_cast<const uint4*>(x);
+      for (int base = threadIdx.x; base < kc; base += 32 * kGsConsumers * kGsStageBatch) {
+        uint4 gv[kGsStageBatch], uv[kSwiGLU ? kGsStageBatch : 1];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const float gf = to_f32(ge[t]);
-            const float act = to_f32(from_f32<T>(gf / (1.0f + expf(-gf))));
-            oe[t] = from_f32<T>(act * to_f32(ue[t]));
+        for (int u = 0; u < kGsStageBatch; ++u) {
+          const int i = base + u * 32 * kGsConsumers;
+          if (i < kc) {
+            gv[u] = xg[i];
+            if constexpr (kSwiGLU) uv[u] = reinterpret_cast<const uint4*>(x + K)[i];
           }
-          xs[i] = o;
-        } else {
-          xs[i] = reinterpret_cast<const uint4*>(x)[i];
+        }
+#pragma unroll
+        for (int u = 0; u < kGsStageBatch; ++u) {
+          const int i = base + u * 32 * kGsConsumers;
+          if (i < kc) {
+            if constexpr (kSwiGLU) {
+              const T* ge = reinterpret_cast<const T*>(&gv[u]);
+              const T* ue = reinterpret_cast<const T*>(&uv[u]);
+              uint4 o;
+              T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                const float gf = to_f32(ge[t]);
+                const float act = to_f32(from_f32<T>(gf / (1.0f + expf(-gf))));
+                oe[t] = from_f32<T>(act * to_f32(ue[t]));
+              }
+              xs[i] = o;
+            } else {
+              xs[i] = gv[u];
+            }
+          }
         }
       }
     }
