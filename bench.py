@@ -871,7 +871,9 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None, summary=T
                     launch_list(prof, launches, 3)
         del graph
         nccl_ms = None
-        if dec.use_peer_sums:  # the same graph with the collective library's all-reduce for the sums
+        # the same graph with the sums as separate launches: a GEMV, the collective library's
+        # all-reduce (N > 1) and the residual add + norm kernel, then the next GEMV
+        if dec.use_peer_sums:
             dec.use_peer_sums = False
             graph, out = dec.capture(tok, n)
 
@@ -889,7 +891,7 @@ def time_cfg5_tp(steps, warmup, dev, dist, rank, world, launches=None, summary=T
     del dec
     torch.cuda.empty_cache()
     return {"eager_ms": eager_ms, "graph_ms": graph_ms, "nccl_graph_ms": nccl_ms, "splice_ms": splice_ms,
-            "launches_serial": serial,
+            "launches_serial": serial, "world": world,
             "bytes": shard_bytes + LAYERS * (4096 // world * n + 16384 // world),
             "top1_ok": bool(top1_ok and (graph_tok is None or graph_tok == ref_top1)), "token": step_tok,
             "sdpa_token": ref_top1, "logit_corr": round(corr, 6),
@@ -1154,14 +1156,18 @@ def run_ours(args, rank, local, world, dist):
                "graph_ms": None if tp["graph_ms"] is None else round(tp["graph_ms"], 3),
                "splice_ms": round(tp["splice_ms"], 3), "bytes_per_rank": tp["bytes"],
                "ideal_ms": round(tp["bytes"] / (hbm * 1e9) * 1e3, 3),
-               "nccl_graph_ms": None if tp["nccl_graph_ms"] is None else round(tp["nccl_graph_ms"], 3),
+               ("nccl_graph_ms" if world > 1 else "separate_sums_graph_ms"):
+                   None if tp["nccl_graph_ms"] is None else round(tp["nccl_graph_ms"], 3),
                "top1_ok": tp["top1_ok"], "token": tp["token"], "sdpa_token": tp["sdpa_token"],
                "logit_corr": tp["logit_corr"], "logit_max_abs": tp["logit_max_abs"],
                "what": f"one greedy decode token of random-init Qwen3-4B over the spliced 98,304-token cache, "
                        f"tensor-parallel over {world} GPU(s) (threadcut_b200.tp.TPDecoder: KV heads, their query "
-                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 sums over the ranks per layer, through "
-                       f"peer memory fused into the projection and the norm (nccl_graph_ms: the same graph with NCCL "
-                       f"all-reduces instead)), next token read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
+                       f"heads, 1/{world} of the MLP and vocabulary per rank; 2 sums over the ranks per layer through "
+                       f"peer memory, each completed into the residual by the row-split projection, the next "
+                       f"projection staging RMSNorm of it: 5 launches per layer (nccl_graph_ms, N > 1, or "
+                       f"separate_sums_graph_ms, N = 1: the same graph with separate GEMV, NCCL all-reduce (N > 1) "
+                       f"and residual add + norm launches instead)), next token "
+                       f"read back each step; eager and CUDA graph; max over ranks; top1_ok: the eager, "
                        f"graph and gathered-logit tokens equal HF's SDPA forward over the same spliced full cache "
                        f"(sdpa_token) on every rank; ideal_ms = one rank's weight + K/V bytes at the measured HBM "
                        f"peak (collectives not counted); launches_serial: the step's graph captured with programmatic "
@@ -1313,6 +1319,85 @@ def time_gemv(steps, warmup, dev, n, k, layers):
             "frac": round(gbs / hbm, 4), "peak_kind": kind}
 
 
+def time_gemv_chain(steps, warmup, dev, tp_world, layers, dist=None):
+    """The projections of the tensor-parallel step alone, one GPU with the per-rank shapes of
+    `tp_world` ranks (Qwen3-4B): per layer q|k|v with the input norm staged (tc_gemv_rmsnorm),
+    o_proj completing its sum into the residual (tc_gemv_allreduce_residual, world 1), gate|up with
+    the post-attention norm staged, down_proj of the SwiGLU activation completing its sum; the
+    attention output is a fixed input. `layers` distinct weight sets, replayed from a CUDA graph,
+    with programmatic dependent launch on and off. Returns µs per layer, the weight bytes per layer
+    and the per-kernel serialized shares."""
+    from torch.profiler import ProfilerActivity, profile
+    from threadcut_b200._lib import lib
+    from threadcut_b200.peer import AllReduce
+    hid, inter, d = 2560, 9728 // tp_world, 128
+    nq, nkv = 32 // tp_world, 8 // tp_world
+    g = torch.Generator(device=dev).manual_seed(4)
+    bf = torch.bfloat16
+
+    def mat(n, k):
+        return (torch.randn(n, k, generator=g, device=dev) * k ** -0.5).to(bf)
+
+    ws = [(mat((nq + 2 * nkv) * d, hid), mat(hid, nq * d), mat(2 * inter, hid), mat(hid, inter)) for _ in range(layers)]
+    norm = (1 + 0.1 * torch.randn(hid, generator=g, device=dev)).to(bf)
+    o_in = torch.randn(1, nq * d, generator=g, device=dev).to(bf)
+    h0 = torch.randn(1, hid, generator=g, device=dev).to(bf)
+    ar = AllReduce(hid, dev, world=1)
+    h = h0.clone()
+    wbytes = sum(t.numel() * 2 for t in ws[0])
+
+    def chain():
+        h.copy_(h0)
+        ar.gemv_residual(o_in, ws[0][1], h)  # records the first sums of squares
+        for wq, wo, wgu, wd in ws:
+            ar.gemv_norm(h, norm, wq, 1e-6)
+            ar.gemv_residual(o_in, wo, h)
+            gu = ar.gemv_norm(h, norm, wgu, 1e-6)
+            ar.gemv_residual(gu, wd, h, swiglu=True)
+
+    res = {"tp_world": tp_world, "layers": layers, "weight_mb_per_layer": round(wbytes / 1e6, 2)}
+    for mode in (1, 0):
+        prev = lib().tc_set_pdl(mode)
+        try:
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                chain()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(graph, stream=s):
+                    chain()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize()
+        finally:
+            lib().tc_set_pdl(prev)
+        ms = time_graph(graph, steps, warmup, None)
+        key = "pdl" if mode else "serial"
+        res[key + "_us_per_layer"] = round(ms * 1000 / layers, 3)
+        if not mode:
+            prof = profile(activities=[ProfilerActivity.CUDA])
+            prof.start()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            prof.stop()
+            rows = {}
+            for ev in prof.events():
+                if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time_total > 0:
+                    r = rows.setdefault(kernel_family(ev.name), [0, 0.0])
+                    r[0] += 1
+                    r[1] += ev.device_time_total
+            res["serial_kernels"] = [[k, c // 3, round(us / c, 2)] for k, (c, us) in
+                                     sorted(rows.items(), key=lambda kv: -kv[1][1])]
+        del graph
+    hbm, _ = peaks()
+    res["pdl_frac"] = round(wbytes / (res["pdl_us_per_layer"] * 1e-6) / 1e9 / hbm, 4)
+    torch.cuda.synchronize()
+    ar.close()
+    return res
+
+
 def launch_list(prof, path, steps):
     """Kernel launch list of a torch.profiler run: per kernel name, launches, total device µs and
     share, from the CUDA activity records (the device's own start/end stamps; nothing replayed)."""
@@ -1351,6 +1436,8 @@ def run_partial(args, rank, local, world, dist):
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in tp.items()}, world=world)
     elif args.only == "gemv":
         out.update(time_gemv(args.steps, args.warmup, dev, args.gemv_n, args.gemv_k, args.layers))
+    elif args.only == "gemvchain":
+        out.update(time_gemv_chain(args.steps, args.warmup, dev, args.heads, args.layers))
     elif args.only == "cfg5":
         c5 = time_cfg5_step(args.steps, args.warmup, dev)
         out.update({k: (round(v, 3) if isinstance(v, float) else v) for k, v in c5.items()})
@@ -1409,9 +1496,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5", "cfg5tp", "gemv"], default="all",
+    ap.add_argument("--only", choices=["all", "decode", "shift", "cfg5", "cfg5tp", "gemv", "gemvchain"],
+                    default="all",
                     help="profiling runs: time only the decode graph, the splice, the config-5 model step, its "
-                         "tensor-parallel form, or the step's GEMV (smaller JSON line)")
+                         "tensor-parallel form, the step's GEMV, or its chain of projections with the sums in "
+                         "residual form at one GPU (--heads = the tensor-parallel width whose shapes it uses; "
+                         "smaller JSON line)")
     ap.add_argument("--launches", default=None,
                     help="profiling runs (cfg5tp): rank 0 writes the kernel launch list of 3 graph-replayed steps "
                          "(torch.profiler's CUDA activity records: device time per kernel, no replay) to this file")

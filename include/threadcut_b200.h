@@ -484,6 +484,27 @@ int tc_gemv_allreduce_swiglu(const void* gate_up, const void* w, int64_t n, int 
 int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
                              int world, int dtype, void* stream);
 
+/* The residual form, with no summing kernel: tc_gemv_allreduce_residual sends its rows like
+ * tc_gemv_allreduce, then each CTA waits (bounded; TC_DEVERR_PEER_TIMEOUT) for the other ranks'
+ * words of its own rows and adds the sum into the residual: h[i] = dtype(h[i] + dtype(sum over
+ * ranks, rank order)), the arithmetic of tc_allreduce_add_rmsnorm (every rank ends with the same
+ * bits of h [n]); it also records, in this rank's region, the sum of squares of the new h. With
+ * world == 1 no word is sent (regions[0] is this rank's region) and h += the rounded product.
+ * tc_gemv_rmsnorm, after it: out [n] = RMSNorm(h) * norm_weight (hidden = k, eps; 1/rms from the
+ * recorded sums of squares, in a fixed order) times w [n][k]^T — the norm is the GEMV's input
+ * staging. Together they replace the transformers Qwen3 residual add + RMSNorm + next projection
+ * of the per-token model call (threadcut/engine.py:66-73) in the tensor-parallel step, two
+ * launches where tc_gemv_allreduce + tc_allreduce_add_rmsnorm + tc_gemv are three. Every rank
+ * calls them in the same order, each residual sum followed by one tc_gemv_rmsnorm before the next
+ * residual sum; the region must be tc_allreduce_region_bytes(world, n) bytes, zeroed. */
+int tc_gemv_allreduce_residual(const void* x, const void* w, int64_t n, int k, void* const* regions, int world,
+                               int rank, void* h, int dtype, void* stream);
+/* tc_gemv_allreduce_residual of the SwiGLU activation of gate_up [2k], as tc_gemv_swiglu. */
+int tc_gemv_allreduce_residual_swiglu(const void* gate_up, const void* w, int64_t n, int k, void* const* regions,
+                                      int world, int rank, void* h, int dtype, void* stream);
+int tc_gemv_rmsnorm(const void* h, const void* norm_weight, const void* region, float eps, const void* w, void* out,
+                    int64_t n, int k, int dtype, void* stream);
+
 /* All-gather + log-sum-exp merge of sequence-shard partials through peer memory, one launch: every
  * rank's fp32 partial o_local [rows][d] (normalised) and natural-log lse_local [rows] of its token
  * slice (tc_decode_attention_partial*) are pushed into every other rank's region (regions as for

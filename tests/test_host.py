@@ -387,7 +387,8 @@ def test_peer_sum_argument_validation_without_a_gpu():
     """The peer-memory sums check their arguments before touching the device."""
     L = _lib.lib()
     assert L.tc_peer_handle_bytes() == 64
-    assert L.tc_allreduce_region_bytes(8, 2560) == 256 + 2 * 8 * 2560 * 8
+    # 2 KB of control (sequence, CTA count, the residual form's sums of squares), then 2 slots of words
+    assert L.tc_allreduce_region_bytes(8, 2560) == 2048 + 2 * 8 * 2560 * 8
     assert L.tc_allreduce_region_bytes(9, 2560) == 0 and L.tc_allreduce_region_bytes(2, 0) == 0
     regs = (ctypes.c_void_p * 2)(256, 512)
     assert L.tc_gemv_allreduce(16, 16, 2560, 512, regs, 2, 0, 0, None) == 3        # fp32: dtype
@@ -398,6 +399,15 @@ def test_peer_sum_argument_validation_without_a_gpu():
     assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 9000, 1e-6, 256, 2, 2, None) == 1  # hidden too large
     assert L.tc_allreduce_add_rmsnorm(16, 16, 16, 2560, 1e-6, 100, 2, 2, None) == 1  # region misaligned
     assert L.tc_peer_open(None, None) == 1 and L.tc_peer_close(None) == 1 and L.tc_peer_free(None) == 1
+    # residual form and the normalised-input projection
+    assert L.tc_gemv_allreduce_residual(16, 16, 2560, 512, regs, 2, 0, None, 2, None) == 1    # no residual
+    assert L.tc_gemv_allreduce_residual(16, 16, 2560, 512, regs, 2, 0, 32, 0, None) == 3      # fp32: dtype
+    assert L.tc_gemv_allreduce_residual_swiglu(16, 16, 2560, 500, regs, 2, 0, 32, 2, None) == 1  # k % 8
+    assert L.tc_gemv_rmsnorm(16, 16, 256, 1e-6, 16, 16, 64, 2560, 0, None) == 3               # fp32: dtype
+    assert L.tc_gemv_rmsnorm(16, 16, 256, 1e-6, 16, 16, 64, 2561, 2, None) == 1               # k % 8
+    assert L.tc_gemv_rmsnorm(16, 16, 256, -1.0, 16, 16, 64, 2560, 2, None) == 1               # eps < 0
+    assert L.tc_gemv_rmsnorm(8, 16, 256, 1e-6, 16, 16, 64, 2560, 2, None) == 2                # h misaligned
+    assert L.tc_gemv_rmsnorm(16, 16, None, 1e-6, 16, 16, 64, 2560, 2, None) == 1              # no region
 
 
 def test_peer_gather_argument_validation_without_a_gpu():

@@ -169,3 +169,41 @@ def test_attention_with_norm_rope_rejects_what_it_cannot_fuse():
     qb, kb, rb, wb = (t.to(torch.bfloat16) for t in (q, k, row, w))
     with pytest.raises(ValueError):
         fd.decode_attention_append_rope(qb, kb, kb.clone(), rb, rb, wb[:64], wb, wb, wb, 1e-6, 0.1)
+
+
+@pytest.mark.parametrize("hidden,k,n,swiglu", [(2560, 4096, 19456, False), (2560, 9728, 6144, True),
+                                               (256, 512, 300, False), (2048, 64, 24, True)])
+def test_residual_sum_and_norm_staging_equal_the_separate_launches(hidden, k, n, swiglu):
+    """World 1 of the residual-form sums (peer.AllReduce.gemv_residual, then gemv_norm): h after the
+    projection has exactly the bits of tc_gemv (or tc_gemv_swiglu) followed by tc_add_rmsnorm's
+    residual add, and the next projection of RMSNorm(h) equals tc_add_rmsnorm + tc_gemv within one
+    rounding step (its 1/rms adds the squares in another order), nearly all bit-identical. Several
+    rounds in a row, so the recorded sums of squares are always the last residual sum's."""
+    from threadcut_b200.peer import AllReduce
+    dt = torch.bfloat16
+    gen = torch.Generator(device=DEV).manual_seed(hidden + k + n)
+    ar = AllReduce(hidden, DEV, world=1)
+    try:
+        h_a = torch.randn(1, hidden, generator=gen, device=DEV).to(dt)
+        h_b = h_a.clone()
+        nw = (1 + 0.1 * torch.randn(hidden, generator=gen, device=DEV)).to(dt)
+        for rnd in range(3):
+            x = (torch.randn(1, 2 * k if swiglu else k, generator=gen, device=DEV) * (1 + rnd)).to(dt)
+            w = (torch.randn(hidden, k, generator=gen, device=DEV) * k ** -0.5).to(dt)
+            w2 = (torch.randn(n, hidden, generator=gen, device=DEV) * hidden ** -0.5).to(dt)
+            # separate launches
+            part = tp._gemv_swiglu(x, w) if swiglu else tp._gemv(x, w)
+            xn = torch.empty_like(h_a)
+            tp._add_rmsnorm(h_a, part, nw, xn, 1e-6)
+            want = tp._gemv(xn, w2)
+            # residual form
+            ar.gemv_residual(x[0], w, h_b, swiglu=swiglu)
+            got = ar.gemv_norm(h_b, nw, w2, 1e-6)
+            torch.cuda.synchronize()
+            assert torch.equal(h_b, h_a), rnd
+            diff = (got.float() - want.float()).abs()
+            assert bool((diff <= 2 ** -6 * want.float().abs().clamp(min=1.0)).all()), (rnd, float(diff.max()))
+            assert float((got == want).float().mean()) >= 0.9, rnd
+    finally:
+        torch.cuda.synchronize()
+        ar.close()

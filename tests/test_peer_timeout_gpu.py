@@ -76,3 +76,26 @@ def test_gather_wait_for_a_missing_rank_times_out():
     torch.cuda.synchronize()
     assert _lib.device_errors(clear=True) == 0
     _free(ptrs)
+
+
+def test_residual_sum_wait_for_a_missing_rank_times_out():
+    """The residual form: each CTA of the projection waits for rank 1's words of its own rows, which
+    never come; every wait runs out, the residual gets rank 0's part alone, the bit is set."""
+    torch.cuda.set_device(DEV)
+    L = _lib.lib()
+    _lib.device_errors(clear=True)
+    hidden, k = 256, 64
+    ptrs = _regions(L.tc_allreduce_region_bytes(2, hidden))
+    arr = (ctypes.c_void_p * 2)(*ptrs)
+    x = torch.randn(1, k, device=DEV).to(torch.bfloat16)
+    w = torch.randn(hidden, k, device=DEV).to(torch.bfloat16)
+    h = torch.zeros(1, hidden, device=DEV).to(torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.tc_gemv_allreduce_residual(x.data_ptr(), w.data_ptr(), hidden, k, arr, 2, 0, h.data_ptr(),
+                                        _lib.TC_BF16, st) == 0
+    assert _lib.device_errors(clear=True) == PEER_TIMEOUT
+    mine = (x.float() @ w.float().t()).to(torch.bfloat16)
+    torch.testing.assert_close(h.float(), mine.float(), rtol=2 ** -7, atol=1e-2)
+    torch.cuda.synchronize()
+    assert _lib.device_errors(clear=True) == 0
+    _free(ptrs)

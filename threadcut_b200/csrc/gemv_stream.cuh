@@ -14,8 +14,14 @@
 // too made the 19456 x 2560 projection 31 % slower, 24.5 vs 18.8 us). Each lane sums the row's
 // 16-byte columns lane, lane + 32, ... in order and the lanes reduce by xor shuffles: the same order as gemv_kernel with one row per warp, so the result
 // bits are those of tc_gemv's single-row pass. Epilogues: the row rounded to T into `out`, or (kAR)
-// the fp32 row as a (value, epoch) word into every rank's region (as gemv_allreduce_kernel).
-// kSwiGLU: x is gate|up [2K] and the staged input is the SwiGLU activation (stage_x).
+// the fp32 row as a (value, epoch) word into every rank's region (as gemv_allreduce_kernel); in
+// the residual form (ar.h set) the CTA then waits for the other ranks' words of its own rows, adds
+// them in rank order into the residual h (h = T(h + T(sum)), the arithmetic of
+// tc_allreduce_add_rmsnorm) and records its rows' sum of squares of the new h, so that no separate
+// summing kernel runs.
+// Inputs: x [K]; kSwiGLU: x is gate|up [2K] and the staged input is the SwiGLU activation
+// (stage_x); kNormIn: the staged input is RMSNorm(h) * weight, its 1/rms computed from the sums of
+// squares a residual-form projection recorded (ni.ss; every CTA adds them in the same order).
 #pragma once
 
 #include <stdint.h>
@@ -28,6 +34,15 @@ constexpr int kGsMaxStages = 16;
 constexpr int kGsSmemBudget = 200 * 1024;          // x + ring, of the 227 KB a CTA may use
 constexpr int kGsMaxRowsPerCta = 64;               // kAR: rows whose results are kept for the stores
 constexpr int kGsStageBatch = 6;                   // x chunks per thread loaded before use (one batch: K <= 12288)
+
+// kNormIn: x = T(weight * T(h * rsqrt(sum(ss) * inv_h + eps))), ss the kArSsParts partial sums of
+// squares of h written by the residual-form projection before (unused entries 0).
+struct NormIn {
+  const void* h;
+  const void* weight;
+  const float* ss;
+  float inv_h, eps;
+};
 
 struct GsPlan {
   int rs;          // rows per stage
@@ -55,14 +70,16 @@ __device__ __forceinline__ void consumer_bar() {
 }
 
 // The rows [r0, r1) of CTA c: an even split of N rows over gridDim.x CTAs.
-template <typename T, bool kSwiGLU, bool kAR>
+template <typename T, bool kSwiGLU, bool kAR, bool kNormIn>
 __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                     T* __restrict__ out, int64_t N, int K,
                                                                     const __grid_constant__ ArPeers ar,
-                                                                    const GsPlan g) {
+                                                                    const GsPlan g,
+                                                                    const __grid_constant__ NormIn ni) {
   extern __shared__ __align__(128) uint8_t gs_smem[];
   __shared__ uint64_t full[kGsMaxStages], empty[kGsMaxStages];
   __shared__ float res[kAR ? kGsMaxRowsPerCta : 1];
+  __shared__ float red[kGsConsumers];
   uint4* xs = reinterpret_cast<uint4*>(gs_smem);
   uint8_t* ring = gs_smem + g.x_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -108,19 +125,49 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
   } else {
     pdl_launch();
     pdl_wait();  // x is the previous kernel's output
+    // residual form: this sum's number and this thread's residual element, loaded now so that the
+    // epilogue does not wait for them
+    unsigned int sq_pre = 0u;
+    float h_pre = 0.f;
+    if constexpr (kAR) {
+      sq_pre = *ar.seq;
+      if (ar.h != nullptr && (int)threadIdx.x < nrows) h_pre = to_f32(static_cast<const T*>(ar.h)[r0 + threadIdx.x]);
+    }
     {
       // each thread issues the loads of up to kGsStageBatch of its 16-byte chunks before using any,
       // so staging x costs one L2 round trip per batch instead of one per chunk
       const int kc = K / 8;
-      const uint4* xg = reinterpret_cast<const uint4*>(x);
-      for (int base = threadIdx.x; base < kc; base += 32 * kGsConsumers * kGsStageBatch) {
-        uint4 gv[kGsStageBatch], uv[kSwiGLU ? kGsStageBatch : 1];
+      float rn = 0.f;
+      float sv[kNormIn ? kArSsParts / 32 : 1];
+      if constexpr (kNormIn) {
+#pragma unroll
+        for (int q = 0; q < kArSsParts / 32; ++q) sv[q] = ni.ss[lane + 32 * q];
+      }
+      const uint4* xg = reinterpret_cast<const uint4*>(kNormIn ? ni.h : static_cast<const void*>(x));
+      const uint4* nw = reinterpret_cast<const uint4*>(ni.weight);
+      constexpr int kStride = 32 * kGsConsumers * kGsStageBatch;
+      // every consumer thread runs the first pass (the 1/rms reduction below needs whole warps)
+      for (int base = threadIdx.x;; base += kStride) {
+        uint4 gv[kGsStageBatch], uv[(kSwiGLU || kNormIn) ? kGsStageBatch : 1];
 #pragma unroll
         for (int u = 0; u < kGsStageBatch; ++u) {
           const int i = base + u * 32 * kGsConsumers;
           if (i < kc) {
             gv[u] = xg[i];
             if constexpr (kSwiGLU) uv[u] = reinterpret_cast<const uint4*>(x + K)[i];
+            if constexpr (kNormIn) uv[u] = nw[i];
+          }
+        }
+        if constexpr (kNormIn) {
+          if (base == (int)threadIdx.x) {
+            // 1/rms of h: lane l adds parts l, l + 32, ... in order, then a xor butterfly (every
+            // warp of every CTA computes the same value)
+            float t = 0.f;
+#pragma unroll
+            for (int q = 0; q < kArSsParts / 32; ++q) t += sv[q];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+            rn = rsqrtf(t * ni.inv_h + ni.eps);
           }
         }
 #pragma unroll
@@ -139,11 +186,21 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
                 oe[t] = from_f32<T>(act * to_f32(ue[t]));
               }
               xs[i] = o;
+            } else if constexpr (kNormIn) {
+              // the arithmetic of add_rmsnorm_kernel's output: T(weight * T(h * rn))
+              const T* he = reinterpret_cast<const T*>(&gv[u]);
+              const T* we = reinterpret_cast<const T*>(&uv[u]);
+              uint4 o;
+              T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) oe[t] = from_f32<T>(to_f32(we[t]) * to_f32(from_f32<T>(to_f32(he[t]) * rn)));
+              xs[i] = o;
             } else {
               xs[i] = gv[u];
             }
           }
         }
+        if (base + kStride >= kc) break;
       }
     }
     consumer_bar();
@@ -183,12 +240,70 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
     }
     if constexpr (kAR) {
       consumer_bar();  // every row's result is in res
-      const unsigned int sq = *ar.seq;
+      const unsigned int sq = sq_pre;
       const uint64_t ep = (uint64_t)(sq + 1u) << 32;
-      const int64_t slot_off = (int64_t)(sq % kArSlots) * ar.world * ar.rows + (int64_t)ar.rank * ar.rows;
-      for (int idx = threadIdx.x; idx < ar.world * nrows; idx += 32 * kGsConsumers) {
-        const int p = idx / nrows, i = idx - p * nrows;
-        st_sys_u64(ar.data[p] + slot_off + r0 + i, ep | __float_as_uint(res[i]));
+      const int64_t slot = (int64_t)(sq % kArSlots) * ar.world * ar.rows;
+      const int64_t slot_off = slot + (int64_t)ar.rank * ar.rows;
+      if (ar.world > 1 || ar.h == nullptr) {
+        for (int idx = threadIdx.x; idx < ar.world * nrows; idx += 32 * kGsConsumers) {
+          const int p = idx / nrows, i = idx - p * nrows;
+          st_sys_u64(ar.data[p] + slot_off + r0 + i, ep | __float_as_uint(res[i]));
+        }
+      }
+      if (ar.h != nullptr) {
+        // residual form: the sum of this CTA's rows over the ranks (rank order), into h
+        T* hh = static_cast<T*>(ar.h);
+        float sq2 = 0.f;
+        const int i = threadIdx.x;  // at most kGsMaxRowsPerCta rows: one per consumer thread
+        if (i < nrows) {
+          const uint64_t* mine = ar.data[ar.rank] + slot + r0 + i;
+          uint64_t wv[kArMaxWorld];
+#pragma unroll
+          for (int r = 0; r < kArMaxWorld; ++r)
+            if (r < ar.world && r != ar.rank) wv[r] = ld_sys_u64(mine + (int64_t)r * ar.rows);
+          float sum = 0.f;
+#pragma unroll
+          for (int r = 0; r < kArMaxWorld; ++r) {
+            if (r >= ar.world) continue;
+            float v = res[i];
+            if (r != ar.rank) {
+              uint32_t spin = 0;
+              while ((uint32_t)(wv[r] >> 32) != (uint32_t)(sq + 1u)) {
+                if (++spin >= kSpinLimit / 64) {
+                  raise_error(TC_DEVERR_PEER_TIMEOUT);
+                  wv[r] = ep;  // value 0
+                  break;
+                }
+                __nanosleep(64);
+                wv[r] = ld_sys_u64(mine + (int64_t)r * ar.rows);
+              }
+              v = __uint_as_float((uint32_t)wv[r]);
+            }
+            sum += v;
+          }
+          const T nh = from_f32<T>(h_pre + to_f32(from_f32<T>(sum)));
+          hh[r0 + i] = nh;
+          sq2 = to_f32(nh) * to_f32(nh);
+        }
+        // the CTA's sum of squares, in a fixed order: each warp's xor butterfly, then the warps in order
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq2 += __shfl_xor_sync(0xffffffffu, sq2, o);
+        if (lane == 0) red[warp] = sq2;
+        consumer_bar();  // also: every consumer thread has read *ar.seq and its words
+        if (threadIdx.x == 0) {
+          float t = 0.f;
+#pragma unroll
+          for (int q = 0; q < kGsConsumers; ++q) t += red[q];
+          ar.ss[blockIdx.x] = t;
+          if (ar.world > 1) {
+            __threadfence();
+            const unsigned int prev = atomicAdd(ar.done, 1u);
+            if (prev == gridDim.x - 1) {  // the last CTA: every CTA has read seq; the sum is complete
+              *ar.done = 0u;
+              *const_cast<unsigned int*>(ar.seq) = sq + 1u;
+            }
+          }
+        }
       }
     }
   }

@@ -10,11 +10,15 @@
 // order on every rank, so every rank holds the same bits), rounds the sum to the model dtype (the
 // projection's output dtype) and continues as tc_add_rmsnorm: residual add, RMSNorm.
 //
-// Region of each rank (zeroed at creation): [0, 256) control (word 0: this rank's count of
-// completed sums, `seq`; read and advanced only by its own kernels), then the data
-// [kArSlots][world][rows] of uint64 words. The sum number s uses slot s % kArSlots and epoch s + 1.
-// Two slots suffice: a rank writes sum s + 2 into slot s % 2 of rank r only after its own sum s + 1
-// has received r's rows of s + 1, which r sends after it finished reading sum s.
+// Region of each rank (zeroed at creation): [0, kArDataOffset) control (word 0: this rank's count
+// of completed sums, `seq`; word 1: CTAs of the current residual sum done; at kArSsOffset the
+// residual sum's per-CTA sums of squares, kArSsParts floats; all read and written only by this
+// rank's kernels), then the data [kArSlots][world][rows] of uint64 words. The sum number s uses
+// slot s % kArSlots and epoch s + 1. Two slots suffice: a rank writes sum s + 2 into slot s % 2 of
+// rank r only after its own sum s + 1 has received r's rows of s + 1, which r sends after it
+// finished reading sum s. (The residual form completes the sum inside the projection: its CTA c
+// waits only for the other ranks' rows of c's own block, and the same argument holds block by
+// block, every rank splitting the rows over its CTAs alike.)
 #pragma once
 
 #include <stdint.h>
@@ -23,7 +27,10 @@ namespace tc {
 
 constexpr int kArSlots = 2;
 constexpr int kArMaxWorld = 8;
-constexpr int kArCtrlBytes = 256;
+constexpr int kArCtrlBytes = 256;     // control bytes of a gather region (below)
+constexpr int kArDataOffset = 2048;  // start of the words in a sum region
+constexpr int kArSsOffset = 1024;    // the residual sum's per-CTA sums of squares in a sum region
+constexpr int kArSsParts = 256;      // their count (CTAs of a residual sum; unused entries stay 0)
 constexpr int kArRows = 16;          // GEMV rows per CTA (2 per warp)
 constexpr int kArThreads = 256;
 constexpr int kArNormThreads = 1024;
@@ -34,6 +41,12 @@ struct ArPeers {
   const unsigned int* seq;      // this rank's completed-sum count (its own region's control word)
   int world, rank;
   int64_t rows;                 // words per (slot, rank): the hidden size
+  // residual form (h != null): the projection completes the sum itself, h[i] = T(h[i] + T(sum)),
+  // writes each CTA's sum of squares of the new h to ss[blockIdx.x], and the last CTA done
+  // (count in *done) advances *seq
+  void* h;
+  float* ss;
+  unsigned int* done;
 };
 
 __device__ __forceinline__ void st_sys_u64(uint64_t* p, uint64_t v) {

@@ -1445,22 +1445,34 @@ int gemv_stream_budget() {
   return b;
 }
 
-template <typename T>
-cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
-                            const void* w, void* out, int64_t n, int k, int sms, int dev) {
-  const GsPlan g = gs_plan(k, gemv_stream_budget());
+// CTAs of a streaming GEMV: one per SM (at most one per row), more when a CTA would keep more than
+// kGsMaxRowsPerCta results (the sum forms).
+int64_t stream_ctas(int64_t n, int sms, bool ar_mode) {
   int64_t c = n < sms ? n : sms;
   if (ar_mode && (n + c - 1) / c > kGsMaxRowsPerCta) c = (n + kGsMaxRowsPerCta - 1) / kGsMaxRowsPerCta;
+  return c;
+}
+
+template <typename T>
+cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
+                            const void* w, void* out, int64_t n, int k, int sms, int dev,
+                            const NormIn* norm_in = nullptr) {
+  const GsPlan g = gs_plan(k, gemv_stream_budget());
+  const int64_t c = stream_ctas(n, sms, ar_mode);
   const int smem = g.x_bytes + g.nstages * g.stage_bytes;
   const T* xp = static_cast<const T*>(x);
   const T* wp = static_cast<const T*>(w);
   T* op = static_cast<T*>(out);
-  auto fn = ar_mode ? (swiglu ? gemv_stream_kernel<T, true, true> : gemv_stream_kernel<T, false, true>)
-                    : (swiglu ? gemv_stream_kernel<T, true, false> : gemv_stream_kernel<T, false, false>);
+  NormIn ni;
+  std::memset(&ni, 0, sizeof(ni));
+  if (norm_in != nullptr) ni = *norm_in;
+  auto fn = norm_in != nullptr ? gemv_stream_kernel<T, false, false, true>
+            : ar_mode ? (swiglu ? gemv_stream_kernel<T, true, true, false> : gemv_stream_kernel<T, false, true, false>)
+                      : (swiglu ? gemv_stream_kernel<T, true, false, false> : gemv_stream_kernel<T, false, false, false>);
   // the opt-in is set once per (kernel, device) by set_smem: ask for the budget every plan fits in
   const cudaError_t e = set_smem(reinterpret_cast<const void*>(fn), kGsSmemBudget, dev);
   if (e != cudaSuccess) return e;
-  return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar, g);
+  return launch_pdl(fn, dim3((unsigned)c), dim3(kGsThreads), (size_t)smem, st, xp, wp, op, n, k, ar, g, ni);
 }
 
 template <typename T>
@@ -1576,13 +1588,15 @@ int tc_peer_free(void* dev_ptr) {
 
 size_t tc_allreduce_region_bytes(int world, int64_t rows) {
   if (world < 1 || world > kArMaxWorld || rows < 1 || rows > 8192) return 0;
-  return (size_t)kArCtrlBytes + (size_t)kArSlots * world * rows * sizeof(uint64_t);
+  return (size_t)kArDataOffset + (size_t)kArSlots * world * rows * sizeof(uint64_t);
 }
 
 namespace {
 int run_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* const* regions, int world, int rank,
-                       int dtype, void* stream, bool swiglu) {
+                       int dtype, void* stream, bool swiglu, void* residual = nullptr) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (residual != nullptr && (!gemv_stream_enabled() || (reinterpret_cast<uintptr_t>(residual) & 1)))
+    return TC_ERR_INVALID;  // the residual form is a streaming-GEMV epilogue
   if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world || regions == nullptr) return TC_ERR_INVALID;
   if (n < 1 || n > 8192 || k < 8 || k % 8 || k > 24576) return TC_ERR_INVALID;
   if (x == nullptr || w == nullptr) return TC_ERR_INVALID;
@@ -1591,13 +1605,20 @@ int run_gemv_allreduce(const void* x, const void* w, int64_t n, int k, void* con
   std::memset(&ar, 0, sizeof(ar));
   for (int p = 0; p < world; ++p) {
     if (regions[p] == nullptr || (reinterpret_cast<uintptr_t>(regions[p]) & 255)) return TC_ERR_INVALID;
-    ar.data[p] = reinterpret_cast<uint64_t*>(static_cast<char*>(regions[p]) + kArCtrlBytes);
+    ar.data[p] = reinterpret_cast<uint64_t*>(static_cast<char*>(regions[p]) + kArDataOffset);
   }
   ar.seq = static_cast<const unsigned int*>(regions[rank]);
   ar.world = world;
   ar.rank = rank;
   ar.rows = n;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (residual != nullptr) {
+    const int dev = current_device();
+    if (stream_ctas(n, sm_count(dev), true) > kArSsParts) return TC_ERR_INVALID;
+    ar.h = residual;
+    ar.ss = reinterpret_cast<float*>(static_cast<char*>(regions[rank]) + kArSsOffset);
+    ar.done = static_cast<unsigned int*>(regions[rank]) + 1;
+  }
   if (gemv_stream_enabled()) {
     const int dev = current_device();
     const cudaError_t e =
@@ -1640,6 +1661,45 @@ int tc_gemv_allreduce_swiglu(const void* gate_up, const void* w, int64_t n, int 
   return run_gemv_allreduce(gate_up, w, n, k, regions, world, rank, dtype, stream, true);
 }
 
+int tc_gemv_allreduce_residual(const void* x, const void* w, int64_t n, int k, void* const* regions, int world,
+                               int rank, void* h, int dtype, void* stream) {
+  if (h == nullptr) return TC_ERR_INVALID;
+  return run_gemv_allreduce(x, w, n, k, regions, world, rank, dtype, stream, false, h);
+}
+
+int tc_gemv_allreduce_residual_swiglu(const void* gate_up, const void* w, int64_t n, int k, void* const* regions,
+                                      int world, int rank, void* h, int dtype, void* stream) {
+  if (h == nullptr) return TC_ERR_INVALID;
+  return run_gemv_allreduce(gate_up, w, n, k, regions, world, rank, dtype, stream, true, h);
+}
+
+int tc_gemv_rmsnorm(const void* h, const void* norm_weight, const void* region, float eps, const void* w, void* out,
+                    int64_t n, int k, int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (n < 0 || k < 8 || k % 8 || k > 8 * kGsStageBatch * 32 * kGsConsumers || !(eps >= 0.f)) return TC_ERR_INVALID;
+  if (n == 0) return TC_OK;
+  if (h == nullptr || norm_weight == nullptr || region == nullptr || w == nullptr || out == nullptr)
+    return TC_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(region)) & 15)
+    return TC_ERR_ALIGN;
+  if (!gemv_stream_enabled()) return TC_ERR_INVALID;  // the normalised input is a streaming-GEMV staging mode
+  NormIn ni;
+  ni.h = h;
+  ni.weight = norm_weight;
+  ni.ss = reinterpret_cast<const float*>(static_cast<const char*>(region) + kArSsOffset);
+  ni.inv_h = 1.0f / (float)k;
+  ni.eps = eps;
+  ArPeers none;
+  std::memset(&none, 0, sizeof(none));
+  const int dev = current_device();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      dtype == TC_BF16 ? launch_stream_t<__nv_bfloat16>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni)
+                       : launch_stream_t<__half>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni);
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
 int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden, float eps, void* region,
                              int world, int dtype, void* stream) {
   if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
@@ -1648,7 +1708,7 @@ int tc_allreduce_add_rmsnorm(void* h, const void* weight, void* out, int hidden,
   if (h == nullptr || weight == nullptr || out == nullptr || region == nullptr) return TC_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(region) & 255) return TC_ERR_INVALID;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const uint64_t* mine = reinterpret_cast<const uint64_t*>(static_cast<char*>(region) + kArCtrlBytes);
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(static_cast<char*>(region) + kArDataOffset);
   unsigned int* seq = static_cast<unsigned int*>(region);
   const int64_t rows = hidden;
   cudaError_t e;

@@ -8,8 +8,11 @@ region of its own memory mapped into every other rank's address space: the libra
 handle bytes), and each rank maps the others' (tc_peer_open). `AllReduce` keeps one such region
 per decoder and runs the fused sum: the row-split projection writes its rows into every rank's
 region (tc_gemv_allreduce), and the next kernel adds them up with the residual add and RMSNorm
-(tc_allreduce_add_rmsnorm). No collective library runs on that path; all ranks must make the same
-sequence of calls.
+(tc_allreduce_add_rmsnorm); or, in the residual form the tensor-parallel step uses, each CTA of the
+projection waits for the other ranks' rows of its own block and adds them into the residual itself
+(tc_gemv_allreduce_residual), and the next projection stages RMSNorm of the residual as its input
+(tc_gemv_rmsnorm). No collective library runs on that path; all ranks must make the same sequence
+of calls.
 """
 import ctypes
 
@@ -24,12 +27,16 @@ __all__ = ["PeerRegion", "AllReduce", "GatherMerge"]
 class PeerRegion:
     """`nbytes` of zeroed device memory on every rank of `group`, each rank's region mapped into
     every other rank's process. `ptrs[p]` is rank p's region as seen from this process. Collective:
-    every rank of the group constructs it at the same point."""
+    every rank of the group constructs it at the same point (world=1: this process's region alone,
+    not collective)."""
 
-    def __init__(self, nbytes, device, group=None):
+    def __init__(self, nbytes, device, group=None, world=None):
         self.device = torch.device(device)
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if world == 1:  # a region of this process only (no exchange, whatever group exists)
+            self.world, self.rank = 1, 0
+        else:
+            self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+            self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         L = lib()
         hb = L.tc_peer_handle_bytes()
         handle = (ctypes.c_uint8 * hb)()
@@ -70,17 +77,22 @@ class PeerRegion:
 
 
 class AllReduce:
-    """The sums of the tensor-parallel step over the ranks of `group`, for vectors of `hidden`
-    elements: gemv(x, w) starts one (w's rows are split over the ranks' columns: each rank holds a
-    partial product), add_rmsnorm(h, weight, out, eps) finishes it."""
+    """The sums of the tensor-parallel step over the ranks of `group` (world=1: one process, no
+    group), for vectors of `hidden` elements. Two forms:
+      gemv(x, w) starts one (w's rows are split over the ranks' columns: each rank holds a partial
+      product), add_rmsnorm(h, weight, out, eps) finishes it: h += sum, out = RMSNorm(h) * weight;
+      gemv_residual(x, w, h) does both halves of the sum in the projection (h += sum), and
+      gemv_norm(h, weight, w2, eps) is the next projection of RMSNorm(h) * weight (two launches
+      where the first form and the next projection take three)."""
 
-    def __init__(self, hidden, device, group=None):
+    def __init__(self, hidden, device, group=None, world=None):
         self.hidden = int(hidden)
-        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if world is None:
+            world = dist.get_world_size(group) if dist.is_initialized() else 1
         nbytes = lib().tc_allreduce_region_bytes(world, self.hidden)
         if nbytes == 0:
             raise ValueError(f"AllReduce: {world} ranks x {hidden} elements is outside the supported range")
-        self.region = PeerRegion(nbytes, device, group)
+        self.region = PeerRegion(nbytes, device, group, world=world)
 
     def gemv(self, x, w, swiglu=False):
         """Starts the sum of x @ w^T over the ranks (w [hidden, k], x [k]); swiglu: x is gate|up
@@ -93,6 +105,38 @@ class AllReduce:
         fn = lib().tc_gemv_allreduce_swiglu if swiglu else lib().tc_gemv_allreduce
         check("tc_gemv_allreduce", fn(x.data_ptr(), w.data_ptr(), n, k, r._arr, r.world, r.rank,
                                       dtype_code(x, "gemv_allreduce"), stream_ptr(x.device)))
+
+    def gemv_residual(self, x, w, h, swiglu=False):
+        """h [hidden] += the sum over the ranks of x @ w^T, completed inside the projection
+        (tc_gemv_allreduce_residual[_swiglu]); swiglu as for gemv. Every rank ends with the same h."""
+        require_cuda(x, w, h, what="gemv_allreduce_residual")
+        n, k = w.shape
+        if (n != self.hidden or x.numel() != (2 * k if swiglu else k) or h.numel() != n
+                or not (x.is_contiguous() and w.is_contiguous() and h.is_contiguous())
+                or not (x.dtype == w.dtype == h.dtype)):
+            raise ValueError("gemv_allreduce_residual: w [hidden, k], x [k] (gate|up [2k]), h [hidden], contiguous, "
+                             "one dtype")
+        r = self.region
+        fn = lib().tc_gemv_allreduce_residual_swiglu if swiglu else lib().tc_gemv_allreduce_residual
+        check("tc_gemv_allreduce_residual", fn(x.data_ptr(), w.data_ptr(), n, k, r._arr, r.world, r.rank, h.data_ptr(),
+                                               dtype_code(x, "gemv_allreduce_residual"), stream_ptr(x.device)))
+
+    def gemv_norm(self, h, weight, w, eps):
+        """[1, n] = (RMSNorm(h) * weight) @ w^T for w [n, hidden], right after a gemv_residual that
+        left h (tc_gemv_rmsnorm: the norm is the projection's input staging, its 1/rms from the sums
+        of squares that gemv_residual recorded)."""
+        require_cuda(h, weight, w, what="gemv_rmsnorm")
+        n, k = w.shape
+        if (k != self.hidden or h.numel() != k or weight.numel() != k
+                or not (h.is_contiguous() and weight.is_contiguous() and w.is_contiguous())
+                or not (h.dtype == weight.dtype == w.dtype)):
+            raise ValueError("gemv_rmsnorm: h and weight [hidden], w [n, hidden], contiguous, one dtype")
+        out = torch.empty((1, n), dtype=h.dtype, device=h.device)
+        r = self.region
+        check("tc_gemv_rmsnorm", lib().tc_gemv_rmsnorm(h.data_ptr(), weight.data_ptr(), r.ptrs[r.rank], float(eps),
+                                                       w.data_ptr(), out.data_ptr(), n, k, dtype_code(h, "gemv_rmsnorm"),
+                                                       stream_ptr(h.device)))
+        return out
 
     def add_rmsnorm(self, h, weight, out, eps):
         require_cuda(h, weight, out, what="allreduce_add_rmsnorm")

@@ -194,14 +194,15 @@ class TPDecoder:
         # q/k norm + RoPE inside the attention launch (the tensor-core decode kernel's shapes)
         self.fuse_rope = (self.dev.type == "cuda" and self.dtype in (torch.bfloat16, torch.float16)
                           and self.d in (64, 128, 256))
-        # the two sums per layer: through peer memory (one-shot, fused into the projection and the
-        # norm after it) on more than one rank unless peer_sums is False, else the collective library
+        # the two sums per layer: the residual form of the peer-memory sums (the row-split
+        # projection completes the sum into h, the next projection stages RMSNorm(h) as its input;
+        # at world 1 the same two kernels with no peer) unless peer_sums is False, else a separate
+        # GEMV, the collective library's all-reduce and the residual add + norm kernel
         self._ar = None
         self.use_peer_sums = False
-        if (self.world > 1 and peer_sums and self.dev.type == "cuda"
-                and self.dtype in (torch.bfloat16, torch.float16)):
+        if peer_sums and self.dev.type == "cuda" and self.dtype in (torch.bfloat16, torch.float16):
             from .peer import AllReduce
-            self._ar = AllReduce(cfg.hidden_size, self.dev, group)
+            self._ar = AllReduce(cfg.hidden_size, self.dev, group, world=self.world)
             self.use_peer_sums = True
 
     # ------------------------------------------------------------------ cache
@@ -238,50 +239,75 @@ class TPDecoder:
             dist.all_reduce(x, group=self.group)
         return x
 
-    def _final_hidden(self, token, pos):
-        """The step's arithmetic up to the final norm: [1, hidden] (appends the token's K/V row).
-        Per layer: the q/k/v projection, attention with the q/k norm + RoPE and the append fused
-        in (or the norm + RoPE as a launch of its own where the decode kernel cannot take it),
-        o_proj, sum over ranks, residual add + post-attention norm (one launch), the gate/up
-        projection, down_proj of the SwiGLU activation (computed by the projection's input staging),
-        sum over ranks, and the residual add fused with the next layer's input norm (the final norm
-        after the last layer). Every kernel launches with programmatic dependent launch: it starts
-        while its predecessor finishes (the projections pulling their weights into L2) and waits for
-        it before reading what it wrote."""
-        hr, d, g = self.h1 - self.h0, self.d, self.g
-        nq, eps = hr * g, self.eps
-        h = self.embed[token]  # [1, hidden], a fresh tensor (advanced indexing copies)
-        x = torch.empty_like(h)
+    def _rope(self, pos):
         ang = float(pos) * self.inv_freq
         emb = torch.cat((ang, ang))
-        cos = (emb.cos() * self.attn_scaling).to(self.dtype)
-        sin = (emb.sin() * self.attn_scaling).to(self.dtype)
+        return (emb.cos() * self.attn_scaling).to(self.dtype), (emb.sin() * self.attn_scaling).to(self.dtype)
+
+    def _attention(self, w, layer, qkv, cos, sin):
+        """The rank's attention of one layer from its q|k|v projection row (appends the K/V row):
+        q/k norm + RoPE inside the attention launch, or as a launch of its own where the decode
+        kernel cannot take it. Returns [1, local query heads * d]."""
+        hr, d, g = self.h1 - self.h0, self.d, self.g
+        nq = hr * g
+        q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
+        if self.fuse_rope:
+            o = _attend_rope(layer, q.view(hr, g, d), k, v, w.q_norm, w.k_norm, cos, sin, self.eps, self.scale)
+        else:
+            _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, self.eps)
+            o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
+        return o.reshape(1, nq * d)
+
+    def _logits_part(self, token, pos):
+        """This rank's vocabulary slice of the next-token logits, [1, v_local] (appends the token's
+        K/V row). With the residual sums (peer_sums, the default on a GPU), per layer: the q/k/v
+        projection with the input norm as its staging (the first layer: after its own norm
+        launch), attention, o_proj completing the sum over ranks into the residual, the gate/up
+        projection with the post-attention norm as its staging, down_proj of the SwiGLU activation
+        completing its sum; the final norm is the staging of lm_head: 5 launches per layer. Every
+        kernel launches with programmatic dependent launch: it starts while its predecessor
+        finishes (the projections pulling their weights into shared memory) and waits for it before
+        reading what it wrote."""
+        if not self.use_peer_sums:
+            return _gemv(self._final_hidden(token, pos), self.lm_head)
+        ar, eps = self._ar, self.eps
+        h = self.embed[token]  # [1, hidden], a fresh tensor (advanced indexing copies)
+        x = torch.empty_like(h)
+        cos, sin = self._rope(pos)
+        _add_rmsnorm(h, None, self.layers_w[0].in_norm, x, eps)
+        for i, (w, layer) in enumerate(zip(self.layers_w, self.layers)):
+            qkv = _gemv(x, w.wqkv)[0] if i == 0 else ar.gemv_norm(h, w.in_norm, w.wqkv, eps)[0]
+            ar.gemv_residual(self._attention(w, layer, qkv, cos, sin), w.wo, h)
+            ar.gemv_residual(ar.gemv_norm(h, w.post_norm, w.wgu, eps), w.wd, h, swiglu=True)
+        return ar.gemv_norm(h, self.final_norm, self.lm_head, eps)
+
+    def _final_hidden(self, token, pos):
+        """The step's arithmetic up to the final norm without the residual sums: [1, hidden]
+        (appends the token's K/V row). Per layer: the q/k/v projection, attention, o_proj, sum over
+        ranks (the collective library), residual add + post-attention norm (one launch), the gate/up
+        projection, down_proj of the SwiGLU activation (computed by the projection's input staging),
+        sum over ranks, and the residual add fused with the next layer's input norm (the final norm
+        after the last layer)."""
+        eps = self.eps
+        h = self.embed[token]  # [1, hidden], a fresh tensor (advanced indexing copies)
+        x = torch.empty_like(h)
+        cos, sin = self._rope(pos)
         _add_rmsnorm(h, None, self.layers_w[0].in_norm, x, eps)
         nxt = [w.in_norm for w in self.layers_w[1:]] + [self.final_norm]
         for w, layer, norm_next in zip(self.layers_w, self.layers, nxt):
-            qkv = _gemv(x, w.wqkv)[0]
-            q, k, v = qkv[:nq * d].view(nq, d), qkv[nq * d:(nq + hr) * d].view(hr, d), qkv[(nq + hr) * d:].view(hr, d)
-            if self.fuse_rope:
-                o = _attend_rope(layer, q.view(hr, g, d), k, v, w.q_norm, w.k_norm, cos, sin, eps, self.scale)
-            else:
-                _qk_norm_rope(q, k, w.q_norm, w.k_norm, cos, sin, eps)
-                o = _attend(layer, q.view(hr, g, d), k, v, self.scale)
-            self._sum_add_norm(o.reshape(1, nq * d), w.wo, h, w.post_norm, x)
+            o = self._attention(w, layer, _gemv(x, w.wqkv)[0], cos, sin)
+            self._sum_add_norm(o, w.wo, h, w.post_norm, x)
             gu = _gemv(x, w.wgu)
             self._sum_add_norm(gu, w.wd, h, norm_next, x, swiglu=True)
         return x
 
     def _sum_add_norm(self, a, w, h, norm, x, swiglu=False):
         """h += sum over ranks of a @ w^T (w: this rank's columns of a row-split projection), then
-        x = RMSNorm(h) * norm: through peer memory (tc_gemv_allreduce + tc_allreduce_add_rmsnorm)
-        or a collective all-reduce between tc_gemv and tc_add_rmsnorm. swiglu: a is gate|up and the
-        projection's input is its SwiGLU activation, computed by the GEMV as it stages its input."""
-        if self.use_peer_sums:
-            self._ar.gemv(a, w, swiglu=swiglu)
-            self._ar.add_rmsnorm(h, norm, x, self.eps)
-        else:
-            part = _gemv_swiglu(a, w) if swiglu else _gemv(a, w)
-            _add_rmsnorm(h, self._all_reduce(part), norm, x, self.eps)
+        x = RMSNorm(h) * norm, with a collective all-reduce between tc_gemv and tc_add_rmsnorm.
+        swiglu: a is gate|up and the projection's input is its SwiGLU activation, computed by the
+        GEMV as it stages its input."""
+        part = _gemv_swiglu(a, w) if swiglu else _gemv(a, w)
+        _add_rmsnorm(h, self._all_reduce(part), norm, x, self.eps)
 
     def close(self):
         """Releases the peer-memory region of the sums (collective: every rank calls it, after the
@@ -296,7 +322,7 @@ class TPDecoder:
     def step(self, token, pos):
         """Decode `token` (int64 device tensor [1]) at position `pos` (the cache length before the
         step); returns the greedy next token (int64 device tensor [1])."""
-        logits = _gemv(self._final_hidden(token, pos), self.lm_head)[0]  # this rank's vocabulary slice
+        logits = self._logits_part(token, pos)[0]  # this rank's vocabulary slice
         idx = logits.argmax()  # first index of the slice's maximum
         if self.world == 1:
             return idx.view(1)
@@ -345,7 +371,7 @@ class TPDecoder:
     def step_logits(self, token, pos):
         """The next-token logits in the model dtype, [1, vocab] (as the HF model's lm_head returns
         them), of `token` at `pos`; appends the token's row like step."""
-        part = _gemv(self._final_hidden(token, pos), self.lm_head)
+        part = self._logits_part(token, pos)
         if self.world == 1:
             return part
         parts = [torch.empty_like(part) for _ in range(self.world)]
@@ -355,7 +381,7 @@ class TPDecoder:
     def logits(self, token, pos):
         """The full next-token logits (fp32 [vocab]) of `token` at `pos`, for checks: the step's
         arithmetic with the vocabulary slices all-gathered. Appends the token's row like step."""
-        part = _gemv(self._final_hidden(token, pos), self.lm_head)[0].float()
+        part = self._logits_part(token, pos)[0].float()
         if self.world == 1:
             return part
         parts = [torch.empty_like(part) for _ in range(self.world)]
@@ -421,3 +447,4 @@ def restore(model):
     if saved is not None:
         model.forward = saved[1]
         del model._threadcut_fused_step
+        saved[0].close()
