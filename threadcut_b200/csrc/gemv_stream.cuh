@@ -2,10 +2,10 @@
 // persistent CTA per SM, the CTA's contiguous block of weight rows streamed through a shared-memory
 // ring by 1-D bulk copies (cp.async.bulk, mbarrier completion).
 //
-// The weights do not depend on the previous kernel, so the producer lane fills the whole ring
-// BEFORE griddepcontrol.wait: with programmatic dependent launch the first ~190 KB per SM (the
-// whole matrix for the tensor-parallel shards at 8 GPUs) are in shared memory by the time the
-// previous kernel finishes; x (the previous kernel's output) is read after the wait.
+// The weights do not depend on the previous kernel, so the producer lane starts the first
+// kGsPreWait stages BEFORE griddepcontrol.wait (with programmatic dependent launch they arrive while
+// the previous kernel finishes) and the rest of the ring after it; x (the previous kernel's output)
+// is read after the wait.
 //
 // Rows: each stage holds rs = max(1, 16 KB / row bytes) whole rows. With at least 8 stage chunks per
 // CTA, consumer warp j % 8 takes chunk j (8 stages consumed at once); with fewer, every consumer warp
@@ -34,6 +34,12 @@ constexpr int kGsMaxStages = 16;
 constexpr int kGsSmemBudget = 200 * 1024;          // x + ring, of the 227 KB a CTA may use
 constexpr int kGsMaxRowsPerCta = 64;               // kAR: rows whose results are kept for the stores
 constexpr int kGsStageBatch = 6;                   // x chunks per thread loaded before use (one batch: K <= 12288)
+// Stages the producer fills before griddepcontrol.wait. Filling the whole ring early (up to
+// ~190 KB per SM as soon as the CTA is resident) competes with the previous kernel's last CTAs for
+// HBM and delays its end: measured over the tensor-parallel step's projection chain (36 layers,
+// graph-timed) whole ring 54.6 us/layer at 1 GPU and 21.0 at the 8-GPU shapes, 4 stages 51.4 /
+// 20.7, none 50.7 / 20.0, 2 stages 49.4 / 19.8; the same 2 stages as L2 prefetches instead 52.3 / 20.2.
+constexpr int kGsPreWait = 2;
 
 // kNormIn: x = T(weight * T(h * rsqrt(sum(ss) * inv_h + eps))), ss the kArSsParts partial sums of
 // squares of h written by the residual-form projection before (unused entries 0).
@@ -97,12 +103,13 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
   }
   __syncthreads();
   if (warp == kGsConsumers) {
-    // producer: the whole ring is filled before waiting for the previous kernel (weights are
-    // constant), the rest as consumers free stages
+    // producer: kGsPreWait stages before waiting for the previous kernel (weights are constant),
+    // the rest of the ring after it, then each stage again as the consumers free it
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const char* base = reinterpret_cast<const char*>(w) + r0 * row_bytes;
-      const int pre = nchunks < g.nstages ? nchunks : g.nstages;
+      int pre = nchunks < g.nstages ? nchunks : g.nstages;
+      if (pre > kGsPreWait) pre = kGsPreWait;
       for (int j = 0; j < pre; ++j) {
         const int rows = nrows - j * g.rs < g.rs ? nrows - j * g.rs : g.rs;
         mbar_arrive_expect_tx(&full[j], (uint32_t)(rows * row_bytes));
@@ -110,6 +117,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
                  &full[j], pol);
       }
       pdl_launch();
+      pdl_wait();  // the rest of the ring only once the previous kernel is done (see kGsPreWait)
       for (int j = pre; j < nchunks; ++j) {
         const int s = j % g.nstages;
         if (!mbar_wait(&empty[s], ((j / g.nstages) - 1) & 1, TC_DEVERR_PIPE_TIMEOUT)) break;
