@@ -1103,6 +1103,19 @@ def run_ours(args, rank, local, world, dist):
         del g2, q2, k2, v2, o2
     if world == 1:
         sweep[str(N_CTX)] = {"us_per_layer": round(us_layer_rank, 3), "frac": round(achieved / hbm, 4)}
+    # configs 1 and 2 as decode steps: 1,536-token layers, and the 6,144 rows left after the
+    # config-2 splice as views of 8,192-row buffers (the GrowingLayer layout after a splice)
+    short = {}
+    for name, n, cap in (("cfg1_1536", 1536, 1536), ("cfg2_6144_of_8192", 6144, 8192)):
+        k2, v2 = workloads.layer_kv(n, LAYERS, dev, seed=3000 + n, cap=cap)
+        gq2 = torch.Generator(device=dev).manual_seed(4000 + n)
+        q2 = [torch.randn(8, 4, 128, generator=gq2, device=dev).to(torch.bfloat16) for _ in range(LAYERS)]
+        o2 = [torch.empty_like(q) for q in q2]
+        g2 = capture_step(q2, k2, v2, o2, dev)
+        t = max_over_ranks(time_graph(g2, args.steps, args.warmup, dist), dist)
+        short[name] = {"us_per_layer": round(t * 1000 / LAYERS, 3), "bytes_per_layer": 4096 * n + 16384,
+                       "frac": round((4096 * n + 16384) / (t * 1e-3 / LAYERS) / 1e9 / hbm, 4)}
+        del g2, q2, k2, v2, o2
     torch.cuda.empty_cache()
     shift_ms = max_over_ranks(time_shift(args.steps, args.warmup, dev, dist), dist)
     shift_gbs = SHIFT_BYTES_PER_LAYER * LAYERS / (shift_ms * 1e-3) / 1e9
@@ -1236,6 +1249,9 @@ def run_ours(args, rank, local, world, dist):
                   "workload": "cfg2 splice Split(2048,4096,4096) of an 8192-token bf16 cache, 36 layers in one "
                               "in-place launch; K rotated + V moved, read+write bytes"},
         "cfg3_sweep": sweep,
+        "cfg1_cfg2_decode": dict(short, what="36-layer decode graphs (stable rows) of config 1's 1,536-token layers and "
+                                              "of config 2's 6,144 rows after the splice (views of 8,192-row buffers); "
+                                              "launch-bound at these sizes"),
         "cfg4_ragged": cfg4,
         "append_16k": {"fused_us_per_layer": round(fused_ms * 1000.0 / LAYERS, 3),
                        "copy_then_decode_us_per_layer": round(unfused_ms * 1000.0 / LAYERS, 3),
