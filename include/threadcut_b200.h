@@ -504,6 +504,15 @@ int tc_gemv_allreduce_residual_swiglu(const void* gate_up, const void* w, int64_
                                       int world, int rank, void* h, int dtype, void* stream);
 int tc_gemv_rmsnorm(const void* h, const void* norm_weight, const void* region, float eps, const void* w, void* out,
                     int64_t n, int k, int dtype, void* stream);
+/* tc_gemv_rmsnorm of the MLP's gate/up projection with its rows interleaved (row 2i: the gate row
+ * of intermediate i, row 2i + 1: its up row; n even), writing the SwiGLU activation instead of
+ * the projection: out [n/2], out[i] = T(T(silu(gate_i)) * up_i) with gate_i and up_i the
+ * projection's outputs rounded to the dtype, tc_silu_mul's arithmetic. The down projection after it
+ * then takes a plain input (tc_gemv_allreduce_residual) instead of computing the activation in
+ * every CTA (tc_gemv_allreduce_residual_swiglu). Replaces the gate_proj/up_proj + act_fn * up of
+ * transformers' Qwen3 MLP in the per-token model call (threadcut/engine.py:66-73). */
+int tc_gemv_rmsnorm_swiglu(const void* h, const void* norm_weight, const void* region, float eps, const void* w,
+                           void* out, int64_t n, int k, int dtype, void* stream);
 
 /* All-gather + log-sum-exp merge of sequence-shard partials through peer memory, one launch: every
  * rank's fp32 partial o_local [rows][d] (normalised) and natural-log lse_local [rows] of its token

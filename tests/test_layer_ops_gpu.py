@@ -207,3 +207,42 @@ def test_residual_sum_and_norm_staging_equal_the_separate_launches(hidden, k, n,
     finally:
         torch.cuda.synchronize()
         ar.close()
+
+
+@pytest.mark.parametrize("hidden,inter", [(2560, 9728), (2560, 1216), (256, 304), (2048, 8)])
+def test_gate_up_with_swiglu_epilogue_equals_projection_then_silu_mul(hidden, inter):
+    """peer.AllReduce.gemv_norm_swiglu (tc_gemv_rmsnorm_swiglu: the gate/up projection of RMSNorm(h)
+    with interleaved rows, writing silu(gate) * up from its epilogue) against gemv_norm of the same
+    rows as [gate | up] followed by tc_silu_mul: bit for bit, after a residual sum as in the step.
+    The down projection of that activation (plain input) equals the SwiGLU-staging down projection
+    bit for bit too. Three rounds in a row."""
+    from threadcut_b200.peer import AllReduce
+    dt = torch.bfloat16
+    gen = torch.Generator(device=DEV).manual_seed(hidden + inter)
+    ar = AllReduce(hidden, DEV, world=1)
+    try:
+        h = torch.randn(1, hidden, generator=gen, device=DEV).to(dt)
+        nw = (1 + 0.1 * torch.randn(hidden, generator=gen, device=DEV)).to(dt)
+        for rnd in range(3):
+            o = (torch.randn(1, 512, generator=gen, device=DEV) * (1 + rnd)).to(dt)
+            wo = (torch.randn(hidden, 512, generator=gen, device=DEV) * 512 ** -0.5).to(dt)
+            gate = (torch.randn(inter, hidden, generator=gen, device=DEV) * hidden ** -0.5).to(dt)
+            up = (torch.randn(inter, hidden, generator=gen, device=DEV) * hidden ** -0.5).to(dt)
+            wd = (torch.randn(hidden, inter, generator=gen, device=DEV) * inter ** -0.5).to(dt)
+            ar.gemv_residual(o[0], wo, h)
+            gu = ar.gemv_norm(h, nw, torch.cat((gate, up)), 1e-6)
+            want = torch.empty(1, inter, dtype=dt, device=DEV)
+            tp._silu_mul(gu, want)
+            inter_rows = torch.stack((gate, up), dim=1).reshape(2 * inter, hidden).contiguous()
+            got = ar.gemv_norm_swiglu(h, nw, inter_rows, 1e-6)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (rnd, float((got.float() - want.float()).abs().max()))
+            h_a, h_b = h.clone(), h.clone()
+            ar.gemv_residual(gu[0], wd, h_a, swiglu=True)
+            ar.gemv_residual(got[0], wd, h_b)
+            torch.cuda.synchronize()
+            assert torch.equal(h_a, h_b), rnd
+            h = h_b
+    finally:
+        torch.cuda.synchronize()
+        ar.close()

@@ -87,6 +87,7 @@ SIGNATURES = {
     "tc_gemv_allreduce_residual": (_i, [_vp, _vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _vp, _i, _vp]),
     "tc_gemv_allreduce_residual_swiglu": (_i, [_vp, _vp, _i64, _i, ctypes.POINTER(_vp), _i, _i, _vp, _i, _vp]),
     "tc_gemv_rmsnorm": (_i, [_vp, _vp, _vp, _f, _vp, _vp, _i64, _i, _i, _vp]),
+    "tc_gemv_rmsnorm_swiglu": (_i, [_vp, _vp, _vp, _f, _vp, _vp, _i64, _i, _i, _vp]),
     "tc_gather_region_bytes": (_sz, [_i, _i64, _i]),
     "tc_peer_gather_merge": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i64, ctypes.POINTER(_vp), _i, _i, _i, _vp]),
 }

@@ -22,6 +22,11 @@
 // Inputs: x [K]; kSwiGLU: x is gate|up [2K] and the staged input is the SwiGLU activation
 // (stage_x); kNormIn: the staged input is RMSNorm(h) * weight, its 1/rms computed from the sums of
 // squares a residual-form projection recorded (ni.ss; every CTA adds them in the same order).
+// kActOut (the gate/up projection of the MLP, its rows interleaved: row 2i the gate row of
+// intermediate i, row 2i + 1 its up row): each CTA holds whole pairs, keeps its rows rounded to T
+// in shared memory and writes out[i] = T(T(silu(gate_i)) * up_i), silu_mul_kernel's arithmetic, so
+// that the down projection stages a plain input: the activation is computed once per element
+// instead of by every CTA of the down projection.
 #pragma once
 
 #include <stdint.h>
@@ -33,6 +38,7 @@ constexpr int kGsThreads = 32 * (kGsConsumers + 1);
 constexpr int kGsMaxStages = 16;
 constexpr int kGsSmemBudget = 200 * 1024;          // x + ring, of the 227 KB a CTA may use
 constexpr int kGsMaxRowsPerCta = 64;               // kAR: rows whose results are kept for the stores
+constexpr int kGsMaxActRows = 256;                 // kActOut: rows (gate/up pairs x 2) per CTA
 constexpr int kGsStageBatch = 6;                   // x chunks per thread loaded before use (one batch: K <= 12288)
 // Stages the producer fills before griddepcontrol.wait. Filling the whole ring early (up to
 // ~190 KB per SM as soon as the CTA is resident) competes with the previous kernel's last CTAs for
@@ -76,7 +82,7 @@ __device__ __forceinline__ void consumer_bar() {
 }
 
 // The rows [r0, r1) of CTA c: an even split of N rows over gridDim.x CTAs.
-template <typename T, bool kSwiGLU, bool kAR, bool kNormIn>
+template <typename T, bool kSwiGLU, bool kAR, bool kNormIn, bool kActOut = false>
 __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                     T* __restrict__ out, int64_t N, int K,
                                                                     const __grid_constant__ ArPeers ar,
@@ -84,12 +90,14 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
                                                                     const __grid_constant__ NormIn ni) {
   extern __shared__ __align__(128) uint8_t gs_smem[];
   __shared__ uint64_t full[kGsMaxStages], empty[kGsMaxStages];
-  __shared__ float res[kAR ? kGsMaxRowsPerCta : 1];
+  __shared__ float res[kAR ? kGsMaxRowsPerCta : (kActOut ? kGsMaxActRows : 1)];
   __shared__ float red[kGsConsumers];
   uint4* xs = reinterpret_cast<uint4*>(gs_smem);
   uint8_t* ring = gs_smem + g.x_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t r0 = N * blockIdx.x / gridDim.x, r1 = N * (blockIdx.x + 1) / gridDim.x;
+  // kActOut: an even split of the N / 2 row pairs
+  const int64_t r0 = kActOut ? 2 * ((N / 2) * blockIdx.x / gridDim.x) : N * blockIdx.x / gridDim.x;
+  const int64_t r1 = kActOut ? 2 * ((N / 2) * (blockIdx.x + 1) / gridDim.x) : N * (blockIdx.x + 1) / gridDim.x;
   const int nrows = (int)(r1 - r0);
   const int nchunks = (nrows + g.rs - 1) / g.rs;
   const int64_t row_bytes = (int64_t)K * 2;
@@ -239,12 +247,22 @@ __global__ void __launch_bounds__(kGsThreads, 1) gemv_stream_kernel(const T* __r
         if (lane == 0) {
           if constexpr (kAR)
             res[local] = acc;
+          else if constexpr (kActOut)
+            res[local] = to_f32(from_f32<T>(acc));  // the projection's output, rounded as stored
           else
             out[r0 + local] = from_f32<T>(acc);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if constexpr (kActOut) {
+      consumer_bar();  // every row's result is in res
+      for (int i = threadIdx.x; 2 * i < nrows; i += 32 * kGsConsumers) {
+        const float gf = res[2 * i];
+        const float act = to_f32(from_f32<T>(gf / (1.0f + expf(-gf))));
+        out[r0 / 2 + i] = from_f32<T>(act * res[2 * i + 1]);
+      }
     }
     if constexpr (kAR) {
       consumer_bar();  // every row's result is in res

@@ -1456,9 +1456,14 @@ int64_t stream_ctas(int64_t n, int sms, bool ar_mode) {
 template <typename T>
 cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaStream_t st, const void* x,
                             const void* w, void* out, int64_t n, int k, int sms, int dev,
-                            const NormIn* norm_in = nullptr) {
+                            const NormIn* norm_in = nullptr, bool act_out = false) {
   const GsPlan g = gs_plan(k, gemv_stream_budget());
-  const int64_t c = stream_ctas(n, sms, ar_mode);
+  int64_t c = stream_ctas(n, sms, ar_mode);
+  if (act_out) {  // whole gate/up pairs per CTA, at most kGsMaxActRows rows
+    const int64_t pairs = n / 2;
+    c = pairs < sms ? pairs : sms;
+    if (2 * ((pairs + c - 1) / c) > kGsMaxActRows) c = (pairs + kGsMaxActRows / 2 - 1) / (kGsMaxActRows / 2);
+  }
   const int smem = g.x_bytes + g.nstages * g.stage_bytes;
   const T* xp = static_cast<const T*>(x);
   const T* wp = static_cast<const T*>(w);
@@ -1466,7 +1471,8 @@ cudaError_t launch_stream_t(bool swiglu, bool ar_mode, const ArPeers& ar, cudaSt
   NormIn ni;
   std::memset(&ni, 0, sizeof(ni));
   if (norm_in != nullptr) ni = *norm_in;
-  auto fn = norm_in != nullptr ? gemv_stream_kernel<T, false, false, true>
+  auto fn = act_out            ? gemv_stream_kernel<T, false, false, true, true>
+            : norm_in != nullptr ? gemv_stream_kernel<T, false, false, true>
             : ar_mode ? (swiglu ? gemv_stream_kernel<T, true, true, false> : gemv_stream_kernel<T, false, true, false>)
                       : (swiglu ? gemv_stream_kernel<T, true, false, false> : gemv_stream_kernel<T, false, false, false>);
   // the opt-in is set once per (kernel, device) by set_smem: ask for the budget every plan fits in
@@ -1697,6 +1703,35 @@ int tc_gemv_rmsnorm(const void* h, const void* norm_weight, const void* region, 
   const cudaError_t e =
       dtype == TC_BF16 ? launch_stream_t<__nv_bfloat16>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni)
                        : launch_stream_t<__half>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni);
+  return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
+}
+
+int tc_gemv_rmsnorm_swiglu(const void* h, const void* norm_weight, const void* region, float eps, const void* w,
+                           void* out, int64_t n, int k, int dtype, void* stream) {
+  if (dtype != TC_BF16 && dtype != TC_F16) return TC_ERR_DTYPE;
+  if (n < 0 || n % 2 || k < 8 || k % 8 || k > 8 * kGsStageBatch * 32 * kGsConsumers || !(eps >= 0.f))
+    return TC_ERR_INVALID;
+  if (n == 0) return TC_OK;
+  if (h == nullptr || norm_weight == nullptr || region == nullptr || w == nullptr || out == nullptr)
+    return TC_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(w) |
+       reinterpret_cast<uintptr_t>(region)) & 15)
+    return TC_ERR_ALIGN;
+  if (!gemv_stream_enabled()) return TC_ERR_INVALID;  // a streaming-GEMV staging mode and epilogue
+  NormIn ni;
+  ni.h = h;
+  ni.weight = norm_weight;
+  ni.ss = reinterpret_cast<const float*>(static_cast<const char*>(region) + kArSsOffset);
+  ni.inv_h = 1.0f / (float)k;
+  ni.eps = eps;
+  ArPeers none;
+  std::memset(&none, 0, sizeof(none));
+  const int dev = current_device();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      dtype == TC_BF16
+          ? launch_stream_t<__nv_bfloat16>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni, true)
+          : launch_stream_t<__half>(false, false, none, st, h, w, out, n, k, sm_count(dev), dev, &ni, true);
   return e == cudaSuccess ? TC_OK : TC_ERR_CUDA;
 }
 

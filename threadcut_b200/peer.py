@@ -138,6 +138,25 @@ class AllReduce:
                                                        stream_ptr(h.device)))
         return out
 
+    def gemv_norm_swiglu(self, h, weight, w, eps):
+        """The SwiGLU activation [1, n/2] of (RMSNorm(h) * weight) @ w^T for the MLP's gate/up
+        projection with interleaved rows (w [n, hidden], row 2i gate_i, row 2i + 1 up_i), right
+        after a gemv_residual (tc_gemv_rmsnorm_swiglu): the projection's epilogue computes
+        silu(gate) * up once per element, so the down projection takes it as a plain input."""
+        require_cuda(h, weight, w, what="gemv_rmsnorm_swiglu")
+        n, k = w.shape
+        if (k != self.hidden or n % 2 or h.numel() != k or weight.numel() != k
+                or not (h.is_contiguous() and weight.is_contiguous() and w.is_contiguous())
+                or not (h.dtype == weight.dtype == w.dtype)):
+            raise ValueError("gemv_rmsnorm_swiglu: h and weight [hidden], w [n, hidden] (n even), contiguous, "
+                             "one dtype")
+        out = torch.empty((1, n // 2), dtype=h.dtype, device=h.device)
+        r = self.region
+        check("tc_gemv_rmsnorm_swiglu", lib().tc_gemv_rmsnorm_swiglu(
+            h.data_ptr(), weight.data_ptr(), r.ptrs[r.rank], float(eps), w.data_ptr(), out.data_ptr(), n, k,
+            dtype_code(h, "gemv_rmsnorm_swiglu"), stream_ptr(h.device)))
+        return out
+
     def add_rmsnorm(self, h, weight, out, eps):
         require_cuda(h, weight, out, what="allreduce_add_rmsnorm")
         if h.numel() != self.hidden:

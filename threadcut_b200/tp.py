@@ -124,7 +124,7 @@ def _attend_rope(layer, q, k, v, wq, wk, cos, sin, eps, scale):
 class _Shard:
     """One layer's weights on this rank."""
 
-    def __init__(self, layer, h0, h1, g, d, i0, i1, dev):
+    def __init__(self, layer, h0, h1, g, d, i0, i1, dev, interleave_gu=False):
         at, mlp = layer.self_attn, layer.mlp
 
         def rows(w, lo, hi):
@@ -141,7 +141,13 @@ class _Shard:
         self.k_norm = at.k_norm.weight.detach().to(dev)
         self.in_norm = layer.input_layernorm.weight.detach().to(dev)
         self.post_norm = layer.post_attention_layernorm.weight.detach().to(dev)
-        self.wgu = torch.cat((rows(mlp.gate_proj.weight, i0, i1), rows(mlp.up_proj.weight, i0, i1)))  # gate | up
+        gate, up = rows(mlp.gate_proj.weight, i0, i1), rows(mlp.up_proj.weight, i0, i1)
+        # gate | up, or interleaved (row 2i gate_i, row 2i + 1 up_i) for the projection whose
+        # epilogue computes the SwiGLU activation (tc_gemv_rmsnorm_swiglu)
+        self.gu_interleaved = interleave_gu
+        self.wgu = (torch.stack((gate, up), dim=1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
+                    if interleave_gu else torch.cat((gate, up)))
+        del gate, up
         self.wd = cols(mlp.down_proj.weight, i0, i1)
         for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
             if getattr(at, name).bias is not None:
@@ -180,7 +186,9 @@ class TPDecoder:
         v1 = cfg.vocab_size * (self.rank + 1) // self.world
         self.eps = cfg.rms_norm_eps
         base = model.model
-        self.layers_w = [_Shard(layer, self.h0, self.h1, self.g, self.d, i0, i1, self.dev) for layer in base.layers]
+        peer_capable = self.dev.type == "cuda" and base.embed_tokens.weight.dtype in (torch.bfloat16, torch.float16)
+        self.layers_w = [_Shard(layer, self.h0, self.h1, self.g, self.d, i0, i1, self.dev,
+                                interleave_gu=peer_sums and peer_capable) for layer in base.layers]
         self.embed = base.embed_tokens.weight.detach().to(self.dev)
         self.final_norm = base.norm.weight.detach().to(self.dev)
         self.lm_head = model.lm_head.weight.detach()[self.v0:v1].to(self.dev).contiguous()
@@ -278,7 +286,10 @@ class TPDecoder:
         for i, (w, layer) in enumerate(zip(self.layers_w, self.layers)):
             qkv = _gemv(x, w.wqkv)[0] if i == 0 else ar.gemv_norm(h, w.in_norm, w.wqkv, eps)[0]
             ar.gemv_residual(self._attention(w, layer, qkv, cos, sin), w.wo, h)
-            ar.gemv_residual(ar.gemv_norm(h, w.post_norm, w.wgu, eps), w.wd, h, swiglu=True)
+            if w.gu_interleaved:  # the SwiGLU activation from the gate/up projection's epilogue
+                ar.gemv_residual(ar.gemv_norm_swiglu(h, w.post_norm, w.wgu, eps)[0], w.wd, h)
+            else:
+                ar.gemv_residual(ar.gemv_norm(h, w.post_norm, w.wgu, eps), w.wd, h, swiglu=True)
         return ar.gemv_norm(h, self.final_norm, self.lm_head, eps)
 
     def _final_hidden(self, token, pos):
@@ -298,6 +309,8 @@ class TPDecoder:
             o = self._attention(w, layer, _gemv(x, w.wqkv)[0], cos, sin)
             self._sum_add_norm(o, w.wo, h, w.post_norm, x)
             gu = _gemv(x, w.wgu)
+            if w.gu_interleaved:  # [gate_0, up_0, gate_1, ...] -> [gate | up]
+                gu = gu.view(-1, 2).t().reshape(1, -1)
             self._sum_add_norm(gu, w.wd, h, norm_next, x, swiglu=True)
         return x
 
