@@ -408,6 +408,13 @@ def test_peer_sum_argument_validation_without_a_gpu():
     assert L.tc_gemv_rmsnorm(16, 16, 256, -1.0, 16, 16, 64, 2560, 2, None) == 1               # eps < 0
     assert L.tc_gemv_rmsnorm(8, 16, 256, 1e-6, 16, 16, 64, 2560, 2, None) == 2                # h misaligned
     assert L.tc_gemv_rmsnorm(16, 16, None, 1e-6, 16, 16, 64, 2560, 2, None) == 1              # no region
+    # the gate/up projection with the SwiGLU epilogue (interleaved rows: n even)
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 16, 16, 64, 2560, 0, None) == 3        # fp32: dtype
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 16, 16, 63, 2560, 2, None) == 1        # n odd
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 16, 16, 64, 2561, 2, None) == 1        # k % 8
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 24, 16, 64, 2560, 2, None) == 2        # w misaligned
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 16, None, 64, 2560, 2, None) == 1      # no output
+    assert L.tc_gemv_rmsnorm_swiglu(16, 16, 256, 1e-6, 16, 16, 0, 2560, 2, None) == 0         # nothing to do
 
 
 def test_peer_gather_argument_validation_without_a_gpu():
