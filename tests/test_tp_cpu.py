@@ -80,13 +80,18 @@ def _model():
     return AutoModelForCausalLM.from_config(cfg, dtype=torch.float32, attn_implementation="eager").eval()
 
 
-def _run(rank, world, n_ctx=20):
+def _run(rank, world, n_ctx=20, interleave=False):
     model = _model()
     ids = torch.randint(0, 512, (1, n_ctx + 1), generator=torch.Generator().manual_seed(1))
     with torch.no_grad():
         ref = model(input_ids=ids).logits[0, -1]  # logits after the last token, full context
         out = model(input_ids=ids[:, :n_ctx], use_cache=True)
         dec = tp.TPDecoder(model, "cpu", world=world, rank=rank, group=None)
+        if interleave:  # the GPU layout of gate|up (row 2i gate_i, row 2i + 1 up_i)
+            for w in dec.layers_w:
+                gate, up = w.wgu.chunk(2)
+                w.wgu = torch.stack((gate, up), dim=1).reshape(-1, gate.shape[1]).contiguous()
+                w.gu_interleaved = True
         for i, layer in enumerate(out.past_key_values.layers):
             dec.load(i, layer.keys, layer.values)
         assert dec.get_seq_length() == n_ctx
@@ -101,6 +106,15 @@ def _run(rank, world, n_ctx=20):
 def test_one_rank_equals_the_hf_forward(monkeypatch):
     _cpu_ops(monkeypatch.setattr)
     ref, logits, tok = _run(0, 1)
+    torch.testing.assert_close(logits, ref, atol=1e-4, rtol=0)
+    assert int(tok) == int(ref.argmax())
+
+
+def test_interleaved_gate_up_rows_on_the_separate_sums_path(monkeypatch):
+    """With the gate/up rows interleaved (as the GPU decoder stores them for the SwiGLU epilogue),
+    the separate-sums step de-interleaves the projection's output and still equals the HF forward."""
+    _cpu_ops(monkeypatch.setattr)
+    ref, logits, tok = _run(0, 1, interleave=True)
     torch.testing.assert_close(logits, ref, atol=1e-4, rtol=0)
     assert int(tok) == int(ref.argmax())
 
