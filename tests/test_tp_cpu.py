@@ -125,24 +125,24 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, interleave=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         _cpu_ops(setattr)
-        ref, logits, tok = _run(rank, world)
+        ref, logits, tok = _run(rank, world, interleave=interleave)
         err = float((logits - ref).abs().max())
         q.put((rank, err, int(tok), int(ref.argmax())))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_two_gloo_ranks_equal_the_hf_forward(world):
+@pytest.mark.parametrize("world,interleave", [(2, False), (2, True)])
+def test_two_gloo_ranks_equal_the_hf_forward(world, interleave):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, interleave)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
